@@ -1,0 +1,110 @@
+"""ctypes binding of ``libaceflow_cuda.so`` (include/aceflow_cuda.h).
+
+This is the Python twin of the Rust ``extern "C"`` block a maintainer adds to
+aceflow-core: every symbol is declared with its C signature, every status
+code is checked, and failures raise the exception type the reference raises
+for the same fault (``ValueError`` for shape errors, as PyO3's
+``PyValueError`` in aceflow-core/src/cpu/mod.rs; ``RuntimeError`` for CUDA
+errors).  There is no fallback: when the library is missing, every CUDA op
+raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("ACEFLOW_CUDA_LIB", os.path.join(_HERE, "lib", "libaceflow_cuda.so"))
+
+AF_OK, AF_ERR_ARG, AF_ERR_CUDA, AF_ERR_NCCL, AF_ERR_TIMEOUT, AF_ERR_STATE = range(6)
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_i64 = ctypes.c_int64
+_f = ctypes.c_float
+_sz = ctypes.c_size_t
+
+# name -> argtypes (all return int status unless listed in _RESTYPE)
+SIGNATURES = {
+    "af_abi_version": [],
+    "af_last_error": [],
+    "af_cuda_init": [_i, ctypes.POINTER(_vp)],
+    "af_cuda_destroy": [_vp],
+    "af_reserve_workspace": [_vp, _sz],
+    "af_launch_count": [_vp, ctypes.POINTER(_i64)],
+    "af_retention_step": [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i, _i, _i, _vp],
+    "af_retention_scan": [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp],
+    "af_rmsnorm_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp],
+    "af_rmsnorm_bf16": [_vp, _vp, _vp, _vp, _i, _i, _f, _vp],
+    "af_swiglu_packed_f32": [_vp, _vp, _vp, _i, _i, _vp],
+    "af_silu_mul_f32": [_vp, _vp, _vp, _vp, _i64, _vp],
+    "af_add_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _f, _vp],
+    "af_linear_f32": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
+    "af_msr_decode_step_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
+}
+_RESTYPE = {"af_last_error": ctypes.c_char_p}
+
+_lib = None
+_lock = threading.Lock()
+_contexts: dict[int, int] = {}
+
+
+class CudaLibraryMissing(RuntimeError):
+    pass
+
+
+def lib():
+    """Load the library once; raise if it is absent (no CPU fallback)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise CudaLibraryMissing(
+                        f"{LIB_PATH} is not built; run `python -m aceflow_b200.build` (needs nvcc)")
+                L = ctypes.CDLL(LIB_PATH)
+                for name, args in SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.argtypes = args
+                    fn.restype = _RESTYPE.get(name, ctypes.c_int)
+                _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    msg = lib().af_last_error()
+    return msg.decode() if msg else ""
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc == AF_OK:
+        return
+    msg = last_error() or what
+    if rc == AF_ERR_ARG:
+        raise ValueError(msg)
+    raise RuntimeError(f"[af status {rc}] {msg}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)
+
+
+def context(device_index: int) -> int:
+    """One af_ctx per device, created on first use (cached for the process)."""
+    ctx = _contexts.get(device_index)
+    if ctx is None:
+        with _lock:
+            ctx = _contexts.get(device_index)
+            if ctx is None:
+                p = ctypes.c_void_p()
+                check(lib().af_cuda_init(device_index, ctypes.byref(p)), "af_cuda_init")
+                ctx = p.value
+                _contexts[device_index] = ctx
+    return ctx
+
+
+def launch_count(device_index: int) -> int:
+    n = ctypes.c_int64()
+    check(lib().af_launch_count(context(device_index), ctypes.byref(n)))
+    return int(n.value)

@@ -1,0 +1,99 @@
+// Context, workspace and error plumbing of the C ABI (include/aceflow_cuda.h).
+#include "common.cuh"
+
+#include <new>
+
+namespace af {
+
+static thread_local char g_error[1024] = "";
+
+void set_error(const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+}
+
+int enter(af_ctx *ctx, const char *fn) {
+  if (ctx == nullptr || ctx->magic != kCtxMagic)
+    return fail(AF_ERR_STATE, "%s: invalid or destroyed af_ctx", fn);
+  int cur = -1;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: cudaGetDevice: %s", fn, cudaGetErrorString(e));
+  if (cur != ctx->device) {
+    e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: cudaSetDevice: %s", fn, cudaGetErrorString(e));
+  }
+  return AF_OK;
+}
+
+int workspace(af_ctx *ctx, size_t bytes, void **out, const char *fn) {
+  bytes = (bytes + 255) & ~size_t(255);
+  if (bytes > ctx->workspace_bytes) {
+    if (ctx->workspace) {
+      cudaError_t e = cudaFree(ctx->workspace);
+      ctx->workspace = nullptr;
+      ctx->workspace_bytes = 0;
+      if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: cudaFree(workspace): %s", fn, cudaGetErrorString(e));
+    }
+    cudaError_t e = cudaMalloc(&ctx->workspace, bytes);
+    if (e != cudaSuccess)
+      return fail(AF_ERR_CUDA, "%s: cudaMalloc(workspace, %zu): %s", fn, bytes, cudaGetErrorString(e));
+    ctx->workspace_bytes = bytes;
+  }
+  *out = ctx->workspace;
+  return AF_OK;
+}
+
+}  // namespace af
+
+extern "C" {
+
+int af_abi_version(void) { return 1; }
+
+const char *af_last_error(void) { return af::g_error; }
+
+int af_cuda_init(int device, af_ctx **out) {
+  if (out == nullptr) return af::fail(AF_ERR_ARG, "af_cuda_init: out is NULL");
+  *out = nullptr;
+  int n = 0;
+  AF_CUDA(cudaGetDeviceCount(&n), "af_cuda_init");
+  if (device < 0 || device >= n)
+    return af::fail(AF_ERR_ARG, "af_cuda_init: device %d out of range (%d devices)", device, n);
+  AF_CUDA(cudaSetDevice(device), "af_cuda_init");
+  cudaDeviceProp prop;
+  AF_CUDA(cudaGetDeviceProperties(&prop, device), "af_cuda_init");
+  if (prop.major != 10)
+    return af::fail(AF_ERR_ARG, "af_cuda_init: device %d is sm_%d%d; this library is built for sm_100a",
+                    device, prop.major, prop.minor);
+  af_ctx *ctx = new (std::nothrow) af_ctx();
+  if (!ctx) return af::fail(AF_ERR_ARG, "af_cuda_init: out of host memory");
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  ctx->magic = kCtxMagic;
+  *out = ctx;
+  return AF_OK;
+}
+
+int af_cuda_destroy(af_ctx *ctx) {
+  AF_ENTER(ctx, "af_cuda_destroy");
+  if (ctx->workspace) cudaFree(ctx->workspace);
+  ctx->magic = 0;
+  delete ctx;
+  return AF_OK;
+}
+
+int af_reserve_workspace(af_ctx *ctx, size_t bytes) {
+  AF_ENTER(ctx, "af_reserve_workspace");
+  void *p = nullptr;
+  return af::workspace(ctx, bytes, &p, "af_reserve_workspace");
+}
+
+int af_launch_count(af_ctx *ctx, int64_t *count) {
+  AF_ENTER(ctx, "af_launch_count");
+  if (!count) return af::fail(AF_ERR_ARG, "af_launch_count: count is NULL");
+  *count = ctx->launches;
+  return AF_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,95 @@
+// Shared host/device helpers for the sm_100a retention kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <cstdio>
+#include <cstdarg>
+
+#include "../../include/aceflow_cuda.h"
+
+struct af_ctx {
+  int device = 0;
+  int num_sms = 0;
+  uint32_t magic = 0;
+  void *workspace = nullptr;
+  size_t workspace_bytes = 0;
+  int64_t launches = 0;
+};
+
+constexpr uint32_t kCtxMagic = 0xACEF1011u;
+
+namespace af {
+
+// Thread-local message for af_last_error().
+void set_error(const char *fmt, ...);
+
+inline int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  set_error("%s", buf);
+  return code;
+}
+
+// Validates the context and makes its device current.
+int enter(af_ctx *ctx, const char *fn);
+
+// Grows the context workspace to at least `bytes` (256-byte aligned base).
+int workspace(af_ctx *ctx, size_t bytes, void **out, const char *fn);
+
+// Checks the launch that was just issued and counts it.
+inline int launched(af_ctx *ctx, const char *fn) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: launch failed: %s", fn, cudaGetErrorString(e));
+  ctx->launches++;
+  return AF_OK;
+}
+
+inline cudaStream_t stream_of(af_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace af
+
+#define AF_ENTER(ctx, fn)                       \
+  do {                                          \
+    int _rc = af::enter((ctx), (fn));           \
+    if (_rc != AF_OK) return _rc;               \
+  } while (0)
+
+#define AF_REQUIRE(cond, fn, ...)                                      \
+  do {                                                                 \
+    if (!(cond)) return af::fail(AF_ERR_ARG, fn ": " __VA_ARGS__);     \
+  } while (0)
+
+#define AF_CUDA(call, fn)                                                               \
+  do {                                                                                  \
+    cudaError_t _e = (call);                                                            \
+    if (_e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: %s: %s", fn, #call,        \
+                                           cudaGetErrorString(_e));                     \
+  } while (0)
+
+// ------------------------------------------------------------------ device
+__device__ __forceinline__ float4 ld_stream(const float4 *p) {
+  float4 v;
+  asm volatile("ld.global.cs.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void st_stream(float4 *p, float4 v) {
+  asm volatile("st.global.cs.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}

@@ -1,0 +1,187 @@
+"""Device-level ops: torch CUDA tensors in, C-ABI calls out.
+
+torch supplies device memory, the current stream and dtype bookkeeping;
+every byte of arithmetic runs in ``libaceflow_cuda.so``.  Each function
+validates what the C side cannot see (device, dtype, contiguity) and then
+makes exactly one ABI call on the tensor's current stream.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+F32 = torch.float32
+BF16 = torch.bfloat16
+
+
+def _dev(t: torch.Tensor) -> int:
+    if not t.is_cuda:
+        raise ValueError(f"expected a CUDA tensor, got device {t.device}")
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
+def _ctx(t: torch.Tensor) -> int:
+    return _lib.context(_dev(t))
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, dtype, name: str, contiguous: bool = True) -> None:
+    if t.dtype != dtype:
+        raise ValueError(f"{name}: expected {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name}: must be contiguous")
+
+
+def gammas(num_heads: int, device) -> torch.Tensor:
+    """gamma_h = 1 - 2^(-5-h) (aceflow/nn/retention.py:33), fp32 on `device`."""
+    return torch.tensor([1.0 - 2.0 ** (-5.0 - h) for h in range(num_heads)], dtype=F32, device=device)
+
+
+def retention_step(state: torch.Tensor, gamma: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """One recurrent step for B streams.  state [B,H,dh,dh] (or any layout with
+    a uniform stride between streams); q,k,v [B, H*dh] row views sharing a row
+    stride (e.g. slices of a packed [B, 3d] qkv)."""
+    B, H, dh, _ = state.shape
+    _need(gamma, F32, "gamma")
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        if t.dtype != F32 or t.dim() != 2 or t.shape[0] != B or t.shape[1] != H * dh or t.stride(1) != 1:
+            raise ValueError(f"{n}: expected fp32 [{B}, {H * dh}] rows with unit column stride")
+    if not (q.stride(0) == k.stride(0) == v.stride(0)):
+        raise ValueError("q, k, v must share one row stride")
+    if state.dtype != F32 or state.stride(3) != 1 or state.stride(2) != dh or state.stride(1) != dh * dh:
+        raise ValueError("state must be fp32 with each stream's [H, dh, dh] contiguous")
+    if out is None:
+        out = torch.empty(B, H * dh, dtype=F32, device=state.device)
+    _lib.call("af_retention_step", _ctx(state), _p(state), state.stride(0), _p(gamma), _p(q), _p(k), _p(v),
+              q.stride(0), _p(out), B, H, dh, _stream(state))
+    return out
+
+
+def retention_scan(state: torch.Tensor, gamma: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
+                   v: torch.Tensor) -> torch.Tensor:
+    """Token-serial retention over T tokens: q,k,v [B, T, H*dh] views with a
+    shared token stride; returns every token's output [B, T, H*dh]."""
+    B, H, dh, _ = state.shape
+    T = q.shape[1]
+    for n, t in (("q", q), ("k", k), ("v", v)):
+        if t.dtype != F32 or t.shape != (B, T, H * dh) or t.stride(2) != 1 or t.stride(0) != T * t.stride(1):
+            raise ValueError(f"{n}: expected fp32 [{B}, {T}, {H * dh}] with dense token rows")
+    if not (q.stride(1) == k.stride(1) == v.stride(1)):
+        raise ValueError("q, k, v must share one token stride")
+    if state.dtype != F32 or state.stride(3) != 1 or state.stride(2) != dh or state.stride(1) != dh * dh:
+        raise ValueError("state must be fp32 with each stream's [H, dh, dh] contiguous")
+    out = torch.empty(B, T, H * dh, dtype=F32, device=state.device)
+    _lib.call("af_retention_scan", _ctx(state), _p(state), state.stride(0), _p(gamma), _p(q), _p(k), _p(v),
+              q.stride(1), _p(out), B, T, H, dh, _stream(state))
+    return out
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: torch.Tensor | None = None,
+             sum_out: torch.Tensor | None = None) -> torch.Tensor:
+    d = x.shape[-1]
+    _need(w, F32, "weight")
+    if w.numel() != d:
+        raise ValueError(f"weight has {w.numel()} elements, expected {d}")
+    rows = x.numel() // d if d else 0
+    y = torch.empty_like(x)
+    if x.dtype == F32:
+        _need(x, F32, "x")
+        if residual is not None:
+            _need(residual, F32, "residual")
+            if residual.shape != x.shape:
+                raise ValueError("residual shape mismatch")
+        _lib.call("af_rmsnorm_f32", _ctx(x), _p(x), _p(residual), _p(w), _p(y), _p(sum_out), rows, d, float(eps),
+                  _stream(x))
+    elif x.dtype == BF16:
+        _need(x, BF16, "x")
+        if residual is not None:
+            raise ValueError("residual add is fp32-only")
+        _lib.call("af_rmsnorm_bf16", _ctx(x), _p(x), _p(w), _p(y), rows, d, float(eps), _stream(x))
+    else:
+        raise ValueError(f"rms_norm: unsupported dtype {x.dtype}")
+    return y
+
+
+def swiglu_packed(gate_up: torch.Tensor) -> torch.Tensor:
+    _need(gate_up, F32, "gate_up")
+    f = gate_up.shape[-1] // 2
+    rows = gate_up.numel() // (2 * f) if f else 0
+    h = torch.empty(*gate_up.shape[:-1], f, dtype=F32, device=gate_up.device)
+    _lib.call("af_swiglu_packed_f32", _ctx(gate_up), _p(gate_up), _p(h), rows, f, _stream(gate_up))
+    return h
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor | None = None) -> torch.Tensor:
+    _need(gate, F32, "gate")
+    if up is not None:
+        _need(up, F32, "up")
+        if up.shape != gate.shape:
+            raise ValueError("gate/up shape mismatch")
+    out = torch.empty_like(gate)
+    _lib.call("af_silu_mul_f32", _ctx(gate), _p(gate), _p(up), _p(out), gate.numel(), _stream(gate))
+    return out
+
+
+def add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a + b with b either a's shape or a trailing-dimension broadcast (bias)."""
+    _need(a, F32, "a")
+    _need(b, F32, "b")
+    if b.numel() == 0 or a.numel() % b.numel() != 0 or tuple(a.shape[a.dim() - b.dim():]) != tuple(b.shape):
+        raise ValueError(f"cannot broadcast {tuple(b.shape)} onto {tuple(a.shape)}")
+    out = torch.empty_like(a)
+    _lib.call("af_add_f32", _ctx(a), _p(a), _p(b), _p(out), a.numel(), b.numel(), 0.0, _stream(a))
+    return out
+
+
+def add_scalar(a: torch.Tensor, s: float) -> torch.Tensor:
+    _need(a, F32, "a")
+    out = torch.empty_like(a)
+    _lib.call("af_add_f32", _ctx(a), _p(a), None, _p(out), a.numel(), 1, float(s), _stream(a))
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """x [..., K] . W[N, K]^T (+ bias[N]) in fp32."""
+    _need(x, F32, "x")
+    _need(w, F32, "weight")
+    K = x.shape[-1]
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"weight shape {tuple(w.shape)} does not match input features {K}")
+    if bias is not None:
+        _need(bias, F32, "bias")
+        if bias.numel() != N:
+            raise ValueError("bias size mismatch")
+    M = x.numel() // K
+    y = torch.empty(*x.shape[:-1], N, dtype=F32, device=x.device)
+    _lib.call("af_linear_f32", _ctx(x), _p(x), _p(w), _p(bias), _p(y), M, N, K, _stream(x))
+    return y
+
+
+def msr_decode_step(x: torch.Tensor, state: torch.Tensor, gamma: torch.Tensor, w_qkv: torch.Tensor,
+                    w_o: torch.Tensor, ret_norm_w: torch.Tensor, eps: float,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused MSR decode step (af_msr_decode_step_f32): x [B, d] -> [B, d]."""
+    B, d = x.shape
+    H = state.shape[1]
+    for n, t in (("x", x), ("state", state), ("gamma", gamma), ("w_qkv", w_qkv), ("w_o", w_o),
+                 ("ret_norm_w", ret_norm_w)):
+        _need(t, F32, n)
+    if tuple(state.shape) != (B, H, d // H, d // H):
+        raise ValueError(f"state shape {tuple(state.shape)} != {(B, H, d // H, d // H)}")
+    if tuple(w_qkv.shape) != (3 * d, d) or tuple(w_o.shape) != (d, d):
+        raise ValueError("w_qkv must be [3d, d] and w_o [d, d]")
+    if out is None:
+        out = torch.empty(B, d, dtype=F32, device=x.device)
+    _lib.call("af_msr_decode_step_f32", _ctx(x), _p(x), _p(state), _p(gamma), _p(w_qkv), _p(w_o), _p(ret_norm_w),
+              float(eps), B, d, H, _p(out), _stream(x))
+    return out

@@ -1,0 +1,151 @@
+"""MultiScaleRetention (mirrors aceflow/nn/retention.py:15-69).
+
+Same constructor, parameters (w_q, w_k, w_v, w_o, ret_norm) and seeded
+initialisation order as the reference, so a seeded script builds identical
+weights.  Semantics per head h (retention.py:33,51-61; recurrence.rs:28-39):
+
+    gamma_h = 1 - 2^(-5-h)
+    parallel:   O = (Q K^T * D) V,  D[i,j] = gamma^(i-j) for i >= j
+    recurrent:  S = gamma S + k^T v;  o = q S  (updated S)
+    then RMSNorm over d_model (eps 1e-6) and @ W_o^T.
+
+Methods:
+  forward / forward_parallel(x [B,T,d]) -> [B,T,d]   (reference API)
+  forward_recurrent(x_t [B,d], state) -> (out, state) (promised by the
+      reference docstring, retention.py:22, absent there)
+  forward_chunkwise(x, chunk, state) -> (out, state)
+  init_state(batch) -> zero state [B, H, dh, dh] fp32
+
+On CUDA: fp32 inputs run the exact fp32 kernels (projection GEMM, state
+scan / step, fused RMSNorm); the fused decode step is one ABI call.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import numpy as np
+
+from ..core.tensor import Tensor
+from .layers import RMSNorm
+from .module import Module, Parameter
+
+
+class MultiScaleRetention(Module):
+    """Multi-Scale Retention (MSR) layer."""
+
+    def __init__(self, d_model: int, num_heads: int):
+        super().__init__()
+        if num_heads <= 0 or d_model % num_heads != 0:
+            raise ValueError(f"d_model ({d_model}) must be divisible by num_heads ({num_heads})")
+        self.d_model = d_model
+        self.num_heads = num_heads
+        self.head_dim = d_model // num_heads
+        self.gamma = np.array([1.0 - 2.0 ** (-5.0 - h) for h in range(num_heads)], dtype=np.float32)
+        k = 1.0 / math.sqrt(d_model)
+        self.w_q = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
+        self.w_k = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
+        self.w_v = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
+        self.w_o = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
+        self.ret_norm = RMSNorm(d_model)
+        self._dev = None  # packed device weights
+
+    # ------------------------------------------------------------ device pack
+    def _on_device(self) -> None:
+        self._dev = None
+        if self.w_q.device.is_cuda:
+            import torch
+
+            from .. import cuda_ops
+
+            dev = self.w_q.torch.device
+            self._dev = dict(
+                w_qkv=torch.cat([self.w_q.torch, self.w_k.torch, self.w_v.torch], 0).contiguous(),
+                w_o=self.w_o.torch,
+                gamma=cuda_ops.gammas(self.num_heads, dev),
+            )
+
+    def _packed(self, x: Tensor) -> dict:
+        if self._dev is None:
+            self._on_device()
+        if self._dev is None or self._dev["w_o"].device != x.torch.device:
+            raise ValueError(f"module weights are on {self.w_q.device}, input on {x.device}; call .to(device)")
+        return self._dev
+
+    def init_state(self, batch: int, device=None) -> Tensor:
+        """Zero recurrent state [batch, H, dh, dh] fp32 (AceEngine.reset_memory,
+        aceflow-core/src/cpu/mod.rs:115-117)."""
+        dev = self.w_q.device if device is None else device
+        return Tensor.zeros([batch, self.num_heads, self.head_dim, self.head_dim], dev)
+
+    # ------------------------------------------------------------ forward
+    def forward_parallel(self, x: Tensor) -> Tensor:
+        if x.device.is_cuda:
+            out, _ = self.forward_chunkwise(x)
+            return out
+        arr = x.numpy()
+        b, n, d = arr.shape
+        H, hd = self.num_heads, self.head_dim
+        q = np.matmul(arr, self.w_q.numpy().T).reshape(b, n, H, hd).transpose(0, 2, 1, 3)
+        k = np.matmul(arr, self.w_k.numpy().T).reshape(b, n, H, hd).transpose(0, 2, 1, 3)
+        v = np.matmul(arr, self.w_v.numpy().T).reshape(b, n, H, hd).transpose(0, 2, 1, 3)
+        idx = np.arange(n)
+        dist = idx[:, None] - idx[None, :]
+        decay = np.zeros((H, n, n), dtype=np.float32)
+        for h in range(H):
+            decay[h] = np.where(dist >= 0, self.gamma[h] ** dist, 0.0)
+        out = np.matmul(np.matmul(q, k.transpose(0, 1, 3, 2)) * decay[None], v)
+        out = out.transpose(0, 2, 1, 3).reshape(b, n, d)
+        normed = self.ret_norm(Tensor(out, x.device))
+        return Tensor(np.matmul(normed.numpy(), self.w_o.numpy().T), x.device)
+
+    def forward(self, x: Tensor) -> Tensor:
+        return self.forward_parallel(x)
+
+    def forward_chunkwise(self, x: Tensor, chunk: int = 64,
+                          state: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
+        """Prefill x [B, T, d] from `state` (zeros if None); returns the layer
+        output and the state after the last token."""
+        B, T, d = x.shape
+        if state is None:
+            state = self.init_state(B, x.device)
+        if not x.device.is_cuda:
+            outs = []
+            for t in range(T):
+                o, state = self.forward_recurrent(Tensor(x.numpy()[:, t]), state)
+                outs.append(o.numpy())
+            return Tensor(np.stack(outs, 1), x.device), state
+        from .. import cuda_ops
+
+        p = self._packed(x)
+        st = state.torch
+        if x.torch.dtype != st.dtype:
+            raise ValueError("bfloat16 prefill is served by the tensor-core chunkwise kernel")
+        qkv = cuda_ops.linear(x.torch.reshape(B * T, d), p["w_qkv"]).reshape(B, T, 3 * d)
+        o = cuda_ops.retention_scan(st, p["gamma"], qkv[:, :, :d], qkv[:, :, d:2 * d], qkv[:, :, 2 * d:])
+        normed = cuda_ops.rms_norm(o, self.ret_norm.weight.torch, self.ret_norm.eps)
+        out = cuda_ops.linear(normed, p["w_o"])
+        return Tensor._wrap(out, x.device), state
+
+    def forward_recurrent(self, x_t: Tensor, state: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
+        """One decode step for B streams: x_t [B, d] -> ([B, d], state)."""
+        B, d = x_t.shape
+        if state is None:
+            state = self.init_state(B, x_t.device)
+        if x_t.device.is_cuda:
+            from .. import cuda_ops
+
+            p = self._packed(x_t)
+            out = cuda_ops.msr_decode_step(x_t.torch, state.torch, p["gamma"], p["w_qkv"], p["w_o"],
+                                           self.ret_norm.weight.torch, self.ret_norm.eps)
+            return Tensor._wrap(out, x_t.device), state
+        H, hd = self.num_heads, self.head_dim
+        arr = x_t.numpy()
+        q = (arr @ self.w_q.numpy().T).reshape(B, H, hd)
+        k = (arr @ self.w_k.numpy().T).reshape(B, H, hd)
+        v = (arr @ self.w_v.numpy().T).reshape(B, H, hd)
+        S = state.numpy()
+        S = self.gamma[None, :, None, None] * S + k[:, :, :, None] * v[:, :, None, :]
+        o = np.einsum("bhi,bhij->bhj", q, S).reshape(B, d).astype(np.float32)
+        normed = self.ret_norm(Tensor(o, x_t.device))
+        return Tensor(normed.numpy() @ self.w_o.numpy().T, x_t.device), Tensor(S.astype(np.float32), x_t.device)

@@ -1,0 +1,137 @@
+/*
+ * aceflow_cuda.h — C ABI of the B200 (sm_100a) retention hot path.
+ *
+ * This is the drop-in boundary under AceFlow's af.nn.MultiScaleRetention /
+ * Linear / RMSNorm / SwiGLU, af.ops and AceEngine APIs.  Each entry point
+ * names the reference interface it replaces (paths relative to the
+ * 42Wor/aceflow checkout).  A Rust `extern "C"` block, a PyO3 method or a
+ * Python ctypes stub binds these symbols directly.
+ *
+ * Conventions
+ *  - Every pointer argument except `af_ctx*` and host-side parameters is a
+ *    DEVICE pointer on the context's device, owned by the caller.  The
+ *    library never frees caller memory.
+ *  - Matrices are row-major and contiguous unless a stride argument says
+ *    otherwise.  Weights use the PyTorch (out, in) layout that the reference
+ *    uses (aceflow/nn/layers.py:19-20, aceflow-core/src/nn/mod.rs:34-39).
+ *  - `af_stream_t` is a cudaStream_t (NULL = the legacy default stream).
+ *    Every call is asynchronous on that stream.
+ *  - Every call returns an af_status.  On failure, af_last_error() gives a
+ *    message for the calling thread.  No exception crosses the ABI.  Shape
+ *    errors are the analogue of the reference's PyValueError
+ *    (aceflow-core/src/cpu/mod.rs:64-68,188-238,615-644).
+ *  - Scratch memory comes from the context's workspace, grown on first use
+ *    (af_reserve_workspace() sizes it up front, e.g. before graph capture).
+ *  - One context per device per host thread.
+ */
+#ifndef ACEFLOW_CUDA_H_
+#define ACEFLOW_CUDA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  AF_OK = 0,
+  AF_ERR_ARG = 1,     /* bad shape, null pointer, unsupported size */
+  AF_ERR_CUDA = 2,    /* a CUDA runtime/driver call failed */
+  AF_ERR_NCCL = 3,    /* reserved for collective calls */
+  AF_ERR_TIMEOUT = 4, /* a bounded device-side wait gave up */
+  AF_ERR_STATE = 5    /* context misuse (wrong device, destroyed context) */
+} af_status;
+
+typedef struct af_ctx af_ctx;
+typedef void *af_stream_t;
+
+/* ------------------------------------------------------------------ context */
+int af_abi_version(void);
+const char *af_last_error(void);
+/* Creates a context on `device` (no reference counterpart: the reference's
+ * CPU engine needs none; its GPU context is wgpu/context.rs:54-91). */
+int af_cuda_init(int device, af_ctx **ctx);
+int af_cuda_destroy(af_ctx *ctx);
+int af_reserve_workspace(af_ctx *ctx, size_t bytes);
+/* Number of this library's kernel launches issued through `ctx` so far. */
+int af_launch_count(af_ctx *ctx, int64_t *count);
+
+/* ------------------------------------------------------------- retention */
+/* Recurrent retention step for `batch` independent streams.
+ * Replaces retention_step_core (aceflow-core/src/cpu/recurrence.rs:3-42) as
+ * called by AceEngine.retention_step / retention_step_packed
+ * (aceflow-core/src/cpu/mod.rs:486-545).
+ *   state  [batch][num_heads][head_dim][head_dim] fp32, updated in place;
+ *          consecutive streams are `state_batch_stride` floats apart.
+ *   q,k,v  row b at q + b*qkv_row_stride (fp32), head h at h*head_dim.
+ *   out    [batch][num_heads*head_dim] fp32 (o = q . S with the UPDATED S).
+ * Any head_dim; multiples of 4 up to 1024 take the vectorised kernel. */
+int af_retention_step(af_ctx *ctx, float *state, int64_t state_batch_stride, const float *gamma,
+                      const float *q, const float *k, const float *v, int64_t qkv_row_stride,
+                      float *out, int batch, int num_heads, int head_dim, af_stream_t stream);
+
+/* Token-serial retention over T tokens for `batch` streams; writes every
+ * token's output.  Replaces AceEngine.prefill_recurrent
+ * (aceflow-core/src/cpu/mod.rs:547-587), which returns only the last row.
+ *   q,k,v  token t of stream b at (b*T + t)*qkv_row_stride.
+ *   out    [batch][T][num_heads*head_dim]. */
+int af_retention_scan(af_ctx *ctx, float *state, int64_t state_batch_stride, const float *gamma,
+                      const float *q, const float *k, const float *v, int64_t qkv_row_stride,
+                      float *out, int batch, int T, int num_heads, int head_dim,
+                      af_stream_t stream);
+
+/* ----------------------------------------------------------- norms, FFN */
+/* y = x / sqrt(mean(x^2) + eps) * w over rows of length d.
+ * Replaces RMSNorm.forward / ops.rms_norm (aceflow/nn/layers.py:45-49,
+ * aceflow/ops/functional.py:18-25) and rmsnorm_core
+ * (aceflow-core/src/cpu/norm.rs:6-59).  If `residual` is non-NULL the input
+ * is x + residual, which is also written to `sum_out` when that is non-NULL
+ * (the pre-norm residual add of cpu/mod.rs:679-683). */
+int af_rmsnorm_f32(af_ctx *ctx, const float *x, const float *residual, const float *w, float *y,
+                   float *sum_out, int rows, int d, float eps, af_stream_t stream);
+/* Same on bf16 rows (fp32 math, bf16 out); w stays fp32. */
+int af_rmsnorm_bf16(af_ctx *ctx, const uint16_t *x, const float *w, uint16_t *y, int rows, int d,
+                    float eps, af_stream_t stream);
+
+/* hidden = silu(gate) * up with gate_up packed [rows][2f], gate first.
+ * Replaces swiglu_forward (aceflow-core/src/cpu/swiglu.rs:4-18). */
+int af_swiglu_packed_f32(af_ctx *ctx, const float *gate_up, float *hidden, int rows, int f,
+                         af_stream_t stream);
+/* out = silu(gate) * up elementwise (ops.silu when up == NULL,
+ * aceflow/ops/functional.py:44-46; SwiGLU.forward's product, layers.py:83-87). */
+int af_silu_mul_f32(af_ctx *ctx, const float *gate, const float *up, float *out, int64_t n,
+                    af_stream_t stream);
+
+/* out = a + b (b repeats every b_period elements: the bias broadcast of
+ * Tensor + bias, aceflow/core/tensor.py:104-118) or a + scalar if b == NULL. */
+int af_add_f32(af_ctx *ctx, const float *a, const float *b, float *out, int64_t n, int64_t b_period,
+               float scalar, af_stream_t stream);
+
+/* ----------------------------------------------------------------- GEMM */
+/* y[M][N] = x[M][K] . W[N][K]^T (+ bias[N]), fp32 in/out with fp32-accurate
+ * accumulation.  Replaces Linear.forward (aceflow/nn/layers.py:29-33) ->
+ * Tensor::matmul (aceflow-core/src/tensor/mod.rs:182-196) and gemv /
+ * batched_gemv (aceflow-core/src/cpu/gemv.rs:164-194). */
+int af_linear_f32(af_ctx *ctx, const float *x, const float *w, const float *bias, float *y, int M,
+                  int N, int K, af_stream_t stream);
+
+/* ------------------------------------------------------- fused MSR layer */
+/* One recurrent decode step of a MultiScaleRetention layer for `batch`
+ * streams: qkv = x W_qkv^T; retention step; RMSNorm(eps, ret_norm_w) over
+ * d_model; out = normed W_o^T.  The recurrent counterpart of
+ * MultiScaleRetention.forward_parallel (aceflow/nn/retention.py:44-66), i.e.
+ * AceEngine.forward_layer_internal's retention half
+ * (aceflow-core/src/cpu/mod.rs:651-678).
+ *   x [batch][d] fp32; w_qkv [3d][d] (rows q, k, v); w_o [d][d];
+ *   state [batch][H][d/H][d/H] fp32 in place; out [batch][d] fp32.
+ * Uses workspace scratch of (4*d + H) * batch floats. */
+int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state, const float *gamma,
+                           const float *w_qkv, const float *w_o, const float *ret_norm_w,
+                           float eps, int batch, int d_model, int num_heads, float *out,
+                           af_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ACEFLOW_CUDA_H_ */

@@ -1,0 +1,72 @@
+"""The C-ABI library loads and exports every symbol the headers declare.
+
+No compute call is made (no GPU here); af_cuda_init on a machine without a
+GPU must fail cleanly with a status, not crash.
+"""
+import ctypes
+import glob
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADERS = sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
+
+
+def declared_symbols():
+    names = set()
+    for h in HEADERS:
+        text = open(h).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        for m in re.finditer(r"^\s*(?:const\s+)?(?:int|void|char|size_t)\s*\*?\s*(af_\w+)\s*\(", text, re.M):
+            names.add(m.group(1))
+    return names
+
+
+@pytest.fixture(scope="module")
+def libpath():
+    from aceflow_b200 import build
+
+    return build.build()
+
+
+def test_headers_declare_entry_points():
+    names = declared_symbols()
+    assert "af_msr_decode_step_f32" in names and "af_retention_step" in names
+    assert len(names) >= 10
+
+
+def test_library_exports_every_declared_symbol(libpath):
+    out = subprocess.run(["nm", "-D", "--defined-only", libpath], capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    missing = declared_symbols() - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+    lib = ctypes.CDLL(libpath)
+    for name in declared_symbols():
+        assert hasattr(lib, name)
+
+
+def test_python_binding_covers_header(libpath):
+    from aceflow_b200 import _lib
+
+    assert declared_symbols() == set(_lib.SIGNATURES), "ctypes declarations must match the header"
+
+
+def test_library_has_no_torch_dependency(libpath):
+    out = subprocess.run(["ldd", libpath], capture_output=True, text=True).stdout
+    assert "torch" not in out and "libc10" not in out
+
+
+def test_init_without_gpu_fails_cleanly(libpath):
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from aceflow_b200 import _lib
+
+    p = ctypes.c_void_p()
+    rc = _lib.lib().af_cuda_init(0, ctypes.byref(p))
+    assert rc != 0 and not p.value
+    assert _lib.last_error()
