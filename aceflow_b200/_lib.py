@@ -33,6 +33,7 @@ SIGNATURES = {
     "af_cuda_destroy": [_vp],
     "af_reserve_workspace": [_vp, _sz],
     "af_launch_count": [_vp, ctypes.POINTER(_i64)],
+    "af_check_device": [_vp, ctypes.POINTER(_i), _i],
     "af_retention_step": [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i, _i, _i, _vp],
     "af_retention_scan": [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp],
     "af_rmsnorm_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp],
@@ -41,7 +42,10 @@ SIGNATURES = {
     "af_silu_mul_f32": [_vp, _vp, _vp, _vp, _i64, _vp],
     "af_add_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _f, _vp],
     "af_linear_f32": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
+    "af_linear_bf16": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "af_msr_decode_step_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
+    "af_retention_chunkwise_bf16": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
+    "af_msr_prefill_bf16": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp],
 }
 _RESTYPE = {"af_last_error": ctypes.c_char_p}
 
@@ -102,6 +106,13 @@ def context(device_index: int) -> int:
                 ctx = p.value
                 _contexts[device_index] = ctx
     return ctx
+
+
+def check_device(device_index: int, reset: bool = True) -> int:
+    """Synchronises and raises if a device-side bounded wait timed out."""
+    flags = ctypes.c_int()
+    check(lib().af_check_device(context(device_index), ctypes.byref(flags), int(reset)), "af_check_device")
+    return int(flags.value)
 
 
 def launch_count(device_index: int) -> int:

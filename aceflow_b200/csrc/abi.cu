@@ -70,6 +70,12 @@ int af_cuda_init(int device, af_ctx **out) {
   if (!ctx) return af::fail(AF_ERR_ARG, "af_cuda_init: out of host memory");
   ctx->device = device;
   ctx->num_sms = prop.multiProcessorCount;
+  cudaError_t e = cudaMalloc(&ctx->dev_err, 256);
+  if (e == cudaSuccess) e = cudaMemset(ctx->dev_err, 0, 256);
+  if (e != cudaSuccess) {
+    delete ctx;
+    return af::fail(AF_ERR_CUDA, "af_cuda_init: device error word: %s", cudaGetErrorString(e));
+  }
   ctx->magic = kCtxMagic;
   *out = ctx;
   return AF_OK;
@@ -78,6 +84,7 @@ int af_cuda_init(int device, af_ctx **out) {
 int af_cuda_destroy(af_ctx *ctx) {
   AF_ENTER(ctx, "af_cuda_destroy");
   if (ctx->workspace) cudaFree(ctx->workspace);
+  if (ctx->dev_err) cudaFree(ctx->dev_err);
   ctx->magic = 0;
   delete ctx;
   return AF_OK;
@@ -87,6 +94,17 @@ int af_reserve_workspace(af_ctx *ctx, size_t bytes) {
   AF_ENTER(ctx, "af_reserve_workspace");
   void *p = nullptr;
   return af::workspace(ctx, bytes, &p, "af_reserve_workspace");
+}
+
+int af_check_device(af_ctx *ctx, int *flags, int reset) {
+  AF_ENTER(ctx, "af_check_device");
+  int h = 0;
+  AF_CUDA(cudaMemcpy(&h, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost), "af_check_device");
+  if (reset && h) AF_CUDA(cudaMemset(ctx->dev_err, 0, sizeof(int)), "af_check_device");
+  if (flags) *flags = h;
+  if (h & (1 << AF_ERR_TIMEOUT))
+    return af::fail(AF_ERR_TIMEOUT, "af_check_device: a device-side wait timed out (flags 0x%x)", h);
+  return AF_OK;
 }
 
 int af_launch_count(af_ctx *ctx, int64_t *count) {

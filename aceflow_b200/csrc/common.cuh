@@ -16,6 +16,7 @@ struct af_ctx {
   void *workspace = nullptr;
   size_t workspace_bytes = 0;
   int64_t launches = 0;
+  int *dev_err = nullptr;  // device error word: bit AF_ERR_TIMEOUT set by bounded waits
 };
 
 constexpr uint32_t kCtxMagic = 0xACEF1011u;
@@ -48,6 +49,24 @@ inline int launched(af_ctx *ctx, const char *fn) {
   ctx->launches++;
   return AF_OK;
 }
+
+// Epilogue of the tensor-core GEMM (gemm_tc.cu).
+struct GemmEpilogueArgs {
+  void *out = nullptr;
+  int64_t ldo = 0;
+  int out_bf16 = 0;
+  const float *bias = nullptr;
+  const float *row_parts = nullptr;  // per-row partial sums of squares -> 1/rms scale
+  int nparts = 0;
+  float inv_d = 0.f, eps = 0.f;
+  const float *residual = nullptr;  // fp32 [M][ldr] added after scaling
+  int64_t ldr = 0;
+  int swiglu = 0;  // (16 gate, 16 up) column groups -> silu(g)*u, N/2 outputs
+};
+
+bool tc_gemm_ok(const void *A, int64_t lda, const void *B, int64_t ldb, int K, bool fp32);
+int tc_gemm(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, bool fp32,
+            const GemmEpilogueArgs &a, cudaStream_t st, const char *fn);
 
 inline cudaStream_t stream_of(af_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -74,6 +74,27 @@ int launch_sgemm_nt(af_ctx *ctx, const float *x, const float *w, const float *bi
   sgemm_nt_kernel<<<grid, 256, 0, st>>>(x, w, bias, y, M, N, K, parts, nparts, inv_d, eps);
   return launched(ctx, fn);
 }
+// fp32 GEMM dispatch: the 3xTF32 tensor-core kernel when the operands meet
+// TMA's alignment rules, else the SIMT kernel.  Optional fused row scale.
+int linear_f32(af_ctx *ctx, const float *x, int64_t ldx, const float *w, int64_t ldw, const float *bias, float *y,
+               int64_t ldy, int M, int N, int K, const float *parts, int nparts, float inv_d, float eps,
+               cudaStream_t st, const char *fn) {
+  if (M == 0 || N == 0) return AF_OK;
+  if (tc_gemm_ok(x, ldx, w, ldw, K, true) && M <= 65535 * 128) {
+    GemmEpilogueArgs ep;
+    ep.out = y;
+    ep.ldo = ldy;
+    ep.bias = bias;
+    ep.row_parts = parts;
+    ep.nparts = nparts;
+    ep.inv_d = inv_d;
+    ep.eps = eps;
+    return tc_gemm(ctx, x, ldx, w, ldw, M, N, K, true, ep, st, fn);
+  }
+  if (ldx != K || ldw != K || ldy != N) return fail(AF_ERR_ARG, "%s: strided operands need 16-byte alignment", fn);
+  return launch_sgemm_nt(ctx, x, w, bias, y, M, N, K, parts, nparts, inv_d, eps, st, fn);
+}
+
 }  // namespace af
 
 extern "C" int af_linear_f32(af_ctx *ctx, const float *x, const float *w, const float *bias, float *y, int M, int N,
@@ -83,5 +104,22 @@ extern "C" int af_linear_f32(af_ctx *ctx, const float *x, const float *w, const 
   AF_REQUIRE(x && w && y, "af_linear_f32", "null pointer");
   AF_REQUIRE(M >= 0 && N >= 0 && K > 0, "af_linear_f32", "bad sizes M=%d N=%d K=%d", M, N, K);
   AF_REQUIRE(M <= 65535 * 64, "af_linear_f32", "M=%d too large", M);
-  return af::launch_sgemm_nt(ctx, x, w, bias, y, M, N, K, nullptr, 0, 0.f, 0.f, af::stream_of(stream), fn);
+  return af::linear_f32(ctx, x, K, w, K, bias, y, N, M, N, K, nullptr, 0, 0.f, 0.f, af::stream_of(stream), fn);
+}
+
+extern "C" int af_linear_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w, const float *bias, void *y,
+                              int y_bf16, int M, int N, int K, af_stream_t stream) {
+  const char *fn = "af_linear_bf16";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(x && w && y, "af_linear_bf16", "null pointer");
+  AF_REQUIRE(M >= 0 && N >= 0 && K > 0, "af_linear_bf16", "bad sizes M=%d N=%d K=%d", M, N, K);
+  AF_REQUIRE(af::tc_gemm_ok(x, K, w, K, K, false), "af_linear_bf16",
+             "K=%d must be a multiple of 8 and x, W 16-byte aligned", K);
+  AF_REQUIRE(M <= 65535 * 128, "af_linear_bf16", "M=%d too large", M);
+  af::GemmEpilogueArgs ep;
+  ep.out = y;
+  ep.ldo = N;
+  ep.out_bf16 = y_bf16;
+  ep.bias = bias;
+  return af::tc_gemm(ctx, x, K, w, K, M, N, K, false, ep, af::stream_of(stream), fn);
 }

@@ -1,0 +1,373 @@
+// Tensor-core GEMM for sm_100a:  C[M][N] = A[M][K] . B[N][K]^T  (+ epilogue)
+//
+// Both operands K-major (the PyTorch (out, in) weight layout the reference
+// uses, aceflow/nn/layers.py:19-20), accumulated in fp32 in TMEM.
+//
+// CTA = 6 warps, one 128 x BN output tile:
+//   warp 0      TMA producer: A and B K-slices (128-byte rows, 128B swizzle)
+//               into a STAGES-deep shared-memory ring, mbarrier complete_tx.
+//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN) and
+//               tcgen05.commit frees each ring slot when its MMAs retire.
+//   warps 2-5   TF32x3 mode: split each fp32 slice in place into an exact
+//               tf32 hi part and lo = x - hi; then the epilogue: tcgen05.ld of the 128 x BN
+//               accumulator (warp w reads TMEM lanes 32*(w%4)..+31), fused
+//               row scale / bias / residual / SwiGLU, vector stores.
+//
+// Modes:
+//   BF16   : kind::f16 with bf16 operands (prefill projections).
+//   TF32X3 : fp32 operands; acc += A.B + A.B_lo + A_lo.B with kind::tf32 -
+//            the three-term split of Ootomo & Yokota (2022) that restores
+//            fp32 accuracy (~2^-21 relative) on the tensor cores (decode
+//            projections, parity 1e-4 against the fp32 reference).
+//
+// Every mbarrier wait is bounded; a timeout sets the context's device error
+// word (AF_ERR_TIMEOUT) and the CTA drains and frees its TMEM.
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace {
+
+using namespace sm100;
+
+struct GemmEpilogue {
+  void *out;
+  int64_t ldo;
+  int out_bf16;
+  const float *bias;       // [N] or null
+  const float *row_parts;  // [M][nparts] sums of squares, or null
+  int nparts;
+  float inv_d, eps;
+  const float *residual;   // [M][ldr] fp32 added to the result, or null
+  int64_t ldr;
+  int swiglu;              // columns in groups of 16 gate then 16 up -> N/2 outputs
+  int vec_ok;              // out base 16-byte aligned and ldo a whole number of 16-byte units
+};
+
+template <int BN, bool TF32X3>
+struct TileCfg {
+  static constexpr int BM = 128;
+  static constexpr int ELEM = TF32X3 ? 4 : 2;
+  static constexpr int BK = 128 / ELEM;          // one 128-byte swizzle row per K slice
+  static constexpr int UK = 32 / ELEM;           // K per tcgen05.mma (32 bytes)
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = TF32X3 ? 2 * (A_BYTES + B_BYTES) : (A_BYTES + B_BYTES);
+  static constexpr int STAGES = (TF32X3 ? 192 * 1024 : 200 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+  static_assert((BN & (BN - 1)) == 0, "TMEM allocation is a power of two");
+  static_assert(STAGES >= 2, "pipeline depth");
+};
+
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+
+template <int BN, bool TF32X3>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+                     int K, GemmEpilogue ep, int *err) {
+  using C = TileCfg<BN, TF32X3>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)C::STAGES * C::STAGE_BYTES);
+  uint64_t *full = bars;                    // TMA landed
+  uint64_t *conv = bars + C::STAGES;        // lo parts written (TF32X3)
+  uint64_t *empty = bars + 2 * C::STAGES;   // MMAs retired
+  uint64_t *accum = bars + 3 * C::STAGES;   // accumulator complete
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * C::STAGES + 1);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * C::BM, n0 = blockIdx.x * BN;
+  const int nk = (K + C::BK - 1) / C::BK;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto stage_a = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES; };
+  auto stage_b = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + C::A_BYTES; };
+  auto stage_alo = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + C::A_BYTES + C::B_BYTES; };
+  auto stage_blo = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES; };
+  auto fail = [&]() {
+    s_abort = 1;
+    atomicOr(err, 1 << AF_ERR_TIMEOUT);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nk && !s_abort; ++kb) {
+        const int s = kb % C::STAGES;
+        const uint32_t ph = (kb / C::STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1)) { fail(); break; }
+        mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
+        tma_load_2d(stage_a(s), &tmA, &full[s], kb * C::BK, m0);
+        tma_load_2d(stage_b(s), &tmB, &full[s], kb * C::BK, n0);
+        issued = kb + 1;
+      }
+      // drain: every issued load has landed before this CTA may exit
+      for (int kb = issued - C::STAGES < 0 ? 0 : issued - C::STAGES; kb < issued; ++kb)
+        if (!mbar_wait(&full[kb % C::STAGES], (kb / C::STAGES) & 1)) { fail(); break; }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc = idesc_f32acc(TF32X3 ? kFmtTF32 : kFmtBF16, C::BM, BN);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % C::STAGES;
+      const uint32_t ph = (kb / C::STAGES) & 1;
+      if (!mbar_wait(TF32X3 ? &conv[s] : &full[s], ph)) {
+        if (lane == 0) fail();
+        break;
+      }
+      if (s_abort) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint64_t da = sdesc_k_sw128(stage_a(s)), db = sdesc_k_sw128(stage_b(s));
+#pragma unroll
+        for (int k = 0; k < C::BK / C::UK; ++k) {
+          const uint64_t off = (uint64_t)(k * 32) >> 4;  // 32 bytes along K inside the swizzle row
+          if constexpr (TF32X3) {
+            const uint64_t dal = sdesc_k_sw128(stage_alo(s)), dbl = sdesc_k_sw128(stage_blo(s));
+            umma_tf32(tmem, da + off, db + off, idesc, (kb | k) != 0);
+            umma_tf32(tmem, da + off, dbl + off, idesc, 1);
+            umma_tf32(tmem, dal + off, db + off, idesc, 1);
+          } else {
+            umma_bf16(tmem, da + off, db + off, idesc, (kb | k) != 0);
+          }
+        }
+        umma_commit(&empty[s]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) umma_commit(accum);
+    __syncwarp();
+  } else {
+    // ---- warps 2..5
+    const int t = threadIdx.x - 64;  // 0..127
+    if constexpr (TF32X3) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % C::STAGES;
+        const uint32_t ph = (kb / C::STAGES) & 1;
+        if (!mbar_wait(&full[s], ph)) {
+          fail();
+          break;
+        }
+        // x = hi + lo exactly, hi = x with the low 13 mantissa bits cleared
+        // (an exact tf32 value, written back in place), lo = x - hi.
+        float4 *ra = reinterpret_cast<float4 *>(stage_a(s));
+        float4 *rb = reinterpret_cast<float4 *>(stage_b(s));
+        float4 *la = reinterpret_cast<float4 *>(stage_alo(s));
+        float4 *lb = reinterpret_cast<float4 *>(stage_blo(s));
+#pragma unroll 4
+        for (int i = t; i < C::A_BYTES / 16; i += 128) {
+          const float4 v = ra[i];
+          const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+          ra[i] = h;
+          la[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
+#pragma unroll 4
+        for (int i = t; i < C::B_BYTES / 16; i += 128) {
+          const float4 v = rb[i];
+          const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+          rb[i] = h;
+          lb[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv[s]);
+      }
+    }
+    const bool ok = mbar_wait(accum, 0);
+    if (!ok) fail();
+    tc_fence_after();
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = m0 + q * 32 + lane;
+    const bool row_ok = row < M;
+    float scale = 1.f;
+    if (ep.row_parts && row_ok) {
+      float s = 0.f;
+      for (int p = 0; p < ep.nparts; ++p) s += ep.row_parts[(size_t)row * ep.nparts + p];
+      scale = 1.0f / sqrtf(s * ep.inv_d + ep.eps);
+    }
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    if (ep.swiglu) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float g[16], u[16];
+        __syncwarp();
+        tmem_ld16(tbase + c, g);
+        tmem_ld16(tbase + c + 16, u);
+        tmem_wait_ld();
+        const int nout = (n0 + c) / 2;  // first output column of this group
+        if (ok && row_ok && n0 + c + 32 <= N) {
+          float h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float gg = g[j] * scale, uu = u[j] * scale;
+            h[j] = gg / (1.0f + expf(-gg)) * uu;
+          }
+          float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + nout;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4 *>(o + j) = make_float4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+        }
+      }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        __syncwarp();
+        tmem_ld16(tbase + c, v);
+        tmem_wait_ld();
+        const int n = n0 + c;
+        if (!ok || !row_ok || n >= N) continue;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          v[j] *= scale;
+          if (ep.bias && n + j < N) v[j] += ep.bias[n + j];
+        }
+        if (ep.residual) {
+          const float *r = ep.residual + (size_t)row * ep.ldr + n;
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (n + j < N) v[j] += r[j];
+        }
+        if (ep.out_bf16) {
+          __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + n;
+          if (n + 16 <= N && ep.vec_ok) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+              pk[j] = *reinterpret_cast<uint32_t *>(&b2);
+            }
+            reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          } else {
+            for (int j = 0; j < 16 && n + j < N; ++j) o[j] = __float2bfloat16(v[j]);
+          }
+        } else {
+          float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + n;
+          if (n + 16 <= N && ep.vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+            for (int j = 0; j < 16 && n + j < N; ++j) o[j] = v[j];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encoder(const char *fn) {
+  if (g_encode) return AF_OK;
+  void *p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p)
+    return af::fail(AF_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", fn);
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  return AF_OK;
+}
+
+// K-major 2-D tensor map: rows x K elements, row stride ld elements; box =
+// (128 bytes of K) x box_rows, 128-byte swizzle, zero fill out of bounds.
+int make_kmajor_map(CUtensorMap *map, const void *base, bool fp32, int rows, int K, int64_t ld, int box_rows,
+                    const char *fn) {
+  const int elem = fp32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * elem};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / elem), (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return af::fail(AF_ERR_ARG, "%s: cuTensorMapEncodeTiled failed (%d)", fn, (int)r);
+  return AF_OK;
+}
+
+template <int BN, bool TF32X3>
+int launch_tc(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
+              const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
+  using C = TileCfg<BN, TF32X3>;
+  CUtensorMap ta, tb;
+  int rc = make_kmajor_map(&ta, A, TF32X3, M, K, lda, C::BM, fn);
+  if (rc) return rc;
+  rc = make_kmajor_map(&tb, B, TF32X3, N, K, ldb, BN, fn);
+  if (rc) return rc;
+  static bool attr_done = false;  // per template instance
+  if (!attr_done) {
+    cudaError_t e =
+        cudaFuncSetAttribute(umma_gemm_kernel<BN, TF32X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
+    attr_done = true;
+  }
+  const dim3 grid((N + BN - 1) / BN, (M + C::BM - 1) / C::BM);
+  umma_gemm_kernel<BN, TF32X3><<<grid, 192, C::SMEM, st>>>(ta, tb, M, N, K, ep, ctx->dev_err);
+  return af::launched(ctx, fn);
+}
+
+}  // namespace
+
+namespace af {
+
+// Dispatches a tensor-core GEMM.  Operands must be K-major with 16-byte
+// aligned bases and row strides; callers fall back to the SIMT GEMM
+// otherwise (check tc_gemm_ok first).
+bool tc_gemm_ok(const void *A, int64_t lda, const void *B, int64_t ldb, int K, bool fp32) {
+  const int elem = fp32 ? 4 : 2;
+  return aligned16(A) && aligned16(B) && (lda * elem) % 16 == 0 && (ldb * elem) % 16 == 0 && K > 0 &&
+         ((int64_t)K * elem) % 16 == 0;
+}
+
+int tc_gemm(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, bool fp32,
+            const GemmEpilogueArgs &a, cudaStream_t st, const char *fn) {
+  int rc = get_encoder(fn);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return AF_OK;
+  const bool vec = af::aligned16(a.out) && (a.ldo * (a.out_bf16 ? 2 : 4)) % 16 == 0;
+  if (a.swiglu && (!vec || a.out_bf16 || N % 32 != 0))
+    return af::fail(AF_ERR_ARG, "%s: SwiGLU epilogue needs fp32 aligned output and N %% 32 == 0", fn);
+  GemmEpilogue ep{a.out,      a.ldo, a.out_bf16,  a.bias, a.row_parts, a.nparts, a.inv_d,
+                  a.eps,      a.residual, a.ldr, a.swiglu, vec ? 1 : 0};
+  if (fp32) {
+    // small M (decode batches): narrow tiles so the grid covers the SMs
+    const int64_t tiles128 = (int64_t)((N + 127) / 128) * ((M + 127) / 128);
+    if (tiles128 < ctx->num_sms) return launch_tc<64, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+    return launch_tc<128, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  }
+  const int64_t tiles256 = (int64_t)((N + 255) / 256) * ((M + 127) / 128);
+  if (tiles256 < ctx->num_sms) return launch_tc<128, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  return launch_tc<256, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+}
+
+}  // namespace af

@@ -1,7 +1,7 @@
 // Fused MultiScaleRetention layer entry points.
 //
 // Decode step (one token per stream, fp32, state in HBM):
-//   1. qkv = x . W_qkv^T                        (projection GEMM)
+//   1. qkv = x . W_qkv^T                        (3xTF32 tensor-core GEMM)
 //   2. retention step per (b, h), writing o * ret_norm_w and per-head sum o^2
 //   3. out = diag(1/rms) (o * w) . W_o^T         (GEMM, norm applied per row)
 // This is AceEngine.forward_layer_internal's retention half
@@ -13,8 +13,9 @@ namespace af {
 int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
                           int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn);
-int launch_sgemm_nt(af_ctx *ctx, const float *x, const float *w, const float *bias, float *y, int M, int N, int K,
-                    const float *parts, int nparts, float inv_d, float eps, cudaStream_t st, const char *fn);
+int linear_f32(af_ctx *ctx, const float *x, int64_t ldx, const float *w, int64_t ldw, const float *bias, float *y,
+               int64_t ldy, int M, int N, int K, const float *parts, int nparts, float inv_d, float eps,
+               cudaStream_t st, const char *fn);
 
 // Workspace layout of the decode step, in floats: qkv [B][3d], o [B][d],
 // sumsq [B][H].
@@ -29,12 +30,12 @@ int msr_decode_step_impl(af_ctx *ctx, const float *x, float *state, const float 
   float *qkv = scratch;
   float *o = qkv + (size_t)B * 3 * d;
   float *sumsq = o + (size_t)B * d;
-  int rc = launch_sgemm_nt(ctx, x, w_qkv, nullptr, qkv, B, 3 * d, d, nullptr, 0, 0.f, 0.f, st, fn);
+  int rc = linear_f32(ctx, x, d, w_qkv, d, nullptr, qkv, 3 * d, B, 3 * d, d, nullptr, 0, 0.f, 0.f, st, fn);
   if (rc) return rc;
   rc = launch_retention_step(ctx, state, (int64_t)H * dh * dh, gamma, qkv, qkv + d, qkv + 2 * d, 3 * (int64_t)d, o,
                              d, B, H, dh, ret_norm_w, sumsq, st, fn);
   if (rc) return rc;
-  return launch_sgemm_nt(ctx, o, w_o, nullptr, out, B, d, d, sumsq, H, 1.0f / (float)d, eps, st, fn);
+  return linear_f32(ctx, o, d, w_o, d, nullptr, out, d, B, d, d, sumsq, H, 1.0f / (float)d, eps, st, fn);
 }
 
 int check_msr_decode(const char *fn, const float *x, float *state, const float *gamma, const float *w_qkv,
@@ -64,4 +65,75 @@ extern "C" int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state,
   if (rc) return rc;
   return af::msr_decode_step_impl(ctx, x, state, gamma, w_qkv, w_o, ret_norm_w, eps, B, d, H, out,
                                   static_cast<float *>(ws), af::stream_of(stream), fn);
+}
+
+// ---------------------------------------------------------------------------
+// Prefill on the bf16 tensor cores (chunkwise form):
+//   1. qkv = x . W_qkv^T        bf16 GEMM -> bf16 [B*T][3d]
+//   2. chunkwise retention      -> bf16 O * ret_norm_w, per-row partial sum O^2, final state
+//   3. out = diag(1/rms) (O*w) . W_o^T   bf16 GEMM with the row scale in its epilogue
+namespace af {
+int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
+                             const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
+                             cudaStream_t st, const char *fn);
+int chunkwise_head_dim();
+int chunkwise_parts();
+}  // namespace af
+
+extern "C" int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int B, int T, int H, const float *gamma,
+                                           const float *state_in, float *state_out, uint16_t *out,
+                                           const float *norm_w, float *sumsq, af_stream_t stream) {
+  const char *fn = "af_retention_chunkwise_bf16";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(qkv && gamma && out, "af_retention_chunkwise_bf16", "null pointer");
+  AF_REQUIRE(B >= 0 && T >= 0 && H > 0, "af_retention_chunkwise_bf16", "bad sizes B=%d T=%d H=%d", B, T, H);
+  AF_REQUIRE(af::aligned16(qkv), "af_retention_chunkwise_bf16", "qkv must be 16-byte aligned");
+  if (B == 0 || T == 0) return AF_OK;
+  return af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, out, norm_w, sumsq,
+                                      af::stream_of(stream), fn);
+}
+
+extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv, const uint16_t *w_o,
+                                   const float *ret_norm_w, const float *gamma, float eps, int B, int T, int d, int H,
+                                   const float *state_in, float *state_out, void *out, int out_bf16,
+                                   af_stream_t stream) {
+  const char *fn = "af_msr_prefill_bf16";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(x && w_qkv && w_o && ret_norm_w && gamma && out, "af_msr_prefill_bf16", "null pointer");
+  AF_REQUIRE(B >= 0 && T >= 0 && H > 0 && d == H * af::chunkwise_head_dim(), "af_msr_prefill_bf16",
+             "the tensor-core prefill needs head_dim %d (d_model %d, heads %d)", af::chunkwise_head_dim(), d, H);
+  AF_REQUIRE(af::aligned16(x) && af::aligned16(w_qkv) && af::aligned16(w_o), "af_msr_prefill_bf16",
+             "x and weights must be 16-byte aligned");
+  AF_REQUIRE((int64_t)B * T <= 65535LL * 128, "af_msr_prefill_bf16", "B*T too large");
+  if (B == 0 || T == 0) return AF_OK;
+  const int64_t N = (int64_t)B * T;
+  const int parts = H * af::chunkwise_parts();
+  const size_t qkv_bytes = ((size_t)N * 3 * d * 2 + 255) & ~size_t(255);
+  const size_t o_bytes = ((size_t)N * d * 2 + 255) & ~size_t(255);
+  const size_t ss_bytes = (size_t)N * parts * 4;
+  void *ws = nullptr;
+  int rc = af::workspace(ctx, qkv_bytes + o_bytes + ss_bytes, &ws, fn);
+  if (rc) return rc;
+  uint8_t *base = static_cast<uint8_t *>(ws);
+  void *qkv = base;
+  void *o = base + qkv_bytes;
+  float *ss = reinterpret_cast<float *>(base + qkv_bytes + o_bytes);
+  cudaStream_t st = af::stream_of(stream);
+  af::GemmEpilogueArgs e1;
+  e1.out = qkv;
+  e1.ldo = 3 * d;
+  e1.out_bf16 = 1;
+  rc = af::tc_gemm(ctx, x, d, w_qkv, d, (int)N, 3 * d, d, false, e1, st, fn);
+  if (rc) return rc;
+  rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, o, ret_norm_w, ss, st, fn);
+  if (rc) return rc;
+  af::GemmEpilogueArgs e2;
+  e2.out = out;
+  e2.ldo = d;
+  e2.out_bf16 = out_bf16;
+  e2.row_parts = ss;
+  e2.nparts = parts;
+  e2.inv_d = 1.0f / (float)d;
+  e2.eps = eps;
+  return af::tc_gemm(ctx, o, d, w_o, d, (int)N, d, d, false, e2, st, fn);
 }

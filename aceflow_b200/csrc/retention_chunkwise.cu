@@ -1,0 +1,445 @@
+// Chunkwise-parallel retention (prefill) on the sm_100a bf16 tensor cores.
+//
+// Reference semantics: the parallel form O = (Q K^T * D) V with
+// D[i,j] = gamma^(i-j) (aceflow/nn/retention.py:51-61), equal to the
+// recurrence of aceflow-core/src/cpu/recurrence.rs:28-39.  Per chunk of C
+// tokens starting at t0, with S the state after token t0-1:
+//     O_c = D_c (Q_c S + P' V_c),   D_c = diag(gamma^(i+1)),
+//           P'[i,j] = (q_i . k_j) gamma^-(j+1)  for j <= i, else 0
+//     S  <- gamma^L S + (K_c^T) (diag(gamma^(L-1-j)) V_c)       (L = chunk length)
+// (pulling D_c out of the intra term lets one TMEM accumulator hold both
+// terms; gamma^-(j+1) <= gamma^-64 stays small).
+//
+// One CTA owns one (stream b, head h, 128-wide slice of the value dim) and
+// walks the chunks in order; the fp32 state slice lives in TMEM for the whole
+// sequence, transposed (S^T: TMEM lane = value index v, column = key index k),
+// so every MMA operand is either a TMA tile as stored in global memory or a
+// tile the math warps write themselves:
+//   scores  Sc  = Q_c K_c^T         M=64  N=64  K=256  A,B K-major (TMA)
+//   output  O^T = S^T Q_c^T         M=128 N=64  K=256  A = bf16(S^T) K-major (written)
+//              + V_c^T P'^T                       K=64   A = V_c MN-major (TMA), B = P' (written)
+//   update  S^T += Vs^T K_c        M=128 N=256 K=64   A = decay-scaled V (written), B = K_c MN-major
+// Warp roles (192 threads): warp 0 TMA producer; warp 1 TMEM allocator and
+// single-thread tcgen05.mma issuer; warps 2-5 math (TMEM ld/st, decay masks
+// generated in registers, bf16 operand tiles, output + RMSNorm partials).
+//
+// Inputs come straight from the bf16 QKV projection [B*T][3d] through one
+// 3-D tensor map (d_model fastest, then T, then B) so the T edge zero-fills.
+// Outputs: O * ret_norm_w as bf16 [B*T][d] (the A operand of the W_o GEMM),
+// per-row partial sums of O^2 (the GEMM applies 1/rms per row), and the
+// final state in the decode layout [B][H][k][v] fp32.
+#include "common.cuh"
+#include "sm100.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace {
+
+using namespace sm100;
+
+constexpr int C = 64;       // chunk length (tokens)
+constexpr int DH = 256;     // head dim
+constexpr int VS = 128;     // value slice per CTA
+constexpr int NSL = DH / VS;
+
+constexpr int Q_OFF = 0, Q_BYTES = C * DH * 2;             // 4 K-slices [64 x 64] bf16, 8 KB each
+constexpr int K_OFF = Q_OFF + Q_BYTES, K_BYTES = C * DH * 2;
+constexpr int V_OFF = K_OFF + K_BYTES, V_BYTES = C * VS * 2;  // 2 boxes [64 tok x 64 v]
+constexpr int SOP_OFF = V_OFF + V_BYTES, SOP_BYTES = VS * DH * 2;  // 4 K-slices [128 v x 64 k], 16 KB each
+constexpr int P_OFF = SOP_OFF + SOP_BYTES, P_BYTES = C * C * 2;    // [64 i x 64 j]
+constexpr int VT_OFF = P_OFF + P_BYTES, VT_BYTES = V_BYTES;         // decay-scaled V, V's layout
+constexpr int TILE_BYTES = VT_OFF + VT_BYTES;                       // 168 KB
+// tail: 6 mbarriers + TMEM slot (64 B), gamma^n (C+1), gamma^-(j+1) (C), [4][C] partials
+constexpr size_t TAIL_BYTES = 64 + 4 * ((C + 1) + C + 4 * C);
+constexpr size_t SMEM = 1024 + TILE_BYTES + ((TAIL_BYTES + 255) / 256) * 256;
+constexpr int BOX = 64 * 64 * 2;  // one TMA box: 64 rows x 128 bytes
+
+constexpr uint32_t TM_S = 0, TM_SC = 256, TM_O = 320, TM_COLS = 512;
+
+struct ChunkParams {
+  int B, T, H;
+  const float *gamma;
+  const float *state_in;  // [B][H][DH][DH] or null
+  float *state_out;       // [B][H][DH][DH] or null
+  __nv_bfloat16 *out;     // [B*T][H*DH]
+  const float *norm_w;    // [H*DH] or null
+  float *sumsq;           // [B*T][H*NSL] or null
+  int *err;
+};
+
+// MN-major SW128 descriptor: 64-element MN blocks `lbo` bytes apart, 8-row
+// K groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_mn_sw128(const void *tile, uint32_t lbo) {
+  const uint64_t addr = smem_u32(tile);
+  return ((addr >> 4) & 0x3FFFull) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+// Byte offset of 16-byte chunk `c16` of row `r` in a 128B-swizzled tile.
+__device__ __forceinline__ uint32_t sw128(int r, int c16) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c16 ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+__device__ __forceinline__ void math_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__global__ void __launch_bounds__(192, 1)
+    retention_chunkwise_kernel(const __grid_constant__ CUtensorMap tm, ChunkParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + TILE_BYTES);
+  uint64_t *bar_load = bars + 0, *bar_sc = bars + 1, *bar_math = bars + 2, *bar_o = bars + 3, *bar_upd = bars + 4,
+           *bar_out = bars + 5;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 6);
+  float *gpow = reinterpret_cast<float *>(bars + 8);   // gamma^n, n = 0..C
+  float *ginv = gpow + (C + 1);                        // gamma^-(j+1), j = 0..C-1
+  float *red = ginv + C;                               // [4][C] per-warp partial sums
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slice = blockIdx.x % NSL;
+  const int bh = blockIdx.x / NSL;
+  const int b = bh / p.H, h = bh % p.H;
+  const int d = p.H * DH;
+  const int nch = (p.T + C - 1) / C;
+  const float g = p.gamma[h];
+  const float lg = log2f(g);
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    mbar_init(bar_load, 1);
+    mbar_init(bar_sc, 1);
+    mbar_init(bar_math, 128);
+    mbar_init(bar_o, 1);
+    mbar_init(bar_upd, 1);
+    mbar_init(bar_out, 128);
+    fence_barrier_init();
+    prefetch_tmap(&tm);
+  }
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + C + 1) {
+    const int n = threadIdx.x - 64;
+    gpow[n] = exp2f((float)n * lg);
+    if (n < C) ginv[n] = exp2f(-(float)(n + 1) * lg);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&]() {
+    s_abort = 1;
+    atomicOr(p.err, 1 << AF_ERR_TIMEOUT);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int c = 0; c < nch && !s_abort; ++c) {
+        if (c > 0 && !mbar_wait(bar_upd, (c - 1) & 1)) { fail(); break; }
+        const int t0 = c * C;
+        mbar_arrive_expect_tx(bar_load, Q_BYTES + K_BYTES + V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          tma_load_3d(sm + Q_OFF + kk * BOX, &tm, bar_load, h * DH + kk * 64, t0, b);
+          tma_load_3d(sm + K_OFF + kk * BOX, &tm, bar_load, d + h * DH + kk * 64, t0, b);
+        }
+#pragma unroll
+        for (int vb = 0; vb < 2; ++vb)
+          tma_load_3d(sm + V_OFF + vb * BOX, &tm, bar_load, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
+        issued = c + 1;
+      }
+      if (issued > 0 && !mbar_wait(bar_load, (issued - 1) & 1)) fail();  // last load landed
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t id_sc = idesc_f32acc(kFmtBF16, 64, 64);
+    constexpr uint32_t id_inter = idesc_f32acc(kFmtBF16, 128, 64);
+    constexpr uint32_t id_intra = idesc_f32acc(kFmtBF16, 128, 64) | (1u << 15);         // A MN-major
+    constexpr uint32_t id_upd = idesc_f32acc(kFmtBF16, 128, 256) | (1u << 15) | (1u << 16);  // A, B MN-major
+    for (int c = 0; c < nch; ++c) {
+      bool ok = mbar_wait(bar_load, c & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || s_abort) { if (!ok && lane == 0) fail(); break; }
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t da = sdesc_k_sw128(sm + Q_OFF + kk * BOX) + ((k * 32) >> 4);
+            const uint64_t db = sdesc_k_sw128(sm + K_OFF + kk * BOX) + ((k * 32) >> 4);
+            umma_bf16(tmem + TM_SC, da, db, id_sc, (kk | k) != 0);
+          }
+        umma_commit(bar_sc);
+      }
+      __syncwarp();
+      ok = mbar_wait(bar_math, c & 1);
+      if (ok && c > 0) ok = mbar_wait(bar_out, (c - 1) & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || s_abort) { if (!ok && lane == 0) fail(); break; }
+      tc_fence_after();
+      if (lane == 0) {
+        // O^T = bf16(S^T) . Q^T  (K = 256 keys)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t da = sdesc_k_sw128(sm + SOP_OFF + kk * 2 * BOX) + ((k * 32) >> 4);
+            const uint64_t db = sdesc_k_sw128(sm + Q_OFF + kk * BOX) + ((k * 32) >> 4);
+            umma_bf16(tmem + TM_O, da, db, id_inter, (kk | k) != 0);
+          }
+        //     + V^T . P'^T  (K = 64 tokens)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t da = sdesc_mn_sw128(sm + V_OFF + k * 2048, BOX);
+          const uint64_t db = sdesc_k_sw128(sm + P_OFF) + ((k * 32) >> 4);
+          umma_bf16(tmem + TM_O, da, db, id_intra, 1);
+        }
+        umma_commit(bar_o);
+        // S^T += Vs^T . K  (K = 64 tokens, N = 256 keys)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t da = sdesc_mn_sw128(sm + VT_OFF + k * 2048, BOX);
+          const uint64_t db = sdesc_mn_sw128(sm + K_OFF + k * 2048, BOX);
+          umma_bf16(tmem + TM_S, da, db, id_upd, 1);
+        }
+        umma_commit(bar_upd);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ math warps
+    const int q = warp & 3;
+    const int mt = threadIdx.x - 64;   // 0..127
+    const int v = q * 32 + lane;       // TMEM lane of this thread = value index in the slice
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    // initial state S^T[v][k] = S[k][v]
+    {
+      const float *sin = p.state_in ? p.state_in + ((size_t)(b * p.H + h) * DH) * DH + slice * VS + v : nullptr;
+#pragma unroll 1
+      for (int k0 = 0; k0 < DH; k0 += 16) {
+        float x[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[j] = sin ? sin[(size_t)(k0 + j) * DH] : 0.f;
+        __syncwarp();
+        tmem_st16(tmem + lane_base + TM_S + k0, x);
+      }
+      tmem_wait_st();
+    }
+    for (int c = 0; c < nch; ++c) {
+      const int t0 = c * C;
+      const int L = min(C, p.T - t0);
+      bool ok = true;
+      if (c > 0) ok = mbar_wait(bar_upd, (c - 1) & 1);
+      if (!ok) s_abort = 1;
+      math_sync();
+      if (s_abort) break;
+      tc_fence_after();
+      // (a) S_op = bf16(S^T) (K-major [v][k]); S^T *= gamma^L in TMEM
+      const float gL = gpow[L];
+#pragma unroll 1
+      for (int k0 = 0; k0 < DH; k0 += 16) {
+        float x[16];
+        __syncwarp();
+        tmem_ld16(tmem + lane_base + TM_S + k0, x);
+        tmem_wait_ld();
+        uint8_t *slice_base = sm + SOP_OFF + (k0 >> 6) * (2 * BOX);
+        const int c16 = (k0 & 63) >> 3;
+        uint4 w0 = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
+        uint4 w1 = make_uint4(pack_bf16(x[8], x[9]), pack_bf16(x[10], x[11]), pack_bf16(x[12], x[13]),
+                              pack_bf16(x[14], x[15]));
+        *reinterpret_cast<uint4 *>(slice_base + sw128(v, c16)) = w0;
+        *reinterpret_cast<uint4 *>(slice_base + sw128(v, c16 + 1)) = w1;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[j] *= gL;
+        __syncwarp();
+        tmem_st16(tmem + lane_base + TM_S + k0, x);
+      }
+      tmem_wait_st();
+      // (b) Vs = diag(gamma^(L-1-j)) V, same swizzled layout as V
+      ok = mbar_wait(bar_load, c & 1);
+      if (!ok) s_abort = 1;
+      if (ok) {
+#pragma unroll 2
+        for (int i = mt; i < V_BYTES / 16; i += 128) {
+          const int off = i * 16;
+          const int j = (off % BOX) / 128;  // token row of this 16-byte chunk
+          const float sc = j < L ? gpow[L - 1 - j] : 0.f;
+          uint4 raw = *reinterpret_cast<const uint4 *>(sm + V_OFF + off);
+          __nv_bfloat162 *e = reinterpret_cast<__nv_bfloat162 *>(&raw);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float2 f = __bfloat1622float2(e[u]);
+            e[u] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+          }
+          *reinterpret_cast<uint4 *>(sm + VT_OFF + off) = raw;
+        }
+      }
+      // (c) P'[i][j] = Sc[i][j] * gamma^-(j+1) for j <= i (rows i = 16q + lane, lanes < 16)
+      ok = ok && mbar_wait(bar_sc, c & 1);
+      if (!ok) s_abort = 1;
+      if (ok) {
+        tc_fence_after();
+        const int i = q * 16 + lane;
+#pragma unroll 1
+        for (int j0 = 0; j0 < C; j0 += 16) {
+          float x[16];
+          __syncwarp();
+          tmem_ld16(tmem + lane_base + TM_SC + j0, x);
+          tmem_wait_ld();
+          if (lane < 16) {
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+              const int j = j0 + u;
+              x[u] = (j <= i) ? x[u] * ginv[j] : 0.f;
+            }
+            uint4 w0 = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
+                                  pack_bf16(x[6], x[7]));
+            uint4 w1 = make_uint4(pack_bf16(x[8], x[9]), pack_bf16(x[10], x[11]), pack_bf16(x[12], x[13]),
+                                  pack_bf16(x[14], x[15]));
+            *reinterpret_cast<uint4 *>(sm + P_OFF + sw128(i, j0 >> 3)) = w0;
+            *reinterpret_cast<uint4 *>(sm + P_OFF + sw128(i, (j0 >> 3) + 1)) = w1;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_math);
+      math_sync();
+      if (s_abort) break;
+      // (d) O = gamma^(i+1) * O^T[v][i]; store bf16 O * w; partial sum of O^2 per token
+      ok = mbar_wait(bar_o, c & 1);
+      if (!ok) s_abort = 1;
+      math_sync();
+      if (s_abort) break;
+      tc_fence_after();
+      const int col = h * DH + slice * VS + v;
+      const float wv = p.norm_w ? p.norm_w[col] : 1.f;
+      __nv_bfloat16 *orow = p.out + ((size_t)b * p.T + t0) * d + col;
+#pragma unroll 1
+      for (int i0 = 0; i0 < C; i0 += 16) {
+        float x[16];
+        __syncwarp();
+        tmem_ld16(tmem + lane_base + TM_O + i0, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int i = i0 + u;
+          const float o = x[u] * gpow[i + 1];
+          if (i < L) orow[(size_t)i * d] = __float2bfloat16(o * wv);
+          float s2 = o * o;
+          s2 = warp_sum(s2);
+          if (lane == 0) red[q * C + i] = s2;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_out);
+      math_sync();
+      if (p.sumsq && mt < L) {
+        const float s2 = red[mt] + red[C + mt] + red[2 * C + mt] + red[3 * C + mt];
+        p.sumsq[((size_t)b * p.T + t0 + mt) * (p.H * NSL) + h * NSL + slice] = s2;
+      }
+    }
+    // final state: S[k][v] = S^T[v][k]
+    if (!s_abort && p.state_out) {
+      bool ok = mbar_wait(bar_upd, (nch - 1) & 1);
+      if (!ok) s_abort = 1;
+      math_sync();
+      if (!s_abort) {
+        tc_fence_after();
+        float *so = p.state_out + ((size_t)(b * p.H + h) * DH) * DH + slice * VS + v;
+#pragma unroll 1
+        for (int k0 = 0; k0 < DH; k0 += 16) {
+          float x[16];
+          __syncwarp();
+          tmem_ld16(tmem + lane_base + TM_S + k0, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) so[(size_t)(k0 + j) * DH] = x[j];
+        }
+      }
+    } else if (!s_abort && nch > 0) {
+      if (!mbar_wait(bar_upd, (nch - 1) & 1)) s_abort = 1;  // last MMAs retired before TMEM is freed
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode3 = nullptr;
+
+}  // namespace
+
+namespace af {
+
+// Chunkwise retention over a bf16 QKV buffer [B*T][3d] (row stride 3d).
+int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
+                             const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
+                             cudaStream_t st, const char *fn) {
+  if (!g_encode3) {
+    void *fp = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fp, cudaEnableDefault, &qr) != cudaSuccess || !fp)
+      return fail(AF_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", fn);
+    g_encode3 = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fp);
+  }
+  const int d = H * DH;
+  CUtensorMap tm;
+  cuuint64_t dims[3] = {(cuuint64_t)(3 * d), (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)3 * d * 2, (cuuint64_t)T * 3 * d * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)C, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode3(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(qkv), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: tensor map encode failed (%d)", fn, (int)r);
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(retention_chunkwise_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SMEM);
+    if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    attr = true;
+  }
+  ChunkParams p{B, T, H, gamma, state_in, state_out, reinterpret_cast<__nv_bfloat16 *>(out), norm_w, sumsq,
+                ctx->dev_err};
+  retention_chunkwise_kernel<<<B * H * NSL, 192, SMEM, st>>>(tm, p);
+  return launched(ctx, fn);
+}
+
+int chunkwise_head_dim() { return DH; }
+int chunkwise_parts() { return NSL; }
+
+}  // namespace af

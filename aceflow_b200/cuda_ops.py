@@ -185,3 +185,69 @@ def msr_decode_step(x: torch.Tensor, state: torch.Tensor, gamma: torch.Tensor, w
     _lib.call("af_msr_decode_step_f32", _ctx(x), _p(x), _p(state), _p(gamma), _p(w_qkv), _p(w_o), _p(ret_norm_w),
               float(eps), B, d, H, _p(out), _stream(x))
     return out
+
+
+def linear_bf16(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+                out_dtype=torch.float32) -> torch.Tensor:
+    """bf16 x [..., K] . W[N, K]^T on the bf16 tensor cores (fp32 accumulate)."""
+    _need(x, BF16, "x")
+    _need(w, BF16, "weight")
+    K = x.shape[-1]
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"weight shape {tuple(w.shape)} does not match input features {K}")
+    if bias is not None:
+        _need(bias, F32, "bias")
+    M = x.numel() // K
+    y = torch.empty(*x.shape[:-1], N, dtype=out_dtype, device=x.device)
+    _lib.call("af_linear_bf16", _ctx(x), _p(x), _p(w), _p(bias), _p(y), int(out_dtype == BF16), M, N, K, _stream(x))
+    return y
+
+
+def retention_chunkwise_bf16(qkv: torch.Tensor, B: int, T: int, H: int, gamma: torch.Tensor,
+                             state_in: torch.Tensor | None = None, norm_w: torch.Tensor | None = None,
+                             want_state: bool = True):
+    """Tensor-core chunkwise retention over a bf16 QKV buffer [B*T, 3*H*256].
+    Returns (out bf16 [B*T, H*256] (times norm_w), sumsq [B*T, 2H], state_out
+    [B, H, 256, 256] fp32 or None)."""
+    _need(qkv, BF16, "qkv")
+    d = H * 256
+    if tuple(qkv.shape) != (B * T, 3 * d):
+        raise ValueError(f"qkv must be [{B * T}, {3 * d}] (head_dim 256), got {tuple(qkv.shape)}")
+    _need(gamma, F32, "gamma")
+    if state_in is not None:
+        _need(state_in, F32, "state_in")
+        if tuple(state_in.shape) != (B, H, 256, 256):
+            raise ValueError("state_in must be [B, H, 256, 256]")
+    if norm_w is not None:
+        _need(norm_w, F32, "norm_w")
+    out = torch.empty(B * T, d, dtype=BF16, device=qkv.device)
+    sumsq = torch.empty(B * T, 2 * H, dtype=F32, device=qkv.device)
+    state_out = torch.empty(B, H, 256, 256, dtype=F32, device=qkv.device) if want_state else None
+    _lib.call("af_retention_chunkwise_bf16", _ctx(qkv), _p(qkv), B, T, H, _p(gamma), _p(state_in), _p(state_out),
+              _p(out), _p(norm_w), _p(sumsq), _stream(qkv))
+    return out, sumsq, state_out
+
+
+def msr_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, ret_norm_w: torch.Tensor,
+                     gamma: torch.Tensor, eps: float, state_in: torch.Tensor | None = None,
+                     out_dtype=torch.float32, want_state: bool = True):
+    """MultiScaleRetention prefill on the bf16 tensor cores: x [B, T, d] bf16
+    -> (out [B, T, d] out_dtype, final state [B, H, 256, 256] fp32 or None)."""
+    _need(x, BF16, "x")
+    B, T, d = x.shape
+    H = d // 256
+    if d % 256:
+        raise ValueError(f"the tensor-core prefill needs head_dim 256 (d_model {d})")
+    _need(w_qkv, BF16, "w_qkv")
+    _need(w_o, BF16, "w_o")
+    _need(ret_norm_w, F32, "ret_norm_w")
+    if tuple(w_qkv.shape) != (3 * d, d) or tuple(w_o.shape) != (d, d):
+        raise ValueError("w_qkv must be [3d, d] and w_o [d, d]")
+    if state_in is not None:
+        _need(state_in, F32, "state_in")
+    out = torch.empty(B, T, d, dtype=out_dtype, device=x.device)
+    state_out = torch.empty(B, H, 256, 256, dtype=F32, device=x.device) if want_state else None
+    _lib.call("af_msr_prefill_bf16", _ctx(x), _p(x), _p(w_qkv), _p(w_o), _p(ret_norm_w), _p(gamma), float(eps),
+              B, T, d, H, _p(state_in), _p(state_out), _p(out), int(out_dtype == BF16), _stream(x))
+    return out, state_out

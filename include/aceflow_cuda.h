@@ -54,6 +54,11 @@ const char *af_last_error(void);
 int af_cuda_init(int device, af_ctx **ctx);
 int af_cuda_destroy(af_ctx *ctx);
 int af_reserve_workspace(af_ctx *ctx, size_t bytes);
+/* Synchronises the device and reads the context's device error word: a
+ * kernel whose bounded wait gave up sets bit AF_ERR_TIMEOUT instead of
+ * hanging.  Returns AF_ERR_TIMEOUT if set; `flags` (may be NULL) receives the
+ * word; `reset` clears it. */
+int af_check_device(af_ctx *ctx, int *flags, int reset);
 /* Number of this library's kernel launches issued through `ctx` so far. */
 int af_launch_count(af_ctx *ctx, int64_t *count);
 
@@ -115,6 +120,11 @@ int af_add_f32(af_ctx *ctx, const float *a, const float *b, float *out, int64_t 
  * batched_gemv (aceflow-core/src/cpu/gemv.rs:164-194). */
 int af_linear_f32(af_ctx *ctx, const float *x, const float *w, const float *bias, float *y, int M,
                   int N, int K, af_stream_t stream);
+/* Same with bf16 x [M][K] and W [N][K] on the bf16 tensor cores, fp32
+ * accumulation; y is fp32 (y_bf16 == 0) or bf16 (y_bf16 != 0).  The bf16
+ * path of Linear.forward for the tensor-core prefill. */
+int af_linear_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w, const float *bias, void *y,
+                   int y_bf16, int M, int N, int K, af_stream_t stream);
 
 /* ------------------------------------------------------- fused MSR layer */
 /* One recurrent decode step of a MultiScaleRetention layer for `batch`
@@ -130,6 +140,32 @@ int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state, const floa
                            const float *w_qkv, const float *w_o, const float *ret_norm_w,
                            float eps, int batch, int d_model, int num_heads, float *out,
                            af_stream_t stream);
+
+/* Chunkwise-parallel retention core on the bf16 tensor cores (head_dim 256,
+ * chunk 64).  The parallel form (aceflow/nn/retention.py:51-61) computed
+ * chunk by chunk with the carried state of recurrence.rs:28-39.
+ *   qkv       [batch*T][3*H*256] bf16: q | k | v per row (a QKV projection).
+ *   state_in  [batch][H][256][256] fp32 initial state, or NULL for zeros.
+ *   state_out same layout, the state after the last token, or NULL.
+ *   out       [batch*T][H*256] bf16: retention output times norm_w (or 1).
+ *   sumsq     [batch*T][2*H] fp32 partial sums of the unscaled output's
+ *             squares (row r's RMS is sqrt(sum(sumsq[r]) / d)), or NULL. */
+int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int batch, int T, int num_heads,
+                                const float *gamma, const float *state_in, float *state_out,
+                                uint16_t *out, const float *norm_w, float *sumsq, af_stream_t stream);
+
+/* MultiScaleRetention forward over a prompt on the bf16 tensor cores:
+ * x [batch*T][d] bf16 -> out [batch*T][d] (fp32, or bf16 if out_bf16).
+ * Replaces MultiScaleRetention.forward_parallel (aceflow/nn/retention.py:44-66)
+ * for bf16 inputs (fp32 accumulation, tolerance 2e-2) and the token-serial
+ * AceEngine.prefill_recurrent (aceflow-core/src/cpu/mod.rs:547-587).
+ *   w_qkv [3d][d] bf16 (rows q, k, v); w_o [d][d] bf16; ret_norm_w [d] fp32;
+ *   state_in/state_out as for af_retention_chunkwise_bf16.
+ * head_dim must be 256.  Workspace: batch*T*(8*d + 8*H) bytes. */
+int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv, const uint16_t *w_o,
+                        const float *ret_norm_w, const float *gamma, float eps, int batch, int T,
+                        int d_model, int num_heads, const float *state_in, float *state_out,
+                        void *out, int out_bf16, af_stream_t stream);
 
 #ifdef __cplusplus
 }

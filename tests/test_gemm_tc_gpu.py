@@ -1,0 +1,66 @@
+"""Tensor-core (tcgen05) GEMM parity, through the C ABI.
+
+bf16 operands: compared with an fp64 product of the same bf16 values (the
+only difference is fp32 accumulation order).  fp32 operands (3xTF32 split):
+compared with fp64, must hold fp32-level accuracy (<= 1e-5 relative).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def _check(dev):
+    from aceflow_b200 import _lib
+
+    assert _lib.check_device(0) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (1, 16, 8), (300, 200, 136), (256, 6144, 2048),
+                                   (4096, 2048, 2048), (77, 512, 1000)])
+def test_bf16_gemm_matches_fp64(dev, M, N, K):
+    from aceflow_b200 import cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(M * 7 + N + K)
+    x = torch.randn(M, K, generator=g, device=dev).bfloat16()
+    w = (0.02 * torch.randn(N, K, generator=g, device=dev)).bfloat16()
+    b = torch.randn(N, generator=g, device=dev)
+    y = cuda_ops.linear_bf16(x, w, b)
+    ref = x.double() @ w.double().T + b.double()
+    assert rel_err(y.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+    yb = cuda_ops.linear_bf16(x, w, out_dtype=torch.bfloat16)
+    assert rel_err(yb.float().cpu().numpy(), (x.double() @ w.double().T).cpu().numpy()) < 1e-2
+    _check(dev)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 32), (256, 6144, 2048), (256, 2048, 2048), (3, 40, 48),
+                                   (130, 2048, 5632), (1000, 264, 96)])
+def test_tf32x3_gemm_is_fp32_accurate(dev, M, N, K):
+    from aceflow_b200 import cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(M + N * 3 + K)
+    x = torch.randn(M, K, generator=g, device=dev)
+    w = 0.02 * torch.randn(N, K, generator=g, device=dev)
+    y = cuda_ops.linear(x, w)
+    ref = x.double() @ w.double().T
+    err = rel_err(y.cpu().numpy(), ref.cpu().numpy())
+    assert err < 1e-5, err
+    _check(dev)
+
+
+def test_unaligned_k_uses_simt_path(dev):
+    from aceflow_b200 import cuda_ops
+
+    x = torch.randn(5, 13, device=dev)
+    w = torch.randn(7, 13, device=dev)
+    assert rel_err(cuda_ops.linear(x, w).cpu().numpy(), (x.double() @ w.double().T).cpu().numpy()) < 1e-6

@@ -1,0 +1,116 @@
+"""GPU parity of the tensor-core chunkwise prefill (bf16 operands, fp32
+accumulation) against the float64 oracle.  Tolerance for the bf16 path:
+max|y - y_ref| / max|y_ref| <= 2e-2."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle import retention_ref as R
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def _qkv(B, T, H, seed, dev, scale=1.0):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    d = H * 256
+    return (scale * torch.randn(B * T, 3 * d, generator=g, device=dev)).bfloat16()
+
+
+def _core_ref(qkv, B, T, H, state0=None):
+    d = H * 256
+    a = qkv.float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256)
+    q, k, v = (a[:, :, i].transpose(0, 2, 1, 3) for i in range(3))
+    o, S = R.retention_chunkwise64(q, k, v, R.gammas(H), 64, state0)
+    return o.transpose(0, 2, 1, 3).reshape(B * T, d), S
+
+
+@pytest.mark.parametrize("B,T,H", [(1, 64, 1), (2, 100, 2), (1, 257, 2), (3, 200, 1), (1, 1000, 8)])
+def test_chunkwise_core_matches_oracle(dev, B, T, H):
+    from aceflow_b200 import _lib, cuda_ops
+
+    qkv = _qkv(B, T, H, B * 1000 + T + H, dev, scale=0.5)
+    gamma = cuda_ops.gammas(H, dev)
+    w = (1 + 0.1 * torch.randn(H * 256, device=dev))
+    out, ss, st = cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=w)
+    torch.cuda.synchronize()
+    assert _lib.check_device(0) == 0
+    ref, S = _core_ref(qkv, B, T, H)
+    wn = w.cpu().numpy().astype(np.float64)
+    assert rel_err(out.float().cpu().numpy(), ref * wn) < TOL
+    assert rel_err(st.cpu().numpy(), S) < TOL
+    rs = ss.cpu().numpy().sum(1)
+    assert rel_err(rs, (ref * ref).sum(1)) < TOL
+
+
+def test_chunkwise_state_carry(dev):
+    """Two calls chained through the state equal one call over the whole
+    sequence (and a non-zero initial state is honoured)."""
+    from aceflow_b200 import cuda_ops
+
+    B, H, T1, T2 = 2, 2, 130, 70
+    qkv = _qkv(B, T1 + T2, H, 7, dev, scale=0.5)
+    gamma = cuda_ops.gammas(H, dev)
+    full, _, S_full = cuda_ops.retention_chunkwise_bf16(qkv, B, T1 + T2, H, gamma)
+    q3 = qkv.view(B, T1 + T2, -1)
+    a = q3[:, :T1].contiguous().view(B * T1, -1)
+    b = q3[:, T1:].contiguous().view(B * T2, -1)
+    o1, _, S1 = cuda_ops.retention_chunkwise_bf16(a, B, T1, H, gamma)
+    o2, _, S2 = cuda_ops.retention_chunkwise_bf16(b, B, T2, H, gamma, state_in=S1)
+    f = full.float().view(B, T1 + T2, -1)
+    assert rel_err(o1.float().view(B, T1, -1).cpu().numpy(), f[:, :T1].cpu().numpy()) < 1e-2
+    assert rel_err(o2.float().view(B, T2, -1).cpu().numpy(), f[:, T1:].cpu().numpy()) < TOL
+    assert rel_err(S2.cpu().numpy(), S_full.cpu().numpy()) < TOL
+
+
+@pytest.mark.parametrize("B,T,H", [(2, 96, 2), (1, 300, 8)])
+def test_msr_prefill_matches_float64(dev, B, T, H):
+    from aceflow_b200 import _lib, cuda_ops
+
+    d = H * 256
+    rng = np.random.default_rng(B + T + H)
+    x = rng.standard_normal((B, T, d)).astype(np.float32)
+    wq, wk, wv, wo = ((0.02 * rng.standard_normal((d, d))).astype(np.float32) for _ in range(4))
+    rw = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    tb = lambda a: torch.from_numpy(a).to(dev).bfloat16()  # noqa: E731
+    xb, wqkv, wob = tb(x), tb(np.concatenate([wq, wk, wv])), tb(wo)
+    out, st = cuda_ops.msr_prefill_bf16(xb, wqkv, wob, torch.from_numpy(rw).to(dev), cuda_ops.gammas(H, dev), 1e-6)
+    torch.cuda.synchronize()
+    assert _lib.check_device(0) == 0
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    wq_, wk_, wv_ = np.split(f(wqkv), 3)
+    ref = R.msr_forward64(f(xb), wq_, wk_, wv_, f(wob), H, rw, 1e-6)
+    assert rel_err(out.cpu().numpy(), ref) < TOL
+    # against the fp32 weights/inputs too (the bf16 quantisation is inside the tolerance)
+    ref32 = R.msr_forward64(x, wq, wk, wv, wo, H, rw, 1e-6)
+    assert rel_err(out.cpu().numpy(), ref32) < TOL
+
+
+def test_prefill_then_decode_continues_the_state(dev):
+    """Prefill T tokens, then one fp32 decode step from the returned state,
+    equals the recurrence over T+1 tokens."""
+    from aceflow_b200 import cuda_ops
+
+    B, H, T = 2, 2, 77
+    d = H * 256
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((B, T + 1, d)).astype(np.float32)
+    w = [(0.02 * rng.standard_normal((d, d))).astype(np.float32) for _ in range(4)]
+    w = [torch.from_numpy(a).to(dev).bfloat16().float() for a in w]  # bf16-representable weights
+    xb = torch.from_numpy(x).to(dev).bfloat16()
+    rw = torch.ones(d, device=dev)
+    gamma = cuda_ops.gammas(H, dev)
+    wqkv = torch.cat(w[:3]).contiguous()
+    _, st = cuda_ops.msr_prefill_bf16(xb[:, :T].contiguous(), wqkv.bfloat16(), w[3].bfloat16(), rw, gamma, 1e-6)
+    out = cuda_ops.msr_decode_step(xb[:, T].float().contiguous(), st, gamma, wqkv, w[3], rw, 1e-6)
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    ref = R.msr_forward64(f(xb), *(f(a) for a in w), H, None, 1e-6)[:, T]
+    assert rel_err(out.cpu().numpy(), ref) < TOL
