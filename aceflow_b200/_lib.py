@@ -46,6 +46,13 @@ SIGNATURES = {
     "af_msr_decode_step_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
     "af_retention_chunkwise_bf16": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "af_msr_prefill_bf16": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp],
+    "af_pack_gate_up": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "af_decoder_layer_decode": [_vp, _vp, _i, _vp, _vp, _i64, _vp, _f, _i, _i, _i, _i, _vp],
+    "af_decoder_layer_prefill": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _i, _vp],
+    "af_embed_gather": [_vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _vp],
+    "af_rmsnorm_to_bf16": [_vp, _vp, _vp, _vp, _i, _i, _f, _vp],
+    "af_argmax_rows": [_vp, _vp, _i, _i, _vp, _vp],
+    "af_lm_head_argmax": [_vp, _vp, _vp, _f, _vp, _i, _i, _i, _i, _vp, _vp, _vp],
 }
 _RESTYPE = {"af_last_error": ctypes.c_char_p}
 

@@ -1,0 +1,347 @@
+// Decoder-stack kernels: the pieces of AceEngine (aceflow-core/src/cpu/mod.rs)
+// around the retention layer, batched over streams.
+//
+//   embed_gather      embedding rows for token ids (generate_stream_internal,
+//                     cpu/mod.rs:721-726 and 757-763)
+//   rmsnorm_to_bf16   RMSNorm of the fp32 residual stream into the bf16 A
+//                     operand of the next projection (cpu/norm.rs:74-78)
+//   argmax_rows       greedy sampling: first maximum wins (sampler.rs:118-128)
+//   pack_gate_up      [gate; up] rows -> 16-row interleave for the SwiGLU
+//                     GEMM epilogue (swiglu.rs:7-8 layout in, fused layout out)
+#include "common.cuh"
+
+namespace {
+
+// x[r] = E[tok[r]] (bf16 or fp32 table -> fp32 rows).  An out-of-range id in
+// a prompt keeps the previous row's embedding (the reference copies only
+// when the row exists and otherwise leaves `current` unchanged,
+// cpu/mod.rs:721-726); `zero_oob` selects the generated-token rule
+// (cpu/mod.rs:757-763: zeros).  Rows are grouped in sequences of length T.
+__global__ void embed_gather_kernel(const void *__restrict__ table, int table_bf16, const int32_t *__restrict__ tok,
+                                    float *__restrict__ x, int rows, int T, int V, int d, int zero_oob) {
+  const int r = blockIdx.x;
+  if (r >= rows) return;
+  int t = tok[r];
+  if (t < 0 || t >= V) {
+    if (zero_oob) {
+      t = -1;
+    } else {
+      // last in-range id earlier in the same sequence, else zeros
+      const int s0 = (r / T) * T;
+      t = -1;
+      for (int q = r - 1; q >= s0; --q) {
+        const int u = tok[q];
+        if (u >= 0 && u < V) {
+          t = u;
+          break;
+        }
+      }
+    }
+  }
+  float *xo = x + (size_t)r * d;
+  if (t < 0) {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xo[i] = 0.f;
+    return;
+  }
+  if (table_bf16) {
+    const __nv_bfloat16 *e = reinterpret_cast<const __nv_bfloat16 *>(table) + (size_t)t * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xo[i] = __bfloat162float(e[i]);
+  } else {
+    const float *e = reinterpret_cast<const float *>(table) + (size_t)t * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xo[i] = e[i];
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    rmsnorm_to_bf16_kernel(const float *__restrict__ x, const float *__restrict__ w, __nv_bfloat16 *__restrict__ y,
+                           int d, float eps) {
+  extern __shared__ float row[];
+  __shared__ float red[32];
+  const size_t off = (size_t)blockIdx.x * d;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float a = x[off + i];
+    row[i] = a;
+    ss += a * a;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) t += red[i];
+  if (w == nullptr) {  // plain fp32 -> bf16 conversion
+    for (int i = threadIdx.x; i < d; i += blockDim.x) y[off + i] = __float2bfloat16(row[i]);
+    return;
+  }
+  const float inv = 1.0f / sqrtf(t / (float)d + eps);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) y[off + i] = __float2bfloat16(row[i] * (inv * w[i]));
+}
+
+// One CTA per row; ties resolve to the smallest index, NaN never wins (the
+// reference's strict `>` scan from index 0).
+__global__ void __launch_bounds__(512) argmax_rows_kernel(const float *__restrict__ logits, int V,
+                                                          int32_t *__restrict__ out) {
+  const float *l = logits + (size_t)blockIdx.x * V;
+  float best = l[0];
+  int bi = 0;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = l[i];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  // a NaN at index 0 makes the reference return 0
+  __shared__ float sb[512];
+  __shared__ int si[512];
+  sb[threadIdx.x] = best;
+  si[threadIdx.x] = bi;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) {
+      const float ob = sb[threadIdx.x + s];
+      const int oi = si[threadIdx.x + s];
+      if (ob > sb[threadIdx.x] || (ob == sb[threadIdx.x] && oi < si[threadIdx.x])) {
+        sb[threadIdx.x] = ob;
+        si[threadIdx.x] = oi;
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[blockIdx.x] = (l[0] != l[0]) ? 0 : si[0];
+}
+
+// dst row p: group g = p / 32, j = p % 32; j < 16 -> gate row 16g + j,
+// else up row 16g + j - 16 (src rows: gate 0..f-1, then up f..2f-1).
+__global__ void pack_gate_up_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int f,
+                                    int row_bytes) {
+  const int p = blockIdx.x;
+  const int g = p / 32, j = p % 32;
+  const int s = j < 16 ? 16 * g + j : f + 16 * g + (j - 16);
+  const uint8_t *a = src + (size_t)s * row_bytes;
+  uint8_t *b = dst + (size_t)p * row_bytes;
+  for (int i = threadIdx.x * 16; i < row_bytes; i += blockDim.x * 16)
+    *reinterpret_cast<uint4 *>(b + i) = *reinterpret_cast<const uint4 *>(a + i);
+}
+
+}  // namespace
+
+extern "C" {
+
+int af_embed_gather(af_ctx *ctx, const void *table, int table_bf16, const int32_t *tokens, float *x, int rows, int T,
+                    int vocab, int d, int zero_oob, af_stream_t stream) {
+  const char *fn = "af_embed_gather";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(table && tokens && x, "af_embed_gather", "null pointer");
+  AF_REQUIRE(rows >= 0 && T > 0 && vocab > 0 && d > 0, "af_embed_gather", "bad sizes");
+  if (rows == 0) return AF_OK;
+  embed_gather_kernel<<<rows, 256, 0, af::stream_of(stream)>>>(table, table_bf16, tokens, x, rows, T, vocab, d,
+                                                               zero_oob);
+  return af::launched(ctx, fn);
+}
+
+int af_rmsnorm_to_bf16(af_ctx *ctx, const float *x, const float *w, uint16_t *y, int rows, int d, float eps,
+                       af_stream_t stream) {
+  const char *fn = "af_rmsnorm_to_bf16";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(x && y, "af_rmsnorm_to_bf16", "null pointer");
+  AF_REQUIRE(rows >= 0 && d > 0 && d <= 12288, "af_rmsnorm_to_bf16", "bad sizes rows=%d d=%d", rows, d);
+  if (rows == 0) return AF_OK;
+  rmsnorm_to_bf16_kernel<<<rows, 256, (size_t)d * 4, af::stream_of(stream)>>>(x, w,
+                                                                             reinterpret_cast<__nv_bfloat16 *>(y),
+                                                                             d, eps);
+  return af::launched(ctx, fn);
+}
+
+int af_argmax_rows(af_ctx *ctx, const float *logits, int rows, int V, int32_t *out, af_stream_t stream) {
+  const char *fn = "af_argmax_rows";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(logits && out && rows >= 0 && V > 0, "af_argmax_rows", "bad arguments");
+  if (rows == 0) return AF_OK;
+  argmax_rows_kernel<<<rows, 512, 0, af::stream_of(stream)>>>(logits, V, out);
+  return af::launched(ctx, fn);
+}
+
+int af_pack_gate_up(af_ctx *ctx, const void *src, void *dst, int f, int d, int elem_bytes, af_stream_t stream) {
+  const char *fn = "af_pack_gate_up";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(src && dst && src != dst, "af_pack_gate_up", "src and dst must be distinct buffers");
+  AF_REQUIRE(f > 0 && f % 16 == 0, "af_pack_gate_up", "ffn dim %d must be a multiple of 16", f);
+  AF_REQUIRE((elem_bytes == 2 || elem_bytes == 4) && ((int64_t)d * elem_bytes) % 16 == 0 && af::aligned16(src) &&
+                 af::aligned16(dst),
+             "af_pack_gate_up", "rows must be 16-byte aligned");
+  pack_gate_up_kernel<<<2 * f, 128, 0, af::stream_of(stream)>>>(static_cast<const uint8_t *>(src),
+                                                               static_cast<uint8_t *>(dst), f, d * elem_bytes);
+  return af::launched(ctx, fn);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decoder layer (AceEngine.forward_layer_internal, cpu/mod.rs:646-706) for a
+// batch of streams:
+//   h = RMSNorm1(x); qkv = h W_qkv^T; o = retention(qkv)     (state in place)
+//   x += W_o RMSNorm_ret(o)        (1/rms applied per row in the GEMM epilogue,
+//                                   residual added in the same epilogue)
+//   h = RMSNorm2(x); x += W_down (silu(g) * u),  [g|u] = h W_gate_up^T
+//                                  (SwiGLU in the gate/up GEMM epilogue)
+namespace af {
+int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
+                          const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
+                          int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn, int out_bf16);
+int launch_rmsnorm_f32(af_ctx *ctx, const float *x, const float *res, const float *w, float *y, float *sum_out,
+                       int rows, int d, float eps, cudaStream_t st, const char *fn);
+int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
+                             const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
+                             cudaStream_t st, const char *fn);
+int chunkwise_head_dim();
+int chunkwise_parts();
+
+static int gemm(af_ctx *ctx, const void *A, const void *B, int M, int N, int K, bool fp32, void *out, int out_bf16,
+                const float *residual, const float *parts, int nparts, float inv_d, float eps, int swiglu,
+                cudaStream_t st, const char *fn) {
+  GemmEpilogueArgs e;
+  e.out = out;
+  e.ldo = swiglu ? N / 2 : N;
+  e.out_bf16 = out_bf16;
+  e.residual = residual;
+  e.ldr = N;
+  e.row_parts = parts;
+  e.nparts = nparts;
+  e.inv_d = inv_d;
+  e.eps = eps;
+  e.swiglu = swiglu;
+  return tc_gemm(ctx, A, K, B, K, M, N, K, fp32, e, st, fn);
+}
+
+static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
+
+static int check_layer(const af_layer_weights *w, int B, int d, int H, int f, const char *fn) {
+  if (!w || !w->w_qkv || !w->w_o || !w->w_gate_up || !w->w_down || !w->norm1 || !w->norm2 || !w->ret_norm)
+    return fail(AF_ERR_ARG, "%s: null weight pointer", fn);
+  if (B < 0 || d <= 0 || H <= 0 || d % H || f <= 0 || f % 16)
+    return fail(AF_ERR_ARG, "%s: bad sizes batch=%d d=%d heads=%d ffn=%d (ffn must be a multiple of 16)", fn, B, d,
+                H, f);
+  if (d % 8 || f % 8) return fail(AF_ERR_ARG, "%s: d_model and ffn must be multiples of 8", fn);
+  return AF_OK;
+}
+}  // namespace af
+
+extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, int weights_bf16, float *x,
+                                       float *state, int64_t state_batch_stride, const float *gamma, float eps,
+                                       int B, int d, int H, int f, af_stream_t stream) {
+  const char *fn = "af_decoder_layer_decode";
+  AF_ENTER(ctx, fn);
+  int rc = af::check_layer(w, B, d, H, f, fn);
+  if (rc) return rc;
+  AF_REQUIRE(x && state && gamma && af::aligned16(x) && af::aligned16(state), "af_decoder_layer_decode",
+             "x and state must be non-null and 16-byte aligned");
+  const int dh = d / H;
+  AF_REQUIRE(dh == 64 || dh == 128 || dh == 256, "af_decoder_layer_decode", "head_dim %d must be 64, 128 or 256",
+             dh);
+  AF_REQUIRE(state_batch_stride >= (int64_t)H * dh * dh && state_batch_stride % 4 == 0, "af_decoder_layer_decode",
+             "bad state_batch_stride");
+  if (B == 0) return AF_OK;
+  const bool fp32 = !weights_bf16;
+  const size_t ab = fp32 ? 4 : 2;  // activation bytes feeding the GEMMs
+  const size_t h_b = af::align256((size_t)B * d * ab), qkv_b = af::align256((size_t)B * 3 * d * 4),
+               o_b = af::align256((size_t)B * d * ab), ss_b = af::align256((size_t)B * H * 4),
+               hid_b = af::align256((size_t)B * f * ab);
+  void *ws = nullptr;
+  rc = af::workspace(ctx, h_b + qkv_b + o_b + ss_b + hid_b, &ws, fn);
+  if (rc) return rc;
+  uint8_t *p = static_cast<uint8_t *>(ws);
+  void *h = p;
+  float *qkv = reinterpret_cast<float *>(p + h_b);
+  void *o = p + h_b + qkv_b;
+  float *ss = reinterpret_cast<float *>(p + h_b + qkv_b + o_b);
+  void *hid = p + h_b + qkv_b + o_b + ss_b;
+  cudaStream_t st = af::stream_of(stream);
+  if (fp32) rc = af::launch_rmsnorm_f32(ctx, x, nullptr, w->norm1, (float *)h, nullptr, B, d, eps, st, fn);
+  else rc = af_rmsnorm_to_bf16(ctx, x, w->norm1, (uint16_t *)h, B, d, eps, stream);
+  if (rc) return rc;
+  rc = af::gemm(ctx, h, w->w_qkv, B, 3 * d, d, fp32, qkv, 0, nullptr, nullptr, 0, 0.f, 0.f, 0, st, fn);
+  if (rc) return rc;
+  rc = af::launch_retention_step(ctx, state, state_batch_stride, gamma, qkv, qkv + d, qkv + 2 * d, 3 * (int64_t)d,
+                                 (float *)o, d, B, H, dh, w->ret_norm, ss, st, fn, fp32 ? 0 : 1);
+  if (rc) return rc;
+  rc = af::gemm(ctx, o, w->w_o, B, d, d, fp32, x, 0, x, ss, H, 1.0f / (float)d, eps, 0, st, fn);
+  if (rc) return rc;
+  if (fp32) rc = af::launch_rmsnorm_f32(ctx, x, nullptr, w->norm2, (float *)h, nullptr, B, d, eps, st, fn);
+  else rc = af_rmsnorm_to_bf16(ctx, x, w->norm2, (uint16_t *)h, B, d, eps, stream);
+  if (rc) return rc;
+  rc = af::gemm(ctx, h, w->w_gate_up, B, 2 * f, d, fp32, hid, fp32 ? 0 : 1, nullptr, nullptr, 0, 0.f, 0.f, 1, st, fn);
+  if (rc) return rc;
+  return af::gemm(ctx, hid, w->w_down, B, d, f, fp32, x, 0, x, nullptr, 0, 0.f, 0.f, 0, st, fn);
+}
+
+extern "C" int af_decoder_layer_prefill(af_ctx *ctx, const af_layer_weights *w, float *x, const float *state_in,
+                                        float *state_out, const float *gamma, float eps, int B, int T, int d, int H,
+                                        int f, af_stream_t stream) {
+  const char *fn = "af_decoder_layer_prefill";
+  AF_ENTER(ctx, fn);
+  int rc = af::check_layer(w, B, d, H, f, fn);
+  if (rc) return rc;
+  AF_REQUIRE(x && gamma && af::aligned16(x), "af_decoder_layer_prefill", "x must be non-null and 16-byte aligned");
+  AF_REQUIRE(d == H * af::chunkwise_head_dim(), "af_decoder_layer_prefill", "head_dim must be %d",
+             af::chunkwise_head_dim());
+  AF_REQUIRE((int64_t)B * T <= 65535LL * 128, "af_decoder_layer_prefill", "batch*T too large");
+  if (B == 0 || T == 0) return AF_OK;
+  const int N = B * T;
+  const int parts = H * af::chunkwise_parts();
+  const size_t h_b = af::align256((size_t)N * d * 2), qkv_b = af::align256((size_t)N * 3 * d * 2),
+               o_b = af::align256((size_t)N * d * 2), ss_b = af::align256((size_t)N * parts * 4),
+               hid_b = af::align256((size_t)N * f * 2);
+  void *ws = nullptr;
+  rc = af::workspace(ctx, h_b + qkv_b + o_b + ss_b + hid_b, &ws, fn);
+  if (rc) return rc;
+  uint8_t *p = static_cast<uint8_t *>(ws);
+  uint16_t *h = reinterpret_cast<uint16_t *>(p);
+  void *qkv = p + h_b;
+  void *o = p + h_b + qkv_b;
+  float *ss = reinterpret_cast<float *>(p + h_b + qkv_b + o_b);
+  void *hid = p + h_b + qkv_b + o_b + ss_b;
+  cudaStream_t st = af::stream_of(stream);
+  rc = af_rmsnorm_to_bf16(ctx, x, w->norm1, h, N, d, eps, stream);
+  if (rc) return rc;
+  rc = af::gemm(ctx, h, w->w_qkv, N, 3 * d, d, false, qkv, 1, nullptr, nullptr, 0, 0.f, 0.f, 0, st, fn);
+  if (rc) return rc;
+  rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, o, w->ret_norm, ss, st, fn);
+  if (rc) return rc;
+  rc = af::gemm(ctx, o, w->w_o, N, d, d, false, x, 0, x, ss, parts, 1.0f / (float)d, eps, 0, st, fn);
+  if (rc) return rc;
+  rc = af_rmsnorm_to_bf16(ctx, x, w->norm2, h, N, d, eps, stream);
+  if (rc) return rc;
+  rc = af::gemm(ctx, h, w->w_gate_up, N, 2 * f, d, false, hid, 1, nullptr, nullptr, 0, 0.f, 0.f, 1, st, fn);
+  if (rc) return rc;
+  return af::gemm(ctx, hid, w->w_down, N, d, f, false, x, 0, x, nullptr, 0, 0.f, 0.f, 0, st, fn);
+}
+
+// logits = table . norm(x) (tied LM head, sampler.rs:67-81) then first-max
+// argmax.  `final_norm` (may be NULL) is AceEngine's optional final RMSNorm.
+extern "C" int af_lm_head_argmax(af_ctx *ctx, const float *x, const float *final_norm, float eps, const void *table,
+                                 int table_bf16, int B, int V, int d, float *logits, int32_t *tokens,
+                                 af_stream_t stream) {
+  const char *fn = "af_lm_head_argmax";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(x && table && logits && tokens && B >= 0 && V > 0 && d > 0 && d % 8 == 0, "af_lm_head_argmax",
+             "bad arguments");
+  if (B == 0) return AF_OK;
+  cudaStream_t st = af::stream_of(stream);
+  const bool fp32 = !table_bf16;
+  void *ws = nullptr;
+  int rc = af::workspace(ctx, af::align256((size_t)B * d * 4), &ws, fn);
+  if (rc) return rc;
+  if (fp32) {
+    if (final_norm) rc = af::launch_rmsnorm_f32(ctx, x, nullptr, final_norm, (float *)ws, nullptr, B, d, eps, st, fn);
+    else rc = (cudaMemcpyAsync(ws, x, (size_t)B * d * 4, cudaMemcpyDeviceToDevice, st) == cudaSuccess)
+                  ? AF_OK
+                  : af::fail(AF_ERR_CUDA, "%s: copy failed", fn);
+  } else {
+    rc = af_rmsnorm_to_bf16(ctx, x, final_norm, (uint16_t *)ws, B, d, final_norm ? eps : -1.f, stream);
+  }
+  if (rc) return rc;
+  rc = af::gemm(ctx, ws, table, B, V, d, fp32, logits, 0, nullptr, nullptr, 0, 0.f, 0.f, 0, st, fn);
+  if (rc) return rc;
+  return af_argmax_rows(ctx, logits, B, V, tokens, stream);
+}

@@ -134,11 +134,12 @@ __global__ void __launch_bounds__(192, 1)
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % C::STAGES;
       const uint32_t ph = (kb / C::STAGES) & 1;
-      if (!mbar_wait(TF32X3 ? &conv[s] : &full[s], ph)) {
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(TF32X3 ? &conv[s] : &full[s], ph));
+      if (!ok) {
         if (lane == 0) fail();
         break;
       }
-      if (s_abort) break;
+      if (__any_sync(0xffffffffu, s_abort != 0)) break;
       tc_fence_after();
       if (lane == 0) {
         const uint64_t da = sdesc_k_sw128(stage_a(s)), db = sdesc_k_sw128(stage_b(s));
@@ -218,15 +219,28 @@ __global__ void __launch_bounds__(192, 1)
         tmem_wait_ld();
         const int nout = (n0 + c) / 2;  // first output column of this group
         if (ok && row_ok && n0 + c + 32 <= N) {
-          float h[16];
+          float hh[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const float gg = g[j] * scale, uu = u[j] * scale;
-            h[j] = gg / (1.0f + expf(-gg)) * uu;
+            hh[j] = gg / (1.0f + expf(-gg)) * uu;
           }
-          float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + nout;
+          if (ep.out_bf16) {
+            __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + nout;
+            uint32_t pk[8];
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4 *>(o + j) = make_float4(h[j], h[j + 1], h[j + 2], h[j + 3]);
+            for (int j = 0; j < 8; ++j) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(hh[2 * j], hh[2 * j + 1]);
+              pk[j] = *reinterpret_cast<uint32_t *>(&b2);
+            }
+            reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          } else {
+            float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + nout;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4 *>(o + j) = make_float4(hh[j], hh[j + 1], hh[j + 2], hh[j + 3]);
+          }
         }
       }
     } else {
@@ -355,19 +369,25 @@ int tc_gemm(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb,
   if (rc) return rc;
   if (M == 0 || N == 0) return AF_OK;
   const bool vec = af::aligned16(a.out) && (a.ldo * (a.out_bf16 ? 2 : 4)) % 16 == 0;
-  if (a.swiglu && (!vec || a.out_bf16 || N % 32 != 0))
-    return af::fail(AF_ERR_ARG, "%s: SwiGLU epilogue needs fp32 aligned output and N %% 32 == 0", fn);
+  if (a.swiglu && (!vec || N % 32 != 0))
+    return af::fail(AF_ERR_ARG, "%s: SwiGLU epilogue needs an aligned output and N %% 32 == 0", fn);
   GemmEpilogue ep{a.out,      a.ldo, a.out_bf16,  a.bias, a.row_parts, a.nparts, a.inv_d,
                   a.eps,      a.residual, a.ldr, a.swiglu, vec ? 1 : 0};
+  // Pick the widest tile that still puts a CTA on every SM (decode-sized M
+  // needs narrow tiles so the weight stream is spread over all SMs).
+  const int64_t mt = (M + 127) / 128;
+  auto tiles = [&](int bn) { return mt * ((N + bn - 1) / bn); };
+  const int64_t sms = ctx->num_sms;
   if (fp32) {
-    // small M (decode batches): narrow tiles so the grid covers the SMs
-    const int64_t tiles128 = (int64_t)((N + 127) / 128) * ((M + 127) / 128);
-    if (tiles128 < ctx->num_sms) return launch_tc<64, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-    return launch_tc<128, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+    if (tiles(128) >= sms) return launch_tc<128, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+    if (tiles(64) >= sms || a.swiglu) return launch_tc<64, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+    return launch_tc<32, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
   }
-  const int64_t tiles256 = (int64_t)((N + 255) / 256) * ((M + 127) / 128);
-  if (tiles256 < ctx->num_sms) return launch_tc<128, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-  return launch_tc<256, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  if (tiles(256) >= sms) return launch_tc<256, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  if (tiles(128) >= sms) return launch_tc<128, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  if (tiles(64) >= sms) return launch_tc<64, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  if (tiles(32) >= sms || a.swiglu) return launch_tc<32, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  return launch_tc<16, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
 }
 
 }  // namespace af

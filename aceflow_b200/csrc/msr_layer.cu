@@ -12,7 +12,8 @@
 namespace af {
 int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
-                          int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn);
+                          int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn,
+                          int out_bf16);
 int linear_f32(af_ctx *ctx, const float *x, int64_t ldx, const float *w, int64_t ldw, const float *bias, float *y,
                int64_t ldy, int M, int N, int K, const float *parts, int nparts, float inv_d, float eps,
                cudaStream_t st, const char *fn);
@@ -33,7 +34,7 @@ int msr_decode_step_impl(af_ctx *ctx, const float *x, float *state, const float 
   int rc = linear_f32(ctx, x, d, w_qkv, d, nullptr, qkv, 3 * d, B, 3 * d, d, nullptr, 0, 0.f, 0.f, st, fn);
   if (rc) return rc;
   rc = launch_retention_step(ctx, state, (int64_t)H * dh * dh, gamma, qkv, qkv + d, qkv + 2 * d, 3 * (int64_t)d, o,
-                             d, B, H, dh, ret_norm_w, sumsq, st, fn);
+                             d, B, H, dh, ret_norm_w, sumsq, st, fn, 0);
   if (rc) return rc;
   return linear_f32(ctx, o, d, w_o, d, nullptr, out, d, B, d, d, sumsq, H, 1.0f / (float)d, eps, st, fn);
 }

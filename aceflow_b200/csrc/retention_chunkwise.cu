@@ -108,6 +108,19 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
 
 __device__ __forceinline__ void math_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Named barrier over the 128 math threads that also ORs a predicate, so every
+// participant leaves with the same answer (s_abort may change concurrently).
+__device__ __forceinline__ bool math_sync_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred)
+      : "memory");
+  return r != 0;
+}
+
 __global__ void __launch_bounds__(192, 1)
     retention_chunkwise_kernel(const __grid_constant__ CUtensorMap tm, ChunkParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -188,7 +201,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int c = 0; c < nch; ++c) {
       bool ok = mbar_wait(bar_load, c & 1);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok || s_abort) { if (!ok && lane == 0) fail(); break; }
+      if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
       tc_fence_after();
       if (lane == 0) {
 #pragma unroll
@@ -205,7 +218,7 @@ __global__ void __launch_bounds__(192, 1)
       ok = mbar_wait(bar_math, c & 1);
       if (ok && c > 0) ok = mbar_wait(bar_out, (c - 1) & 1);
       ok = __all_sync(0xffffffffu, ok);
-      if (!ok || s_abort) { if (!ok && lane == 0) fail(); break; }
+      if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
       tc_fence_after();
       if (lane == 0) {
         // O^T = bf16(S^T) . Q^T  (K = 256 keys)
@@ -261,8 +274,7 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       if (c > 0) ok = mbar_wait(bar_upd, (c - 1) & 1);
       if (!ok) s_abort = 1;
-      math_sync();
-      if (s_abort) break;
+      if (math_sync_or(s_abort != 0)) break;
       tc_fence_after();
       // (a) S_op = bf16(S^T) (K-major [v][k]); S^T *= gamma^L in TMEM
       const float gL = gpow[L];
@@ -334,13 +346,11 @@ __global__ void __launch_bounds__(192, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(bar_math);
-      math_sync();
-      if (s_abort) break;
+      if (math_sync_or(s_abort != 0)) break;
       // (d) O = gamma^(i+1) * O^T[v][i]; store bf16 O * w; partial sum of O^2 per token
       ok = mbar_wait(bar_o, c & 1);
       if (!ok) s_abort = 1;
-      math_sync();
-      if (s_abort) break;
+      if (math_sync_or(s_abort != 0)) break;
       tc_fence_after();
       const int col = h * DH + slice * VS + v;
       const float wv = p.norm_w ? p.norm_w[col] : 1.f;
@@ -370,11 +380,11 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     // final state: S[k][v] = S^T[v][k]
-    if (!s_abort && p.state_out) {
+    const bool aborted = math_sync_or(s_abort != 0);
+    if (!aborted && p.state_out) {
       bool ok = mbar_wait(bar_upd, (nch - 1) & 1);
       if (!ok) s_abort = 1;
-      math_sync();
-      if (!s_abort) {
+      if (!math_sync_or(s_abort != 0)) {
         tc_fence_after();
         float *so = p.state_out + ((size_t)(b * p.H + h) * DH) * DH + slice * VS + v;
 #pragma unroll 1
@@ -387,7 +397,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int j = 0; j < 16; ++j) so[(size_t)(k0 + j) * DH] = x[j];
         }
       }
-    } else if (!s_abort && nch > 0) {
+    } else if (!aborted && nch > 0) {
       if (!mbar_wait(bar_upd, (nch - 1) & 1)) s_abort = 1;  // last MMAs retired before TMEM is freed
     }
   }

@@ -69,7 +69,7 @@ __device__ __forceinline__ float4 step_rows(float *__restrict__ S, float g, cons
 template <int DH, int THREADS>
 __device__ __forceinline__ void finish_head(float4 acc, float4 *red, float *__restrict__ o_out,
                                             const float *__restrict__ norm_w_head,
-                                            float *__restrict__ sumsq_out, int cg, int rg) {
+                                            float *__restrict__ sumsq_out, int cg, int rg, bool out_bf16 = false) {
   using Sh = StepShape<DH, THREADS>;
   red[rg * Sh::NCG + cg] = acc;
   __syncthreads();
@@ -93,7 +93,13 @@ __device__ __forceinline__ void finish_head(float4 acc, float4 *red, float *__re
       o.z *= w.z;
       o.w *= w.w;
     }
-    reinterpret_cast<float4 *>(o_out)[threadIdx.x] = o;
+    if (out_bf16) {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y), hi = __floats2bfloat162_rn(o.z, o.w);
+      reinterpret_cast<uint2 *>(o_out)[threadIdx.x] =
+          make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+    } else {
+      reinterpret_cast<float4 *>(o_out)[threadIdx.x] = o;
+    }
   }
   if (sumsq_out) {
     ss = warp_sum(ss);
@@ -115,7 +121,7 @@ __global__ void __launch_bounds__(THREADS)
                           const float *__restrict__ q, const float *__restrict__ k,
                           const float *__restrict__ v, int64_t qs, float *__restrict__ out,
                           int64_t out_rs, int H, const float *__restrict__ norm_w,
-                          float *__restrict__ sumsq) {
+                          float *__restrict__ sumsq, int out_bf16) {
   using Sh = StepShape<DH, THREADS>;
   __shared__ float sk[DH], sq[DH];
   __shared__ float4 red[Sh::RG * Sh::NCG];
@@ -133,9 +139,11 @@ __global__ void __launch_bounds__(THREADS)
   __syncthreads();
   float *S = state + (size_t)b * state_bs + (size_t)h * DH * DH;
   const float4 acc = step_rows<DH, THREADS>(S, g, sk, sq, vv, cg, rg);
-  finish_head<DH, THREADS>(acc, red, out + (size_t)b * out_rs + (size_t)h * DH,
-                           norm_w ? norm_w + (size_t)h * DH : nullptr,
-                           sumsq ? sumsq + blockIdx.x : nullptr, cg, rg);
+  float *o_out = out_bf16 ? reinterpret_cast<float *>(reinterpret_cast<__nv_bfloat16 *>(out) + (size_t)b * out_rs +
+                                                   (size_t)h * DH)
+                         : out + (size_t)b * out_rs + (size_t)h * DH;
+  finish_head<DH, THREADS>(acc, red, o_out, norm_w ? norm_w + (size_t)h * DH : nullptr,
+                           sumsq ? sumsq + blockIdx.x : nullptr, cg, rg, out_bf16 != 0);
 }
 
 // Token-serial scan: the same per-token work, T tokens in order.
@@ -304,30 +312,33 @@ namespace af {
 int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs,
                           int batch, int H, int dh, const float *norm_w, float *sumsq, cudaStream_t st,
-                          const char *fn) {
+                          const char *fn, int out_bf16) {
   if (batch == 0) return AF_OK;
   const dim3 grid((unsigned)(batch * H));
+  if (out_bf16 && !(dh == 256 || dh == 128 || dh == 64) )
+    return fail(AF_ERR_ARG, "%s: bf16 output needs head_dim 64, 128 or 256", fn);
   if (dh % 4 != 0 || dh > 1024 || state_bs % 4 != 0 || !aligned16(state)) {
     if (norm_w || sumsq) return fail(AF_ERR_ARG, "%s: fused norm needs head_dim %% 4 == 0 and <= 1024", fn);
     retention_step_scalar<<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, 1, H, dh);
     return launched(ctx, fn);
   }
   bool fast = (out_rs % 4 == 0) && aligned16(out) && (norm_w == nullptr || aligned16(norm_w));
+  if (out_bf16 && !fast) return fail(AF_ERR_ARG, "%s: bf16 output needs an aligned output buffer", fn);
   if (fast && dh == 256) {
     retention_step_kernel<256, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                          norm_w, sumsq);
+                                                          norm_w, sumsq, out_bf16);
   } else if (fast && dh == 128) {
     retention_step_kernel<128, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                          norm_w, sumsq);
+                                                          norm_w, sumsq, out_bf16);
   } else if (fast && dh == 64) {
     retention_step_kernel<64, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                         norm_w, sumsq);
+                                                         norm_w, sumsq, out_bf16);
   } else if (fast && dh == 32) {
     retention_step_kernel<32, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                         norm_w, sumsq);
+                                                         norm_w, sumsq, out_bf16);
   } else if (fast && dh == 16) {
     retention_step_kernel<16, 64><<<grid, 64, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                       norm_w, sumsq);
+                                                       norm_w, sumsq, out_bf16);
   } else {
     const int ncg = dh / 4;
     int rgs = 256 / ncg;
@@ -351,7 +362,7 @@ extern "C" int af_retention_step(af_ctx *ctx, float *state, int64_t state_bs, co
   int rc = check_common(fn, state, gamma, q, k, v, out, batch, H, dh, state_bs, qs);
   if (rc) return rc;
   return af::launch_retention_step(ctx, state, state_bs, gamma, q, k, v, qs, out, (int64_t)H * dh, batch, H, dh,
-                                   nullptr, nullptr, af::stream_of(stream), fn);
+                                   nullptr, nullptr, af::stream_of(stream), fn, 0);
 }
 
 extern "C" int af_retention_scan(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,

@@ -1,0 +1,322 @@
+"""AceEngine on the GPU (mirrors aceflow-core/src/cpu/mod.rs:30-612).
+
+Same constructor and method names as the reference's PyO3 class, batched
+over `batch` independent streams (the reference engine is one stream; a
+1-D argument here means stream 0 of a batch of one).  Weights live on the
+device in fp32 (exact parity path: 3xTF32 tensor cores, fp32 activations) or
+bf16 (throughput path: bf16 tensor cores, tensor-core chunkwise prefill).
+
+State layout: one device tensor [num_layers][batch][H][dh][dh] fp32 (layer
+major, so each layer's slice is the [batch][H][k][v] layout every retention
+kernel takes).
+
+Supported sampling: greedy (temperature <= 1e-4) with repetition_penalty 1.0,
+the configuration the decoder-stack workload uses; other settings raise
+NotImplementedError rather than silently differing from the reference.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib, cuda_ops
+
+
+class _LayerWeights(ctypes.Structure):
+    """Mirror of af_layer_weights (include/aceflow_cuda.h)."""
+
+    _fields_ = [("w_qkv", ctypes.c_void_p), ("w_o", ctypes.c_void_p), ("w_gate_up", ctypes.c_void_p),
+                ("w_down", ctypes.c_void_p), ("norm1", ctypes.c_void_p), ("norm2", ctypes.c_void_p),
+                ("ret_norm", ctypes.c_void_p)]
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32))
+
+
+class AceEngine:
+    """Retention decoder stack on a CUDA device."""
+
+    def __init__(self, num_layers: int, d_model: int, num_heads: int, embedding_table=None, *, batch: int = 1,
+                 device: str = "cuda:0", weight_dtype: str = "float32", eps: float = 1e-5):
+        if num_heads == 0 or d_model % num_heads != 0:
+            raise ValueError(f"d_model ({d_model}) must be divisible by num_heads ({num_heads})")
+        if weight_dtype not in ("float32", "bfloat16"):
+            raise ValueError("weight_dtype must be 'float32' or 'bfloat16'")
+        self.num_layers = num_layers
+        self._d = d_model
+        self._h = num_heads
+        self._dh = d_model // num_heads
+        self.batch = batch
+        self.eps = eps
+        self.device = torch.device(device)
+        self._wdt = torch.float32 if weight_dtype == "float32" else torch.bfloat16
+        self.gamma = cuda_ops.gammas(num_heads, self.device)
+        self.states = torch.zeros(num_layers, batch, num_heads, self._dh, self._dh, device=self.device)
+        self.layers: List[Optional[dict]] = [None] * num_layers
+        self.d_ffn = 4 * d_model
+        self.embedding = None
+        self.final_norm = None
+        self.lm_head = None
+        if embedding_table is not None:
+            self.set_embedding_table(embedding_table)
+
+    # ---------------------------------------------------------------- weights
+    def reset_memory(self) -> None:
+        self.states.zero_()
+
+    def _dev(self, a, dtype=None) -> torch.Tensor:
+        return torch.from_numpy(_f32(a)).to(self.device, dtype or torch.float32).contiguous()
+
+    def set_embedding_table(self, table) -> None:
+        t = _f32(table).reshape(-1)
+        if t.size % self._d:
+            raise ValueError(f"Embedding table length {t.size} must be divisible by d_model {self._d}")
+        self.embedding = self._dev(t.reshape(-1, self._d), self._wdt)
+
+    def load_weights(self, embeddings, final_norm_gamma=None, lm_head=None) -> None:
+        self.set_embedding_table(embeddings)
+        if final_norm_gamma is not None:
+            g = _f32(final_norm_gamma).reshape(-1)
+            if g.size != self._d:
+                raise ValueError(f"final_norm_gamma length {g.size} must match d_model {self._d}")
+            self.final_norm = self._dev(g)
+        if lm_head is not None:
+            h = _f32(lm_head).reshape(-1)
+            if h.size != self.vocab_size * self._d:
+                raise ValueError(f"lm_head length {h.size} must match vocab_size * d_model "
+                                 f"({self.vocab_size} * {self._d})")
+            self.lm_head = self._dev(h.reshape(-1, self._d), self._wdt)
+        else:
+            self.lm_head = None
+
+    def load_layer_weights(self, layer_idx: int, w_qkv, w_o, w_gate_up, w_down, norm1_gamma, norm2_gamma,
+                           ret_norm_gamma=None) -> None:
+        """Same argument order and checks as AceEngine.load_layer_weights
+        (aceflow-core/src/cpu/mod.rs:177-269); w_gate_up is [gate; up]."""
+        d = self._d
+        if layer_idx >= self.num_layers:
+            raise ValueError(f"layer_idx {layer_idx} exceeds num_layers {self.num_layers}")
+        qkv, o, gu, dn = (_f32(a).reshape(-1) for a in (w_qkv, w_o, w_gate_up, w_down))
+        n1, n2 = _f32(norm1_gamma).reshape(-1), _f32(norm2_gamma).reshape(-1)
+        if qkv.size != 3 * d * d:
+            raise ValueError(f"w_qkv size {qkv.size} must match 3 * d_model^2 ({3 * d * d})")
+        if o.size != d * d:
+            raise ValueError(f"w_o size {o.size} must match d_model^2 ({d * d})")
+        if gu.size % (2 * d):
+            raise ValueError(f"w_gate_up size {gu.size} must be divisible by 2 * d_model ({2 * d})")
+        f = gu.size // (2 * d)
+        if dn.size != d * f:
+            raise ValueError(f"w_down size {dn.size} must match d_model * d_ffn ({d} * {f})")
+        if n1.size != d or n2.size != d:
+            raise ValueError(f"norm1 ({n1.size}) and norm2 ({n2.size}) must match d_model ({d})")
+        rn = np.ones(d, np.float32) if ret_norm_gamma is None else _f32(ret_norm_gamma).reshape(-1)
+        if rn.size != d:
+            raise ValueError(f"ret_norm_gamma length {rn.size} must match d_model {d}")
+        gu_dev = self._dev(gu.reshape(2 * f, d), self._wdt)
+        packed = torch.empty_like(gu_dev)
+        _lib.call("af_pack_gate_up", _lib.context(self.device.index or 0), gu_dev.data_ptr(), packed.data_ptr(), f, d,
+                  gu_dev.element_size(), torch.cuda.current_stream(self.device).cuda_stream)
+        L = dict(w_qkv=self._dev(qkv.reshape(3 * d, d), self._wdt), w_o=self._dev(o.reshape(d, d), self._wdt),
+                 w_gate_up=packed, w_down=self._dev(dn.reshape(d, f), self._wdt), norm1=self._dev(n1),
+                 norm2=self._dev(n2), ret_norm=self._dev(rn), d_ffn=f)
+        s = _LayerWeights(*(L[k].data_ptr() for k in ("w_qkv", "w_o", "w_gate_up", "w_down", "norm1", "norm2",
+                                                          "ret_norm")))
+        L["struct"] = s
+        self.layers[layer_idx] = L
+        self.d_ffn = f
+
+    # ---------------------------------------------------------------- helpers
+    @property
+    def d_model(self) -> int:
+        return self._d
+
+    @property
+    def num_heads(self) -> int:
+        return self._h
+
+    @property
+    def head_dim(self) -> int:
+        return self._dh
+
+    @property
+    def vocab_size(self) -> int:
+        return 0 if self.embedding is None else int(self.embedding.shape[0])
+
+    def state_memory_kb(self) -> int:
+        return self.states.numel() * 4 // 1024
+
+    def _ctx(self) -> int:
+        return _lib.context(self.device.index or 0)
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def _check_layer(self, i: int) -> dict:
+        if i >= self.num_layers:
+            raise ValueError(f"layer_idx {i} out of range (total layers: {self.num_layers})")
+        L = self.layers[i]
+        if L is None:
+            raise ValueError(f"Layer {i} weights are not loaded.")
+        return L
+
+    def _rows(self, x) -> tuple:
+        a = _f32(x)
+        one = a.ndim == 1
+        a = a.reshape(-1, self._d) if not one else a.reshape(1, -1)
+        if a.shape[1] != self._d:
+            raise ValueError(f"x length {a.shape[1]} must match d_model {self._d}")
+        if a.shape[0] != self.batch:
+            raise ValueError(f"expected {self.batch} stream rows, got {a.shape[0]}")
+        return a, one
+
+    # ---------------------------------------------------------------- layer ops
+    def forward_layer_device(self, layer_idx: int, x: torch.Tensor) -> torch.Tensor:
+        """In place on a device tensor x [batch, d] fp32."""
+        L = self._check_layer(layer_idx)
+        _lib.call("af_decoder_layer_decode", self._ctx(), ctypes.byref(L["struct"]), int(self._wdt == torch.bfloat16),
+                  x.data_ptr(), self.states[layer_idx].data_ptr(), self._h * self._dh * self._dh,
+                  self.gamma.data_ptr(), float(self.eps), self.batch, self._d, self._h, L["d_ffn"], self._stream())
+        return x
+
+    def forward_layer(self, layer_idx: int, x):
+        """AceEngine.forward_layer: x is updated in place (numpy, [d] or [batch, d])."""
+        a, one = self._rows(x)
+        t = torch.from_numpy(a).to(self.device)
+        self.forward_layer_device(layer_idx, t)
+        res = t.cpu().numpy()
+        if isinstance(x, np.ndarray) and x.dtype == np.float32:
+            x[...] = res.reshape(x.shape)
+        return res[0] if one else res
+
+    def retention_step(self, layer_idx: int, q, k, v):
+        """AceEngine.retention_step (cpu/mod.rs:486-512) for the batch."""
+        if layer_idx >= self.num_layers:
+            raise ValueError(f"layer_idx {layer_idx} out of range (total layers: {self.num_layers})")
+        rows = [self._rows(a)[0] for a in (q, k, v)]
+        one = np.asarray(q).ndim == 1
+        qkv = torch.from_numpy(np.concatenate(rows, axis=1)).to(self.device)
+        d = self._d
+        out = cuda_ops.retention_step(self.states[layer_idx], self.gamma, qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:])
+        res = out.cpu().numpy()
+        return res[0] if one else res
+
+    def retention_step_packed(self, layer_idx: int, qkv):
+        a = _f32(qkv)
+        if a.shape[-1] != 3 * self._d:
+            raise ValueError(f"Expected packed QKV vector of length {3 * self._d}, got {a.shape[-1]}")
+        d = self._d
+        return self.retention_step(layer_idx, a[..., :d], a[..., d:2 * d], a[..., 2 * d:])
+
+    def prefill_recurrent(self, layer_idx: int, seq_len: int, q_seq, k_seq, v_seq):
+        """AceEngine.prefill_recurrent (cpu/mod.rs:547-587): token-serial over
+        seq_len tokens; returns the last token's output."""
+        if layer_idx >= self.num_layers:
+            raise ValueError(f"layer_idx {layer_idx} out of range (total layers: {self.num_layers})")
+        d = self._d
+        arrs = [_f32(a).reshape(self.batch, -1) for a in (q_seq, k_seq, v_seq)]
+        if any(a.shape[1] != seq_len * d for a in arrs):
+            raise ValueError(f"Expected sequence vectors of length {seq_len * d} (seq_len {seq_len} * d_model {d})")
+        qkv = torch.from_numpy(np.concatenate([a.reshape(self.batch, seq_len, d) for a in arrs], 2)).to(self.device)
+        out = cuda_ops.retention_scan(self.states[layer_idx], self.gamma, qkv[..., :d], qkv[..., d:2 * d],
+                                      qkv[..., 2 * d:])
+        res = out[:, -1].cpu().numpy() if seq_len else np.zeros((self.batch, d), np.float32)
+        return res[0] if self.batch == 1 and np.asarray(q_seq).ndim == 1 else res
+
+    # ---------------------------------------------------------------- generation
+    def _check_generate(self, temperature, repetition_penalty):
+        if self.embedding is None:
+            raise ValueError("Embedding table not loaded.")
+        for i, L in enumerate(self.layers):
+            if L is None:
+                raise ValueError(f"Layer {i} weights are not loaded.")
+        if temperature > 1e-4 or repetition_penalty != 1.0:
+            raise NotImplementedError("only greedy decoding (temperature <= 1e-4, repetition_penalty 1.0) runs on "
+                                      "the GPU engine")
+
+    def prefill_device(self, x: torch.Tensor, T: int) -> None:
+        """All layers over a [batch*T, d] fp32 device tensor of prompt
+        embeddings, in place, leaving each layer's state after the prompt."""
+        if self._wdt == torch.bfloat16 and self._dh == 256:
+            for i in range(self.num_layers):
+                L = self.layers[i]
+                st = self.states[i]
+                _lib.call("af_decoder_layer_prefill", self._ctx(), ctypes.byref(L["struct"]), x.data_ptr(),
+                          st.data_ptr(), st.data_ptr(), self.gamma.data_ptr(), float(self.eps), self.batch, T,
+                          self._d, self._h, L["d_ffn"], self._stream())
+            return
+        # token-serial (exact) path: the reference's own prefill order
+        xv = x.view(self.batch, T, self._d)
+        for t in range(T):
+            row = xv[:, t].contiguous()
+            for i in range(self.num_layers):
+                self.forward_layer_device(i, row)
+            xv[:, t] = row
+
+    def generate_batch(self, prompts, max_new_tokens: int, stop_at_eos: bool = False, teacher=None,
+                       return_logits: bool = False):
+        """Greedy generation for `batch` streams: prompts [batch, P] ids.
+        Returns tokens [batch, max_new_tokens] (-1 after a stream stopped at
+        EOS id 2 when stop_at_eos) and optionally the logits per step.
+        `teacher` [batch, max_new_tokens] feeds given ids instead of the
+        argmax (for parity checks)."""
+        self._check_generate(0.0, 1.0)
+        pr = torch.as_tensor(np.asarray(prompts, np.int32)).to(self.device)
+        B, P = pr.shape
+        if B != self.batch:
+            raise ValueError(f"expected {self.batch} prompts, got {B}")
+        V, d = self.vocab_size, self._d
+        head = self.lm_head if self.lm_head is not None else self.embedding
+        bf = int(self._wdt == torch.bfloat16)
+        st = self._stream()
+        x = torch.empty(B * P, d, device=self.device)
+        _lib.call("af_embed_gather", self._ctx(), self.embedding.data_ptr(), bf, pr.data_ptr(), x.data_ptr(), B * P, P,
+                  V, d, 0, st)
+        self.prefill_device(x, P)
+        cur = x.view(B, P, d)[:, -1].contiguous()
+        logits = torch.empty(B, V, device=self.device)
+        toks = torch.empty(B, dtype=torch.int32, device=self.device)
+        out = torch.full((B, max_new_tokens), -1, dtype=torch.int32, device=self.device)
+        all_logits = [] if return_logits else None
+        fn = self.final_norm
+        teach = None if teacher is None else torch.as_tensor(np.asarray(teacher, np.int32)).to(self.device)
+        alive = torch.ones(B, dtype=torch.bool, device=self.device)
+        for s in range(max_new_tokens):
+            _lib.call("af_lm_head_argmax", self._ctx(), cur.data_ptr(), None if fn is None else fn.data_ptr(),
+                      float(self.eps), head.data_ptr(), bf, B, V, d, logits.data_ptr(), toks.data_ptr(), st)
+            out[:, s] = torch.where(alive, toks, torch.full_like(toks, -1))
+            if return_logits:
+                all_logits.append(logits.clone())
+            nxt = toks if teach is None else teach[:, s].contiguous()
+            if stop_at_eos:
+                alive = alive & (nxt != 2)
+            if s + 1 == max_new_tokens:
+                break
+            _lib.call("af_embed_gather", self._ctx(), self.embedding.data_ptr(), bf, nxt.data_ptr(), cur.data_ptr(), B,
+                      1, V, d, 1, st)
+            for i in range(self.num_layers):
+                self.forward_layer_device(i, cur)
+        res = out.cpu().numpy()
+        if return_logits:
+            return res, torch.stack(all_logits, 1).cpu().numpy()
+        return res
+
+    def generate_stream(self, prompt_tokens: Sequence[int], max_new_tokens: int, temperature: float = 0.7,
+                        top_k: int = 40, top_p: float = 0.9, repetition_penalty: float = 1.2) -> List[int]:
+        """AceEngine.generate_stream (cpu/mod.rs:454-484) for a one-stream
+        engine: greedy only; stops after EOS id 2 like the reference."""
+        self._check_generate(temperature, repetition_penalty)
+        if self.batch != 1:
+            raise ValueError("generate_stream drives one stream; use generate_batch")
+        toks = self.generate_batch([list(prompt_tokens)], max_new_tokens, stop_at_eos=True)[0]
+        res = []
+        for t in toks:
+            if t < 0:
+                break
+            res.append(int(t))
+            if t == 2:
+                break
+        return res

@@ -167,6 +167,66 @@ int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv, c
                         int d_model, int num_heads, const float *state_in, float *state_out,
                         void *out, int out_bf16, af_stream_t stream);
 
+/* ------------------------------------------------------- decoder stack */
+/* Weights of one decoder layer (AceEngine's LayerWeights,
+ * aceflow-core/src/cpu/mod.rs:18-28), device pointers.  Matrices are fp32 or
+ * bf16 (one dtype per layer), (out, in) layout.  w_gate_up must be in the
+ * 16-row interleave produced by af_pack_gate_up from AceEngine's
+ * [gate rows; up rows] layout.  Norm weights are fp32. */
+typedef struct {
+  const void *w_qkv;     /* [3d][d], rows q, k, v */
+  const void *w_o;       /* [d][d] */
+  const void *w_gate_up; /* [2f][d], interleaved */
+  const void *w_down;    /* [d][f] */
+  const float *norm1, *norm2, *ret_norm; /* [d] */
+} af_layer_weights;
+
+/* Row permutation [gate; up] -> (16 gate rows, 16 up rows) groups, the
+ * layout the fused SwiGLU epilogue reads.  f % 16 == 0; elem_bytes 2 or 4. */
+int af_pack_gate_up(af_ctx *ctx, const void *src, void *dst, int f, int d, int elem_bytes,
+                    af_stream_t stream);
+
+/* One decoder layer at one token for `batch` streams, in place on x [batch][d]
+ * fp32 and the layer's state slice (streams `state_batch_stride` floats
+ * apart).  AceEngine.forward_layer (aceflow-core/src/cpu/mod.rs:423-444 ->
+ * 646-706) batched.  weights_bf16 selects bf16 weights (bf16 tensor cores,
+ * bf16 activations into the GEMMs) or fp32 weights (3xTF32, fp32 accuracy).
+ * head_dim 64, 128 or 256; f % 16 == 0. */
+int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, int weights_bf16, float *x,
+                            float *state, int64_t state_batch_stride, const float *gamma, float eps,
+                            int batch, int d_model, int num_heads, int d_ffn, af_stream_t stream);
+
+/* One decoder layer over T prompt tokens per stream (bf16 weights, tensor-core
+ * chunkwise retention), in place on x [batch*T][d] fp32; replaces running
+ * forward_layer_internal token by token over the prompt
+ * (generate_stream_internal, cpu/mod.rs:721-730).  state_in/state_out
+ * [batch][H][256][256] fp32 (either may be NULL: zeros / not written). */
+int af_decoder_layer_prefill(af_ctx *ctx, const af_layer_weights *w, float *x, const float *state_in,
+                             float *state_out, const float *gamma, float eps, int batch, int T,
+                             int d_model, int num_heads, int d_ffn, af_stream_t stream);
+
+/* x[r] = table[tokens[r]] (fp32 or bf16 table [vocab][d] -> fp32 rows).  An
+ * out-of-range prompt id keeps the previous row of its sequence (cpu/mod.rs:
+ * 721-726); zero_oob = 1 gives the generated-token rule (zeros, 757-763).
+ * Rows form sequences of T. */
+int af_embed_gather(af_ctx *ctx, const void *table, int table_bf16, const int32_t *tokens, float *x,
+                    int rows, int T, int vocab, int d, int zero_oob, af_stream_t stream);
+
+/* y = bf16(RMSNorm(x) * w) for fp32 rows; w == NULL gives a plain cast. */
+int af_rmsnorm_to_bf16(af_ctx *ctx, const float *x, const float *w, uint16_t *y, int rows, int d,
+                       float eps, af_stream_t stream);
+
+/* Greedy pick per row, first maximum wins (sampler.rs:118-128). */
+int af_argmax_rows(af_ctx *ctx, const float *logits, int rows, int vocab, int32_t *out,
+                   af_stream_t stream);
+
+/* logits [batch][vocab] = table . RMSNorm_final(x) (tied LM head,
+ * project_logits, sampler.rs:67-81; final_norm may be NULL as in AceEngine's
+ * default), then tokens[b] = argmax.  table fp32 or bf16 [vocab][d]. */
+int af_lm_head_argmax(af_ctx *ctx, const float *x, const float *final_norm, float eps,
+                      const void *table, int table_bf16, int batch, int vocab, int d,
+                      float *logits, int32_t *tokens, af_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

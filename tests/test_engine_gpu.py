@@ -1,0 +1,118 @@
+"""Decoder stack (AceEngine twin) parity against the C restatement of
+AceEngine (oracle/cpu_ref.c: forward_layer_internal + greedy generation).
+
+fp32 weights: logits within 1e-4 relative and identical greedy tokens.
+bf16 weights: the oracle runs on the same bf16-rounded weights in fp32;
+logits within 2e-2 under teacher forcing (oracle tokens fed back), so one
+near-tie cannot cascade.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+from oracle import cpu_ref
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def _model(L, d, f, V, seed, bf16):
+    rng = np.random.default_rng(seed)
+    r = (lambda a: torch.from_numpy(a).bfloat16().float().numpy()) if bf16 else (lambda a: a)
+    layers = []
+    for _ in range(L):
+        layers.append(dict(
+            w_qkv=r((0.02 * rng.standard_normal((3 * d, d))).astype(np.float32)),
+            w_o=r((0.02 * rng.standard_normal((d, d))).astype(np.float32)),
+            w_gate_up=r((0.02 * rng.standard_normal((2 * f, d))).astype(np.float32)),
+            w_down=r((0.02 * rng.standard_normal((d, f))).astype(np.float32)),
+            norm1=(1 + 0.1 * rng.standard_normal(d)).astype(np.float32),
+            norm2=(1 + 0.1 * rng.standard_normal(d)).astype(np.float32),
+            ret_norm=(1 + 0.1 * rng.standard_normal(d)).astype(np.float32)))
+    emb = r(rng.standard_normal((V, d)).astype(np.float32))
+    return layers, emb
+
+
+def _engine(layers, emb, H, B, dtype, eps):
+    from aceflow_b200.engine import AceEngine
+
+    L = len(layers)
+    d = emb.shape[1]
+    eng = AceEngine(L, d, H, emb, batch=B, weight_dtype=dtype, eps=eps)
+    for i, w in enumerate(layers):
+        eng.load_layer_weights(i, w["w_qkv"], w["w_o"], w["w_gate_up"], w["w_down"], w["norm1"], w["norm2"],
+                               w["ret_norm"])
+    return eng
+
+
+def test_forward_layer_fp32_matches_oracle(dev):
+    L, d, H, f, V, B = 1, 256, 2, 96, 50, 3
+    layers, emb = _model(L, d, f, V, 1, False)
+    eng = _engine(layers, emb, H, B, "float32", 1e-5)
+    rng = np.random.default_rng(5)
+    states = np.zeros((B, L, H, d // H, d // H), np.float32)
+    for _ in range(4):
+        x = rng.standard_normal((B, d)).astype(np.float32)
+        ref = cpu_ref.forward_layer(x.copy(), layers, 0, states, np.array(
+            [1 - 2.0 ** (-5 - h) for h in range(H)], np.float32), 1e-5)
+        got = eng.forward_layer(0, x.copy())
+        assert rel_err(got, ref) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_generate_matches_oracle(dev, dtype):
+    bf16 = dtype == "bfloat16"
+    L, d, H, f, V, B, P, n = 2, 512, 2, 256, 300, 3, 20, 6
+    layers, emb = _model(L, d, f, V, 2, bf16)
+    rng = np.random.default_rng(9)
+    prompts = rng.integers(0, V, (B, P)).astype(np.int32)
+    toks_ref, logits_ref, _, _ = cpu_ref.generate_greedy(layers, emb, prompts, n, H, 1e-6, want_logits=True)
+    eng = _engine(layers, emb, H, B, dtype, 1e-6)
+    toks, logits = eng.generate_batch(prompts, n, teacher=toks_ref, return_logits=True)
+    tol = 2e-2 if bf16 else 1e-4
+    assert rel_err(logits, logits_ref) < tol
+    if not bf16:
+        assert np.array_equal(toks, toks_ref)
+    else:
+        top2 = np.sort(logits_ref, -1)[..., -2:]
+        clear = (top2[..., 1] - top2[..., 0]) > 0.05 * np.abs(logits_ref).max()
+        assert np.array_equal(toks[clear], toks_ref[clear])
+
+
+def test_generate_stream_api(dev):
+    L, d, H, f, V = 1, 256, 1, 64, 40
+    layers, emb = _model(L, d, f, V, 4, False)
+    eng = _engine(layers, emb, H, 1, "float32", 1e-5)
+    out = eng.generate_stream([3, 7, 1], 5, temperature=0.0, repetition_penalty=1.0)
+    ref, _, _, _ = cpu_ref.generate_greedy(layers, emb, np.array([[3, 7, 1]], np.int32), 5, H, 1e-5,
+                                           stop_at_eos=True)
+    exp = []
+    for t in ref[0]:
+        if t < 0:
+            break
+        exp.append(int(t))
+        if t == 2:
+            break
+    assert out == exp
+    with pytest.raises(NotImplementedError):
+        eng.generate_stream([1], 2)  # default temperature 0.7: sampling is not on the GPU path
+
+
+def test_engine_validation(dev):
+    from aceflow_b200.engine import AceEngine
+
+    with pytest.raises(ValueError):
+        AceEngine(1, 10, 3)
+    eng = AceEngine(1, 64, 1)
+    with pytest.raises(ValueError):
+        eng.load_layer_weights(0, np.zeros(10), np.zeros(64 * 64), np.zeros(2 * 64 * 64), np.zeros(64 * 64),
+                               np.ones(64), np.ones(64))
+    with pytest.raises(ValueError):
+        eng.forward_layer(0, np.zeros(64, np.float32))  # weights not loaded
