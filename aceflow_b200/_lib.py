@@ -57,7 +57,7 @@ SIGNATURES = {
 _RESTYPE = {"af_last_error": ctypes.c_char_p}
 
 _lib = None
-_lock = threading.Lock()
+_lock = threading.RLock()
 _contexts: dict[int, int] = {}
 
 
@@ -105,11 +105,12 @@ def context(device_index: int) -> int:
     """One af_ctx per device, created on first use (cached for the process)."""
     ctx = _contexts.get(device_index)
     if ctx is None:
+        L = lib()  # load outside the context lock
         with _lock:
             ctx = _contexts.get(device_index)
             if ctx is None:
                 p = ctypes.c_void_p()
-                check(lib().af_cuda_init(device_index, ctypes.byref(p)), "af_cuda_init")
+                check(L.af_cuda_init(device_index, ctypes.byref(p)), "af_cuda_init")
                 ctx = p.value
                 _contexts[device_index] = ctx
     return ctx

@@ -183,14 +183,15 @@ __global__ void __launch_bounds__(256)
     retention_step_generic(float *__restrict__ state, int64_t state_bs, const float *__restrict__ gamma,
                            const float *__restrict__ q, const float *__restrict__ k,
                            const float *__restrict__ v, int64_t qs, float *__restrict__ out,
-                           int64_t out_rs, int T, int H, int dh, const float *__restrict__ norm_w,
+                           int64_t out_rs, int T, int H, int dh, int rgs, const float *__restrict__ norm_w,
                            float *__restrict__ sumsq) {
+  // rgs (row groups) comes from the host, which sized `red` for rgs * ncg
+  // entries; blockDim.x may exceed rgs * ncg (rounded up to whole warps).
   extern __shared__ float smem[];
   float *sk = smem, *sq = smem + dh;
   float4 *red = reinterpret_cast<float4 *>(smem + 2 * dh);
   __shared__ float warp_part[8];
   const int ncg = dh / 4;
-  const int rgs = blockDim.x / ncg;
   const int b = blockIdx.x / H, h = blockIdx.x % H;
   const int cg = threadIdx.x % ncg, rg = threadIdx.x / ncg;
   const bool active = rg < rgs;
@@ -347,7 +348,7 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
     const int threads = ((ncg * rgs + 31) / 32) * 32;
     const size_t smem = (size_t)2 * dh * sizeof(float) + (size_t)rgs * ncg * sizeof(float4);
     retention_step_generic<<<grid, threads, smem, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, 1, H,
-                                                        dh, norm_w, sumsq);
+                                                        dh, rgs, norm_w, sumsq);
   }
   return launched(ctx, fn);
 }
@@ -395,7 +396,7 @@ extern "C" int af_retention_scan(af_ctx *ctx, float *state, int64_t state_bs, co
     const int threads = ((ncg * rgs + 31) / 32) * 32;
     const size_t smem = (size_t)2 * dh * sizeof(float) + (size_t)rgs * ncg * sizeof(float4);
     retention_step_generic<<<grid, threads, smem, st>>>(state, state_bs, gamma, q, k, v, qs, out, (int64_t)H * dh,
-                                                        T, H, dh, nullptr, nullptr);
+                                                        T, H, dh, rgs, nullptr, nullptr);
   }
   return af::launched(ctx, fn);
 }

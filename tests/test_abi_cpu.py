@@ -70,3 +70,17 @@ def test_init_without_gpu_fails_cleanly(libpath):
     rc = _lib.lib().af_cuda_init(0, ctypes.byref(p))
     assert rc != 0 and not p.value
     assert _lib.last_error()
+
+
+def test_first_call_through_context_does_not_deadlock(libpath):
+    """The first ABI use may be a context lookup (it loads the library inside
+    its lock); it must return (an error without a GPU), not hang."""
+    import subprocess
+    import sys
+
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "from aceflow_b200 import _lib\n"
+            "try:\n    _lib.context(0)\nexcept Exception as e:\n    print('raised', type(e).__name__)\n"
+            "else:\n    print('ok')\n") % ROOT
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and ("raised" in r.stdout or "ok" in r.stdout), r.stdout + r.stderr
