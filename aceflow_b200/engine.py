@@ -69,12 +69,15 @@ class AceEngine:
         self.states.zero_()
 
     def _dev(self, a, dtype=None) -> torch.Tensor:
+        if isinstance(a, torch.Tensor):  # already a tensor (e.g. generated on the device)
+            return a.detach().to(self.device, dtype or torch.float32).contiguous()
         return torch.from_numpy(_f32(a)).to(self.device, dtype or torch.float32).contiguous()
 
     def set_embedding_table(self, table) -> None:
-        t = _f32(table).reshape(-1)
-        if t.size % self._d:
-            raise ValueError(f"Embedding table length {t.size} must be divisible by d_model {self._d}")
+        t = table.reshape(-1) if isinstance(table, torch.Tensor) else _f32(table).reshape(-1)
+        n = t.numel() if isinstance(t, torch.Tensor) else t.size
+        if n % self._d:
+            raise ValueError(f"Embedding table length {n} must be divisible by d_model {self._d}")
         self.embedding = self._dev(t.reshape(-1, self._d), self._wdt)
 
     def load_weights(self, embeddings, final_norm_gamma=None, lm_head=None) -> None:
@@ -100,21 +103,23 @@ class AceEngine:
         d = self._d
         if layer_idx >= self.num_layers:
             raise ValueError(f"layer_idx {layer_idx} exceeds num_layers {self.num_layers}")
-        qkv, o, gu, dn = (_f32(a).reshape(-1) for a in (w_qkv, w_o, w_gate_up, w_down))
-        n1, n2 = _f32(norm1_gamma).reshape(-1), _f32(norm2_gamma).reshape(-1)
-        if qkv.size != 3 * d * d:
-            raise ValueError(f"w_qkv size {qkv.size} must match 3 * d_model^2 ({3 * d * d})")
-        if o.size != d * d:
-            raise ValueError(f"w_o size {o.size} must match d_model^2 ({d * d})")
-        if gu.size % (2 * d):
-            raise ValueError(f"w_gate_up size {gu.size} must be divisible by 2 * d_model ({2 * d})")
-        f = gu.size // (2 * d)
-        if dn.size != d * f:
-            raise ValueError(f"w_down size {dn.size} must match d_model * d_ffn ({d} * {f})")
-        if n1.size != d or n2.size != d:
-            raise ValueError(f"norm1 ({n1.size}) and norm2 ({n2.size}) must match d_model ({d})")
-        rn = np.ones(d, np.float32) if ret_norm_gamma is None else _f32(ret_norm_gamma).reshape(-1)
-        if rn.size != d:
+        flat = lambda a: a.reshape(-1) if isinstance(a, torch.Tensor) else _f32(a).reshape(-1)  # noqa: E731
+        qkv, o, gu, dn = (flat(a) for a in (w_qkv, w_o, w_gate_up, w_down))
+        n1, n2 = flat(norm1_gamma), flat(norm2_gamma)
+        size = lambda a: a.numel() if isinstance(a, torch.Tensor) else a.size  # noqa: E731
+        if size(qkv) != 3 * d * d:
+            raise ValueError(f"w_qkv size {size(qkv)} must match 3 * d_model^2 ({3 * d * d})")
+        if size(o) != d * d:
+            raise ValueError(f"w_o size {size(o)} must match d_model^2 ({d * d})")
+        if size(gu) % (2 * d):
+            raise ValueError(f"w_gate_up size {size(gu)} must be divisible by 2 * d_model ({2 * d})")
+        f = size(gu) // (2 * d)
+        if size(dn) != d * f:
+            raise ValueError(f"w_down size {size(dn)} must match d_model * d_ffn ({d} * {f})")
+        if size(n1) != d or size(n2) != d:
+            raise ValueError(f"norm1 ({size(n1)}) and norm2 ({size(n2)}) must match d_model ({d})")
+        rn = np.ones(d, np.float32) if ret_norm_gamma is None else flat(ret_norm_gamma)
+        if size(rn) != d:
             raise ValueError(f"ret_norm_gamma length {rn.size} must match d_model {d}")
         gu_dev = self._dev(gu.reshape(2 * f, d), self._wdt)
         packed = torch.empty_like(gu_dev)
@@ -256,8 +261,22 @@ class AceEngine:
                 self.forward_layer_device(i, row)
             xv[:, t] = row
 
+    def _decode_step(self, cur, toks, logits, head, bf, gather_from=None):
+        """One greedy step on device buffers: (optionally) embed `gather_from`
+        ids into cur, run every layer, LM head + argmax into toks."""
+        st = self._stream()
+        V, d, B = self.vocab_size, self._d, self.batch
+        if gather_from is not None:
+            _lib.call("af_embed_gather", self._ctx(), self.embedding.data_ptr(), bf, gather_from.data_ptr(),
+                      cur.data_ptr(), B, 1, V, d, 1, st)
+        for i in range(self.num_layers):
+            self.forward_layer_device(i, cur)
+        fn = self.final_norm
+        _lib.call("af_lm_head_argmax", self._ctx(), cur.data_ptr(), None if fn is None else fn.data_ptr(),
+                  float(self.eps), head.data_ptr(), bf, B, V, d, logits.data_ptr(), toks.data_ptr(), st)
+
     def generate_batch(self, prompts, max_new_tokens: int, stop_at_eos: bool = False, teacher=None,
-                       return_logits: bool = False):
+                       return_logits: bool = False, use_graph: bool = False, timing: dict | None = None):
         """Greedy generation for `batch` streams: prompts [batch, P] ids.
         Returns tokens [batch, max_new_tokens] (-1 after a stream stopped at
         EOS id 2 when stop_at_eos) and optionally the logits per step.
@@ -273,9 +292,16 @@ class AceEngine:
         bf = int(self._wdt == torch.bfloat16)
         st = self._stream()
         x = torch.empty(B * P, d, device=self.device)
+        if timing is not None:
+            e_pre = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+            e_pre[0].record()
         _lib.call("af_embed_gather", self._ctx(), self.embedding.data_ptr(), bf, pr.data_ptr(), x.data_ptr(), B * P, P,
                   V, d, 0, st)
         self.prefill_device(x, P)
+        if timing is not None:
+            e_pre[1].record()
+            torch.cuda.synchronize()
+            timing["prefill_ms"] = e_pre[0].elapsed_time(e_pre[1])
         cur = x.view(B, P, d)[:, -1].contiguous()
         logits = torch.empty(B, V, device=self.device)
         toks = torch.empty(B, dtype=torch.int32, device=self.device)
@@ -284,6 +310,8 @@ class AceEngine:
         fn = self.final_norm
         teach = None if teacher is None else torch.as_tensor(np.asarray(teacher, np.int32)).to(self.device)
         alive = torch.ones(B, dtype=torch.bool, device=self.device)
+        if use_graph and teacher is None and not return_logits and not stop_at_eos:
+            return self._generate_graph(cur, logits, toks, out, head, bf, max_new_tokens, timing)
         for s in range(max_new_tokens):
             _lib.call("af_lm_head_argmax", self._ctx(), cur.data_ptr(), None if fn is None else fn.data_ptr(),
                       float(self.eps), head.data_ptr(), bf, B, V, d, logits.data_ptr(), toks.data_ptr(), st)
@@ -303,6 +331,46 @@ class AceEngine:
         if return_logits:
             return res, torch.stack(all_logits, 1).cpu().numpy()
         return res
+
+    def _generate_graph(self, cur, logits, toks, out, head, bf, n, timing):
+        """Greedy decode with each step (embed, all layers, LM head, argmax)
+        replayed from one captured CUDA graph."""
+        st = self._stream()
+        V, d, B = self.vocab_size, self._d, self.batch
+        fn = self.final_norm
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        ev[0].record()
+        _lib.call("af_lm_head_argmax", self._ctx(), cur.data_ptr(), None if fn is None else fn.data_ptr(),
+                  float(self.eps), head.data_ptr(), bf, B, V, d, logits.data_ptr(), toks.data_ptr(), st)
+        out[:, 0] = toks
+        ev[1].record()
+        if n > 1:
+            nxt = toks.clone()
+            # eager step sizes the workspace and loads every kernel before capture
+            saved = self.states.clone()
+            cur_saved = cur.clone()
+            self._decode_step(cur, toks, logits, head, bf, gather_from=nxt)
+            self.states.copy_(saved)
+            cur.copy_(cur_saved)
+            del saved
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._decode_step(cur, toks, logits, head, bf, gather_from=nxt)
+            torch.cuda.synchronize()
+            toks.copy_(out[:, 0])
+            ev[1].record()
+            for s in range(1, n):
+                nxt.copy_(toks)
+                g.replay()
+                out[:, s] = toks
+            ev[2].record()
+            torch.cuda.synchronize()
+            if timing is not None:
+                timing["first_token_ms"] = ev[0].elapsed_time(ev[1])
+                timing["decode_ms"] = ev[1].elapsed_time(ev[2])
+                timing["decode_steps"] = n - 1
+            del g
+        return out.cpu().numpy()
 
     def generate_stream(self, prompt_tokens: Sequence[int], max_new_tokens: int, temperature: float = 0.7,
                         top_k: int = 40, top_p: float = 0.9, repetition_penalty: float = 1.2) -> List[int]:

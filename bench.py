@@ -311,6 +311,10 @@ def run_ours(args):
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
     }
+    if world == 1 and not args.no_prefill:
+        line["prefill"] = bench_prefill(dev, args.prefill_passes, peaks)
+    if world == 1 and not args.no_stack:
+        line["stack"] = bench_stack(dev, peaks)
     if world == 1 and rank == 0 and not args.no_cpu:
         nthreads = host_threads()
         v, steps, b, el = cpu_decode_sample(args.cpu_seconds, nthreads)
@@ -378,6 +382,119 @@ def run_e2e(args, dev, state, gamma, w_qkv, w_o, ret_w, cuda_ops, barrier):
     return e0.elapsed_time(e1)
 
 
+# ---------------------------------------------------------------- prefill
+PREFILL = dict(B=8, T=4096, d=2048, H=8, C=64)
+
+
+def prefill_flops(B, T, d, H, C):
+    """Algorithmic FLOP of one MSR prefill pass: 4 projections 2*N*d^2 each,
+    intra-chunk 4*N*H*C*dh, inter-chunk + state update 4*N*H*dh^2."""
+    N, dh = B * T, d // H
+    proj = 4 * 2 * N * d * d
+    intra = 4 * N * H * C * dh
+    inter = 4 * N * H * dh * dh
+    return proj, intra, inter
+
+
+def bench_prefill(dev, passes, peaks):
+    import torch
+
+    from aceflow_b200 import _lib, cuda_ops
+
+    c = PREFILL
+    B, T, d, H = c["B"], c["T"], c["d"], c["H"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(B, T, d, generator=g, device=dev).bfloat16()
+    w_qkv = (0.02 * torch.randn(3 * d, d, generator=g, device=dev)).bfloat16()
+    w_o = (0.02 * torch.randn(d, d, generator=g, device=dev)).bfloat16()
+    rw = torch.ones(d, device=dev)
+    gamma = cuda_ops.gammas(H, dev)
+    out = None
+    for _ in range(3):
+        out, _st = cuda_ops.msr_prefill_bf16(x, w_qkv, w_o, rw, gamma, EPS, want_state=False)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(passes):
+        out, _st = cuda_ops.msr_prefill_bf16(x, w_qkv, w_o, rw, gamma, EPS, want_state=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / passes
+    # the retention core alone (chunkwise kernel), CUDA events on its stream
+    qkv = torch.randn(B * T, 3 * d, generator=g, device=dev).bfloat16()
+    for _ in range(2):
+        cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False)
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(passes):
+        cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    core_ms = e2.elapsed_time(e3) / passes
+    _lib.check_device(dev.index or 0)
+    proj, intra, inter = prefill_flops(B, T, d, H, c["C"])
+    total = proj + intra + inter
+    tfl = total / (ms / 1e3) / 1e12
+    core_tfl = (intra + inter) / (core_ms / 1e3) / 1e12
+    return {
+        "metric": "retention prefill tok/s (B=8,T=4096,d=2048)", "value": B * T / (ms / 1e3), "unit": "tok/s",
+        "ms_per_pass": ms, "passes": passes, "dtype": "bf16 (fp32 accumulate)",
+        "config": {"workload": "MultiScaleRetention prefill, d_model=2048, 8 heads, B=8, T=4096, chunk 64",
+                   "l2": "inputs larger than L2 (x 128 MiB, qkv 384 MiB)"},
+        "roofline": {"bound": "tensor", "achieved": tfl, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tfl / peaks["bf16_tflops"], "algorithmic_flop": total},
+        "retention_core": {"kernel": "retention_chunkwise_kernel", "ms": core_ms, "achieved": core_tfl,
+                           "unit": "TFLOP/s", "frac": core_tfl / peaks["bf16_tflops"],
+                           "algorithmic_flop": intra + inter},
+    }
+
+
+# ---------------------------------------------------------------- stack
+STACK = dict(L=24, d=2048, H=8, f=5632, V=32000, B=64, P=512, n=256)
+
+
+def bench_stack(dev, peaks):
+    import torch
+
+    from aceflow_b200 import _lib
+    from aceflow_b200.engine import AceEngine
+
+    c = STACK
+    L, d, H, f, V, B, P, n = (c[k] for k in ("L", "d", "H", "f", "V", "B", "P", "n"))
+    g = torch.Generator(device=dev).manual_seed(11)
+    eng = AceEngine(L, d, H, (0.02 * torch.randn(V, d, generator=g, device=dev)), batch=B,
+                    device=str(dev), weight_dtype="bfloat16", eps=1e-6)
+    for i in range(L):
+        r = lambda *s: 0.02 * torch.randn(*s, generator=g, device=dev)  # noqa: E731
+        one = torch.ones(d, device=dev)
+        eng.load_layer_weights(i, r(3 * d, d), r(d, d), r(2 * f, d), r(d, f), one, one, one)
+    prompts = torch.randint(0, V, (B, P), generator=g, device=dev).cpu().numpy()
+    eng.generate_batch(prompts, 4, use_graph=True)  # warm-up (kernels, workspace)
+    eng.reset_memory()
+    t = {}
+    toks = eng.generate_batch(prompts, n, use_graph=True, timing=t)
+    _lib.check_device(dev.index or 0)
+    params = L * (4 * d * d + 3 * f * d) + V * d
+    pre_flop = 2 * params * B * P + L * sum(prefill_flops(B, P, d, H, 64)[1:])
+    dec_bytes = 2 * params + 2 * L * B * H * (d // H) ** 2 * 4
+    dec_ms = t["decode_ms"] / t["decode_steps"]
+    return {
+        "metric": "24-layer retention decoder: prefill and greedy decode tok/s",
+        "config": {"workload": "24 x [RMSNorm -> MSR -> RMSNorm -> SwiGLU(5632)], d_model=2048, 8 heads, "
+                               "vocab 32000 tied, bf16 weights, batch 64, 512-token prompt, 256 greedy steps",
+                   "eps": 1e-6},
+        "prefill_tok_s": B * P / (t["prefill_ms"] / 1e3), "prefill_ms": t["prefill_ms"],
+        "prefill_tflops": pre_flop / (t["prefill_ms"] / 1e3) / 1e12,
+        "prefill_frac": pre_flop / (t["prefill_ms"] / 1e3) / 1e12 / peaks["bf16_tflops"],
+        "decode_tok_s": B / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
+        "decode_hbm_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
+        "decode_frac": dec_bytes / (dec_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
+        "decode_bytes_per_step": dec_bytes, "first_token_ms": t["first_token_ms"],
+        "tokens_checksum": int(np.asarray(toks, np.int64).sum()),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -386,6 +503,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill workload (N=1 only)")
+    ap.add_argument("--no-stack", action="store_true", help="skip the 24-layer stack workload (N=1 only)")
+    ap.add_argument("--prefill-passes", type=int, default=10)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
