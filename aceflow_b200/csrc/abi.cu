@@ -1,6 +1,7 @@
 // Context, workspace and error plumbing of the C ABI (include/aceflow_cuda.h).
 #include "common.cuh"
 
+#include <cstdlib>
 #include <new>
 
 namespace af {
@@ -76,6 +77,23 @@ int af_cuda_init(int device, af_ctx **out) {
     delete ctx;
     return af::fail(AF_ERR_CUDA, "af_cuda_init: device error word: %s", cudaGetErrorString(e));
   }
+  int lo_prio = 0, hi_prio = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetStreamPriorityRange(&lo_prio, &hi_prio);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&ctx->side[0], cudaStreamNonBlocking, hi_prio);
+  if (e == cudaSuccess) e = cudaStreamCreateWithPriority(&ctx->side[1], cudaStreamNonBlocking, lo_prio);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming);
+  for (int i = 0; i < af_ctx::kMaxSlices && e == cudaSuccess; ++i) {
+    e = cudaEventCreateWithFlags(&ctx->ev_a[i], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->ev_b[i], cudaEventDisableTiming);
+  }
+  if (e != cudaSuccess) {
+    af_ctx *tmp = ctx;
+    ctx->magic = kCtxMagic;
+    af_cuda_destroy(tmp);
+    return af::fail(AF_ERR_CUDA, "af_cuda_init: streams/events: %s", cudaGetErrorString(e));
+  }
+  if (const char *env = getenv("AF_DECODE_SLICE_ROWS")) ctx->decode_slice_rows = atoi(env);
   ctx->magic = kCtxMagic;
   *out = ctx;
   return AF_OK;
@@ -85,6 +103,14 @@ int af_cuda_destroy(af_ctx *ctx) {
   AF_ENTER(ctx, "af_cuda_destroy");
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->dev_err) cudaFree(ctx->dev_err);
+  for (int i = 0; i < 2; ++i)
+    if (ctx->side[i]) cudaStreamDestroy(ctx->side[i]);
+  if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+  if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
+  for (int i = 0; i < af_ctx::kMaxSlices; ++i) {
+    if (ctx->ev_a[i]) cudaEventDestroy(ctx->ev_a[i]);
+    if (ctx->ev_b[i]) cudaEventDestroy(ctx->ev_b[i]);
+  }
   ctx->magic = 0;
   delete ctx;
   return AF_OK;

@@ -17,6 +17,13 @@ struct af_ctx {
   size_t workspace_bytes = 0;
   int64_t launches = 0;
   int *dev_err = nullptr;  // device error word: bit AF_ERR_TIMEOUT set by bounded waits
+  // side streams + events for the overlapped decode step (fork/join on the
+  // caller's stream, so the pattern is also valid under graph capture)
+  cudaStream_t side[2] = {nullptr, nullptr};
+  static constexpr int kMaxSlices = 8;
+  cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+  cudaEvent_t ev_a[kMaxSlices] = {}, ev_b[kMaxSlices] = {};
+  int decode_slice_rows = 128;  // batch rows per overlapped slice (0 disables the overlap)
 };
 
 constexpr uint32_t kCtxMagic = 0xACEF1011u;

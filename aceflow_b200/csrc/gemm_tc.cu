@@ -53,12 +53,22 @@ struct TileCfg {
   static constexpr int UK = 32 / ELEM;           // K per tcgen05.mma (32 bytes)
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
-  static constexpr int STAGE_BYTES = TF32X3 ? 2 * (A_BYTES + B_BYTES) : (A_BYTES + B_BYTES);
-  static constexpr int STAGES = (TF32X3 ? 192 * 1024 : 200 * 1024) / STAGE_BYTES;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  static constexpr int RAW_BYTES = A_BYTES + B_BYTES;  // one TMA ring stage
+  // TF32x3: two split slots (lo parts) double-buffer the converter -> MMA
+  // hand-off, so the TMA ring keeps its full depth for prefetch.
+  static constexpr int LO_SLOTS = TF32X3 ? 2 : 0;
+  static constexpr int STAGES_FIT = (200 * 1024 - LO_SLOTS * RAW_BYTES) / RAW_BYTES;
+  static constexpr int STAGES = STAGES_FIT < 12 ? STAGES_FIT : 12;
+  // TF32x3: the hi.hi products go round-robin over NACC accumulators and the
+  // small hi.lo + lo.hi terms into one more, so each fp32 accumulator sees
+  // fewer tensor-core accumulation steps (its rounding error grows with them).
+  static constexpr int NACC = TF32X3 ? (BN <= 64 ? 4 : 2) : 1;
+  static constexpr int ACC_COLS = (NACC + (TF32X3 ? 1 : 0)) * BN;
+  static constexpr int TMEM_COLS =
+      ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128 : ACC_COLS <= 256 ? 256 : 512;
+  static constexpr size_t SMEM = 1024 + (size_t)(STAGES + LO_SLOTS) * RAW_BYTES + 256;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
-  static_assert((BN & (BN - 1)) == 0, "TMEM allocation is a power of two");
+  static_assert(ACC_COLS <= 512, "TMEM columns");
   static_assert(STAGES >= 2, "pipeline depth");
 };
 
@@ -69,14 +79,17 @@ __global__ void __launch_bounds__(192, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
                      int K, GemmEpilogue ep, int *err) {
   using C = TileCfg<BN, TF32X3>;
+  constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)C::STAGES * C::STAGE_BYTES);
-  uint64_t *full = bars;                    // TMA landed
-  uint64_t *conv = bars + C::STAGES;        // lo parts written (TF32X3)
-  uint64_t *empty = bars + 2 * C::STAGES;   // MMAs retired
-  uint64_t *accum = bars + 3 * C::STAGES;   // accumulator complete
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * C::STAGES + 1);
+  uint8_t *lo_base = smem + (size_t)S * C::RAW_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(lo_base + (size_t)C::LO_SLOTS * C::RAW_BYTES);
+  uint64_t *full = bars;            // [S]  TMA landed
+  uint64_t *empty = bars + S;       // [S]  MMAs reading the stage retired
+  uint64_t *conv = bars + 2 * S;    // [2]  split slot written (TF32x3)
+  uint64_t *lofree = bars + 2 * S + 2;  // [2]  MMAs reading the split slot retired
+  uint64_t *accum = bars + 2 * S + 4;   // accumulators complete
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -85,10 +98,13 @@ __global__ void __launch_bounds__(192, 1)
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 128);
-      mbar_init(&empty[s], 1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int j = 0; j < 2; ++j) {
+      mbar_init(&conv[j], 128);
+      mbar_init(&lofree[j], 1);
     }
     mbar_init(accum, 1);
     fence_barrier_init();
@@ -104,10 +120,10 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto stage_a = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES; };
-  auto stage_b = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + C::A_BYTES; };
-  auto stage_alo = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + C::A_BYTES + C::B_BYTES; };
-  auto stage_blo = [&](int s) { return smem + (size_t)s * C::STAGE_BYTES + 2 * C::A_BYTES + C::B_BYTES; };
+  auto stage_a = [&](int i) { return smem + (size_t)i * C::RAW_BYTES; };
+  auto stage_b = [&](int i) { return smem + (size_t)i * C::RAW_BYTES + C::A_BYTES; };
+  auto lo_a = [&](int j) { return lo_base + (size_t)j * C::RAW_BYTES; };
+  auto lo_b = [&](int j) { return lo_base + (size_t)j * C::RAW_BYTES + C::A_BYTES; };
   auto fail = [&]() {
     s_abort = 1;
     atomicOr(err, 1 << AF_ERR_TIMEOUT);
@@ -117,24 +133,24 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       int issued = 0;
       for (int kb = 0; kb < nk && !s_abort; ++kb) {
-        const int s = kb % C::STAGES;
-        const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1)) { fail(); break; }
-        mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES);
-        tma_load_2d(stage_a(s), &tmA, &full[s], kb * C::BK, m0);
-        tma_load_2d(stage_b(s), &tmB, &full[s], kb * C::BK, n0);
+        const int i = kb % S;
+        const uint32_t ph = (kb / S) & 1;
+        if (!mbar_wait(&empty[i], ph ^ 1)) { fail(); break; }
+        mbar_arrive_expect_tx(&full[i], C::A_BYTES + C::B_BYTES);
+        tma_load_2d(stage_a(i), &tmA, &full[i], kb * C::BK, m0);
+        tma_load_2d(stage_b(i), &tmB, &full[i], kb * C::BK, n0);
         issued = kb + 1;
       }
       // drain: every issued load has landed before this CTA may exit
-      for (int kb = issued - C::STAGES < 0 ? 0 : issued - C::STAGES; kb < issued; ++kb)
-        if (!mbar_wait(&full[kb % C::STAGES], (kb / C::STAGES) & 1)) { fail(); break; }
+      for (int kb = issued - S < 0 ? 0 : issued - S; kb < issued; ++kb)
+        if (!mbar_wait(&full[kb % S], (kb / S) & 1)) { fail(); break; }
     }
   } else if (warp == 1) {
     constexpr uint32_t idesc = idesc_f32acc(TF32X3 ? kFmtTF32 : kFmtBF16, C::BM, BN);
     for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % C::STAGES;
-      const uint32_t ph = (kb / C::STAGES) & 1;
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(TF32X3 ? &conv[s] : &full[s], ph));
+      const int i = kb % S, j = kb & 1;
+      const bool ok = __all_sync(0xffffffffu, TF32X3 ? mbar_wait(&conv[j], (kb >> 1) & 1)
+                                                     : mbar_wait(&full[i], (kb / S) & 1));
       if (!ok) {
         if (lane == 0) fail();
         break;
@@ -142,20 +158,23 @@ __global__ void __launch_bounds__(192, 1)
       if (__any_sync(0xffffffffu, s_abort != 0)) break;
       tc_fence_after();
       if (lane == 0) {
-        const uint64_t da = sdesc_k_sw128(stage_a(s)), db = sdesc_k_sw128(stage_b(s));
+        const uint64_t da = sdesc_k_sw128(stage_a(i)), db = sdesc_k_sw128(stage_b(i));
 #pragma unroll
         for (int k = 0; k < C::BK / C::UK; ++k) {
           const uint64_t off = (uint64_t)(k * 32) >> 4;  // 32 bytes along K inside the swizzle row
           if constexpr (TF32X3) {
-            const uint64_t dal = sdesc_k_sw128(stage_alo(s)), dbl = sdesc_k_sw128(stage_blo(s));
-            umma_tf32(tmem, da + off, db + off, idesc, (kb | k) != 0);
-            umma_tf32(tmem, da + off, dbl + off, idesc, 1);
-            umma_tf32(tmem, dal + off, db + off, idesc, 1);
+            const uint64_t dal = sdesc_k_sw128(lo_a(j)), dbl = sdesc_k_sw128(lo_b(j));
+            const uint32_t acc = tmem + (uint32_t)((kb % C::NACC) * BN);
+            const uint32_t corr = tmem + (uint32_t)(C::NACC * BN);
+            umma_tf32(acc, da + off, db + off, idesc, (kb >= C::NACC || k > 0) ? 1u : 0u);
+            umma_tf32(corr, da + off, dbl + off, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_tf32(corr, dal + off, db + off, idesc, 1);
           } else {
             umma_bf16(tmem, da + off, db + off, idesc, (kb | k) != 0);
           }
         }
-        umma_commit(&empty[s]);
+        umma_commit(&empty[i]);
+        if constexpr (TF32X3) umma_commit(&lofree[j]);
       }
       __syncwarp();
     }
@@ -166,34 +185,24 @@ __global__ void __launch_bounds__(192, 1)
     const int t = threadIdx.x - 64;  // 0..127
     if constexpr (TF32X3) {
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % C::STAGES;
-        const uint32_t ph = (kb / C::STAGES) & 1;
-        if (!mbar_wait(&full[s], ph)) {
+        const int i = kb % S, j = kb & 1;
+        if (!mbar_wait(&full[i], (kb / S) & 1) || !mbar_wait(&lofree[j], ((kb >> 1) & 1) ^ 1)) {
           fail();
           break;
         }
-        // x = hi + lo exactly, hi = x with the low 13 mantissa bits cleared
+        // x = hi + lo exactly: hi = x with the low 13 mantissa bits cleared
         // (an exact tf32 value, written back in place), lo = x - hi.
-        float4 *ra = reinterpret_cast<float4 *>(stage_a(s));
-        float4 *rb = reinterpret_cast<float4 *>(stage_b(s));
-        float4 *la = reinterpret_cast<float4 *>(stage_alo(s));
-        float4 *lb = reinterpret_cast<float4 *>(stage_blo(s));
+        float4 *ra = reinterpret_cast<float4 *>(stage_a(i));
+        float4 *la = reinterpret_cast<float4 *>(lo_a(j));
 #pragma unroll 4
-        for (int i = t; i < C::A_BYTES / 16; i += 128) {
-          const float4 v = ra[i];
+        for (int e = t; e < C::RAW_BYTES / 16; e += 128) {  // A then B, contiguous in both buffers
+          const float4 v = ra[e];
           const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-          ra[i] = h;
-          la[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-        }
-#pragma unroll 4
-        for (int i = t; i < C::B_BYTES / 16; i += 128) {
-          const float4 v = rb[i];
-          const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-          rb[i] = h;
-          lb[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+          ra[e] = h;
+          la[e] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
         }
         fence_proxy_async_smem();
-        mbar_arrive(&conv[s]);
+        mbar_arrive(&conv[j]);
       }
     }
     const bool ok = mbar_wait(accum, 0);
@@ -204,42 +213,63 @@ __global__ void __launch_bounds__(192, 1)
     const bool row_ok = row < M;
     float scale = 1.f;
     if (ep.row_parts && row_ok) {
-      float s = 0.f;
-      for (int p = 0; p < ep.nparts; ++p) s += ep.row_parts[(size_t)row * ep.nparts + p];
-      scale = 1.0f / sqrtf(s * ep.inv_d + ep.eps);
+      float sum = 0.f;
+      for (int p = 0; p < ep.nparts; ++p) sum += ep.row_parts[(size_t)row * ep.nparts + p];
+      scale = 1.0f / sqrtf(sum * ep.inv_d + ep.eps);
     }
     const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    const int nacc = nk < C::NACC ? nk : C::NACC;  // accumulators that received products
+    // Sum of the accumulators for 16 columns starting at `col` (warp-collective).
+    auto load16 = [&](int col, float (&v)[16]) {
+      __syncwarp();
+      tmem_ld16(tbase + col, v);
+      if constexpr (TF32X3) {
+        float w[16];
+        tmem_ld16(tbase + (uint32_t)(C::NACC * BN) + col, w);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] += w[e];
+#pragma unroll 1
+        for (int a = 1; a < nacc; ++a) {
+          __syncwarp();
+          tmem_ld16(tbase + (uint32_t)(a * BN) + col, w);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] += w[e];
+        }
+      } else {
+        tmem_wait_ld();
+      }
+    };
     if (ep.swiglu) {
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         float g[16], u[16];
-        __syncwarp();
-        tmem_ld16(tbase + c, g);
-        tmem_ld16(tbase + c + 16, u);
-        tmem_wait_ld();
+        load16(c, g);
+        load16(c + 16, u);
         const int nout = (n0 + c) / 2;  // first output column of this group
         if (ok && row_ok && n0 + c + 32 <= N) {
           float hh[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float gg = g[j] * scale, uu = u[j] * scale;
-            hh[j] = gg / (1.0f + expf(-gg)) * uu;
+          for (int e = 0; e < 16; ++e) {
+            const float gg = g[e] * scale, uu = u[e] * scale;
+            hh[e] = gg / (1.0f + expf(-gg)) * uu;
           }
           if (ep.out_bf16) {
             __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + nout;
             uint32_t pk[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(hh[2 * j], hh[2 * j + 1]);
-              pk[j] = *reinterpret_cast<uint32_t *>(&b2);
+            for (int e = 0; e < 8; ++e) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(hh[2 * e], hh[2 * e + 1]);
+              pk[e] = *reinterpret_cast<uint32_t *>(&b2);
             }
             reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
           } else {
             float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + nout;
 #pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *reinterpret_cast<float4 *>(o + j) = make_float4(hh[j], hh[j + 1], hh[j + 2], hh[j + 3]);
+            for (int e = 0; e < 16; e += 4)
+              *reinterpret_cast<float4 *>(o + e) = make_float4(hh[e], hh[e + 1], hh[e + 2], hh[e + 3]);
           }
         }
       }
@@ -247,44 +277,42 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         float v[16];
-        __syncwarp();
-        tmem_ld16(tbase + c, v);
-        tmem_wait_ld();
+        load16(c, v);
         const int n = n0 + c;
         if (!ok || !row_ok || n >= N) continue;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          v[j] *= scale;
-          if (ep.bias && n + j < N) v[j] += ep.bias[n + j];
+        for (int e = 0; e < 16; ++e) {
+          v[e] *= scale;
+          if (ep.bias && n + e < N) v[e] += ep.bias[n + e];
         }
         if (ep.residual) {
           const float *r = ep.residual + (size_t)row * ep.ldr + n;
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (n + j < N) v[j] += r[j];
+          for (int e = 0; e < 16; ++e)
+            if (n + e < N) v[e] += r[e];
         }
         if (ep.out_bf16) {
           __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + n;
           if (n + 16 <= N && ep.vec_ok) {
             uint32_t pk[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-              pk[j] = *reinterpret_cast<uint32_t *>(&b2);
+            for (int e = 0; e < 8; ++e) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+              pk[e] = *reinterpret_cast<uint32_t *>(&b2);
             }
             reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
           } else {
-            for (int j = 0; j < 16 && n + j < N; ++j) o[j] = __float2bfloat16(v[j]);
+            for (int e = 0; e < 16 && n + e < N; ++e) o[e] = __float2bfloat16(v[e]);
           }
         } else {
           float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + n;
           if (n + 16 <= N && ep.vec_ok) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            for (int e = 0; e < 16; e += 4)
+              *reinterpret_cast<float4 *>(o + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
           } else {
-            for (int j = 0; j < 16 && n + j < N; ++j) o[j] = v[j];
+            for (int e = 0; e < 16 && n + e < N; ++e) o[e] = v[e];
           }
         }
       }

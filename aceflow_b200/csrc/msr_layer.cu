@@ -31,12 +31,52 @@ int msr_decode_step_impl(af_ctx *ctx, const float *x, float *state, const float 
   float *qkv = scratch;
   float *o = qkv + (size_t)B * 3 * d;
   float *sumsq = o + (size_t)B * d;
-  int rc = linear_f32(ctx, x, d, w_qkv, d, nullptr, qkv, 3 * d, B, 3 * d, d, nullptr, 0, 0.f, 0.f, st, fn);
-  if (rc) return rc;
-  rc = launch_retention_step(ctx, state, (int64_t)H * dh * dh, gamma, qkv, qkv + d, qkv + 2 * d, 3 * (int64_t)d, o,
-                             d, B, H, dh, ret_norm_w, sumsq, st, fn, 0);
-  if (rc) return rc;
-  return linear_f32(ctx, o, d, w_o, d, nullptr, out, d, B, d, d, sumsq, H, 1.0f / (float)d, eps, st, fn);
+  const int64_t sbs = (int64_t)H * dh * dh;
+  auto qkv_gemm = [&](int r0, int rows, cudaStream_t s) {
+    return linear_f32(ctx, x + (size_t)r0 * d, d, w_qkv, d, nullptr, qkv + (size_t)r0 * 3 * d, 3 * d, rows, 3 * d, d,
+                      nullptr, 0, 0.f, 0.f, s, fn);
+  };
+  auto retention = [&](int r0, int rows, cudaStream_t s) {
+    const float *q = qkv + (size_t)r0 * 3 * d;
+    return launch_retention_step(ctx, state + (size_t)r0 * sbs, sbs, gamma, q, q + d, q + 2 * d, 3 * (int64_t)d,
+                                 o + (size_t)r0 * d, d, rows, H, dh, ret_norm_w, sumsq + (size_t)r0 * H, s, fn, 0);
+  };
+  auto out_gemm = [&](int r0, int rows, cudaStream_t s) {
+    return linear_f32(ctx, o + (size_t)r0 * d, d, w_o, d, nullptr, out + (size_t)r0 * d, d, rows, d, d,
+                      sumsq + (size_t)r0 * H, H, 1.0f / (float)d, eps, s, fn);
+  };
+  const int sr = ctx->decode_slice_rows;
+  const int nsl = sr > 0 ? (B + sr - 1) / sr : 1;
+  if (nsl < 2 || nsl > af_ctx::kMaxSlices) {
+    int rc = qkv_gemm(0, B, st);
+    if (rc) return rc;
+    rc = retention(0, B, st);
+    if (rc) return rc;
+    return out_gemm(0, B, st);
+  }
+  // Overlapped: slice i's projection (tensor cores) runs while slice i-1
+  // streams its state (HBM) on a high-priority stream, and slice i-2 runs its
+  // output projection; fork/join through events on the caller's stream.
+  cudaStream_t s_ret = ctx->side[0], s_out = ctx->side[1];
+  AF_CUDA(cudaEventRecord(ctx->ev_fork, st), fn);
+  AF_CUDA(cudaStreamWaitEvent(s_ret, ctx->ev_fork, 0), fn);
+  AF_CUDA(cudaStreamWaitEvent(s_out, ctx->ev_fork, 0), fn);
+  for (int i = 0; i < nsl; ++i) {
+    const int r0 = i * sr, rows = B - r0 < sr ? B - r0 : sr;
+    int rc = qkv_gemm(r0, rows, st);
+    if (rc) return rc;
+    AF_CUDA(cudaEventRecord(ctx->ev_a[i], st), fn);
+    AF_CUDA(cudaStreamWaitEvent(s_ret, ctx->ev_a[i], 0), fn);
+    rc = retention(r0, rows, s_ret);
+    if (rc) return rc;
+    AF_CUDA(cudaEventRecord(ctx->ev_b[i], s_ret), fn);
+    AF_CUDA(cudaStreamWaitEvent(s_out, ctx->ev_b[i], 0), fn);
+    rc = out_gemm(r0, rows, s_out);
+    if (rc) return rc;
+  }
+  AF_CUDA(cudaEventRecord(ctx->ev_join, s_out), fn);
+  AF_CUDA(cudaStreamWaitEvent(st, ctx->ev_join, 0), fn);
+  return AF_OK;
 }
 
 int check_msr_decode(const char *fn, const float *x, float *state, const float *gamma, const float *w_qkv,
