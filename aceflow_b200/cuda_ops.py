@@ -251,3 +251,22 @@ def msr_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, re
     _lib.call("af_msr_prefill_bf16", _ctx(x), _p(x), _p(w_qkv), _p(w_o), _p(ret_norm_w), _p(gamma), float(eps),
               B, T, d, H, _p(state_in), _p(state_out), _p(out), int(out_dtype == BF16), _stream(x))
     return out, state_out
+
+
+def msr_decode_step_noalloc(x: torch.Tensor, state: torch.Tensor, gamma: torch.Tensor, w_qkv: torch.Tensor,
+                            w_o: torch.Tensor, ret_norm_w: torch.Tensor, eps: float,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+    """af_msr_decode_step_f32_noalloc: the decode step with the library's
+    static scratch array (no allocation, no context) on x's device."""
+    B, d = x.shape
+    H = state.shape[1]
+    for n, t in (("x", x), ("state", state), ("gamma", gamma), ("w_qkv", w_qkv), ("w_o", w_o),
+                 ("ret_norm_w", ret_norm_w)):
+        _need(t, F32, n)
+    if out is None:
+        out = torch.empty(B, d, dtype=F32, device=x.device)
+    _dev(x)
+    with torch.cuda.device(x.device):
+        _lib.call("af_msr_decode_step_f32_noalloc", _p(x), _p(state), _p(gamma), _p(w_qkv), _p(w_o), _p(ret_norm_w),
+                  float(eps), B, d, H, _p(out), _stream(x))
+    return out

@@ -141,6 +141,22 @@ int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state, const floa
                            float eps, int batch, int d_model, int num_heads, float *out,
                            af_stream_t stream);
 
+/* The same decode step for callers that cannot allocate device memory at
+ * call time (inside a CUDA-graph capture, or in a process whose device
+ * memory belongs to its own arena allocator).  No reference counterpart: the
+ * reference's CPU engine preallocates its host buffers in AceEngine::new.
+ * Scratch comes from a fixed 16 MiB array inside the library (2^22 floats;
+ * the step needs batch*(4*d_model + num_heads) of them, e.g. batch <= 511 at
+ * d_model 2048), so the call allocates nothing and takes no context; larger
+ * sizes return AF_ERR_ARG.  The current device is used.  The first call on a
+ * device looks up the array's address (and loads the library's kernels):
+ * make it before any stream capture.  All calls on a device share the
+ * array, so calls that overlap on the GPU (concurrent streams) race. */
+int af_msr_decode_step_f32_noalloc(const float *x, float *state, const float *gamma,
+                                   const float *w_qkv, const float *w_o, const float *ret_norm_w,
+                                   float eps, int batch, int d_model, int num_heads, float *out,
+                                   af_stream_t stream);
+
 /* Chunkwise-parallel retention core on the bf16 tensor cores (head_dim 256,
  * chunk 64).  The parallel form (aceflow/nn/retention.py:51-61) computed
  * chunk by chunk with the carried state of recurrence.rs:28-39.
