@@ -23,6 +23,7 @@ struct af_ctx {
   static constexpr int kMaxSlices = 8;
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   cudaEvent_t ev_a[kMaxSlices] = {}, ev_b[kMaxSlices] = {};
+  int allow_split_k = 1;        // small-M GEMMs may split K (fp32 atomics: not bitwise reproducible)
   int decode_slice_rows = 0;  // batch rows per overlapped slice; 0 = one sequential pass (faster today)
 };
 
@@ -74,6 +75,10 @@ struct GemmEpilogueArgs {
 bool tc_gemm_ok(const void *A, int64_t lda, const void *B, int64_t ldb, int K, bool fp32);
 int tc_gemm(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, bool fp32,
             const GemmEpilogueArgs &a, cudaStream_t st, const char *fn);
+int tc_gemm_presplit(af_ctx *ctx, const float *A_hi, const float *A_lo, int64_t lda, const float *B_hi,
+                     const float *B_lo, int64_t ldb, int M, int N, int K, const GemmEpilogueArgs &a, cudaStream_t st,
+                     const char *fn);
+int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn);
 
 inline cudaStream_t stream_of(af_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 

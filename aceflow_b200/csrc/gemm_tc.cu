@@ -13,12 +13,18 @@
 //               accumulator (warp w reads TMEM lanes 32*(w%4)..+31), fused
 //               row scale / bias / residual / SwiGLU, vector stores.
 //
-// Modes:
-//   BF16   : kind::f16 with bf16 operands (prefill projections).
-//   TF32X3 : fp32 operands; acc += A.B + A.B_lo + A_lo.B with kind::tf32 -
-//            the three-term split of Ootomo & Yokota (2022) that restores
-//            fp32 accuracy (~2^-21 relative) on the tensor cores (decode
-//            projections, parity 1e-4 against the fp32 reference).
+// Modes (MODE template argument):
+//   kBF16  : kind::f16 with bf16 operands (prefill projections).
+//   kTF32S : fp32 operands split in shared memory: acc += A.B + A.B_lo + A_lo.B
+//            with kind::tf32 - the three-term split of Ootomo & Yokota (2022)
+//            that restores fp32 accuracy on the tensor cores.
+//   kTF32P : the same products from operands split beforehand (hi and lo
+//            arrays in global memory, four TMA loads per stage, no converter):
+//            weights are split once at load time, activations by the kernel
+//            that produces them.  The decode projections.
+// Split-K: gridDim.z CTAs share one output tile over disjoint K ranges and
+// add their fp32 partials with vector atomics (small-M GEMMs would otherwise
+// leave most SMs idle while the weights stream).
 //
 // Every mbarrier wait is bounded; a timeout sets the context's device error
 // word (AF_ERR_TIMEOUT) and the CTA drains and frees its TMEM.
@@ -43,21 +49,27 @@ struct GemmEpilogue {
   int64_t ldr;
   int swiglu;              // columns in groups of 16 gate then 16 up -> N/2 outputs
   int vec_ok;              // out base 16-byte aligned and ldo a whole number of 16-byte units
+  int atomic;              // split-K: add into out (bias/residual only from split 0)
 };
 
-template <int BN, bool TF32X3>
+constexpr int kBF16 = 0, kTF32S = 1, kTF32P = 2;
+
+template <int BN, int MODE>
 struct TileCfg {
+  static constexpr bool TF32X3 = MODE != kBF16;
+  static constexpr bool PRE = MODE == kTF32P;
   static constexpr int BM = 128;
   static constexpr int ELEM = TF32X3 ? 4 : 2;
   static constexpr int BK = 128 / ELEM;          // one 128-byte swizzle row per K slice
   static constexpr int UK = 32 / ELEM;           // K per tcgen05.mma (32 bytes)
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
-  static constexpr int RAW_BYTES = A_BYTES + B_BYTES;  // one TMA ring stage
-  // TF32x3: two split slots (lo parts) double-buffer the converter -> MMA
+  static constexpr int RAW_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = PRE ? 2 * RAW_BYTES : RAW_BYTES;  // one TMA ring stage
+  // kTF32S: two split slots (lo parts) double-buffer the converter -> MMA
   // hand-off, so the TMA ring keeps its full depth for prefetch.
-  static constexpr int LO_SLOTS = TF32X3 ? 2 : 0;
-  static constexpr int STAGES_FIT = (200 * 1024 - LO_SLOTS * RAW_BYTES) / RAW_BYTES;
+  static constexpr int LO_SLOTS = MODE == kTF32S ? 2 : 0;
+  static constexpr int STAGES_FIT = (200 * 1024 - LO_SLOTS * RAW_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT < 12 ? STAGES_FIT : 12;
   // TF32x3: the hi.hi products go round-robin over NACC accumulators and the
   // small hi.lo + lo.hi terms into one more, so each fp32 accumulator sees
@@ -66,7 +78,7 @@ struct TileCfg {
   static constexpr int ACC_COLS = (NACC + (TF32X3 ? 1 : 0)) * BN;
   static constexpr int TMEM_COLS =
       ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128 : ACC_COLS <= 256 ? 256 : 512;
-  static constexpr size_t SMEM = 1024 + (size_t)(STAGES + LO_SLOTS) * RAW_BYTES + 256;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)LO_SLOTS * RAW_BYTES + 256;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
   static_assert(ACC_COLS <= 512, "TMEM columns");
   static_assert(STAGES >= 2, "pipeline depth");
@@ -74,15 +86,17 @@ struct TileCfg {
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
-template <int BN, bool TF32X3>
+template <int BN, int MODE>
 __global__ void __launch_bounds__(192, 1)
-    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M, int N,
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, int M, int N,
                      int K, GemmEpilogue ep, int *err) {
-  using C = TileCfg<BN, TF32X3>;
+  using C = TileCfg<BN, MODE>;
+  constexpr bool TF32X3 = C::TF32X3;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *lo_base = smem + (size_t)S * C::RAW_BYTES;
+  uint8_t *lo_base = smem + (size_t)S * C::STAGE_BYTES;
   uint64_t *bars = reinterpret_cast<uint64_t *>(lo_base + (size_t)C::LO_SLOTS * C::RAW_BYTES);
   uint64_t *full = bars;            // [S]  TMA landed
   uint64_t *empty = bars + S;       // [S]  MMAs reading the stage retired
@@ -94,7 +108,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.y * C::BM, n0 = blockIdx.x * BN;
-  const int nk = (K + C::BK - 1) / C::BK;
+  const int nk_all = (K + C::BK - 1) / C::BK;
+  // split-K: this CTA's K slices are [kb_base, kb_base + nk)
+  const int kb_base = (int)(((int64_t)blockIdx.z * nk_all) / gridDim.z);
+  const int nk = (int)(((int64_t)(blockIdx.z + 1) * nk_all) / gridDim.z) - kb_base;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -110,6 +127,10 @@ __global__ void __launch_bounds__(192, 1)
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if constexpr (C::PRE) {
+      prefetch_tmap(&tmA2);
+      prefetch_tmap(&tmB2);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -120,10 +141,13 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto stage_a = [&](int i) { return smem + (size_t)i * C::RAW_BYTES; };
-  auto stage_b = [&](int i) { return smem + (size_t)i * C::RAW_BYTES + C::A_BYTES; };
-  auto lo_a = [&](int j) { return lo_base + (size_t)j * C::RAW_BYTES; };
-  auto lo_b = [&](int j) { return lo_base + (size_t)j * C::RAW_BYTES + C::A_BYTES; };
+  auto stage_a = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES; };
+  auto stage_b = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES + C::A_BYTES; };
+  // lo parts: the stage's second half (kTF32P) or a split slot (kTF32S)
+  auto lo_a = [&](int i, int j) {
+    return C::PRE ? smem + (size_t)i * C::STAGE_BYTES + C::RAW_BYTES : lo_base + (size_t)j * C::RAW_BYTES;
+  };
+  auto lo_b = [&](int i, int j) { return lo_a(i, j) + C::A_BYTES; };
   auto fail = [&]() {
     s_abort = 1;
     atomicOr(err, 1 << AF_ERR_TIMEOUT);
@@ -136,9 +160,14 @@ __global__ void __launch_bounds__(192, 1)
         const int i = kb % S;
         const uint32_t ph = (kb / S) & 1;
         if (!mbar_wait(&empty[i], ph ^ 1)) { fail(); break; }
-        mbar_arrive_expect_tx(&full[i], C::A_BYTES + C::B_BYTES);
-        tma_load_2d(stage_a(i), &tmA, &full[i], kb * C::BK, m0);
-        tma_load_2d(stage_b(i), &tmB, &full[i], kb * C::BK, n0);
+        const int kx = (kb_base + kb) * C::BK;
+        mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+        tma_load_2d(stage_a(i), &tmA, &full[i], kx, m0);
+        tma_load_2d(stage_b(i), &tmB, &full[i], kx, n0);
+        if constexpr (C::PRE) {
+          tma_load_2d(lo_a(i, 0), &tmA2, &full[i], kx, m0);
+          tma_load_2d(lo_b(i, 0), &tmB2, &full[i], kx, n0);
+        }
         issued = kb + 1;
       }
       // drain: every issued load has landed before this CTA may exit
@@ -149,8 +178,8 @@ __global__ void __launch_bounds__(192, 1)
     constexpr uint32_t idesc = idesc_f32acc(TF32X3 ? kFmtTF32 : kFmtBF16, C::BM, BN);
     for (int kb = 0; kb < nk; ++kb) {
       const int i = kb % S, j = kb & 1;
-      const bool ok = __all_sync(0xffffffffu, TF32X3 ? mbar_wait(&conv[j], (kb >> 1) & 1)
-                                                     : mbar_wait(&full[i], (kb / S) & 1));
+      const bool ok = __all_sync(0xffffffffu, MODE == kTF32S ? mbar_wait(&conv[j], (kb >> 1) & 1)
+                                                             : mbar_wait(&full[i], (kb / S) & 1));
       if (!ok) {
         if (lane == 0) fail();
         break;
@@ -163,7 +192,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int k = 0; k < C::BK / C::UK; ++k) {
           const uint64_t off = (uint64_t)(k * 32) >> 4;  // 32 bytes along K inside the swizzle row
           if constexpr (TF32X3) {
-            const uint64_t dal = sdesc_k_sw128(lo_a(j)), dbl = sdesc_k_sw128(lo_b(j));
+            const uint64_t dal = sdesc_k_sw128(lo_a(i, j)), dbl = sdesc_k_sw128(lo_b(i, j));
             const uint32_t acc = tmem + (uint32_t)((kb % C::NACC) * BN);
             const uint32_t corr = tmem + (uint32_t)(C::NACC * BN);
             umma_tf32(acc, da + off, db + off, idesc, (kb >= C::NACC || k > 0) ? 1u : 0u);
@@ -174,7 +203,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
         umma_commit(&empty[i]);
-        if constexpr (TF32X3) umma_commit(&lofree[j]);
+        if constexpr (MODE == kTF32S) umma_commit(&lofree[j]);
       }
       __syncwarp();
     }
@@ -183,7 +212,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ---- warps 2..5
     const int t = threadIdx.x - 64;  // 0..127
-    if constexpr (TF32X3) {
+    if constexpr (MODE == kTF32S) {
       for (int kb = 0; kb < nk; ++kb) {
         const int i = kb % S, j = kb & 1;
         if (!mbar_wait(&full[i], (kb / S) & 1) || !mbar_wait(&lofree[j], ((kb >> 1) & 1) ^ 1)) {
@@ -193,7 +222,7 @@ __global__ void __launch_bounds__(192, 1)
         // x = hi + lo exactly: hi = x with the low 13 mantissa bits cleared
         // (an exact tf32 value, written back in place), lo = x - hi.
         float4 *ra = reinterpret_cast<float4 *>(stage_a(i));
-        float4 *la = reinterpret_cast<float4 *>(lo_a(j));
+        float4 *la = reinterpret_cast<float4 *>(lo_a(i, j));
 #pragma unroll 4
         for (int e = t; e < C::RAW_BYTES / 16; e += 128) {  // A then B, contiguous in both buffers
           const float4 v = ra[e];
@@ -280,10 +309,27 @@ __global__ void __launch_bounds__(192, 1)
         load16(c, v);
         const int n = n0 + c;
         if (!ok || !row_ok || n >= N) continue;
+        const bool first = blockIdx.z == 0;
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           v[e] *= scale;
-          if (ep.bias && n + e < N) v[e] += ep.bias[n + e];
+          if (first && ep.bias && n + e < N) v[e] += ep.bias[n + e];
+        }
+        if (ep.atomic) {
+          if (first && ep.residual) {
+            const float *r = ep.residual + (size_t)row * ep.ldr + n;
+            for (int e = 0; e < 16; ++e)
+              if (n + e < N) v[e] += r[e];
+          }
+          float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + n;
+          if (n + 16 <= N && ep.vec_ok) {
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              atomicAdd(reinterpret_cast<float4 *>(o + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
+          } else {
+            for (int e = 0; e < 16 && n + e < N; ++e) atomicAdd(o + e, v[e]);
+          }
+          continue;
         }
         if (ep.residual) {
           const float *r = ep.residual + (size_t)row * ep.ldr + n;
@@ -357,25 +403,108 @@ int make_kmajor_map(CUtensorMap *map, const void *base, bool fp32, int rows, int
   return AF_OK;
 }
 
-template <int BN, bool TF32X3>
-int launch_tc(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
-              const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
-  using C = TileCfg<BN, TF32X3>;
-  CUtensorMap ta, tb;
-  int rc = make_kmajor_map(&ta, A, TF32X3, M, K, lda, C::BM, fn);
+template <int BN, int MODE>
+int launch_tc(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void *B, const void *B2, int64_t ldb,
+              int M, int N, int K, int splits, const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
+  using C = TileCfg<BN, MODE>;
+  CUtensorMap ta, tb, ta2, tb2;
+  const bool fp32 = MODE != kBF16;
+  int rc = make_kmajor_map(&ta, A, fp32, M, K, lda, C::BM, fn);
   if (rc) return rc;
-  rc = make_kmajor_map(&tb, B, TF32X3, N, K, ldb, BN, fn);
+  rc = make_kmajor_map(&tb, B, fp32, N, K, ldb, BN, fn);
   if (rc) return rc;
+  ta2 = ta;
+  tb2 = tb;
+  if (MODE == kTF32P) {
+    rc = make_kmajor_map(&ta2, A2, true, M, K, lda, C::BM, fn);
+    if (rc) return rc;
+    rc = make_kmajor_map(&tb2, B2, true, N, K, ldb, BN, fn);
+    if (rc) return rc;
+  }
   static bool attr_done = false;  // per template instance
   if (!attr_done) {
     cudaError_t e =
-        cudaFuncSetAttribute(umma_gemm_kernel<BN, TF32X3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+        cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
     if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
     attr_done = true;
   }
-  const dim3 grid((N + BN - 1) / BN, (M + C::BM - 1) / C::BM);
-  umma_gemm_kernel<BN, TF32X3><<<grid, 192, C::SMEM, st>>>(ta, tb, M, N, K, ep, ctx->dev_err);
+  const dim3 grid((N + BN - 1) / BN, (M + C::BM - 1) / C::BM, splits);
+  umma_gemm_kernel<BN, MODE><<<grid, 192, C::SMEM, st>>>(ta, tb, ta2, tb2, M, N, K, ep, ctx->dev_err);
   return af::launched(ctx, fn);
+}
+
+// Splits the fp32 array src into an exact tf32 part and the remainder.
+__global__ void split_tf32_kernel(const float *__restrict__ src, float *__restrict__ hi, float *__restrict__ lo,
+                                  int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float x = src[i];
+    const float h = tf32_hi(x);
+    hi[i] = h;
+    lo[i] = x - h;
+  }
+}
+
+// Tile width, split count and launch for one GEMM.  Narrow tiles and split-K
+// put a CTA on every SM for decode-sized M; split-K needs an fp32, non-SwiGLU
+// epilogue (it accumulates with atomics).
+template <int MODE>
+int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void *B, const void *B2, int64_t ldb,
+             int M, int N, int K, const af::GemmEpilogueArgs &a, cudaStream_t st, const char *fn) {
+  int rc = get_encoder(fn);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return AF_OK;
+  const bool vec = af::aligned16(a.out) && (a.ldo * (a.out_bf16 ? 2 : 4)) % 16 == 0;
+  if (a.swiglu && (!vec || N % 32 != 0))
+    return af::fail(AF_ERR_ARG, "%s: SwiGLU epilogue needs an aligned output and N %% 32 == 0", fn);
+  GemmEpilogue ep{a.out, a.ldo,      a.out_bf16, a.bias,   a.row_parts, a.nparts,   a.inv_d,
+                  a.eps, a.residual, a.ldr,      a.swiglu, vec ? 1 : 0, 0};
+  const int64_t mt = (M + 127) / 128;
+  auto tiles = [&](int bn) { return mt * ((N + bn - 1) / bn); };
+  const int64_t sms = ctx->num_sms;
+  constexpr int bk = MODE == kBF16 ? 64 : 32;
+  const int nk = (K + bk - 1) / bk;
+  const bool can_split = !a.swiglu && !a.out_bf16 && ctx->allow_split_k;
+  int bn;
+  if (MODE == kBF16) {
+    bn = tiles(256) >= sms ? 256 : tiles(128) >= sms ? 128 : 64;
+    if (!can_split && tiles(bn) < sms) bn = tiles(32) >= sms || a.swiglu ? (tiles(64) >= sms ? 64 : 32) : 16;
+  } else {
+    bn = tiles(128) >= sms ? 128 : 64;
+    if (!can_split && tiles(bn) < sms) bn = (tiles(64) >= sms || a.swiglu) ? 64 : 32;
+  }
+  int splits = 1;
+  if (can_split && tiles(bn) < sms) {
+    splits = (int)((sms + tiles(bn) - 1) / tiles(bn));
+    const int max_by_k = nk / 4 > 1 ? nk / 4 : 1;  // keep >= 4 K slices per split
+    if (splits > max_by_k) splits = max_by_k;
+    if (splits > 8) splits = 8;
+  }
+  if (splits > 1) {
+    ep.atomic = 1;
+    if (a.residual == a.out) {
+      ep.residual = nullptr;  // out already holds the residual: every split adds its partial into it
+    } else {
+      cudaError_t e = cudaMemsetAsync(a.out, 0, (size_t)M * a.ldo * 4, st);
+      if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: zeroing the split-K output: %s", fn, cudaGetErrorString(e));
+    }
+  }
+#define AF_LAUNCH(BNV) return launch_tc<BNV, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn)
+  switch (bn) {
+    case 256:
+      if constexpr (MODE == kBF16) AF_LAUNCH(256);
+      break;
+    case 128:
+      AF_LAUNCH(128);
+    case 64:
+      AF_LAUNCH(64);
+    case 32:
+      AF_LAUNCH(32);
+    case 16:
+      if constexpr (MODE == kBF16) AF_LAUNCH(16);
+      break;
+  }
+#undef AF_LAUNCH
+  return af::fail(AF_ERR_ARG, "%s: no tile for N=%d", fn, N);
 }
 
 }  // namespace
@@ -393,29 +522,32 @@ bool tc_gemm_ok(const void *A, int64_t lda, const void *B, int64_t ldb, int K, b
 
 int tc_gemm(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K, bool fp32,
             const GemmEpilogueArgs &a, cudaStream_t st, const char *fn) {
-  int rc = get_encoder(fn);
-  if (rc) return rc;
-  if (M == 0 || N == 0) return AF_OK;
-  const bool vec = af::aligned16(a.out) && (a.ldo * (a.out_bf16 ? 2 : 4)) % 16 == 0;
-  if (a.swiglu && (!vec || N % 32 != 0))
-    return af::fail(AF_ERR_ARG, "%s: SwiGLU epilogue needs an aligned output and N %% 32 == 0", fn);
-  GemmEpilogue ep{a.out,      a.ldo, a.out_bf16,  a.bias, a.row_parts, a.nparts, a.inv_d,
-                  a.eps,      a.residual, a.ldr, a.swiglu, vec ? 1 : 0};
-  // Pick the widest tile that still puts a CTA on every SM (decode-sized M
-  // needs narrow tiles so the weight stream is spread over all SMs).
-  const int64_t mt = (M + 127) / 128;
-  auto tiles = [&](int bn) { return mt * ((N + bn - 1) / bn); };
-  const int64_t sms = ctx->num_sms;
-  if (fp32) {
-    if (tiles(128) >= sms) return launch_tc<128, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-    if (tiles(64) >= sms || a.swiglu) return launch_tc<64, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-    return launch_tc<32, true>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-  }
-  if (tiles(256) >= sms) return launch_tc<256, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-  if (tiles(128) >= sms) return launch_tc<128, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-  if (tiles(64) >= sms) return launch_tc<64, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-  if (tiles(32) >= sms || a.swiglu) return launch_tc<32, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-  return launch_tc<16, false>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  if (fp32) return dispatch<kTF32S>(ctx, A, nullptr, lda, B, nullptr, ldb, M, N, K, a, st, fn);
+  return dispatch<kBF16>(ctx, A, nullptr, lda, B, nullptr, ldb, M, N, K, a, st, fn);
+}
+
+// fp32 GEMM from operands split beforehand into (hi, lo) pairs.
+int tc_gemm_presplit(af_ctx *ctx, const float *A_hi, const float *A_lo, int64_t lda, const float *B_hi,
+                     const float *B_lo, int64_t ldb, int M, int N, int K, const GemmEpilogueArgs &a, cudaStream_t st,
+                     const char *fn) {
+  if (!tc_gemm_ok(A_lo, lda, B_lo, ldb, K, true) || !tc_gemm_ok(A_hi, lda, B_hi, ldb, K, true))
+    return fail(AF_ERR_ARG, "%s: split operands must be 16-byte aligned with K %% 4 == 0", fn);
+  return dispatch<kTF32P>(ctx, A_hi, A_lo, lda, B_hi, B_lo, ldb, M, N, K, a, st, fn);
+}
+
+int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn) {
+  if (n == 0) return AF_OK;
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > (int64_t)ctx->num_sms * 16) blocks = (int64_t)ctx->num_sms * 16;
+  split_tf32_kernel<<<(unsigned)blocks, 256, 0, st>>>(src, hi, lo, n);
+  return launched(ctx, fn);
 }
 
 }  // namespace af
+
+extern "C" int af_split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, af_stream_t stream) {
+  const char *fn = "af_split_tf32";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(src && hi && lo && n >= 0, "af_split_tf32", "bad arguments");
+  return af::split_tf32(ctx, src, hi, lo, n, af::stream_of(stream), fn);
+}

@@ -13,7 +13,7 @@ namespace af {
 int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
                           int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn,
-                          int out_bf16);
+                          int out_bf16, float *out_lo = nullptr);
 int linear_f32(af_ctx *ctx, const float *x, int64_t ldx, const float *w, int64_t ldw, const float *bias, float *y,
                int64_t ldy, int M, int N, int K, const float *parts, int nparts, float inv_d, float eps,
                cudaStream_t st, const char *fn);
@@ -79,6 +79,39 @@ int msr_decode_step_impl(af_ctx *ctx, const float *x, float *state, const float 
   return AF_OK;
 }
 
+// Decode step from weights split beforehand (af_split_tf32): the input is
+// split by a small kernel, the retention kernel writes its output split, and
+// both projections run as pre-split 3xTF32 GEMMs (no in-kernel converter).
+// Workspace floats: x hi/lo 2Bd, qkv 3Bd, o hi/lo 2Bd, sumsq BH.
+size_t msr_decode_split_scratch_floats(int B, int d, int H) { return (size_t)B * (7 * (size_t)d + H); }
+
+int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const float *gamma, const float *wq_hi,
+                               const float *wq_lo, const float *wo_hi, const float *wo_lo, const float *ret_norm_w,
+                               float eps, int B, int d, int H, float *out, float *scratch, cudaStream_t st,
+                               const char *fn) {
+  const int dh = d / H;
+  float *x_hi = scratch, *x_lo = x_hi + (size_t)B * d, *qkv = x_lo + (size_t)B * d;
+  float *o_hi = qkv + (size_t)B * 3 * d, *o_lo = o_hi + (size_t)B * d, *sumsq = o_lo + (size_t)B * d;
+  int rc = split_tf32(ctx, x, x_hi, x_lo, (int64_t)B * d, st, fn);
+  if (rc) return rc;
+  GemmEpilogueArgs e1;
+  e1.out = qkv;
+  e1.ldo = 3 * d;
+  rc = tc_gemm_presplit(ctx, x_hi, x_lo, d, wq_hi, wq_lo, d, B, 3 * d, d, e1, st, fn);
+  if (rc) return rc;
+  rc = launch_retention_step(ctx, state, (int64_t)H * dh * dh, gamma, qkv, qkv + d, qkv + 2 * d, 3 * (int64_t)d, o_hi,
+                             d, B, H, dh, ret_norm_w, sumsq, st, fn, 0, o_lo);
+  if (rc) return rc;
+  GemmEpilogueArgs e2;
+  e2.out = out;
+  e2.ldo = d;
+  e2.row_parts = sumsq;
+  e2.nparts = H;
+  e2.inv_d = 1.0f / (float)d;
+  e2.eps = eps;
+  return tc_gemm_presplit(ctx, o_hi, o_lo, d, wo_hi, wo_lo, d, B, d, d, e2, st, fn);
+}
+
 int check_msr_decode(const char *fn, const float *x, float *state, const float *gamma, const float *w_qkv,
                      const float *w_o, const float *ret_norm_w, int B, int d, int H, const float *out) {
   if (!x || !state || !gamma || !w_qkv || !w_o || !ret_norm_w || !out)
@@ -106,6 +139,26 @@ extern "C" int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state,
   if (rc) return rc;
   return af::msr_decode_step_impl(ctx, x, state, gamma, w_qkv, w_o, ret_norm_w, eps, B, d, H, out,
                                   static_cast<float *>(ws), af::stream_of(stream), fn);
+}
+
+extern "C" int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *state, const float *gamma,
+                                            const float *w_qkv_hi, const float *w_qkv_lo, const float *w_o_hi,
+                                            const float *w_o_lo, const float *ret_norm_w, float eps, int B, int d,
+                                            int H, float *out, af_stream_t stream) {
+  const char *fn = "af_msr_decode_step_f32_split";
+  AF_ENTER(ctx, fn);
+  int rc = af::check_msr_decode(fn, x, state, gamma, w_qkv_hi, w_o_hi, ret_norm_w, B, d, H, out);
+  if (rc) return rc;
+  AF_REQUIRE(w_qkv_lo && w_o_lo, "af_msr_decode_step_f32_split", "null weight pointer");
+  const int dh = d / H;
+  AF_REQUIRE((dh == 64 || dh == 128 || dh == 256) && d % 4 == 0 && af::aligned16(x) && af::aligned16(out),
+             "af_msr_decode_step_f32_split", "head_dim must be 64, 128 or 256 and x, out 16-byte aligned");
+  if (B == 0) return AF_OK;
+  void *ws = nullptr;
+  rc = af::workspace(ctx, af::msr_decode_split_scratch_floats(B, d, H) * sizeof(float), &ws, fn);
+  if (rc) return rc;
+  return af::msr_decode_step_split_impl(ctx, x, state, gamma, w_qkv_hi, w_qkv_lo, w_o_hi, w_o_lo, ret_norm_w, eps, B,
+                                        d, H, out, static_cast<float *>(ws), af::stream_of(stream), fn);
 }
 
 // ---------------------------------------------------------------------------

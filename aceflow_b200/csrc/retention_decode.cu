@@ -69,7 +69,8 @@ __device__ __forceinline__ float4 step_rows(float *__restrict__ S, float g, cons
 template <int DH, int THREADS>
 __device__ __forceinline__ void finish_head(float4 acc, float4 *red, float *__restrict__ o_out,
                                             const float *__restrict__ norm_w_head,
-                                            float *__restrict__ sumsq_out, int cg, int rg, bool out_bf16 = false) {
+                                            float *__restrict__ sumsq_out, int cg, int rg, bool out_bf16 = false,
+                                            float *__restrict__ o_lo = nullptr) {
   using Sh = StepShape<DH, THREADS>;
   red[rg * Sh::NCG + cg] = acc;
   __syncthreads();
@@ -93,7 +94,14 @@ __device__ __forceinline__ void finish_head(float4 acc, float4 *red, float *__re
       o.z *= w.z;
       o.w *= w.w;
     }
-    if (out_bf16) {
+    if (o_lo) {  // exact tf32 part + remainder, the operands of the split GEMM
+      const float4 h = make_float4(__uint_as_float(__float_as_uint(o.x) & 0xFFFFE000u),
+                                   __uint_as_float(__float_as_uint(o.y) & 0xFFFFE000u),
+                                   __uint_as_float(__float_as_uint(o.z) & 0xFFFFE000u),
+                                   __uint_as_float(__float_as_uint(o.w) & 0xFFFFE000u));
+      reinterpret_cast<float4 *>(o_out)[threadIdx.x] = h;
+      reinterpret_cast<float4 *>(o_lo)[threadIdx.x] = make_float4(o.x - h.x, o.y - h.y, o.z - h.z, o.w - h.w);
+    } else if (out_bf16) {
       __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y), hi = __floats2bfloat162_rn(o.z, o.w);
       reinterpret_cast<uint2 *>(o_out)[threadIdx.x] =
           make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
@@ -121,7 +129,7 @@ __global__ void __launch_bounds__(THREADS)
                           const float *__restrict__ q, const float *__restrict__ k,
                           const float *__restrict__ v, int64_t qs, float *__restrict__ out,
                           int64_t out_rs, int H, const float *__restrict__ norm_w,
-                          float *__restrict__ sumsq, int out_bf16) {
+                          float *__restrict__ sumsq, int out_bf16, float *__restrict__ out_lo) {
   using Sh = StepShape<DH, THREADS>;
   __shared__ float sk[DH], sq[DH];
   __shared__ float4 red[Sh::RG * Sh::NCG];
@@ -143,7 +151,8 @@ __global__ void __launch_bounds__(THREADS)
                                                    (size_t)h * DH)
                          : out + (size_t)b * out_rs + (size_t)h * DH;
   finish_head<DH, THREADS>(acc, red, o_out, norm_w ? norm_w + (size_t)h * DH : nullptr,
-                           sumsq ? sumsq + blockIdx.x : nullptr, cg, rg, out_bf16 != 0);
+                           sumsq ? sumsq + blockIdx.x : nullptr, cg, rg, out_bf16 != 0,
+                           out_lo ? out_lo + (size_t)b * out_rs + (size_t)h * DH : nullptr);
 }
 
 // Token-serial scan: the same per-token work, T tokens in order.
@@ -313,7 +322,7 @@ namespace af {
 int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs,
                           int batch, int H, int dh, const float *norm_w, float *sumsq, cudaStream_t st,
-                          const char *fn, int out_bf16) {
+                          const char *fn, int out_bf16, float *out_lo) {
   if (batch == 0) return AF_OK;
   const dim3 grid((unsigned)(batch * H));
   if (out_bf16 && !(dh == 256 || dh == 128 || dh == 64) )
@@ -324,22 +333,24 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
     return launched(ctx, fn);
   }
   bool fast = (out_rs % 4 == 0) && aligned16(out) && (norm_w == nullptr || aligned16(norm_w));
-  if (out_bf16 && !fast) return fail(AF_ERR_ARG, "%s: bf16 output needs an aligned output buffer", fn);
+  if ((out_bf16 || out_lo) && !fast) return fail(AF_ERR_ARG, "%s: bf16/split output needs an aligned output", fn);
+  if (out_lo && (!aligned16(out_lo) || !(dh == 256 || dh == 128 || dh == 64)))
+    return fail(AF_ERR_ARG, "%s: split output needs head_dim 64, 128 or 256 and an aligned buffer", fn);
   if (fast && dh == 256) {
     retention_step_kernel<256, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                          norm_w, sumsq, out_bf16);
+                                                          norm_w, sumsq, out_bf16, out_lo);
   } else if (fast && dh == 128) {
     retention_step_kernel<128, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                          norm_w, sumsq, out_bf16);
+                                                          norm_w, sumsq, out_bf16, out_lo);
   } else if (fast && dh == 64) {
     retention_step_kernel<64, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                         norm_w, sumsq, out_bf16);
+                                                         norm_w, sumsq, out_bf16, out_lo);
   } else if (fast && dh == 32) {
     retention_step_kernel<32, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                         norm_w, sumsq, out_bf16);
+                                                         norm_w, sumsq, out_bf16, out_lo);
   } else if (fast && dh == 16) {
     retention_step_kernel<16, 64><<<grid, 64, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                       norm_w, sumsq, out_bf16);
+                                                       norm_w, sumsq, out_bf16, out_lo);
   } else {
     const int ncg = dh / 4;
     int rgs = 256 / ncg;
@@ -363,7 +374,7 @@ extern "C" int af_retention_step(af_ctx *ctx, float *state, int64_t state_bs, co
   int rc = check_common(fn, state, gamma, q, k, v, out, batch, H, dh, state_bs, qs);
   if (rc) return rc;
   return af::launch_retention_step(ctx, state, state_bs, gamma, q, k, v, qs, out, (int64_t)H * dh, batch, H, dh,
-                                   nullptr, nullptr, af::stream_of(stream), fn, 0);
+                                   nullptr, nullptr, af::stream_of(stream), fn, 0, nullptr);
 }
 
 extern "C" int af_retention_scan(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,

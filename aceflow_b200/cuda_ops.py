@@ -270,3 +270,30 @@ def msr_decode_step_noalloc(x: torch.Tensor, state: torch.Tensor, gamma: torch.T
         _lib.call("af_msr_decode_step_f32_noalloc", _p(x), _p(state), _p(gamma), _p(w_qkv), _p(w_o), _p(ret_norm_w),
                   float(eps), B, d, H, _p(out), _stream(x))
     return out
+
+
+def split_tf32(t: torch.Tensor):
+    """(hi, lo) with hi an exact tf32 value and hi + lo == t (af_split_tf32)."""
+    _need(t, F32, "t")
+    hi, lo = torch.empty_like(t), torch.empty_like(t)
+    _lib.call("af_split_tf32", _ctx(t), _p(t), _p(hi), _p(lo), t.numel(), _stream(t))
+    return hi, lo
+
+
+def msr_decode_step_split(x: torch.Tensor, state: torch.Tensor, gamma: torch.Tensor, w_qkv_split, w_o_split,
+                          ret_norm_w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode step from pre-split weights: w_qkv_split = split_tf32(w_qkv),
+    w_o_split = split_tf32(w_o) (af_msr_decode_step_f32_split)."""
+    B, d = x.shape
+    H = state.shape[1]
+    for n, t in (("x", x), ("state", state), ("gamma", gamma), ("ret_norm_w", ret_norm_w), ("w_qkv_hi", w_qkv_split[0]),
+                 ("w_qkv_lo", w_qkv_split[1]), ("w_o_hi", w_o_split[0]), ("w_o_lo", w_o_split[1])):
+        _need(t, F32, n)
+    if tuple(w_qkv_split[0].shape) != (3 * d, d) or tuple(w_o_split[0].shape) != (d, d):
+        raise ValueError("w_qkv must be [3d, d] and w_o [d, d]")
+    if out is None:
+        out = torch.empty(B, d, dtype=F32, device=x.device)
+    _lib.call("af_msr_decode_step_f32_split", _ctx(x), _p(x), _p(state), _p(gamma), _p(w_qkv_split[0]),
+              _p(w_qkv_split[1]), _p(w_o_split[0]), _p(w_o_split[1]), _p(ret_norm_w), float(eps), B, d, H, _p(out),
+              _stream(x))
+    return out

@@ -59,11 +59,12 @@ class MultiScaleRetention(Module):
             from .. import cuda_ops
 
             dev = self.w_q.torch.device
-            self._dev = dict(
-                w_qkv=torch.cat([self.w_q.torch, self.w_k.torch, self.w_v.torch], 0).contiguous(),
-                w_o=self.w_o.torch,
-                gamma=cuda_ops.gammas(self.num_heads, dev),
-            )
+            w_qkv = torch.cat([self.w_q.torch, self.w_k.torch, self.w_v.torch], 0).contiguous()
+            self._dev = dict(w_qkv=w_qkv, w_o=self.w_o.torch, gamma=cuda_ops.gammas(self.num_heads, dev))
+            if self.head_dim in (64, 128, 256):
+                # decode reads tf32-split weights (exact: hi + lo == w), prepared once here
+                self._dev["w_qkv_split"] = cuda_ops.split_tf32(w_qkv)
+                self._dev["w_o_split"] = cuda_ops.split_tf32(self.w_o.torch.contiguous())
 
     def _packed(self, x: Tensor) -> dict:
         if self._dev is None:
@@ -136,8 +137,12 @@ class MultiScaleRetention(Module):
             from .. import cuda_ops
 
             p = self._packed(x_t)
-            out = cuda_ops.msr_decode_step(x_t.torch, state.torch, p["gamma"], p["w_qkv"], p["w_o"],
-                                           self.ret_norm.weight.torch, self.ret_norm.eps)
+            if "w_qkv_split" in p:
+                out = cuda_ops.msr_decode_step_split(x_t.torch.contiguous(), state.torch, p["gamma"], p["w_qkv_split"],
+                                                     p["w_o_split"], self.ret_norm.weight.torch, self.ret_norm.eps)
+            else:
+                out = cuda_ops.msr_decode_step(x_t.torch, state.torch, p["gamma"], p["w_qkv"], p["w_o"],
+                                               self.ret_norm.weight.torch, self.ret_norm.eps)
             return Tensor._wrap(out, x_t.device), state
         H, hd = self.num_heads, self.head_dim
         arr = x_t.numpy()

@@ -234,9 +234,12 @@ def run_ours(args):
     xs = torch.randn(n_pool, B, d, generator=g, device=dev)
     out = torch.empty(B, d, device=dev)
     stream = torch.cuda.current_stream(dev)
+    # weights are prepared once, at load time, like the module's .to(): fp32
+    # split exactly into tf32 hi + lo for the tensor cores
+    w_qkv_s, w_o_s = cuda_ops.split_tf32(w_qkv), cuda_ops.split_tf32(w_o)
 
     def step(i):
-        cuda_ops.msr_decode_step(xs[i % n_pool], state, gamma, w_qkv, w_o, ret_w, EPS, out=out)
+        cuda_ops.msr_decode_step_split(xs[i % n_pool], state, gamma, w_qkv_s, w_o_s, ret_w, EPS, out=out)
 
     def barrier():
         if world > 1:
@@ -281,7 +284,7 @@ def run_ours(args):
         kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
 
         # end to end through the public API with host buffers
-        e2e_ms = run_e2e(args, dev, state, gamma, w_qkv, w_o, ret_w, cuda_ops, barrier)
+        e2e_ms = run_e2e(args, dev, state, gamma, w_qkv_s, w_o_s, ret_w, cuda_ops, barrier)
         e2e_ms = max_over_ranks(e2e_ms)
 
     ms_step = ms_total / args.steps
@@ -329,7 +332,7 @@ def run_ours(args):
     return 0
 
 
-def run_e2e(args, dev, state, gamma, w_qkv, w_o, ret_w, cuda_ops, barrier):
+def run_e2e(args, dev, state, gamma, w_qkv_s, w_o_s, ret_w, cuda_ops, barrier):
     """K steps through the public API with host buffers: each step copies its
     x_t from pinned host memory to the device, runs the decode step and
     copies the output back to pinned host memory.  Copies run on their own
@@ -361,7 +364,7 @@ def run_e2e(args, dev, state, gamma, w_qkv, w_o, ret_w, cuda_ops, barrier):
             s_comp.wait_event(ev_in[j])
             if t >= 2:
                 s_comp.wait_event(ev_out[j])  # dev_out[j] drained
-            cuda_ops.msr_decode_step(dev_in[j], state, gamma, w_qkv, w_o, ret_w, EPS, out=dev_out[j])
+            cuda_ops.msr_decode_step_split(dev_in[j], state, gamma, w_qkv_s, w_o_s, ret_w, EPS, out=dev_out[j])
             ev_comp[j].record(s_comp)
             with torch.cuda.stream(s_d2h):
                 s_d2h.wait_event(ev_comp[j])

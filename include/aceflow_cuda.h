@@ -126,6 +126,11 @@ int af_linear_f32(af_ctx *ctx, const float *x, const float *w, const float *bias
 int af_linear_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w, const float *bias, void *y,
                    int y_bf16, int M, int N, int K, af_stream_t stream);
 
+/* Splits fp32 values into an exact tf32 part (low 13 mantissa bits cleared)
+ * and the remainder: hi + lo == src exactly.  Prepares weights for
+ * af_msr_decode_step_f32_split (done once, at weight-load time). */
+int af_split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, af_stream_t stream);
+
 /* ------------------------------------------------------- fused MSR layer */
 /* One recurrent decode step of a MultiScaleRetention layer for `batch`
  * streams: qkv = x W_qkv^T; retention step; RMSNorm(eps, ret_norm_w) over
@@ -140,6 +145,16 @@ int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state, const floa
                            const float *w_qkv, const float *w_o, const float *ret_norm_w,
                            float eps, int batch, int d_model, int num_heads, float *out,
                            af_stream_t stream);
+
+/* af_msr_decode_step_f32 with the projection weights split beforehand by
+ * af_split_tf32 (w_qkv_hi + w_qkv_lo == w_qkv, w_o_hi + w_o_lo == w_o): the
+ * tensor cores read ready-made tf32 operands, which is faster (the weights
+ * stay fp32-exact; twice the weight bytes are read).  head_dim 64/128/256.
+ * Workspace: batch*(7*d_model + num_heads) floats. */
+int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *state, const float *gamma,
+                                 const float *w_qkv_hi, const float *w_qkv_lo, const float *w_o_hi,
+                                 const float *w_o_lo, const float *ret_norm_w, float eps, int batch,
+                                 int d_model, int num_heads, float *out, af_stream_t stream);
 
 /* The same decode step for callers that cannot allocate device memory at
  * call time (inside a CUDA-graph capture, or in a process whose device

@@ -233,3 +233,29 @@ def test_layers_cuda_match_reference_fixture(dev):
     assert rel_err(lin(x).numpy(), g["linear_out"]) < TOL
     assert rel_err((x @ af.Tensor(g["lin_w"].T.copy(), "cuda:0") + af.Tensor(g["lin_b"], "cuda:0")).numpy(),
                    g["linear_out"]) < TOL
+
+
+@pytest.mark.parametrize("B,d,H", [(256, 2048, 8), (5, 512, 2), (130, 1024, 8)])
+def test_msr_decode_step_split_weights_matches_oracle(dev, B, d, H):
+    """Pre-split (tf32 hi + lo) weights give the fp32 decode step."""
+    from aceflow_b200 import cuda_ops
+
+    rng = np.random.default_rng(B + d)
+    dh = d // H
+    w_qkv = (0.02 * rng.standard_normal((3 * d, d))).astype(np.float32)
+    w_o = (0.02 * rng.standard_normal((d, d))).astype(np.float32)
+    ret_w = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    gamma = R.gammas(H)
+    hi, lo = cuda_ops.split_tf32(T(w_qkv, dev))
+    assert torch.equal(hi + lo, T(w_qkv, dev))
+    assert torch.equal(hi, (hi.view(torch.int32) & ~0x1FFF).view(torch.float32))
+    wq_s, wo_s = (hi, lo), cuda_ops.split_tf32(T(w_o, dev))
+    st = np.zeros((B, H, dh, dh), np.float32)
+    st_d = torch.zeros(B, H, dh, dh, device=dev)
+    for s in range(2):
+        x = rng.standard_normal((B, d)).astype(np.float32)
+        ref = cpu_ref.msr_decode_step(x, st, gamma, w_qkv, w_o, ret_w, 1e-6)
+        out = cuda_ops.msr_decode_step_split(T(x, dev), st_d, T(gamma, dev), wq_s, wo_s, T(ret_w, dev), 1e-6)
+        torch.cuda.synchronize()
+        assert rel_err(out.cpu().numpy(), ref) < TOL, s
+        assert rel_err(st_d.cpu().numpy(), st) < TOL, s
