@@ -45,6 +45,7 @@ SIGNATURES = {
     "af_linear_bf16": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "af_msr_decode_step_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
     "af_split_tf32": [_vp, _vp, _vp, _vp, _i64, _vp],
+    "af_linear_f32_split": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "af_msr_decode_step_f32_split": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
     "af_msr_decode_step_f32_noalloc": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
     "af_retention_chunkwise_bf16": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp],

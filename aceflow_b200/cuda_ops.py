@@ -297,3 +297,18 @@ def msr_decode_step_split(x: torch.Tensor, state: torch.Tensor, gamma: torch.Ten
               _p(w_qkv_split[1]), _p(w_o_split[0]), _p(w_o_split[1]), _p(ret_norm_w), float(eps), B, d, H, _p(out),
               _stream(x))
     return out
+
+
+def linear_f32_split(x_split, w_split, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 x . W^T (+ bias) from (hi, lo) splits of x and W (af_linear_f32_split)."""
+    x_hi, x_lo = x_split
+    w_hi, w_lo = w_split
+    for n, t in (("x_hi", x_hi), ("x_lo", x_lo), ("w_hi", w_hi), ("w_lo", w_lo)):
+        _need(t, F32, n)
+    K = x_hi.shape[-1]
+    N = w_hi.shape[0]
+    M = x_hi.numel() // K
+    y = torch.empty(*x_hi.shape[:-1], N, dtype=F32, device=x_hi.device)
+    _lib.call("af_linear_f32_split", _ctx(x_hi), _p(x_hi), _p(x_lo), _p(w_hi), _p(w_lo), _p(bias), _p(y), M, N, K,
+              _stream(x_hi))
+    return y

@@ -131,6 +131,13 @@ int af_linear_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w, const floa
  * af_msr_decode_step_f32_split (done once, at weight-load time). */
 int af_split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, af_stream_t stream);
 
+/* af_linear_f32 from operands split by af_split_tf32 (x_hi + x_lo == x,
+ * w_hi + w_lo == W): the tensor cores read ready-made tf32 operands.
+ * K % 4 == 0, all pointers 16-byte aligned. */
+int af_linear_f32_split(af_ctx *ctx, const float *x_hi, const float *x_lo, const float *w_hi,
+                        const float *w_lo, const float *bias, float *y, int M, int N, int K,
+                        af_stream_t stream);
+
 /* ------------------------------------------------------- fused MSR layer */
 /* One recurrent decode step of a MultiScaleRetention layer for `batch`
  * streams: qkv = x W_qkv^T; retention step; RMSNorm(eps, ret_norm_w) over
