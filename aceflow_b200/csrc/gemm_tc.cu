@@ -87,6 +87,106 @@ struct TileCfg {
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
+// Epilogue of one 128 x BN tile for the calling warp's 32 rows: reads the
+// accumulator through load16 (warp-collective TMEM loads), applies row scale,
+// bias, residual or SwiGLU, and stores (or atomically adds, for split-K).
+template <int BN, class Load16>
+__device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load16, int row, bool row_ok, int n0,
+                                           int N, bool ok, float scale, bool first) {
+  if (ep.swiglu) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float g[16], u[16];
+      load16(c, g);
+      load16(c + 16, u);
+      const int nout = (n0 + c) / 2;  // first output column of this group
+      if (ok && row_ok && n0 + c + 32 <= N) {
+        float hh[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float gg = g[e] * scale, uu = u[e] * scale;
+          hh[e] = gg / (1.0f + expf(-gg)) * uu;
+        }
+        if (ep.out_bf16) {
+          __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + nout;
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(hh[2 * e], hh[2 * e + 1]);
+            pk[e] = *reinterpret_cast<uint32_t *>(&b2);
+          }
+          reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        } else {
+          float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + nout;
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4 *>(o + e) = make_float4(hh[e], hh[e + 1], hh[e + 2], hh[e + 3]);
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      load16(c, v);
+      const int n = n0 + c;
+      if (!ok || !row_ok || n >= N) continue;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        v[e] *= scale;
+        if (first && ep.bias && n + e < N) v[e] += ep.bias[n + e];
+      }
+      if (ep.atomic) {
+        if (first && ep.residual) {
+          const float *r = ep.residual + (size_t)row * ep.ldr + n;
+          for (int e = 0; e < 16; ++e)
+            if (n + e < N) v[e] += r[e];
+        }
+        float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + n;
+        if (n + 16 <= N && ep.vec_ok) {
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            atomicAdd(reinterpret_cast<float4 *>(o + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
+        } else {
+          for (int e = 0; e < 16 && n + e < N; ++e) atomicAdd(o + e, v[e]);
+        }
+        continue;
+      }
+      if (ep.residual) {
+        const float *r = ep.residual + (size_t)row * ep.ldr + n;
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (n + e < N) v[e] += r[e];
+      }
+      if (ep.out_bf16) {
+        __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + n;
+        if (n + 16 <= N && ep.vec_ok) {
+          uint32_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+            pk[e] = *reinterpret_cast<uint32_t *>(&b2);
+          }
+          reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        } else {
+          for (int e = 0; e < 16 && n + e < N; ++e) o[e] = __float2bfloat16(v[e]);
+        }
+      } else {
+        float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + n;
+        if (n + 16 <= N && ep.vec_ok) {
+#pragma unroll
+          for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4 *>(o + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        } else {
+          for (int e = 0; e < 16 && n + e < N; ++e) o[e] = v[e];
+        }
+      }
+    }
+  }
+}
+
 template <int BN, int MODE>
 __global__ void __launch_bounds__(192, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -271,105 +371,157 @@ __global__ void __launch_bounds__(192, 1)
         tmem_wait_ld();
       }
     };
-    if (ep.swiglu) {
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float g[16], u[16];
-        load16(c, g);
-        load16(c + 16, u);
-        const int nout = (n0 + c) / 2;  // first output column of this group
-        if (ok && row_ok && n0 + c + 32 <= N) {
-          float hh[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float gg = g[e] * scale, uu = u[e] * scale;
-            hh[e] = gg / (1.0f + expf(-gg)) * uu;
-          }
-          if (ep.out_bf16) {
-            __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + nout;
-            uint32_t pk[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(hh[2 * e], hh[2 * e + 1]);
-              pk[e] = *reinterpret_cast<uint32_t *>(&b2);
-            }
-            reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-          } else {
-            float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + nout;
-#pragma unroll
-            for (int e = 0; e < 16; e += 4)
-              *reinterpret_cast<float4 *>(o + e) = make_float4(hh[e], hh[e + 1], hh[e + 2], hh[e + 3]);
-          }
-        }
-      }
-    } else {
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float v[16];
-        load16(c, v);
-        const int n = n0 + c;
-        if (!ok || !row_ok || n >= N) continue;
-        const bool first = blockIdx.z == 0;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          v[e] *= scale;
-          if (first && ep.bias && n + e < N) v[e] += ep.bias[n + e];
-        }
-        if (ep.atomic) {
-          if (first && ep.residual) {
-            const float *r = ep.residual + (size_t)row * ep.ldr + n;
-            for (int e = 0; e < 16; ++e)
-              if (n + e < N) v[e] += r[e];
-          }
-          float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + n;
-          if (n + 16 <= N && ep.vec_ok) {
-#pragma unroll
-            for (int e = 0; e < 16; e += 4)
-              atomicAdd(reinterpret_cast<float4 *>(o + e), make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]));
-          } else {
-            for (int e = 0; e < 16 && n + e < N; ++e) atomicAdd(o + e, v[e]);
-          }
-          continue;
-        }
-        if (ep.residual) {
-          const float *r = ep.residual + (size_t)row * ep.ldr + n;
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if (n + e < N) v[e] += r[e];
-        }
-        if (ep.out_bf16) {
-          __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + n;
-          if (n + 16 <= N && ep.vec_ok) {
-            uint32_t pk[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
-              pk[e] = *reinterpret_cast<uint32_t *>(&b2);
-            }
-            reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-          } else {
-            for (int e = 0; e < 16 && n + e < N; ++e) o[e] = __float2bfloat16(v[e]);
-          }
-        } else {
-          float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + n;
-          if (n + 16 <= N && ep.vec_ok) {
-#pragma unroll
-            for (int e = 0; e < 16; e += 4)
-              *reinterpret_cast<float4 *>(o + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-          } else {
-            for (int e = 0; e < 16 && n + e < N; ++e) o[e] = v[e];
-          }
-        }
-      }
-    }
+    store_tile<BN>(ep, load16, row, row_ok, n0, N, ok, scale, blockIdx.z == 0);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// Persistent bf16 GEMM for large M (prefill): one CTA per SM walks the
+// output tiles (row-band major, so consecutive CTAs share A rows), with two
+// TMEM accumulators so the epilogue of one tile overlaps the MMAs of the
+// next.  The TMA ring and its phases run continuously across tiles.
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                int M, int N, int K, GemmEpilogue ep, int *err) {
+  using C = TileCfg<BN, kBF16>;
+  constexpr int S = C::STAGES;
+  constexpr uint32_t TM_COLS = 2 * BN;  // two accumulators
+  static_assert(2 * BN <= 512 && (BN & (BN - 1)) == 0, "two accumulators must fit TMEM");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * C::STAGE_BYTES);
+  uint64_t *full = bars, *empty = bars + S;
+  uint64_t *accf = bars + 2 * S;      // [2] accumulator b holds a finished tile
+  uint64_t *acce = bars + 2 * S + 2;  // [2] accumulator b has been read out
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (N + BN - 1) / BN, m_tiles = (M + C::BM - 1) / C::BM;
+  const int total = n_tiles * m_tiles;
+  const int nk = (K + C::BK - 1) / C::BK;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 128);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto stage_a = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES; };
+  auto stage_b = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES + C::A_BYTES; };
+  auto fail = [&]() {
+    s_abort = 1;
+    atomicOr(err, 1 << AF_ERR_TIMEOUT);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;  // k slices issued so far, over all tiles
+      for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
+        const int m0 = (t / n_tiles) * C::BM, n0 = (t % n_tiles) * BN;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int i = g % S;
+          if (!mbar_wait(&empty[i], ((g / S) & 1) ^ 1)) { fail(); break; }
+          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+          tma_load_2d(stage_a(i), &tmA, &full[i], kb * C::BK, m0);
+          tma_load_2d(stage_b(i), &tmB, &full[i], kb * C::BK, n0);
+        }
+        if (s_abort) break;
+      }
+      for (int x = g - S < 0 ? 0 : g - S; x < g; ++x)  // drain the loads still in flight
+        if (!mbar_wait(&full[x % S], (x / S) & 1)) { fail(); break; }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc = idesc_f32acc(kFmtBF16, C::BM, BN);
+    int g = 0, it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+      const int b = it & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&acce[b], ((it >> 1) & 1) ^ 1));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t acc = tmem + (uint32_t)(b * BN);
+      for (int kb = 0; kb < nk; ++kb, ++g) {
+        const int i = g % S;
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[i], (g / S) & 1));
+        if (!ok || __any_sync(0xffffffffu, s_abort != 0)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t da = sdesc_k_sw128(stage_a(i)), db = sdesc_k_sw128(stage_b(i));
+#pragma unroll
+          for (int k = 0; k < C::BK / C::UK; ++k) {
+            const uint64_t off = (uint64_t)(k * 32) >> 4;
+            umma_bf16(acc, da + off, db + off, idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[i]);
+        }
+        __syncwarp();
+      }
+      if (lane == 0 && ok) umma_commit(&accf[b]);
+      __syncwarp();
+    }
+    if (!ok && lane == 0) fail();
+  } else {
+    const int q = warp & 3;
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      const int b = it & 1;
+      const bool ok = mbar_wait(&accf[b], (it >> 1) & 1);
+      if (!ok) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (t / n_tiles) * C::BM, n0 = (t % n_tiles) * BN;
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < M;
+      float scale = 1.f;
+      if (ep.row_parts && row_ok) {
+        float sum = 0.f;
+        for (int p = 0; p < ep.nparts; ++p) sum += ep.row_parts[(size_t)row * ep.nparts + p];
+        scale = 1.0f / sqrtf(sum * ep.inv_d + ep.eps);
+      }
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
+      auto load16 = [&](int col, float (&v)[16]) {
+        __syncwarp();
+        tmem_ld16(tbase + col, v);
+        tmem_wait_ld();
+      };
+      store_tile<BN>(ep, load16, row, row_ok, n0, N, true, scale, true);
+      tc_fence_before();
+      mbar_arrive(&acce[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
   }
 }
 
@@ -402,6 +554,28 @@ int make_kmajor_map(CUtensorMap *map, const void *base, bool fp32, int rows, int
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return af::fail(AF_ERR_ARG, "%s: cuTensorMapEncodeTiled failed (%d)", fn, (int)r);
   return AF_OK;
+}
+
+template <int BN>
+int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
+                      const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
+  using C = TileCfg<BN, kBF16>;
+  CUtensorMap ta, tb;
+  int rc = make_kmajor_map(&ta, A, false, M, K, lda, C::BM, fn);
+  if (rc) return rc;
+  rc = make_kmajor_map(&tb, B, false, N, K, ldb, BN, fn);
+  if (rc) return rc;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(umma_gemm_persistent_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)C::SMEM);
+    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
+    attr_done = true;
+  }
+  const int64_t total = (int64_t)((N + BN - 1) / BN) * ((M + C::BM - 1) / C::BM);
+  const int grid = (int)(total < ctx->num_sms ? total : ctx->num_sms);
+  umma_gemm_persistent_kernel<BN><<<grid, 192, C::SMEM, st>>>(ta, tb, M, N, K, ep, ctx->dev_err);
+  return af::launched(ctx, fn);
 }
 
 template <int BN, int MODE>
@@ -502,6 +676,11 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
       cudaError_t e = cudaMemsetAsync(a.out, 0, (size_t)M * a.ldo * 4, st);
       if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: zeroing the split-K output: %s", fn, cudaGetErrorString(e));
     }
+  }
+  // large bf16 GEMMs (two or more waves of tiles): persistent kernel
+  if (MODE == kBF16 && splits == 1 && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms && !getenv("AF_GEMM_NO_PERSIST")) {
+    if (bn == 256) return launch_persistent<256>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+    return launch_persistent<128>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
   }
 #define AF_LAUNCH(BNV) return launch_tc<BNV, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn)
   switch (bn) {

@@ -279,22 +279,24 @@ __global__ void __launch_bounds__(192, 1)
       // (a) S_op = bf16(S^T) (K-major [v][k]); S^T *= gamma^L in TMEM
       const float gL = gpow[L];
 #pragma unroll 1
-      for (int k0 = 0; k0 < DH; k0 += 16) {
-        float x[16];
+      for (int k0 = 0; k0 < DH; k0 += 64) {  // 64 columns per TMEM round trip
+        float x[64];
         __syncwarp();
-        tmem_ld16(tmem + lane_base + TM_S + k0, x);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) tmem_ld16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
         tmem_wait_ld();
         uint8_t *slice_base = sm + SOP_OFF + (k0 >> 6) * (2 * BOX);
-        const int c16 = (k0 & 63) >> 3;
-        uint4 w0 = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
-        uint4 w1 = make_uint4(pack_bf16(x[8], x[9]), pack_bf16(x[10], x[11]), pack_bf16(x[12], x[13]),
-                              pack_bf16(x[14], x[15]));
-        *reinterpret_cast<uint4 *>(slice_base + sw128(v, c16)) = w0;
-        *reinterpret_cast<uint4 *>(slice_base + sw128(v, c16 + 1)) = w1;
 #pragma unroll
-        for (int j = 0; j < 16; ++j) x[j] *= gL;
+        for (int c16 = 0; c16 < 8; ++c16) {
+          const float *y = x + 8 * c16;
+          *reinterpret_cast<uint4 *>(slice_base + sw128(v, c16)) =
+              make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+        }
+#pragma unroll
+        for (int j = 0; j < 64; ++j) x[j] *= gL;
         __syncwarp();
-        tmem_st16(tmem + lane_base + TM_S + k0, x);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) tmem_st16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
       }
       tmem_wait_st();
       // (b) Vs = diag(gamma^(L-1-j)) V, same swizzled layout as V
@@ -322,24 +324,19 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) {
         tc_fence_after();
         const int i = q * 16 + lane;
-#pragma unroll 1
-        for (int j0 = 0; j0 < C; j0 += 16) {
-          float x[16];
-          __syncwarp();
-          tmem_ld16(tmem + lane_base + TM_SC + j0, x);
-          tmem_wait_ld();
-          if (lane < 16) {
+        float x[C];
+        __syncwarp();
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-              const int j = j0 + u;
-              x[u] = (j <= i) ? x[u] * ginv[j] : 0.f;
-            }
-            uint4 w0 = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]), pack_bf16(x[4], x[5]),
-                                  pack_bf16(x[6], x[7]));
-            uint4 w1 = make_uint4(pack_bf16(x[8], x[9]), pack_bf16(x[10], x[11]), pack_bf16(x[12], x[13]),
-                                  pack_bf16(x[14], x[15]));
-            *reinterpret_cast<uint4 *>(sm + P_OFF + sw128(i, j0 >> 3)) = w0;
-            *reinterpret_cast<uint4 *>(sm + P_OFF + sw128(i, (j0 >> 3) + 1)) = w1;
+        for (int u = 0; u < C / 16; ++u) tmem_ld16(tmem + lane_base + TM_SC + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+        tmem_wait_ld();
+        if (lane < 16) {
+#pragma unroll
+          for (int j = 0; j < C; ++j) x[j] = (j <= i) ? x[j] * ginv[j] : 0.f;
+#pragma unroll
+          for (int c16 = 0; c16 < C / 8; ++c16) {
+            const float *y = x + 8 * c16;
+            *reinterpret_cast<uint4 *>(sm + P_OFF + sw128(i, c16)) =
+                make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
           }
         }
       }
@@ -355,24 +352,34 @@ __global__ void __launch_bounds__(192, 1)
       const int col = h * DH + slice * VS + v;
       const float wv = p.norm_w ? p.norm_w[col] : 1.f;
       __nv_bfloat16 *orow = p.out + ((size_t)b * p.T + t0) * d + col;
-#pragma unroll 1
-      for (int i0 = 0; i0 < C; i0 += 16) {
-        float x[16];
-        __syncwarp();
-        tmem_ld16(tmem + lane_base + TM_O + i0, x);
-        tmem_wait_ld();
+      float x[C];
+      __syncwarp();
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          const int i = i0 + u;
-          const float o = x[u] * gpow[i + 1];
-          if (i < L) orow[(size_t)i * d] = __float2bfloat16(o * wv);
-          float s2 = o * o;
-          s2 = warp_sum(s2);
-          if (lane == 0) red[q * C + i] = s2;
+      for (int u = 0; u < C / 16; ++u) tmem_ld16(tmem + lane_base + TM_O + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(bar_out);  // O^T is in registers: the next chunk's MMAs may overwrite it
+#pragma unroll
+      for (int i = 0; i < C; ++i) {
+        x[i] *= gpow[i + 1];
+        if (i < L) orow[(size_t)i * d] = __float2bfloat16(x[i] * wv);
+        x[i] *= x[i];
+      }
+      // column sums of o^2 over the warp's 32 values of v: recursive halving
+      // (lane l ends with tokens 2l and 2l+1), 62 shuffles for 64 tokens
+      static_assert(C == 64, "the halving schedule below is written for 64 tokens");
+#pragma unroll
+      for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+        const bool up = lane & o;
+#pragma unroll
+        for (int j = 0; j < n; ++j) {
+          const float send = up ? x[j] : x[j + n];
+          const float keep = up ? x[j + n] : x[j];
+          x[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
       }
-      tc_fence_before();
-      mbar_arrive(bar_out);
+      red[q * C + 2 * lane] = x[0];
+      red[q * C + 2 * lane + 1] = x[1];
       math_sync();
       if (p.sumsq && mt < L) {
         const float s2 = red[mt] + red[C + mt] + red[2 * C + mt] + red[3 * C + mt];
