@@ -34,6 +34,7 @@ SIGNATURES = {
     "af_reserve_workspace": [_vp, _sz],
     "af_launch_count": [_vp, ctypes.POINTER(_i64)],
     "af_check_device": [_vp, ctypes.POINTER(_i), _i],
+    "af_set_option": [_vp, ctypes.c_char_p, _i64],
     "af_retention_step": [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i, _i, _i, _vp],
     "af_retention_scan": [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp],
     "af_rmsnorm_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp],
@@ -45,6 +46,7 @@ SIGNATURES = {
     "af_linear_bf16": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "af_msr_decode_step_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
     "af_split_tf32": [_vp, _vp, _vp, _vp, _i64, _vp],
+    "af_pack_qkv_heads": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "af_linear_f32_split": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "af_msr_decode_step_f32_split": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
     "af_msr_decode_step_f32_noalloc": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
@@ -118,6 +120,11 @@ def context(device_index: int) -> int:
                 ctx = p.value
                 _contexts[device_index] = ctx
     return ctx
+
+
+def set_option(device_index: int, name: str, value: int) -> None:
+    """af_set_option on the device's context."""
+    check(lib().af_set_option(context(device_index), name.encode(), int(value)), "af_set_option")
 
 
 def check_device(device_index: int, reset: bool = True) -> int:

@@ -2,6 +2,7 @@
 #include "common.cuh"
 
 #include <cstdlib>
+#include <cstring>
 #include <new>
 
 namespace af {
@@ -94,6 +95,7 @@ int af_cuda_init(int device, af_ctx **out) {
     return af::fail(AF_ERR_CUDA, "af_cuda_init: streams/events: %s", cudaGetErrorString(e));
   }
   if (const char *env = getenv("AF_DECODE_SLICE_ROWS")) ctx->decode_slice_rows = atoi(env);
+  if (const char *env = getenv("AF_DECODE_HEAD_GROUPS")) ctx->decode_head_groups = atoi(env);
   ctx->magic = kCtxMagic;
   *out = ctx;
   return AF_OK;
@@ -130,6 +132,23 @@ int af_check_device(af_ctx *ctx, int *flags, int reset) {
   if (flags) *flags = h;
   if (h & (1 << AF_ERR_TIMEOUT))
     return af::fail(AF_ERR_TIMEOUT, "af_check_device: a device-side wait timed out (flags 0x%x)", h);
+  return AF_OK;
+}
+
+int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
+  AF_ENTER(ctx, "af_set_option");
+  if (!name) return af::fail(AF_ERR_ARG, "af_set_option: name is NULL");
+  if (!strcmp(name, "decode_head_groups")) {
+    if (value < 1 || value > af_ctx::kMaxSlices) return af::fail(AF_ERR_ARG, "af_set_option: decode_head_groups 1..8");
+    ctx->decode_head_groups = (int)value;
+  } else if (!strcmp(name, "allow_split_k")) {
+    ctx->allow_split_k = value != 0;
+  } else if (!strcmp(name, "decode_slice_rows")) {
+    if (value < 0) return af::fail(AF_ERR_ARG, "af_set_option: decode_slice_rows >= 0");
+    ctx->decode_slice_rows = (int)value;
+  } else {
+    return af::fail(AF_ERR_ARG, "af_set_option: unknown option '%s'", name);
+  }
   return AF_OK;
 }
 

@@ -24,6 +24,7 @@ struct af_ctx {
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   cudaEvent_t ev_a[kMaxSlices] = {}, ev_b[kMaxSlices] = {};
   int allow_split_k = 1;        // small-M GEMMs may split K (fp32 atomics: not bitwise reproducible)
+  int decode_head_groups = 4;   // head groups pipelined in the split decode step (1 = sequential)
   int decode_slice_rows = 0;  // batch rows per overlapped slice; 0 = one sequential pass (faster today)
 };
 
@@ -70,6 +71,7 @@ struct GemmEpilogueArgs {
   const float *residual = nullptr;  // fp32 [M][ldr] added after scaling
   int64_t ldr = 0;
   int swiglu = 0;  // (16 gate, 16 up) column groups -> silu(g)*u, N/2 outputs
+  int accumulate = 0;  // add (atomically) into out, which the caller initialised
 };
 
 bool tc_gemm_ok(const void *A, int64_t lda, const void *B, int64_t ldb, int K, bool fp32);

@@ -668,7 +668,10 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
     const int v = atoi(e);
     if (v >= 1 && v <= 16 && (v == 1 || can_split) && v <= nk) splits = v;
   }
-  if (splits > 1) {
+  if (a.accumulate) {
+    if (a.swiglu || a.out_bf16) return af::fail(AF_ERR_ARG, "%s: accumulation needs an fp32 linear epilogue", fn);
+    ep.atomic = 1;  // partial products added into out as it is
+  } else if (splits > 1) {
     ep.atomic = 1;
     if (a.residual == a.out) {
       ep.residual = nullptr;  // out already holds the residual: every split adds its partial into it

@@ -13,7 +13,7 @@ namespace af {
 int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
                           int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn,
-                          int out_bf16, float *out_lo = nullptr);
+                          int out_bf16, float *out_lo = nullptr, int h0 = 0, int hn = 0, int64_t qkv_hs = 0);
 int linear_f32(af_ctx *ctx, const float *x, int64_t ldx, const float *w, int64_t ldw, const float *bias, float *y,
                int64_t ldy, int M, int N, int K, const float *parts, int nparts, float inv_d, float eps,
                cudaStream_t st, const char *fn);
@@ -79,11 +79,53 @@ int msr_decode_step_impl(af_ctx *ctx, const float *x, float *state, const float 
   return AF_OK;
 }
 
-// Decode step from weights split beforehand (af_split_tf32): the input is
-// split by a small kernel, the retention kernel writes its output split, and
-// both projections run as pre-split 3xTF32 GEMMs (no in-kernel converter).
-// Workspace floats: x hi/lo 2Bd, qkv 3Bd, o hi/lo 2Bd, sumsq BH.
-size_t msr_decode_split_scratch_floats(int B, int d, int H) { return (size_t)B * (7 * (size_t)d + H); }
+// Decode step from weights split beforehand.  The QKV weights are packed
+// head-major ([H][q|k|v][dh][d], af_pack_qkv_heads) and split into tf32
+// hi + lo (af_split_tf32); W_o is split as it is.  The input is split by a
+// small kernel, the state-stream kernel writes its output split, and both
+// projections run as pre-split 3xTF32 GEMMs.
+//
+// With G > 1 head groups the step is a three-stream pipeline: the QKV GEMM
+// of group g+1 (tensor cores, caller's stream) runs while group g streams its
+// state (HBM, high-priority side stream) and group g-1's W_o product
+// (tensor cores, second side stream) accumulates into an fp32 buffer; the
+// RMSNorm row scale is applied once at the end.  Head-major packing makes
+// every group's weights a contiguous block, so no weight is read twice.
+// Workspace floats: x hi/lo 2Bd, qkv 3Bd, o hi/lo 2Bd, partial sums Bd, sumsq BH.
+size_t msr_decode_split_scratch_floats(int B, int d, int H) { return (size_t)B * (8 * (size_t)d + H); }
+
+namespace {
+__global__ void rowscale_kernel(const float *__restrict__ P, const float *__restrict__ sumsq, float *__restrict__ out,
+                                int d, int H, float inv_d, float eps) {
+  const int b = blockIdx.x;
+  __shared__ float s_scale;
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int h = 0; h < H; ++h) t += sumsq[(size_t)b * H + h];
+    s_scale = 1.0f / sqrtf(t * inv_d + eps);
+  }
+  __syncthreads();
+  const float sc = s_scale;
+  const float4 *p4 = reinterpret_cast<const float4 *>(P + (size_t)b * d);
+  float4 *o4 = reinterpret_cast<float4 *>(out + (size_t)b * d);
+  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {
+    const float4 v = p4[i];
+    o4[i] = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
+  }
+}
+
+// dst row (h*3 + part)*dh + i  <-  src row part*d + h*dh + i
+__global__ void pack_qkv_heads_kernel(const uint8_t *__restrict__ src, uint8_t *__restrict__ dst, int d, int H,
+                                      int row_bytes) {
+  const int r = blockIdx.x;  // destination row
+  const int dh = d / H;
+  const int h = r / (3 * dh), part = (r / dh) % 3, i = r % dh;
+  const uint8_t *a = src + ((size_t)part * d + (size_t)h * dh + i) * row_bytes;
+  uint8_t *o = dst + (size_t)r * row_bytes;
+  for (int c = threadIdx.x * 16; c < row_bytes; c += blockDim.x * 16)
+    *reinterpret_cast<uint4 *>(o + c) = *reinterpret_cast<const uint4 *>(a + c);
+}
+}  // namespace
 
 int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const float *gamma, const float *wq_hi,
                                const float *wq_lo, const float *wo_hi, const float *wo_lo, const float *ret_norm_w,
@@ -91,25 +133,75 @@ int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const 
                                const char *fn) {
   const int dh = d / H;
   float *x_hi = scratch, *x_lo = x_hi + (size_t)B * d, *qkv = x_lo + (size_t)B * d;
-  float *o_hi = qkv + (size_t)B * 3 * d, *o_lo = o_hi + (size_t)B * d, *sumsq = o_lo + (size_t)B * d;
+  float *o_hi = qkv + (size_t)B * 3 * d, *o_lo = o_hi + (size_t)B * d, *P = o_lo + (size_t)B * d;
+  float *sumsq = P + (size_t)B * d;
+  const int64_t sbs = (int64_t)H * dh * dh;
+  int G = ctx->decode_head_groups;
+  if (G < 2 || H % G != 0 || G > af_ctx::kMaxSlices) G = 1;
+  const int Hg = H / G, Ng = 3 * Hg * dh;
   int rc = split_tf32(ctx, x, x_hi, x_lo, (int64_t)B * d, st, fn);
   if (rc) return rc;
-  GemmEpilogueArgs e1;
-  e1.out = qkv;
-  e1.ldo = 3 * d;
-  rc = tc_gemm_presplit(ctx, x_hi, x_lo, d, wq_hi, wq_lo, d, B, 3 * d, d, e1, st, fn);
+  auto qkv_gemm = [&](int g, cudaStream_t s) {
+    GemmEpilogueArgs e;
+    e.out = qkv + (size_t)g * B * Ng;
+    e.ldo = Ng;
+    return tc_gemm_presplit(ctx, x_hi, x_lo, d, wq_hi + (size_t)g * Ng * d, wq_lo + (size_t)g * Ng * d, d, B, Ng, d, e,
+                            s, fn);
+  };
+  auto retention = [&](int g, cudaStream_t s) {
+    const float *q = qkv + (size_t)g * B * Ng;
+    return launch_retention_step(ctx, state, sbs, gamma, q, q + dh, q + 2 * dh, Ng, o_hi, d, B, H, dh, ret_norm_w,
+                                 sumsq, s, fn, 0, o_lo, g * Hg, Hg, 3 * (int64_t)dh);
+  };
+  if (G == 1) {
+    rc = qkv_gemm(0, st);
+    if (rc) return rc;
+    rc = retention(0, st);
+    if (rc) return rc;
+    GemmEpilogueArgs e2;
+    e2.out = out;
+    e2.ldo = d;
+    e2.row_parts = sumsq;
+    e2.nparts = H;
+    e2.inv_d = 1.0f / (float)d;
+    e2.eps = eps;
+    return tc_gemm_presplit(ctx, o_hi, o_lo, d, wo_hi, wo_lo, d, B, d, d, e2, st, fn);
+  }
+  cudaStream_t s_ret = ctx->side[0], s_out = ctx->side[1];
+  AF_CUDA(cudaEventRecord(ctx->ev_fork, st), fn);
+  AF_CUDA(cudaStreamWaitEvent(s_ret, ctx->ev_fork, 0), fn);
+  AF_CUDA(cudaStreamWaitEvent(s_out, ctx->ev_fork, 0), fn);
+  AF_CUDA(cudaMemsetAsync(P, 0, (size_t)B * d * sizeof(float), s_out), fn);
+  for (int g = 0; g < G; ++g) {
+    rc = qkv_gemm(g, st);
+    if (rc) return rc;
+    AF_CUDA(cudaEventRecord(ctx->ev_a[g], st), fn);
+    AF_CUDA(cudaStreamWaitEvent(s_ret, ctx->ev_a[g], 0), fn);
+    rc = retention(g, s_ret);
+    if (rc) return rc;
+    AF_CUDA(cudaEventRecord(ctx->ev_b[g], s_ret), fn);
+    AF_CUDA(cudaStreamWaitEvent(s_out, ctx->ev_b[g], 0), fn);
+    GemmEpilogueArgs e;
+    e.out = P;
+    e.ldo = d;
+    e.accumulate = 1;
+    const size_t c0 = (size_t)g * Hg * dh;
+    rc = tc_gemm_presplit(ctx, o_hi + c0, o_lo + c0, d, wo_hi + c0, wo_lo + c0, d, B, d, Hg * dh, e, s_out, fn);
+    if (rc) return rc;
+  }
+  rowscale_kernel<<<B, 256, 0, s_out>>>(P, sumsq, out, d, H, 1.0f / (float)d, eps);
+  rc = launched(ctx, fn);
   if (rc) return rc;
-  rc = launch_retention_step(ctx, state, (int64_t)H * dh * dh, gamma, qkv, qkv + d, qkv + 2 * d, 3 * (int64_t)d, o_hi,
-                             d, B, H, dh, ret_norm_w, sumsq, st, fn, 0, o_lo);
-  if (rc) return rc;
-  GemmEpilogueArgs e2;
-  e2.out = out;
-  e2.ldo = d;
-  e2.row_parts = sumsq;
-  e2.nparts = H;
-  e2.inv_d = 1.0f / (float)d;
-  e2.eps = eps;
-  return tc_gemm_presplit(ctx, o_hi, o_lo, d, wo_hi, wo_lo, d, B, d, d, e2, st, fn);
+  AF_CUDA(cudaEventRecord(ctx->ev_join, s_out), fn);
+  AF_CUDA(cudaStreamWaitEvent(st, ctx->ev_join, 0), fn);
+  return AF_OK;
+}
+
+int pack_qkv_heads(af_ctx *ctx, const void *src, void *dst, int d, int H, int elem_bytes, cudaStream_t st,
+                   const char *fn) {
+  pack_qkv_heads_kernel<<<3 * d, 128, 0, st>>>(static_cast<const uint8_t *>(src), static_cast<uint8_t *>(dst), d, H,
+                                                d * elem_bytes);
+  return launched(ctx, fn);
 }
 
 int check_msr_decode(const char *fn, const float *x, float *state, const float *gamma, const float *w_qkv,
@@ -151,8 +243,9 @@ extern "C" int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *
   if (rc) return rc;
   AF_REQUIRE(w_qkv_lo && w_o_lo, "af_msr_decode_step_f32_split", "null weight pointer");
   const int dh = d / H;
-  AF_REQUIRE((dh == 64 || dh == 128 || dh == 256) && d % 4 == 0 && af::aligned16(x) && af::aligned16(out),
-             "af_msr_decode_step_f32_split", "head_dim must be 64, 128 or 256 and x, out 16-byte aligned");
+  AF_REQUIRE((dh == 64 || dh == 128 || dh == 256) && d % 4 == 0 && af::aligned16(x) && af::aligned16(out) &&
+                 af::aligned16(w_qkv_hi) && af::aligned16(w_qkv_lo) && af::aligned16(w_o_hi) && af::aligned16(w_o_lo),
+             "af_msr_decode_step_f32_split", "head_dim must be 64, 128 or 256 and every pointer 16-byte aligned");
   if (B == 0) return AF_OK;
   void *ws = nullptr;
   rc = af::workspace(ctx, af::msr_decode_split_scratch_floats(B, d, H) * sizeof(float), &ws, fn);
@@ -230,4 +323,15 @@ extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_
   e2.inv_d = 1.0f / (float)d;
   e2.eps = eps;
   return af::tc_gemm(ctx, o, d, w_o, d, (int)N, d, d, false, e2, st, fn);
+}
+
+extern "C" int af_pack_qkv_heads(af_ctx *ctx, const void *src, void *dst, int d, int H, int elem_bytes,
+                                 af_stream_t stream) {
+  const char *fn = "af_pack_qkv_heads";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(src && dst && src != dst, "af_pack_qkv_heads", "src and dst must be distinct buffers");
+  AF_REQUIRE(H > 0 && d % H == 0 && (elem_bytes == 2 || elem_bytes == 4) && ((int64_t)d * elem_bytes) % 16 == 0 &&
+                 af::aligned16(src) && af::aligned16(dst),
+             "af_pack_qkv_heads", "d %% H == 0, rows of 16-byte multiples, aligned buffers");
+  return af::pack_qkv_heads(ctx, src, dst, d, H, elem_bytes, af::stream_of(stream), fn);
 }

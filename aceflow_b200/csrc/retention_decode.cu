@@ -20,6 +20,11 @@
 
 namespace {
 
+struct HeadGroup {
+  int h0, n;                // first head and number of heads in this launch
+  int64_t qkv_head_stride;  // floats between consecutive heads' q (and k, v)
+};
+
 template <int DH, int THREADS>
 struct StepShape {
   static constexpr int NCG = DH / 4;            // float4 column groups per row
@@ -129,15 +134,17 @@ __global__ void __launch_bounds__(THREADS)
                           const float *__restrict__ q, const float *__restrict__ k,
                           const float *__restrict__ v, int64_t qs, float *__restrict__ out,
                           int64_t out_rs, int H, const float *__restrict__ norm_w,
-                          float *__restrict__ sumsq, int out_bf16, float *__restrict__ out_lo) {
+                          float *__restrict__ sumsq, int out_bf16, float *__restrict__ out_lo, HeadGroup hg) {
+  // This launch covers heads [hg.h0, hg.h0 + hg.n) of H; q/k/v of head
+  // h0 + j sit j * hg.qkv_head_stride floats after the row's q/k/v pointers.
   using Sh = StepShape<DH, THREADS>;
   __shared__ float sk[DH], sq[DH];
   __shared__ float4 red[Sh::RG * Sh::NCG];
-  const int b = blockIdx.x / H, h = blockIdx.x % H;
+  const int b = blockIdx.x / hg.n, hl = blockIdx.x % hg.n, h = hg.h0 + hl;
   const int cg = threadIdx.x % Sh::NCG, rg = threadIdx.x / Sh::NCG;
-  const float *qh = q + (size_t)b * qs + (size_t)h * DH;
-  const float *kh = k + (size_t)b * qs + (size_t)h * DH;
-  const float *vh = v + (size_t)b * qs + (size_t)h * DH;
+  const float *qh = q + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
+  const float *kh = k + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
+  const float *vh = v + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
   for (int i = threadIdx.x; i < DH; i += THREADS) {
     sk[i] = kh[i];
     sq[i] = qh[i];
@@ -151,7 +158,7 @@ __global__ void __launch_bounds__(THREADS)
                                                    (size_t)h * DH)
                          : out + (size_t)b * out_rs + (size_t)h * DH;
   finish_head<DH, THREADS>(acc, red, o_out, norm_w ? norm_w + (size_t)h * DH : nullptr,
-                           sumsq ? sumsq + blockIdx.x : nullptr, cg, rg, out_bf16 != 0,
+                           sumsq ? sumsq + (size_t)b * H + h : nullptr, cg, rg, out_bf16 != 0,
                            out_lo ? out_lo + (size_t)b * out_rs + (size_t)h * DH : nullptr);
 }
 
@@ -322,13 +329,20 @@ namespace af {
 int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs,
                           int batch, int H, int dh, const float *norm_w, float *sumsq, cudaStream_t st,
-                          const char *fn, int out_bf16, float *out_lo) {
+                          const char *fn, int out_bf16, float *out_lo, int h0, int hn, int64_t qkv_hs) {
   if (batch == 0) return AF_OK;
-  const dim3 grid((unsigned)(batch * H));
+  if (hn <= 0) {  // all heads, q/k/v head-contiguous
+    h0 = 0;
+    hn = H;
+    qkv_hs = dh;
+  }
+  const HeadGroup hgp{h0, hn, qkv_hs};
+  const bool all_heads = h0 == 0 && hn == H && qkv_hs == dh;
+  const dim3 grid((unsigned)(batch * hn));
   if (out_bf16 && !(dh == 256 || dh == 128 || dh == 64) )
     return fail(AF_ERR_ARG, "%s: bf16 output needs head_dim 64, 128 or 256", fn);
   if (dh % 4 != 0 || dh > 1024 || state_bs % 4 != 0 || !aligned16(state)) {
-    if (norm_w || sumsq) return fail(AF_ERR_ARG, "%s: fused norm needs head_dim %% 4 == 0 and <= 1024", fn);
+    if (norm_w || sumsq || !all_heads) return fail(AF_ERR_ARG, "%s: fused norm needs head_dim %% 4 == 0 and <= 1024", fn);
     retention_step_scalar<<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, 1, H, dh);
     return launched(ctx, fn);
   }
@@ -338,20 +352,21 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
     return fail(AF_ERR_ARG, "%s: split output needs head_dim 64, 128 or 256 and an aligned buffer", fn);
   if (fast && dh == 256) {
     retention_step_kernel<256, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                          norm_w, sumsq, out_bf16, out_lo);
+                                                          norm_w, sumsq, out_bf16, out_lo, hgp);
   } else if (fast && dh == 128) {
     retention_step_kernel<128, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                          norm_w, sumsq, out_bf16, out_lo);
+                                                          norm_w, sumsq, out_bf16, out_lo, hgp);
   } else if (fast && dh == 64) {
     retention_step_kernel<64, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                         norm_w, sumsq, out_bf16, out_lo);
+                                                         norm_w, sumsq, out_bf16, out_lo, hgp);
   } else if (fast && dh == 32) {
     retention_step_kernel<32, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                         norm_w, sumsq, out_bf16, out_lo);
+                                                         norm_w, sumsq, out_bf16, out_lo, hgp);
   } else if (fast && dh == 16) {
     retention_step_kernel<16, 64><<<grid, 64, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                       norm_w, sumsq, out_bf16, out_lo);
+                                                       norm_w, sumsq, out_bf16, out_lo, hgp);
   } else {
+    if (!all_heads) return fail(AF_ERR_ARG, "%s: head groups need head_dim 16..256 (power of two)", fn);
     const int ncg = dh / 4;
     int rgs = 256 / ncg;
     if (rgs < 1) rgs = 1;
@@ -374,7 +389,7 @@ extern "C" int af_retention_step(af_ctx *ctx, float *state, int64_t state_bs, co
   int rc = check_common(fn, state, gamma, q, k, v, out, batch, H, dh, state_bs, qs);
   if (rc) return rc;
   return af::launch_retention_step(ctx, state, state_bs, gamma, q, k, v, qs, out, (int64_t)H * dh, batch, H, dh,
-                                   nullptr, nullptr, af::stream_of(stream), fn, 0, nullptr);
+                                   nullptr, nullptr, af::stream_of(stream), fn, 0, nullptr, 0, 0, 0);
 }
 
 extern "C" int af_retention_scan(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,

@@ -280,10 +280,29 @@ def split_tf32(t: torch.Tensor):
     return hi, lo
 
 
+def pack_qkv_heads(w_qkv: torch.Tensor, num_heads: int) -> torch.Tensor:
+    """[3d, d] (rows q, k, v) -> head-major [H][q|k|v][dh] rows (af_pack_qkv_heads)."""
+    if w_qkv.dtype not in (F32, BF16) or not w_qkv.is_contiguous():
+        raise ValueError("w_qkv must be contiguous fp32 or bf16")
+    d = w_qkv.shape[1]
+    if tuple(w_qkv.shape) != (3 * d, d):
+        raise ValueError("w_qkv must be [3d, d]")
+    out = torch.empty_like(w_qkv)
+    _lib.call("af_pack_qkv_heads", _ctx(w_qkv), _p(w_qkv), _p(out), d, num_heads, w_qkv.element_size(),
+              _stream(w_qkv))
+    return out
+
+
+def prepare_decode_weights(w_qkv: torch.Tensor, w_o: torch.Tensor, num_heads: int):
+    """Weights for msr_decode_step_split: (split(pack_qkv_heads(w_qkv)), split(w_o))."""
+    return split_tf32(pack_qkv_heads(w_qkv.contiguous(), num_heads)), split_tf32(w_o.contiguous())
+
+
 def msr_decode_step_split(x: torch.Tensor, state: torch.Tensor, gamma: torch.Tensor, w_qkv_split, w_o_split,
                           ret_norm_w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Decode step from pre-split weights: w_qkv_split = split_tf32(w_qkv),
-    w_o_split = split_tf32(w_o) (af_msr_decode_step_f32_split)."""
+    """Decode step from prepared weights (prepare_decode_weights):
+    w_qkv_split = split_tf32(pack_qkv_heads(w_qkv)), w_o_split = split_tf32(w_o)
+    (af_msr_decode_step_f32_split)."""
     B, d = x.shape
     H = state.shape[1]
     for n, t in (("x", x), ("state", state), ("gamma", gamma), ("ret_norm_w", ret_norm_w), ("w_qkv_hi", w_qkv_split[0]),

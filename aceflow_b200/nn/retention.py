@@ -62,9 +62,9 @@ class MultiScaleRetention(Module):
             w_qkv = torch.cat([self.w_q.torch, self.w_k.torch, self.w_v.torch], 0).contiguous()
             self._dev = dict(w_qkv=w_qkv, w_o=self.w_o.torch, gamma=cuda_ops.gammas(self.num_heads, dev))
             if self.head_dim in (64, 128, 256):
-                # decode reads tf32-split weights (exact: hi + lo == w), prepared once here
-                self._dev["w_qkv_split"] = cuda_ops.split_tf32(w_qkv)
-                self._dev["w_o_split"] = cuda_ops.split_tf32(self.w_o.torch.contiguous())
+                # decode reads head-major, tf32-split weights (exact: hi + lo == w), prepared once here
+                self._dev["w_qkv_split"], self._dev["w_o_split"] = cuda_ops.prepare_decode_weights(
+                    w_qkv, self.w_o.torch, self.num_heads)
 
     def _packed(self, x: Tensor) -> dict:
         if self._dev is None:

@@ -236,7 +236,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     # weights are prepared once, at load time, like the module's .to(): fp32
     # split exactly into tf32 hi + lo for the tensor cores
-    w_qkv_s, w_o_s = cuda_ops.split_tf32(w_qkv), cuda_ops.split_tf32(w_o)
+    w_qkv_s, w_o_s = cuda_ops.prepare_decode_weights(w_qkv, w_o, H)
 
     def step(i):
         cuda_ops.msr_decode_step_split(xs[i % n_pool], state, gamma, w_qkv_s, w_o_s, ret_w, EPS, out=out)

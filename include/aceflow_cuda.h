@@ -59,6 +59,12 @@ int af_reserve_workspace(af_ctx *ctx, size_t bytes);
  * hanging.  Returns AF_ERR_TIMEOUT if set; `flags` (may be NULL) receives the
  * word; `reset` clears it. */
 int af_check_device(af_ctx *ctx, int *flags, int reset);
+/* Tuning switches of a context (no reference counterpart):
+ *   "decode_head_groups" 1..8  head groups pipelined by the split decode step (default 4)
+ *   "allow_split_k"      0/1   small-M GEMMs may split K with fp32 atomics (default 1;
+ *                              0 makes results bitwise reproducible run to run)
+ *   "decode_slice_rows"  >= 0  batch slices of af_msr_decode_step_f32 (default 0: none) */
+int af_set_option(af_ctx *ctx, const char *name, int64_t value);
 /* Number of this library's kernel launches issued through `ctx` so far. */
 int af_launch_count(af_ctx *ctx, int64_t *count);
 
@@ -126,6 +132,13 @@ int af_linear_f32(af_ctx *ctx, const float *x, const float *w, const float *bias
 int af_linear_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w, const float *bias, void *y,
                    int y_bf16, int M, int N, int K, af_stream_t stream);
 
+/* Reorders the fused QKV weight [3d][d] (rows q, k, v as in AceEngine's
+ * w_qkv, aceflow-core/src/cpu/mod.rs:201-207) into head-major rows
+ * [H][q|k|v][head_dim][d], so each head group's projection weights are one
+ * contiguous block.  elem_bytes 2 or 4. */
+int af_pack_qkv_heads(af_ctx *ctx, const void *src, void *dst, int d_model, int num_heads,
+                      int elem_bytes, af_stream_t stream);
+
 /* Splits fp32 values into an exact tf32 part (low 13 mantissa bits cleared)
  * and the remainder: hi + lo == src exactly.  Prepares weights for
  * af_msr_decode_step_f32_split (done once, at weight-load time). */
@@ -153,11 +166,15 @@ int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state, const floa
                            float eps, int batch, int d_model, int num_heads, float *out,
                            af_stream_t stream);
 
-/* af_msr_decode_step_f32 with the projection weights split beforehand by
- * af_split_tf32 (w_qkv_hi + w_qkv_lo == w_qkv, w_o_hi + w_o_lo == w_o): the
- * tensor cores read ready-made tf32 operands, which is faster (the weights
- * stay fp32-exact; twice the weight bytes are read).  head_dim 64/128/256.
- * Workspace: batch*(7*d_model + num_heads) floats. */
+/* af_msr_decode_step_f32 with the projection weights prepared beforehand
+ * (once, at weight-load time): w_qkv packed head-major by af_pack_qkv_heads
+ * and then split by af_split_tf32 into w_qkv_hi + w_qkv_lo; w_o split by
+ * af_split_tf32 as it is.  The tensor cores read ready-made tf32 operands
+ * (fp32-exact weights; twice the weight bytes are read), and the step runs
+ * as a pipeline over head groups: one group's QKV projection overlaps the
+ * previous group's state stream and the one before's W_o product.
+ * head_dim 64/128/256, all pointers 16-byte aligned.
+ * Workspace: batch*(8*d_model + num_heads) floats. */
 int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *state, const float *gamma,
                                  const float *w_qkv_hi, const float *w_qkv_lo, const float *w_o_hi,
                                  const float *w_o_lo, const float *ret_norm_w, float eps, int batch,

@@ -164,6 +164,7 @@ def test_msr_decode_step_matches_oracle(dev, B, d, H, steps):
         torch.cuda.synchronize()
         assert rel_err(out.cpu().numpy(), ref) < TOL, s
         assert rel_err(st_d.cpu().numpy(), st) < TOL, s
+    _lib.set_option(0, "decode_head_groups", 4)
 
 
 def test_msr_decode_step_full_config(dev):
@@ -235,10 +236,13 @@ def test_layers_cuda_match_reference_fixture(dev):
                    g["linear_out"]) < TOL
 
 
-@pytest.mark.parametrize("B,d,H", [(256, 2048, 8), (5, 512, 2), (130, 1024, 8)])
-def test_msr_decode_step_split_weights_matches_oracle(dev, B, d, H):
-    """Pre-split (tf32 hi + lo) weights give the fp32 decode step."""
-    from aceflow_b200 import cuda_ops
+@pytest.mark.parametrize("B,d,H,groups", [(256, 2048, 8, "4"), (256, 2048, 8, "1"), (5, 512, 2, "2"), (130, 1024, 8, "8")])
+def test_msr_decode_step_split_weights_matches_oracle(dev, B, d, H, groups):
+    """Head-major, tf32-split weights give the fp32 decode step, sequential
+    (1 head group) or pipelined over head groups on three streams."""
+    from aceflow_b200 import _lib, cuda_ops
+
+    _lib.set_option(0, "decode_head_groups", int(groups))
 
     rng = np.random.default_rng(B + d)
     dh = d // H
@@ -249,7 +253,10 @@ def test_msr_decode_step_split_weights_matches_oracle(dev, B, d, H):
     hi, lo = cuda_ops.split_tf32(T(w_qkv, dev))
     assert torch.equal(hi + lo, T(w_qkv, dev))
     assert torch.equal(hi, (hi.view(torch.int32) & ~0x1FFF).view(torch.float32))
-    wq_s, wo_s = (hi, lo), cuda_ops.split_tf32(T(w_o, dev))
+    packed = cuda_ops.pack_qkv_heads(T(w_qkv, dev), H)
+    ref_pack = w_qkv.reshape(3, H, dh, d).transpose(1, 0, 2, 3).reshape(3 * d, d)
+    assert np.array_equal(packed.cpu().numpy(), ref_pack)
+    wq_s, wo_s = cuda_ops.prepare_decode_weights(T(w_qkv, dev), T(w_o, dev), H)
     st = np.zeros((B, H, dh, dh), np.float32)
     st_d = torch.zeros(B, H, dh, dh, device=dev)
     for s in range(2):
@@ -259,3 +266,4 @@ def test_msr_decode_step_split_weights_matches_oracle(dev, B, d, H):
         torch.cuda.synchronize()
         assert rel_err(out.cpu().numpy(), ref) < TOL, s
         assert rel_err(st_d.cpu().numpy(), st) < TOL, s
+    _lib.set_option(0, "decode_head_groups", 4)
