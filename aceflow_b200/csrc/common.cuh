@@ -24,7 +24,10 @@ struct af_ctx {
   cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
   cudaEvent_t ev_a[kMaxSlices] = {}, ev_b[kMaxSlices] = {};
   int allow_split_k = 1;        // small-M GEMMs may split K (fp32 atomics: not bitwise reproducible)
-  int decode_head_groups = 4;   // head groups pipelined in the split decode step (1 = sequential)
+  // head groups pipelined in the split decode step; 1 = sequential, the
+  // fastest measured on B200 (the state stream fills every SM, so the
+  // pipelined GEMMs cannot co-reside and only add launches)
+  int decode_head_groups = 1;
   int decode_slice_rows = 0;  // batch rows per overlapped slice; 0 = one sequential pass (faster today)
 };
 

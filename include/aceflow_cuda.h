@@ -60,7 +60,7 @@ int af_reserve_workspace(af_ctx *ctx, size_t bytes);
  * word; `reset` clears it. */
 int af_check_device(af_ctx *ctx, int *flags, int reset);
 /* Tuning switches of a context (no reference counterpart):
- *   "decode_head_groups" 1..8  head groups pipelined by the split decode step (default 4)
+ *   "decode_head_groups" 1..8  head groups pipelined by the split decode step (default 1)
  *   "allow_split_k"      0/1   small-M GEMMs may split K with fp32 atomics (default 1;
  *                              0 makes results bitwise reproducible run to run)
  *   "decode_slice_rows"  >= 0  batch slices of af_msr_decode_step_f32 (default 0: none) */
@@ -170,9 +170,10 @@ int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state, const floa
  * (once, at weight-load time): w_qkv packed head-major by af_pack_qkv_heads
  * and then split by af_split_tf32 into w_qkv_hi + w_qkv_lo; w_o split by
  * af_split_tf32 as it is.  The tensor cores read ready-made tf32 operands
- * (fp32-exact weights; twice the weight bytes are read), and the step runs
- * as a pipeline over head groups: one group's QKV projection overlaps the
- * previous group's state stream and the one before's W_o product.
+ * (fp32-exact weights; twice the weight bytes are read).  Optionally
+ * (af_set_option "decode_head_groups") the step runs as a pipeline over head
+ * groups: one group's QKV projection overlapping the previous group's state
+ * stream and the one before's W_o product.
  * head_dim 64/128/256, all pointers 16-byte aligned.
  * Workspace: batch*(8*d_model + num_heads) floats. */
 int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *state, const float *gamma,

@@ -164,7 +164,6 @@ def test_msr_decode_step_matches_oracle(dev, B, d, H, steps):
         torch.cuda.synchronize()
         assert rel_err(out.cpu().numpy(), ref) < TOL, s
         assert rel_err(st_d.cpu().numpy(), st) < TOL, s
-    _lib.set_option(0, "decode_head_groups", 4)
 
 
 def test_msr_decode_step_full_config(dev):
@@ -266,4 +265,4 @@ def test_msr_decode_step_split_weights_matches_oracle(dev, B, d, H, groups):
         torch.cuda.synchronize()
         assert rel_err(out.cpu().numpy(), ref) < TOL, s
         assert rel_err(st_d.cpu().numpy(), st) < TOL, s
-    _lib.set_option(0, "decode_head_groups", 4)
+    _lib.set_option(0, "decode_head_groups", 1)
