@@ -44,6 +44,13 @@ SIGNATURES = {
     "af_add_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _f, _vp],
     "af_linear_f32": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "af_linear_bf16": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "af_chunkwise_plan": [_i, _i, _i, _i, _i, _vp, _vp],
+    "af_comm_unique_id": [_vp],
+    "af_comm_init": [_vp, _i, _i, _vp],
+    "af_comm_destroy": [_vp],
+    "af_prefill_head_sharded": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp],
+    "af_gemm_bf16": [_vp, _vp, _i64, _i, _vp, _i64, _i, _i, _i, _vp, _i64, _i, _vp, _vp, _i64, _vp, _i, _i, _f, _f, _i,
+                     _vp],
     "af_msr_decode_step_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
     "af_split_tf32": [_vp, _vp, _vp, _vp, _i64, _vp],
     "af_pack_qkv_heads": [_vp, _vp, _vp, _i, _i, _i, _vp],

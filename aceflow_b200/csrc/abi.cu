@@ -103,6 +103,7 @@ int af_cuda_init(int device, af_ctx **out) {
 
 int af_cuda_destroy(af_ctx *ctx) {
   AF_ENTER(ctx, "af_cuda_destroy");
+  af::comm_release(ctx);
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   for (int i = 0; i < 2; ++i)
@@ -143,6 +144,9 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
     ctx->decode_head_groups = (int)value;
   } else if (!strcmp(name, "allow_split_k")) {
     ctx->allow_split_k = value != 0;
+  } else if (!strcmp(name, "chunkwise_segments")) {
+    if (value < 0 || value > 4096) return af::fail(AF_ERR_ARG, "af_set_option: chunkwise_segments 0..4096");
+    ctx->chunk_segments = (int)value;
   } else if (!strcmp(name, "decode_slice_rows")) {
     if (value < 0) return af::fail(AF_ERR_ARG, "af_set_option: decode_slice_rows >= 0");
     ctx->decode_slice_rows = (int)value;

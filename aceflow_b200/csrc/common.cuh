@@ -29,6 +29,10 @@ struct af_ctx {
   // pipelined GEMMs cannot co-reside and only add launches)
   int decode_head_groups = 1;
   int decode_slice_rows = 0;  // batch rows per overlapped slice; 0 = one sequential pass (faster today)
+  int chunk_segments = 0;     // sequence segments per stream in the chunkwise prefill; 0 = fill the SMs
+  // NCCL communicator of the head-sharded prefill (sharded_prefill.cu)
+  void *comm = nullptr;
+  int comm_nranks = 0, comm_rank = 0;
 };
 
 constexpr uint32_t kCtxMagic = 0xACEF1011u;
@@ -75,6 +79,8 @@ struct GemmEpilogueArgs {
   int64_t ldr = 0;
   int swiglu = 0;  // (16 gate, 16 up) column groups -> silu(g)*u, N/2 outputs
   int accumulate = 0;  // add (atomically) into out, which the caller initialised
+  int a_kblock = 0;    // A stored as K/a_kblock blocks [M][a_kblock] back to back (0: plain)
+  int parts_block = 0; // row_parts stored as blocks [M][parts_block] (0: plain [M][nparts])
 };
 
 bool tc_gemm_ok(const void *A, int64_t lda, const void *B, int64_t ldb, int K, bool fp32);
@@ -84,6 +90,22 @@ int tc_gemm_presplit(af_ctx *ctx, const float *A_hi, const float *A_lo, int64_t 
                      const float *B_lo, int64_t ldb, int M, int N, int K, const GemmEpilogueArgs &a, cudaStream_t st,
                      const char *fn);
 int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn);
+
+// Chunkwise prefill (retention_chunkwise.cu).  A plan cuts each stream into
+// nseg segments of seg_len tokens (seg_len a multiple of the chunk length).
+struct ChunkPlan {
+  int nseg, seg_len;
+};
+ChunkPlan chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req);
+size_t chunkwise_seg_state_bytes(int B, int H, const ChunkPlan &pl);
+int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
+                             const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
+                             const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn);
+int chunkwise_head_dim();
+int chunkwise_parts();
+
+// Releases the context's communicator, if any (sharded_prefill.cu).
+void comm_release(af_ctx *ctx);
 
 inline cudaStream_t stream_of(af_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 

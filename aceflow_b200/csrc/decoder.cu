@@ -192,11 +192,6 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
                           float *out_lo = nullptr, int h0 = 0, int hn = 0, int64_t qkv_hs = 0);
 int launch_rmsnorm_f32(af_ctx *ctx, const float *x, const float *res, const float *w, float *y, float *sum_out,
                        int rows, int d, float eps, cudaStream_t st, const char *fn);
-int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
-                             const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
-                             cudaStream_t st, const char *fn);
-int chunkwise_head_dim();
-int chunkwise_parts();
 
 static int gemm(af_ctx *ctx, const void *A, const void *B, int M, int N, int K, bool fp32, void *out, int out_bf16,
                 const float *residual, const float *parts, int nparts, float inv_d, float eps, int swiglu,
@@ -293,8 +288,10 @@ extern "C" int af_decoder_layer_prefill(af_ctx *ctx, const af_layer_weights *w, 
   const size_t h_b = af::align256((size_t)N * d * 2), qkv_b = af::align256((size_t)N * 3 * d * 2),
                o_b = af::align256((size_t)N * d * 2), ss_b = af::align256((size_t)N * parts * 4),
                hid_b = af::align256((size_t)N * f * 2);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments);
+  const size_t seg_b = af::chunkwise_seg_state_bytes(B, H, pl);
   void *ws = nullptr;
-  rc = af::workspace(ctx, h_b + qkv_b + o_b + ss_b + hid_b, &ws, fn);
+  rc = af::workspace(ctx, h_b + qkv_b + o_b + ss_b + hid_b + seg_b, &ws, fn);
   if (rc) return rc;
   uint8_t *p = static_cast<uint8_t *>(ws);
   uint16_t *h = reinterpret_cast<uint16_t *>(p);
@@ -302,12 +299,14 @@ extern "C" int af_decoder_layer_prefill(af_ctx *ctx, const af_layer_weights *w, 
   void *o = p + h_b + qkv_b;
   float *ss = reinterpret_cast<float *>(p + h_b + qkv_b + o_b);
   void *hid = p + h_b + qkv_b + o_b + ss_b;
+  float *seg = seg_b ? reinterpret_cast<float *>(p + h_b + qkv_b + o_b + ss_b + hid_b) : nullptr;
   cudaStream_t st = af::stream_of(stream);
   rc = af_rmsnorm_to_bf16(ctx, x, w->norm1, h, N, d, eps, stream);
   if (rc) return rc;
   rc = af::gemm(ctx, h, w->w_qkv, N, 3 * d, d, false, qkv, 1, nullptr, nullptr, 0, 0.f, 0.f, 0, st, fn);
   if (rc) return rc;
-  rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, o, w->ret_norm, ss, st, fn);
+  rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, o, w->ret_norm, ss, pl, seg, st,
+                                    fn);
   if (rc) return rc;
   rc = af::gemm(ctx, o, w->w_o, N, d, d, false, x, 0, x, ss, parts, 1.0f / (float)d, eps, 0, st, fn);
   if (rc) return rc;

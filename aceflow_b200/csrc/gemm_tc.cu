@@ -51,7 +51,25 @@ struct GemmEpilogue {
   int swiglu;              // columns in groups of 16 gate then 16 up -> N/2 outputs
   int vec_ok;              // out base 16-byte aligned and ldo a whole number of 16-byte units
   int atomic;              // split-K: add into out (bias/residual only from split 0)
+  // Operand layout: A may be K-blocked, i.e. K/a_kb blocks [M][a_kb] stored
+  // one after another (a_kb == K: plain).  Element (m, k) sits at row
+  // (k / a_kb) * M + m, column k % a_kb of a (K/a_kb * M) x a_kb matrix.
+  // row_parts likewise: blocks [M][parts_blk], element (m, p) at
+  // (p / parts_blk) * M * parts_blk + m * parts_blk + p % parts_blk.
+  int a_kb;
+  int parts_blk;
 };
+
+// 1 / rms of one row from its partial sums of squares.
+__device__ __forceinline__ float row_scale(const GemmEpilogue &ep, int row, int M) {
+  float sum = 0.f;
+  const int pb = ep.parts_blk;
+  for (int p0 = 0; p0 < ep.nparts; p0 += pb) {
+    const float *q = ep.row_parts + (size_t)(p0 / pb) * M * pb + (size_t)row * pb;
+    for (int p = 0; p < pb; ++p) sum += q[p];
+  }
+  return 1.0f / sqrtf(sum * ep.inv_d + ep.eps);
+}
 
 constexpr int kBF16 = 0, kTF32S = 1, kTF32P = 2;
 
@@ -262,11 +280,12 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t ph = (kb / S) & 1;
         if (!mbar_wait(&empty[i], ph ^ 1)) { fail(); break; }
         const int kx = (kb_base + kb) * C::BK;
+        const int ka = kx % ep.a_kb, ma = m0 + (kx / ep.a_kb) * M;  // K-blocked A
         mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-        tma_load_2d(stage_a(i), &tmA, &full[i], kx, m0);
+        tma_load_2d(stage_a(i), &tmA, &full[i], ka, ma);
         tma_load_2d(stage_b(i), &tmB, &full[i], kx, n0);
         if constexpr (C::PRE) {
-          tma_load_2d(lo_a(i, 0), &tmA2, &full[i], kx, m0);
+          tma_load_2d(lo_a(i, 0), &tmA2, &full[i], ka, ma);
           tma_load_2d(lo_b(i, 0), &tmB2, &full[i], kx, n0);
         }
         issued = kb + 1;
@@ -342,11 +361,7 @@ __global__ void __launch_bounds__(192, 1)
     const int row = m0 + q * 32 + lane;
     const bool row_ok = row < M;
     float scale = 1.f;
-    if (ep.row_parts && row_ok) {
-      float sum = 0.f;
-      for (int p = 0; p < ep.nparts; ++p) sum += ep.row_parts[(size_t)row * ep.nparts + p];
-      scale = 1.0f / sqrtf(sum * ep.inv_d + ep.eps);
-    }
+    if (ep.row_parts && row_ok) scale = row_scale(ep, row, M);
     const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
     const int nacc = nk < C::NACC ? nk : C::NACC;  // accumulators that received products
     // Sum of the accumulators for 16 columns starting at `col` (warp-collective).
@@ -445,7 +460,8 @@ __global__ void __launch_bounds__(192, 1)
           const int i = g % S;
           if (!mbar_wait(&empty[i], ((g / S) & 1) ^ 1)) { fail(); break; }
           mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-          tma_load_2d(stage_a(i), &tmA, &full[i], kb * C::BK, m0);
+          const int kx = kb * C::BK;
+          tma_load_2d(stage_a(i), &tmA, &full[i], kx % ep.a_kb, m0 + (kx / ep.a_kb) * M);
           tma_load_2d(stage_b(i), &tmB, &full[i], kb * C::BK, n0);
         }
         if (s_abort) break;
@@ -501,11 +517,7 @@ __global__ void __launch_bounds__(192, 1)
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < M;
       float scale = 1.f;
-      if (ep.row_parts && row_ok) {
-        float sum = 0.f;
-        for (int p = 0; p < ep.nparts; ++p) sum += ep.row_parts[(size_t)row * ep.nparts + p];
-        scale = 1.0f / sqrtf(sum * ep.inv_d + ep.eps);
-      }
+      if (ep.row_parts && row_ok) scale = row_scale(ep, row, M);
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
       auto load16 = [&](int col, float (&v)[16]) {
         __syncwarp();
@@ -561,7 +573,7 @@ int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, in
                       const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
   using C = TileCfg<BN, kBF16>;
   CUtensorMap ta, tb;
-  int rc = make_kmajor_map(&ta, A, false, M, K, lda, C::BM, fn);
+  int rc = make_kmajor_map(&ta, A, false, (K / ep.a_kb) * M, ep.a_kb, lda, C::BM, fn);
   if (rc) return rc;
   rc = make_kmajor_map(&tb, B, false, N, K, ldb, BN, fn);
   if (rc) return rc;
@@ -584,14 +596,14 @@ int launch_tc(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const voi
   using C = TileCfg<BN, MODE>;
   CUtensorMap ta, tb, ta2, tb2;
   const bool fp32 = MODE != kBF16;
-  int rc = make_kmajor_map(&ta, A, fp32, M, K, lda, C::BM, fn);
+  int rc = make_kmajor_map(&ta, A, fp32, (K / ep.a_kb) * M, ep.a_kb, lda, C::BM, fn);
   if (rc) return rc;
   rc = make_kmajor_map(&tb, B, fp32, N, K, ldb, BN, fn);
   if (rc) return rc;
   ta2 = ta;
   tb2 = tb;
   if (MODE == kTF32P) {
-    rc = make_kmajor_map(&ta2, A2, true, M, K, lda, C::BM, fn);
+    rc = make_kmajor_map(&ta2, A2, true, (K / ep.a_kb) * M, ep.a_kb, lda, C::BM, fn);
     if (rc) return rc;
     rc = make_kmajor_map(&tb2, B2, true, N, K, ldb, BN, fn);
     if (rc) return rc;
@@ -631,8 +643,14 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
   const bool vec = af::aligned16(a.out) && (a.ldo * (a.out_bf16 ? 2 : 4)) % 16 == 0;
   if (a.swiglu && (!vec || N % 32 != 0))
     return af::fail(AF_ERR_ARG, "%s: SwiGLU epilogue needs an aligned output and N %% 32 == 0", fn);
+  constexpr int bk_elems = MODE == kBF16 ? 64 : 32;
+  if (a.a_kblock && (a.a_kblock % bk_elems != 0 || K % a.a_kblock != 0 || lda < a.a_kblock))
+    return af::fail(AF_ERR_ARG, "%s: K block %d must divide K=%d and be a multiple of %d", fn, a.a_kblock, K, bk_elems);
+  if (a.parts_block && (a.parts_block < 1 || a.nparts % a.parts_block != 0))
+    return af::fail(AF_ERR_ARG, "%s: parts block %d must divide nparts=%d", fn, a.parts_block, a.nparts);
   GemmEpilogue ep{a.out, a.ldo,      a.out_bf16, a.bias,   a.row_parts, a.nparts,   a.inv_d,
-                  a.eps, a.residual, a.ldr,      a.swiglu, vec ? 1 : 0, 0};
+                  a.eps, a.residual, a.ldr,      a.swiglu, vec ? 1 : 0, 0,
+                  a.a_kblock ? a.a_kblock : K, a.parts_block ? a.parts_block : (a.nparts > 0 ? a.nparts : 1)};
   const int64_t mt = (M + 127) / 128;
   auto tiles = [&](int bn) { return mt * ((N + bn - 1) / bn); };
   const int64_t sms = ctx->num_sms;
@@ -762,4 +780,32 @@ extern "C" int af_linear_f32_split(af_ctx *ctx, const float *x_hi, const float *
   ep.ldo = N;
   ep.bias = bias;
   return af::tc_gemm_presplit(ctx, x_hi, x_lo, K, w_hi, w_lo, K, M, N, K, ep, af::stream_of(stream), fn);
+}
+
+extern "C" int af_gemm_bf16(af_ctx *ctx, const uint16_t *A, int64_t lda, int a_kblock, const uint16_t *B,
+                            int64_t ldb, int M, int N, int K, void *out, int64_t ldo, int out_bf16, const float *bias,
+                            const float *residual, int64_t ldr, const float *row_sumsq, int nparts, int parts_block,
+                            float inv_d, float eps, int accumulate, af_stream_t stream) {
+  const char *fn = "af_gemm_bf16";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(A && B && out, "af_gemm_bf16", "null pointer");
+  AF_REQUIRE(M >= 0 && N >= 0 && K > 0 && M <= 65535 * 128, "af_gemm_bf16", "bad sizes M=%d N=%d K=%d", M, N, K);
+  AF_REQUIRE(lda >= (a_kblock ? a_kblock : K) && ldb >= K && ldo >= N && af::tc_gemm_ok(A, lda, B, ldb, K, false),
+             "af_gemm_bf16", "operands must be K-major with 16-byte aligned rows (K %% 8 == 0)");
+  AF_REQUIRE(!accumulate || !out_bf16, "af_gemm_bf16", "accumulation needs an fp32 output");
+  af::GemmEpilogueArgs ep;
+  ep.out = out;
+  ep.ldo = ldo;
+  ep.out_bf16 = out_bf16;
+  ep.bias = bias;
+  ep.residual = residual;
+  ep.ldr = ldr;
+  ep.row_parts = row_sumsq;
+  ep.nparts = nparts;
+  ep.parts_block = parts_block;
+  ep.a_kblock = a_kblock;
+  ep.inv_d = inv_d;
+  ep.eps = eps;
+  ep.accumulate = accumulate;
+  return af::tc_gemm(ctx, A, lda, B, ldb, M, N, K, false, ep, af::stream_of(stream), fn);
 }

@@ -259,13 +259,15 @@ extern "C" int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *
 //   1. qkv = x . W_qkv^T        bf16 GEMM -> bf16 [B*T][3d]
 //   2. chunkwise retention      -> bf16 O * ret_norm_w, per-row partial sum O^2, final state
 //   3. out = diag(1/rms) (O*w) . W_o^T   bf16 GEMM with the row scale in its epilogue
-namespace af {
-int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
-                             const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
-                             cudaStream_t st, const char *fn);
-int chunkwise_head_dim();
-int chunkwise_parts();
-}  // namespace af
+
+extern "C" int af_chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req, int *nseg, int *seg_len) {
+  AF_REQUIRE(num_sms > 0 && B >= 0 && T >= 0 && H > 0 && nseg_req >= 0 && nseg && seg_len, "af_chunkwise_plan",
+             "bad arguments");
+  const af::ChunkPlan pl = af::chunkwise_plan(num_sms, B, T, H, nseg_req);
+  *nseg = pl.nseg;
+  *seg_len = pl.seg_len;
+  return AF_OK;
+}
 
 extern "C" int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int B, int T, int H, const float *gamma,
                                            const float *state_in, float *state_out, uint16_t *out,
@@ -276,8 +278,15 @@ extern "C" int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int
   AF_REQUIRE(B >= 0 && T >= 0 && H > 0, "af_retention_chunkwise_bf16", "bad sizes B=%d T=%d H=%d", B, T, H);
   AF_REQUIRE(af::aligned16(qkv), "af_retention_chunkwise_bf16", "qkv must be 16-byte aligned");
   if (B == 0 || T == 0) return AF_OK;
-  return af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, out, norm_w, sumsq,
-                                      af::stream_of(stream), fn);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments);
+  void *ws = nullptr;
+  const size_t seg_bytes = af::chunkwise_seg_state_bytes(B, H, pl);
+  if (seg_bytes) {
+    int rc = af::workspace(ctx, seg_bytes, &ws, fn);
+    if (rc) return rc;
+  }
+  return af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, out, norm_w, sumsq, pl,
+                                      static_cast<float *>(ws), af::stream_of(stream), fn);
 }
 
 extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv, const uint16_t *w_o,
@@ -297,14 +306,17 @@ extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_
   const int parts = H * af::chunkwise_parts();
   const size_t qkv_bytes = ((size_t)N * 3 * d * 2 + 255) & ~size_t(255);
   const size_t o_bytes = ((size_t)N * d * 2 + 255) & ~size_t(255);
-  const size_t ss_bytes = (size_t)N * parts * 4;
+  const size_t ss_bytes = ((size_t)N * parts * 4 + 255) & ~size_t(255);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments);
+  const size_t seg_bytes = af::chunkwise_seg_state_bytes(B, H, pl);
   void *ws = nullptr;
-  int rc = af::workspace(ctx, qkv_bytes + o_bytes + ss_bytes, &ws, fn);
+  int rc = af::workspace(ctx, qkv_bytes + o_bytes + ss_bytes + seg_bytes, &ws, fn);
   if (rc) return rc;
   uint8_t *base = static_cast<uint8_t *>(ws);
   void *qkv = base;
   void *o = base + qkv_bytes;
   float *ss = reinterpret_cast<float *>(base + qkv_bytes + o_bytes);
+  float *seg = seg_bytes ? reinterpret_cast<float *>(base + qkv_bytes + o_bytes + ss_bytes) : nullptr;
   cudaStream_t st = af::stream_of(stream);
   af::GemmEpilogueArgs e1;
   e1.out = qkv;
@@ -312,7 +324,8 @@ extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_
   e1.out_bf16 = 1;
   rc = af::tc_gemm(ctx, x, d, w_qkv, d, (int)N, 3 * d, d, false, e1, st, fn);
   if (rc) return rc;
-  rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, o, ret_norm_w, ss, st, fn);
+  rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, o, ret_norm_w, ss, pl, seg, st,
+                                    fn);
   if (rc) return rc;
   af::GemmEpilogueArgs e2;
   e2.out = out;

@@ -28,6 +28,17 @@
 // Outputs: O * ret_norm_w as bf16 [B*T][d] (the A operand of the W_o GEMM),
 // per-row partial sums of O^2 (the GEMM applies 1/rms per row), and the
 // final state in the decode layout [B][H][k][v] fp32.
+//
+// Sequence segments.  When B*H*(DH/VS) CTAs cannot fill the GPU (one long
+// stream, few heads per GPU), each stream is cut into nseg segments of
+// seg_len tokens (a multiple of C) and three launches replace one:
+//   1. state pass (STATE_ONLY): per segment, from a zero state,
+//        dS_s = sum_t gamma^(end_s-1-t) k_t^T v_t   (V pre-scaled, no TMEM decay)
+//   2. seg_scan_kernel: S_in[0] = state_in, S_in[s+1] = gamma^seg_len S_in[s] + dS_s
+//   3. full pass: every segment runs the chunk loop from S_in[s]; the last
+//      segment writes the final state.
+// The result equals the single-pass recurrence (the scan is the same
+// recurrence applied at segment granularity).
 #include "common.cuh"
 #include "sm100.cuh"
 
@@ -58,9 +69,10 @@ constexpr uint32_t TM_S = 0, TM_SC = 256, TM_O = 320, TM_COLS = 512;
 
 struct ChunkParams {
   int B, T, H;
+  int nseg, seg_len;      // segments per stream and their length (seg_len % C == 0)
   const float *gamma;
-  const float *state_in;  // [B][H][DH][DH] or null
-  float *state_out;       // [B][H][DH][DH] or null
+  const float *state_in;  // [B][nseg][H][DH][DH] state before each segment, or null (zeros)
+  float *state_out;       // [B][H][DH][DH] final state (STATE_ONLY: [B][nseg][H][DH][DH] segment states), or null
   __nv_bfloat16 *out;     // [B*T][H*DH]
   const float *norm_w;    // [H*DH] or null
   float *sumsq;           // [B*T][H*NSL] or null
@@ -121,6 +133,7 @@ __device__ __forceinline__ bool math_sync_or(bool pred) {
   return r != 0;
 }
 
+template <bool STATE_ONLY>
 __global__ void __launch_bounds__(192, 1)
     retention_chunkwise_kernel(const __grid_constant__ CUtensorMap tm, ChunkParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -136,10 +149,13 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slice = blockIdx.x % NSL;
-  const int bh = blockIdx.x / NSL;
-  const int b = bh / p.H, h = bh % p.H;
+  const int bsh = blockIdx.x / NSL;   // ((b * nseg) + s) * H + h
+  const int h = bsh % p.H, bs = bsh / p.H;
+  const int b = bs / p.nseg, s = bs % p.nseg;
   const int d = p.H * DH;
-  const int nch = (p.T + C - 1) / C;
+  const int tb = s * p.seg_len;                      // first token of this segment
+  const int te = min(p.T, tb + p.seg_len);           // one past its last token
+  const int nch = (te - tb + C - 1) / C;
   const float g = p.gamma[h];
   const float lg = log2f(g);
 
@@ -178,11 +194,11 @@ __global__ void __launch_bounds__(192, 1)
       int issued = 0;
       for (int c = 0; c < nch && !s_abort; ++c) {
         if (c > 0 && !mbar_wait(bar_upd, (c - 1) & 1)) { fail(); break; }
-        const int t0 = c * C;
-        mbar_arrive_expect_tx(bar_load, Q_BYTES + K_BYTES + V_BYTES);
+        const int t0 = tb + c * C;
+        mbar_arrive_expect_tx(bar_load, (STATE_ONLY ? 0 : Q_BYTES) + K_BYTES + V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          tma_load_3d(sm + Q_OFF + kk * BOX, &tm, bar_load, h * DH + kk * 64, t0, b);
+          if (!STATE_ONLY) tma_load_3d(sm + Q_OFF + kk * BOX, &tm, bar_load, h * DH + kk * 64, t0, b);
           tma_load_3d(sm + K_OFF + kk * BOX, &tm, bar_load, d + h * DH + kk * 64, t0, b);
         }
 #pragma unroll
@@ -198,6 +214,25 @@ __global__ void __launch_bounds__(192, 1)
     constexpr uint32_t id_inter = idesc_f32acc(kFmtBF16, 128, 64);
     constexpr uint32_t id_intra = idesc_f32acc(kFmtBF16, 128, 64) | (1u << 15);         // A MN-major
     constexpr uint32_t id_upd = idesc_f32acc(kFmtBF16, 128, 256) | (1u << 15) | (1u << 16);  // A, B MN-major
+    if constexpr (STATE_ONLY) {
+      // only the update: S^T += Vs^T . K once the math warps wrote Vs
+      for (int c = 0; c < nch; ++c) {
+        bool ok = mbar_wait(bar_math, c & 1);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
+        tc_fence_after();
+        if (lane == 0) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t da = sdesc_mn_sw128(sm + VT_OFF + k * 2048, BOX);
+            const uint64_t db = sdesc_mn_sw128(sm + K_OFF + k * 2048, BOX);
+            umma_bf16(tmem + TM_S, da, db, id_upd, 1);
+          }
+          umma_commit(bar_upd);
+        }
+        __syncwarp();
+      }
+    } else
     for (int c = 0; c < nch; ++c) {
       bool ok = mbar_wait(bar_load, c & 1);
       ok = __all_sync(0xffffffffu, ok);
@@ -257,7 +292,7 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     // initial state S^T[v][k] = S[k][v]
     {
-      const float *sin = p.state_in ? p.state_in + ((size_t)(b * p.H + h) * DH) * DH + slice * VS + v : nullptr;
+      const float *sin = (!STATE_ONLY && p.state_in) ? p.state_in + ((size_t)bsh * DH) * DH + slice * VS + v : nullptr;
 #pragma unroll 1
       for (int k0 = 0; k0 < DH; k0 += 16) {
         float x[16];
@@ -268,9 +303,39 @@ __global__ void __launch_bounds__(192, 1)
       }
       tmem_wait_st();
     }
+    if constexpr (STATE_ONLY) {
+      // Vs = diag(gamma^(te-1-t)) V for the chunk's tokens t: decay to the segment end
+      for (int c = 0; c < nch; ++c) {
+        const int t0 = tb + c * C;
+        const int L = min(C, te - t0);
+        const float tail = exp2f((float)(te - t0 - L) * lg);  // gamma^(tokens after this chunk)
+        bool ok = mbar_wait(bar_load, c & 1);
+        if (!ok) s_abort = 1;
+        if (ok) {
+#pragma unroll 2
+          for (int i = mt; i < V_BYTES / 16; i += 128) {
+            const int off = i * 16;
+            const int j = (off % BOX) / 128;
+            const float sc = j < L ? gpow[L - 1 - j] * tail : 0.f;
+            uint4 raw = *reinterpret_cast<const uint4 *>(sm + V_OFF + off);
+            __nv_bfloat162 *e = reinterpret_cast<__nv_bfloat162 *>(&raw);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              float2 f = __bfloat1622float2(e[u]);
+              e[u] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+            }
+            *reinterpret_cast<uint4 *>(sm + VT_OFF + off) = raw;
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar_math);
+        if (math_sync_or(s_abort != 0)) break;
+      }
+    } else
     for (int c = 0; c < nch; ++c) {
-      const int t0 = c * C;
-      const int L = min(C, p.T - t0);
+      const int t0 = tb + c * C;
+      const int L = min(C, te - t0);
       bool ok = true;
       if (c > 0) ok = mbar_wait(bar_upd, (c - 1) & 1);
       if (!ok) s_abort = 1;
@@ -386,14 +451,17 @@ __global__ void __launch_bounds__(192, 1)
         p.sumsq[((size_t)b * p.T + t0 + mt) * (p.H * NSL) + h * NSL + slice] = s2;
       }
     }
-    // final state: S[k][v] = S^T[v][k]
+    // final state: S[k][v] = S^T[v][k] (segment end states in the state pass,
+    // else the last segment's state)
     const bool aborted = math_sync_or(s_abort != 0);
-    if (!aborted && p.state_out) {
+    const bool write_state = p.state_out && (STATE_ONLY || s == p.nseg - 1);
+    if (!aborted && write_state) {
       bool ok = mbar_wait(bar_upd, (nch - 1) & 1);
       if (!ok) s_abort = 1;
       if (!math_sync_or(s_abort != 0)) {
         tc_fence_after();
-        float *so = p.state_out + ((size_t)(b * p.H + h) * DH) * DH + slice * VS + v;
+        const size_t sidx = STATE_ONLY ? (size_t)bsh : (size_t)(b * p.H + h);
+        float *so = p.state_out + (sidx * DH) * DH + slice * VS + v;
 #pragma unroll 1
         for (int k0 = 0; k0 < DH; k0 += 16) {
           float x[16];
@@ -416,16 +484,69 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// Turns segment end states dS_s ([B][nseg][H][DH*DH], zero-start) into the
+// state before each segment, in place:  S_in[0] = state_in (or 0),
+// S_in[s+1] = gamma^seg_len S_in[s] + dS_s.  One thread per 4 state entries.
+__global__ void seg_scan_kernel(float4 *__restrict__ states, const float4 *__restrict__ state_in,
+                                const float *__restrict__ gamma, int B, int nseg, int H, int seg_len) {
+  constexpr int PER = DH * DH / 4;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)B * H * PER) return;
+  const int e = (int)(idx % PER);
+  const int bh = (int)(idx / PER);
+  const int h = bh % H, b = bh / H;
+  const float gl = exp2f((float)seg_len * log2f(gamma[h]));
+  float4 run = state_in ? state_in[(size_t)bh * PER + e] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < nseg; ++s) {
+    float4 *q = states + (((size_t)b * nseg + s) * H + h) * PER + e;
+    const float4 t = *q;
+    *q = run;
+    run = make_float4(gl * run.x + t.x, gl * run.y + t.y, gl * run.z + t.z, gl * run.w + t.w);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode3 = nullptr;
+
+template <bool SO>
+int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const ChunkParams &p, cudaStream_t st, const char *fn) {
+  static bool attr = false;  // per instance
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(retention_chunkwise_kernel<SO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)SMEM);
+    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    attr = true;
+  }
+  retention_chunkwise_kernel<SO><<<p.B * p.nseg * p.H * NSL, 192, SMEM, st>>>(tm, p);
+  return af::launched(ctx, fn);
+}
 
 }  // namespace
 
 namespace af {
 
+ChunkPlan chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req) {
+  ChunkPlan pl{1, T > 0 ? ((T + C - 1) / C) * C : C};
+  if (B <= 0 || T <= 0 || H <= 0) return pl;
+  const int chunks = (T + C - 1) / C;
+  const int ctas = B * H * NSL;
+  int nseg = nseg_req > 0 ? nseg_req : num_sms / ctas;  // one CTA per SM
+  if (nseg < 1) nseg = 1;
+  if (nseg > chunks) nseg = chunks;
+  const int per = (chunks + nseg - 1) / nseg;
+  pl.seg_len = per * C;
+  pl.nseg = (chunks + per - 1) / per;
+  return pl;
+}
+
+size_t chunkwise_seg_state_bytes(int B, int H, const ChunkPlan &pl) {
+  return pl.nseg > 1 ? (size_t)B * pl.nseg * H * DH * DH * sizeof(float) : 0;
+}
+
 // Chunkwise retention over a bf16 QKV buffer [B*T][3d] (row stride 3d).
+// seg_states: chunkwise_seg_state_bytes() of scratch when pl.nseg > 1.
 int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
                              const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
-                             cudaStream_t st, const char *fn) {
+                             const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn) {
   if (!g_encode3) {
     void *fp = nullptr;
     cudaDriverEntryPointQueryResult qr;
@@ -433,6 +554,11 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
       return fail(AF_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", fn);
     g_encode3 = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fp);
   }
+  if (pl.nseg < 1 || pl.seg_len % C != 0 || (int64_t)pl.nseg * pl.seg_len < T ||
+      (int64_t)(pl.nseg - 1) * pl.seg_len >= T)
+    return fail(AF_ERR_ARG, "%s: bad segment plan (%d x %d tokens for T=%d)", fn, pl.nseg, pl.seg_len, T);
+  if (pl.nseg > 1 && !seg_states) return fail(AF_ERR_ARG, "%s: segment states scratch missing", fn);
+  if ((int64_t)B * pl.nseg * H * NSL > 0x7fffffff) return fail(AF_ERR_ARG, "%s: grid too large", fn);
   const int d = H * DH;
   CUtensorMap tm;
   cuuint64_t dims[3] = {(cuuint64_t)(3 * d), (cuuint64_t)T, (cuuint64_t)B};
@@ -443,17 +569,28 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: tensor map encode failed (%d)", fn, (int)r);
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(retention_chunkwise_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)SMEM);
-    if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-    attr = true;
-  }
-  ChunkParams p{B, T, H, gamma, state_in, state_out, reinterpret_cast<__nv_bfloat16 *>(out), norm_w, sumsq,
-                ctx->dev_err};
-  retention_chunkwise_kernel<<<B * H * NSL, 192, SMEM, st>>>(tm, p);
-  return launched(ctx, fn);
+  ChunkParams p{B,       T,         H,       pl.nseg, pl.seg_len, gamma, state_in, state_out,
+                reinterpret_cast<__nv_bfloat16 *>(out), norm_w, sumsq, ctx->dev_err};
+  if (pl.nseg == 1) return launch_chunkwise<false>(ctx, tm, p, st, fn);
+  // 1. segment end states from zero
+  ChunkParams ps = p;
+  ps.state_in = nullptr;
+  ps.state_out = seg_states;
+  ps.out = nullptr;
+  ps.norm_w = nullptr;
+  ps.sumsq = nullptr;
+  int rc = launch_chunkwise<true>(ctx, tm, ps, st, fn);
+  if (rc) return rc;
+  // 2. states before each segment
+  const int64_t n4 = (int64_t)B * H * (DH * DH / 4);
+  seg_scan_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(reinterpret_cast<float4 *>(seg_states),
+                                                                reinterpret_cast<const float4 *>(state_in), gamma, B,
+                                                                pl.nseg, H, pl.seg_len);
+  rc = launched(ctx, fn);
+  if (rc) return rc;
+  // 3. the full pass from each segment's state
+  p.state_in = seg_states;
+  return launch_chunkwise<false>(ctx, tm, p, st, fn);
 }
 
 int chunkwise_head_dim() { return DH; }

@@ -331,3 +331,38 @@ def linear_f32_split(x_split, w_split, bias: torch.Tensor | None = None) -> torc
     _lib.call("af_linear_f32_split", _ctx(x_hi), _p(x_hi), _p(x_lo), _p(w_hi), _p(w_lo), _p(bias), _p(y), M, N, K,
               _stream(x_hi))
     return y
+
+
+def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_sumsq: torch.Tensor | None = None,
+              inv_d: float = 0.0, eps: float = 0.0, accumulate: bool = False, a_kblock: int = 0,
+              parts_block: int = 0) -> torch.Tensor:
+    """out (+)= rowscale * A[M, K] . b[N, K]^T (af_gemm_bf16).
+
+    a: bf16 2-D view with unit column stride.  Plain (a_kblock == 0): a is
+    [M, K].  K-blocked: a is [K/a_kblock * M, a_kblock], the K/a_kblock
+    blocks [M, a_kblock] stacked (an all-gather of column slices).
+    b: bf16 [N, K] view; out: fp32 [M, N] view.  rowscale from row_sumsq
+    ([M, P] or, with parts_block, P/parts_block stacked blocks [M, parts_block])
+    as 1/sqrt(sum/d + eps) when given."""
+    for n, t in (("a", a), ("b", b)):
+        if t.dtype != BF16 or t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError(f"{n}: expected a 2-D bf16 view with unit column stride")
+    if out.dtype != F32 or out.dim() != 2 or out.stride(1) != 1:
+        raise ValueError("out: expected a 2-D fp32 view with unit column stride")
+    N, K = b.shape
+    M = out.shape[0]
+    if a_kblock:
+        if K % a_kblock or a.shape[1] != a_kblock or a.shape[0] != (K // a_kblock) * M:
+            raise ValueError("K-blocked a must be [K/a_kblock * M, a_kblock]")
+    elif tuple(a.shape) != (M, K):
+        raise ValueError("shape mismatch")
+    if out.shape[1] != N:
+        raise ValueError("out must be [M, N]")
+    P = 0
+    if row_sumsq is not None:
+        _need(row_sumsq, F32, "row_sumsq")
+        P = row_sumsq.numel() // M
+    _lib.call("af_gemm_bf16", _ctx(a), _p(a), a.stride(0), int(a_kblock), _p(b), b.stride(0), M, N, K, _p(out),
+              out.stride(0), 0, None, None, 0, _p(row_sumsq), P, int(parts_block), float(inv_d), float(eps),
+              int(accumulate), _stream(a))
+    return out

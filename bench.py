@@ -316,6 +316,8 @@ def run_ours(args):
     }
     if world == 1 and not args.no_prefill:
         line["prefill"] = bench_prefill(dev, args.prefill_passes, peaks)
+    if not args.no_longctx and HEADS_LONGCTX % world == 0:
+        line["longctx"] = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier, max_over_ranks)
     if world == 1 and not args.no_stack:
         line["stack"] = bench_stack(dev, peaks)
     if world == 1 and rank == 0 and not args.no_cpu:
@@ -453,6 +455,67 @@ def bench_prefill(dev, passes, peaks):
     }
 
 
+# ---------------------------------------------------------------- long context
+LONGCTX = dict(B=1, T=65536, d=4096, H=16, C=64)
+HEADS_LONGCTX = LONGCTX["H"]
+
+
+def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks):
+    """Head-sharded prefill of one 65536-token stream (d_model 4096, 16 heads)
+    over all ranks: QKV of the rank's heads, chunkwise retention (sequence
+    segments), NCCL all-gather of head outputs, output projection of the
+    rank's columns.  Total work is fixed, so N GPUs scale it strongly."""
+    import torch
+
+    from aceflow_b200 import _lib
+    from aceflow_b200.sharded import HeadShardedPrefill, chunkwise_plan
+
+    c = LONGCTX
+    B, T, d, H = c["B"], c["T"], c["d"], c["H"]
+    g = torch.Generator(device=dev).manual_seed(11)  # same weights and input on every rank
+    x = torch.randn(B, T, d, generator=g, device=dev).bfloat16()
+    w_qkv = (0.02 * torch.randn(3 * d, d, generator=g, device=dev)).bfloat16()
+    w_o = (0.02 * torch.randn(d, d, generator=g, device=dev)).bfloat16()
+    rw = torch.ones(d, device=dev)
+    sp = HeadShardedPrefill(w_qkv, w_o, rw, H, EPS)
+    del w_qkv
+    out = torch.empty(B, T, d // world, device=dev)
+    for _ in range(2):
+        sp(x, out=out)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(passes):
+        sp(x, out=out)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / passes)
+    _lib.check_device(dev.index or 0)
+    barrier()
+    sp.close()
+    proj, intra, inter = prefill_flops(B, T, d, H, c["C"])
+    total = proj + intra + inter
+    per_gpu_tfl = total / world / (ms / 1e3) / 1e12
+    nseg, seg_len = chunkwise_plan(torch.cuda.get_device_properties(dev).multi_processor_count, B, T, H // world)
+    gather_bytes = (world - 1) * B * T * (d // world) * 2  # bf16 head outputs received per rank
+    return {
+        "metric": "long-context head-sharded prefill tok/s (B=1,T=65536,d=4096,H=16)",
+        "value": B * T / (ms / 1e3), "unit": "tok/s", "ms_per_pass": ms, "passes": passes, "n_gpus": world,
+        "scaling": "strong", "dtype": "bf16 (fp32 accumulate)",
+        "config": {"workload": "MultiScaleRetention prefill, d_model=4096, 16 heads (head_dim 256), B=1, T=65536, "
+                               "chunk 64", "parallelism": f"head-sharded x{world}, {H // world} heads per GPU, "
+                                                          "one NCCL all-gather before W_o",
+                   "segments": {"nseg": nseg, "seg_len": seg_len},
+                   "l2": "inputs larger than L2 (x 512 MiB, qkv per GPU >= 192 MiB)"},
+        "roofline": {"bound": "tensor", "achieved": per_gpu_tfl, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "per": "GPU", "frac": per_gpu_tfl / peaks["bf16_tflops"], "algorithmic_flop": total,
+                     "allgather_bytes_per_rank": gather_bytes},
+    }
+
+
 # ---------------------------------------------------------------- stack
 STACK = dict(L=24, d=2048, H=8, f=5632, V=32000, B=64, P=512, n=256)
 
@@ -509,6 +572,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill workload (N=1 only)")
     ap.add_argument("--no-stack", action="store_true", help="skip the 24-layer stack workload (N=1 only)")
     ap.add_argument("--prefill-passes", type=int, default=10)
+    ap.add_argument("--no-longctx", action="store_true", help="skip the long-context head-sharded prefill")
+    ap.add_argument("--longctx-passes", type=int, default=5)
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -63,7 +63,9 @@ int af_check_device(af_ctx *ctx, int *flags, int reset);
  *   "decode_head_groups" 1..8  head groups pipelined by the split decode step (default 1)
  *   "allow_split_k"      0/1   small-M GEMMs may split K with fp32 atomics (default 1;
  *                              0 makes results bitwise reproducible run to run)
- *   "decode_slice_rows"  >= 0  batch slices of af_msr_decode_step_f32 (default 0: none) */
+ *   "decode_slice_rows"  >= 0  batch slices of af_msr_decode_step_f32 (default 0: none)
+ *   "chunkwise_segments" >= 0  sequence segments per stream in the chunkwise prefill
+ *                              (default 0: enough to put one CTA on every SM; 1: none) */
 int af_set_option(af_ctx *ctx, const char *name, int64_t value);
 /* Number of this library's kernel launches issued through `ctx` so far. */
 int af_launch_count(af_ctx *ctx, int64_t *count);
@@ -144,6 +146,25 @@ int af_pack_qkv_heads(af_ctx *ctx, const void *src, void *dst, int d_model, int 
  * af_msr_decode_step_f32_split (done once, at weight-load time). */
 int af_split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, af_stream_t stream);
 
+/* General bf16 tensor-core GEMM with strided operands and the fused
+ * epilogue: C = rowscale * (A[M][K] . B[N][K]^T) (+ bias) (+ residual), with
+ * A row stride lda, B row stride ldb (elements), output row stride ldo
+ * (replaces the gemm of aceflow-core/src/tensor/ops.rs:71-90 for bf16).
+ * a_kblock > 0: A is K-blocked, K/a_kblock blocks [M][a_kblock] stored one
+ * after another (what an all-gather of per-rank column slices produces);
+ * a_kblock must divide K and be a multiple of 64.  0: plain [M][K].
+ * rowscale[m] = 1/sqrt(sum_p row_sumsq(m, p) * inv_d + eps) when row_sumsq
+ * is non-NULL (the RMSNorm of a retention output), else 1; row_sumsq is
+ * [M][nparts], or with parts_block > 0 nparts/parts_block blocks
+ * [M][parts_block] one after another.  accumulate != 0 adds into out (fp32)
+ * instead of overwriting it.  The head-sharded prefill's output projection
+ * is this GEMM over the gathered head outputs. */
+int af_gemm_bf16(af_ctx *ctx, const uint16_t *A, int64_t lda, int a_kblock, const uint16_t *B,
+                 int64_t ldb, int M, int N, int K, void *out, int64_t ldo, int out_bf16,
+                 const float *bias, const float *residual, int64_t ldr, const float *row_sumsq,
+                 int nparts, int parts_block, float inv_d, float eps, int accumulate,
+                 af_stream_t stream);
+
 /* af_linear_f32 from operands split by af_split_tf32 (x_hi + x_lo == x,
  * w_hi + w_lo == W): the tensor cores read ready-made tf32 operands.
  * K % 4 == 0, all pointers 16-byte aligned. */
@@ -205,10 +226,23 @@ int af_msr_decode_step_f32_noalloc(const float *x, float *state, const float *ga
  *   state_out same layout, the state after the last token, or NULL.
  *   out       [batch*T][H*256] bf16: retention output times norm_w (or 1).
  *   sumsq     [batch*T][2*H] fp32 partial sums of the unscaled output's
- *             squares (row r's RMS is sqrt(sum(sumsq[r]) / d)), or NULL. */
+ *             squares (row r's RMS is sqrt(sum(sumsq[r]) / d)), or NULL.
+ * When batch*H*2 CTAs cannot fill the GPU, each stream is cut into sequence
+ * segments (af_chunkwise_plan): a state pass, a scan over segment states
+ * and the full pass from each segment's state; workspace
+ * batch*nseg*H*256 KiB when nseg > 1. */
 int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int batch, int T, int num_heads,
                                 const float *gamma, const float *state_in, float *state_out,
                                 uint16_t *out, const float *norm_w, float *sumsq, af_stream_t stream);
+
+/* The sequence segmentation the chunkwise prefill uses for `batch` streams
+ * of T tokens and `num_heads` heads on a GPU with num_sms SMs (host-only,
+ * needs no GPU).  nseg_req > 0 forces that many segments (capped by the
+ * chunk count); 0 picks enough for one CTA per SM.  Outputs the segment
+ * count and length (a multiple of 64 tokens; the last segment may be
+ * shorter). */
+int af_chunkwise_plan(int num_sms, int batch, int T, int num_heads, int nseg_req, int *nseg,
+                      int *seg_len);
 
 /* MultiScaleRetention forward over a prompt on the bf16 tensor cores:
  * x [batch*T][d] bf16 -> out [batch*T][d] (fp32, or bf16 if out_bf16).
@@ -282,6 +316,38 @@ int af_argmax_rows(af_ctx *ctx, const float *logits, int rows, int vocab, int32_
 int af_lm_head_argmax(af_ctx *ctx, const float *x, const float *final_norm, float eps,
                       const void *table, int table_bf16, int batch, int vocab, int d,
                       float *logits, int32_t *tokens, af_stream_t stream);
+
+/* ------------------------------------------------------- multi-GPU prefill
+ * One process per GPU.  Rank 0 creates an id with af_comm_unique_id, the
+ * ranks share it out of band (torch.distributed, MPI, a file), then every
+ * rank calls af_comm_init with its context (collective: blocks until all
+ * ranks joined).  NCCL is loaded at run time (libnccl.so.2).  No reference
+ * counterpart: the reference runs on one CPU or one wgpu device. */
+#define AF_COMM_ID_BYTES 128
+int af_comm_unique_id(void *id_out /* AF_COMM_ID_BYTES */);
+int af_comm_init(af_ctx *ctx, int nranks, int rank, const void *unique_id);
+int af_comm_destroy(af_ctx *ctx);
+
+/* Head-sharded MultiScaleRetention prefill (the layer of af_msr_prefill_bf16
+ * split over the ranks of the context's communicator; aceflow/nn/
+ * retention.py:44-66 for the math).  Rank r owns heads [r*H/g, (r+1)*H/g)
+ * and output columns [r*dl, (r+1)*dl), dl = d/g:
+ *   x           [batch*T][d] bf16, the same on every rank
+ *   w_qkv_local [3*dl][d] bf16: rows of W_q, then W_k, then W_v for its heads
+ *   w_o_rows    [dl][d] bf16: rows r*dl..(r+1)*dl-1 of W_o
+ *   ret_norm_w  [d] fp32 and gamma [H] fp32: the full vectors
+ *   state_in/state_out [batch][H/g][256][256] fp32 for its heads, or NULL
+ *   out         [batch*T][dl] fp32 (or bf16 if out_bf16): its columns of
+ *               the layer output.
+ * One ncclAllGather of the head outputs (bf16) and of the per-row partial
+ * sums of squares precedes the output projection.  Every rank must make the
+ * same call.  head_dim 256; H divisible by the rank count.  Workspace
+ * batch*T*(6*dl + 2*d + 8*H) bytes plus segment states. */
+int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv_local,
+                            const uint16_t *w_o_rows, const float *ret_norm_w, const float *gamma,
+                            float eps, int batch, int T, int d_model, int num_heads,
+                            const float *state_in, float *state_out, void *out, int out_bf16,
+                            af_stream_t stream);
 
 #ifdef __cplusplus
 }

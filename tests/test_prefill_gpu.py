@@ -114,3 +114,80 @@ def test_prefill_then_decode_continues_the_state(dev):
     f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
     ref = R.msr_forward64(f(xb), *(f(a) for a in w), H, None, 1e-6)[:, T]
     assert rel_err(out.cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("nseg", [1, 3, 0])
+def test_chunkwise_segments_match_single_pass(dev, nseg):
+    """Sequence segments (state pass + scan + full pass) give the recurrence's
+    result: forced 1 (single pass), 3 (ragged last segment) and auto."""
+    from aceflow_b200 import _lib, cuda_ops
+
+    B, T, H = 1, 777, 2
+    qkv = _qkv(B, T, H, 99, dev, scale=0.5)
+    gamma = cuda_ops.gammas(H, dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    s0 = 0.05 * torch.randn(B, H, 256, 256, generator=g, device=dev)
+    _lib.set_option(0, "chunkwise_segments", nseg)
+    try:
+        out, ss, st = cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, state_in=s0)
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_option(0, "chunkwise_segments", 0)
+    assert _lib.check_device(0) == 0
+    ref, S = _core_ref(qkv, B, T, H, s0.cpu().numpy().astype(np.float64))
+    assert rel_err(out.float().cpu().numpy(), ref) < TOL
+    assert rel_err(st.cpu().numpy(), S) < TOL
+    assert rel_err(ss.cpu().numpy().sum(1), (ref * ref).sum(1)) < TOL
+
+
+def test_gemm_bf16_kblocked_operand_and_blocked_parts(dev):
+    """af_gemm_bf16 reading A as stacked K blocks [K/kb][M][kb] and row sums
+    of squares as stacked blocks [P/pb][M][pb] equals the plain product."""
+    from aceflow_b200 import cuda_ops
+
+    M, N, K, kb, P, pb = 300, 192, 512, 128, 6, 3
+    g = torch.Generator(device=dev).manual_seed(3)
+    a = torch.randn(M, K, generator=g, device=dev).bfloat16()
+    b = (0.05 * torch.randn(N, K, generator=g, device=dev)).bfloat16()
+    parts = torch.rand(M, P, generator=g, device=dev) * 10
+    a_blk = torch.cat([a[:, i * kb:(i + 1) * kb] for i in range(K // kb)], 0).contiguous()
+    p_blk = torch.cat([parts[:, i * pb:(i + 1) * pb] for i in range(P // pb)], 0).contiguous()
+    out = torch.empty(M, N, device=dev)
+    cuda_ops.gemm_bf16(a_blk, b, out, p_blk, inv_d=1.0 / K, eps=1e-6, a_kblock=kb, parts_block=pb)
+    scale = 1.0 / torch.sqrt(parts.double().sum(1, keepdim=True) / K + 1e-6)
+    ref = (a.double() @ b.double().t()) * scale
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+    plain = torch.empty(M, N, device=dev)
+    cuda_ops.gemm_bf16(a, b, plain, parts, inv_d=1.0 / K, eps=1e-6)
+    assert rel_err(plain.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+
+
+def test_head_sharded_prefill_single_rank(dev):
+    """af_prefill_head_sharded on a 1-rank communicator equals the float64
+    layer (and af_msr_prefill_bf16)."""
+    from aceflow_b200 import _lib, cuda_ops
+    from aceflow_b200.sharded import HeadShardedPrefill
+
+    B, T, H = 1, 600, 2
+    d = H * 256
+    rng = np.random.default_rng(21)
+    tb = lambda a: torch.from_numpy(a).to(dev).bfloat16()  # noqa: E731
+    x = tb(rng.standard_normal((B, T, d)).astype(np.float32))
+    wqkv = tb((0.02 * rng.standard_normal((3 * d, d))).astype(np.float32))
+    wo = tb((0.02 * rng.standard_normal((d, d))).astype(np.float32))
+    rw = torch.from_numpy((1 + 0.1 * rng.standard_normal(d)).astype(np.float32)).to(dev)
+    sp = HeadShardedPrefill(wqkv, wo, rw, H, 1e-6)
+    try:
+        st = torch.empty(B, H, 256, 256, device=dev)
+        out = sp(x, state_out=st)
+        torch.cuda.synchronize()
+    finally:
+        sp.close()
+    assert _lib.check_device(0) == 0
+    f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
+    wq_, wk_, wv_ = np.split(f(wqkv), 3)
+    ref = R.msr_forward64(f(x), wq_, wk_, wv_, f(wo), H, f(rw), 1e-6)
+    assert rel_err(out.cpu().numpy(), ref) < TOL
+    one, st1 = cuda_ops.msr_prefill_bf16(x, wqkv, wo, rw, cuda_ops.gammas(H, dev), 1e-6)
+    assert rel_err(out.cpu().numpy(), one.cpu().numpy()) < 1e-3
+    assert rel_err(st.cpu().numpy(), st1.cpu().numpy()) < 1e-3
