@@ -81,6 +81,10 @@ struct GemmEpilogueArgs {
   int accumulate = 0;  // add (atomically) into out, which the caller initialised
   int a_kblock = 0;    // A stored as K/a_kblock blocks [M][a_kblock] back to back (0: plain)
   int parts_block = 0; // row_parts stored as blocks [M][parts_block] (0: plain [M][nparts])
+  int trans = 0;       // store C^T: element (m, n) at out[n * ldo + m] (plain fp32 only)
+  int64_t split_stride = 0;  // split-K z stores its partial at out + z * split_stride (no atomics)
+  int max_partials = 1;      // partial buffers available at out (split_stride != 0)
+  int force_bn = 0, force_splits = 0;  // tile width / split count chosen by the caller (0: dispatch decides)
 };
 
 bool tc_gemm_ok(const void *A, int64_t lda, const void *B, int64_t ldb, int K, bool fp32);
@@ -89,7 +93,10 @@ int tc_gemm(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb,
 int tc_gemm_presplit(af_ctx *ctx, const float *A_hi, const float *A_lo, int64_t lda, const float *B_hi,
                      const float *B_lo, int64_t ldb, int M, int N, int K, const GemmEpilogueArgs &a, cudaStream_t st,
                      const char *fn);
-int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn);
+// hi = tf32 part of src, lo = src - hi (exact); `zero` (n floats, may be
+// NULL) is cleared in the same pass.
+int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn,
+               float *zero = nullptr);
 
 // Chunkwise prefill (retention_chunkwise.cu).  A plan cuts each stream into
 // nseg segments of seg_len tokens (seg_len a multiple of the chunk length).
@@ -106,6 +113,16 @@ int chunkwise_parts();
 
 // Releases the context's communicator, if any (sharded_prefill.cu).
 void comm_release(af_ctx *ctx);
+
+// One decode token of retention for `batch` streams (retention_decode.cu).
+// hn > 0 selects heads [h0, h0 + hn) with q/k/v of consecutive heads qkv_hs
+// floats apart; nsplit > 1 sums q/k/v over partial buffers split_stride
+// floats apart (split-K projection output).
+int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
+                          const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
+                          int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn, int out_bf16,
+                          float *out_lo = nullptr, int h0 = 0, int hn = 0, int64_t qkv_hs = 0, int nsplit = 1,
+                          int64_t split_stride = 0);
 
 inline cudaStream_t stream_of(af_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -186,10 +186,6 @@ int af_pack_gate_up(af_ctx *ctx, const void *src, void *dst, int f, int d, int e
 //   h = RMSNorm2(x); x += W_down (silu(g) * u),  [g|u] = h W_gate_up^T
 //                                  (SwiGLU in the gate/up GEMM epilogue)
 namespace af {
-int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
-                          const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
-                          int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn, int out_bf16,
-                          float *out_lo = nullptr, int h0 = 0, int hn = 0, int64_t qkv_hs = 0);
 int launch_rmsnorm_f32(af_ctx *ctx, const float *x, const float *res, const float *w, float *y, float *sum_out,
                        int rows, int d, float eps, cudaStream_t st, const char *fn);
 

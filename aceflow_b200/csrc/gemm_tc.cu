@@ -58,6 +58,12 @@ struct GemmEpilogue {
   // (p / parts_blk) * M * parts_blk + m * parts_blk + p % parts_blk.
   int a_kb;
   int parts_blk;
+  // Transposed store: element (row, n) goes to out[n * ldo + row] (a product
+  // computed as W . X^T lands as X . W^T).  Plain fp32 only.
+  int trans;
+  // Split-K into separate partial buffers: split z stores (no atomics) at
+  // out + z * split_stride; the consumer sums them.  0: one output.
+  int64_t split_stride;
 };
 
 // 1 / rms of one row from its partial sums of squares.
@@ -88,12 +94,16 @@ struct TileCfg {
   // kTF32S: two split slots (lo parts) double-buffer the converter -> MMA
   // hand-off, so the TMA ring keeps its full depth for prefetch.
   static constexpr int LO_SLOTS = MODE == kTF32S ? 2 : 0;
-  static constexpr int STAGES_FIT = (200 * 1024 - LO_SLOTS * RAW_BYTES) / STAGE_BYTES;
+  // ring depth: as many stages as the 227 KB opt-in limit holds (1 KB
+  // alignment slack, the barrier block and 64 bytes of static shared memory
+  // included) - small GEMMs are bound by the bytes in flight per SM
+  static constexpr int SMEM_LIMIT = 227 * 1024 - 64;
+  static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - 256 - LO_SLOTS * RAW_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_FIT < 12 ? STAGES_FIT : 12;
   // TF32x3: the hi.hi products go round-robin over NACC accumulators and the
   // small hi.lo + lo.hi terms into one more, so each fp32 accumulator sees
   // fewer tensor-core accumulation steps (its rounding error grows with them).
-  static constexpr int NACC = TF32X3 ? (BN <= 64 ? 4 : 2) : 1;
+  static constexpr int NACC = TF32X3 ? (BN <= 64 ? 4 : BN < 256 ? 2 : 1) : 1;
   static constexpr int ACC_COLS = (NACC + (TF32X3 ? 1 : 0)) * BN;
   static constexpr int TMEM_COLS =
       ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128 : ACC_COLS <= 256 ? 256 : 512;
@@ -101,6 +111,8 @@ struct TileCfg {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
   static_assert(ACC_COLS <= 512, "TMEM columns");
   static_assert(STAGES >= 2, "pipeline depth");
+  static_assert(1024 + (size_t)STAGES * STAGE_BYTES + (size_t)LO_SLOTS * RAW_BYTES + 256 <= (size_t)SMEM_LIMIT,
+                "shared memory");
 };
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
@@ -142,6 +154,18 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
             *reinterpret_cast<float4 *>(o + e) = make_float4(hh[e], hh[e + 1], hh[e + 2], hh[e + 3]);
         }
       }
+    }
+  } else if (ep.trans) {
+    float *o = reinterpret_cast<float *>(ep.out) + (size_t)blockIdx.z * ep.split_stride + row;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      load16(c, v);
+      const int n = n0 + c;
+      if (!ok || !row_ok || n >= N) continue;
+#pragma unroll
+      for (int e = 0; e < 16; ++e)  // lanes hold consecutive rows: each store is one 128-byte line
+        if (n + e < N) o[(size_t)(n + e) * ep.ldo] = v[e] * scale;
     }
   } else {
 #pragma unroll 1
@@ -631,6 +655,20 @@ __global__ void split_tf32_kernel(const float *__restrict__ src, float *__restri
   }
 }
 
+// The same over float4s (16-byte aligned arrays, n % 4 == 0); optionally
+// zeroes `zero` (n floats) on the way - the output that a later split-K GEMM
+// of the same step accumulates into.
+__global__ void split_tf32_vec_kernel(const float4 *__restrict__ src, float4 *__restrict__ hi, float4 *__restrict__ lo,
+                                      float4 *__restrict__ zero, int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 x = src[i];
+    const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
+    hi[i] = h;
+    lo[i] = make_float4(x.x - h.x, x.y - h.y, x.z - h.z, x.w - h.w);
+    if (zero) zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
 // Tile width, split count and launch for one GEMM.  Narrow tiles and split-K
 // put a CTA on every SM for decode-sized M; split-K needs an fp32, non-SwiGLU
 // epilogue (it accumulates with atomics).
@@ -650,7 +688,11 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
     return af::fail(AF_ERR_ARG, "%s: parts block %d must divide nparts=%d", fn, a.parts_block, a.nparts);
   GemmEpilogue ep{a.out, a.ldo,      a.out_bf16, a.bias,   a.row_parts, a.nparts,   a.inv_d,
                   a.eps, a.residual, a.ldr,      a.swiglu, vec ? 1 : 0, 0,
-                  a.a_kblock ? a.a_kblock : K, a.parts_block ? a.parts_block : (a.nparts > 0 ? a.nparts : 1)};
+                  a.a_kblock ? a.a_kblock : K, a.parts_block ? a.parts_block : (a.nparts > 0 ? a.nparts : 1),
+                  a.trans, a.split_stride};
+  if ((a.trans || a.split_stride) &&
+      (a.swiglu || a.out_bf16 || a.bias || a.residual || a.row_parts || a.accumulate || a.a_kblock))
+    return af::fail(AF_ERR_ARG, "%s: transposed / partial-buffer output is plain fp32 only", fn);
   const int64_t mt = (M + 127) / 128;
   auto tiles = [&](int bn) { return mt * ((N + bn - 1) / bn); };
   const int64_t sms = ctx->num_sms;
@@ -677,16 +719,45 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
     if (splits > max_split) splits = max_split;
     if (splits < 1) splits = 1;
   }
+  // Pre-split decode GEMMs (one wave or less): pick width and split by a
+  // cost model, waves x tile width x K slices per CTA, which also weighs the
+  // 96-wide tile (a 256 x 6144 QKV projection: 128 CTAs of 96 columns beat
+  // 96 CTAs of 128 on 148 SMs).
+  if (MODE == kTF32P && tiles(widest) < sms) {
+    auto cost = [&](int w, int sp) {
+      const int64_t ctas = tiles(w) * sp;
+      return ((ctas + sms - 1) / sms) * (int64_t)w * ((nk + sp - 1) / sp);
+    };
+    int64_t best = cost(bn, splits);
+    const int widths[4] = {128, 96, 64, 32};
+    for (int w : widths) {
+      const int max_sp = can_split ? (nk / 4 > 1 ? (nk / 4 > 8 ? 8 : nk / 4) : 1) : 1;
+      for (int sp = 1; sp <= max_sp; ++sp) {
+        if (tiles(w) * sp > sms) break;
+        const int64_t c = cost(w, sp);
+        if (c < best) {
+          best = c;
+          bn = w;
+          splits = sp;
+        }
+      }
+    }
+  }
+  if (a.force_bn) bn = a.force_bn;
+  if (a.force_splits) splits = a.force_splits < nk ? a.force_splits : nk;
   // tuning overrides (tile-width / split-K sweeps): AF_GEMM_BN, AF_GEMM_SPLITS
   if (const char *e = getenv("AF_GEMM_BN")) {
     const int v = atoi(e);
-    if (v == 16 || v == 32 || v == 64 || v == 128 || v == 256) bn = v;
+    if (v == 16 || v == 32 || v == 64 || v == 128 || v == 256 || (v == 96 && MODE == kTF32P)) bn = v;
   }
   if (const char *e = getenv("AF_GEMM_SPLITS")) {
     const int v = atoi(e);
     if (v >= 1 && v <= 16 && (v == 1 || can_split) && v <= nk) splits = v;
   }
-  if (a.accumulate) {
+  if (a.split_stride) {
+    if (a.split_stride < (int64_t)(a.trans ? N : M) * a.ldo || splits > a.max_partials)
+      return af::fail(AF_ERR_ARG, "%s: partial buffers too small or too few", fn);
+  } else if (a.accumulate) {
     if (a.swiglu || a.out_bf16) return af::fail(AF_ERR_ARG, "%s: accumulation needs an fp32 linear epilogue", fn);
     ep.atomic = 1;  // partial products added into out as it is
   } else if (splits > 1) {
@@ -699,17 +770,21 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
     }
   }
   // large bf16 GEMMs (two or more waves of tiles): persistent kernel
-  if (MODE == kBF16 && splits == 1 && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms && !getenv("AF_GEMM_NO_PERSIST")) {
+  if (MODE == kBF16 && splits == 1 && !a.trans && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms &&
+      !getenv("AF_GEMM_NO_PERSIST")) {
     if (bn == 256) return launch_persistent<256>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
     return launch_persistent<128>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
   }
 #define AF_LAUNCH(BNV) return launch_tc<BNV, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn)
   switch (bn) {
     case 256:
-      if constexpr (MODE == kBF16) AF_LAUNCH(256);
+      if constexpr (MODE != kTF32S) AF_LAUNCH(256);
       break;
     case 128:
       AF_LAUNCH(128);
+    case 96:
+      if constexpr (MODE == kTF32P) AF_LAUNCH(96);
+      break;
     case 64:
       AF_LAUNCH(64);
     case 32:
@@ -750,8 +825,20 @@ int tc_gemm_presplit(af_ctx *ctx, const float *A_hi, const float *A_lo, int64_t 
   return dispatch<kTF32P>(ctx, A_hi, A_lo, lda, B_hi, B_lo, ldb, M, N, K, a, st, fn);
 }
 
-int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn) {
+int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn,
+               float *zero) {
   if (n == 0) return AF_OK;
+  if (n % 4 == 0 && aligned16(src) && aligned16(hi) && aligned16(lo) && (!zero || aligned16(zero))) {
+    const int64_t n4 = n / 4;
+    int64_t blocks = (n4 + 255) / 256;
+    if (blocks > (int64_t)ctx->num_sms * 8) blocks = (int64_t)ctx->num_sms * 8;
+    split_tf32_vec_kernel<<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const float4 *>(src),
+                                                            reinterpret_cast<float4 *>(hi),
+                                                            reinterpret_cast<float4 *>(lo),
+                                                            reinterpret_cast<float4 *>(zero), n4);
+    return launched(ctx, fn);
+  }
+  if (zero) AF_CUDA(cudaMemsetAsync(zero, 0, (size_t)n * sizeof(float), st), fn);
   int64_t blocks = (n + 255) / 256;
   if (blocks > (int64_t)ctx->num_sms * 16) blocks = (int64_t)ctx->num_sms * 16;
   split_tf32_kernel<<<(unsigned)blocks, 256, 0, st>>>(src, hi, lo, n);

@@ -10,10 +10,6 @@
 #include "common.cuh"
 
 namespace af {
-int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
-                          const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
-                          int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn,
-                          int out_bf16, float *out_lo = nullptr, int h0 = 0, int hn = 0, int64_t qkv_hs = 0);
 int linear_f32(af_ctx *ctx, const float *x, int64_t ldx, const float *w, int64_t ldw, const float *bias, float *y,
                int64_t ldy, int M, int N, int K, const float *parts, int nparts, float inv_d, float eps,
                cudaStream_t st, const char *fn);
@@ -92,7 +88,25 @@ int msr_decode_step_impl(af_ctx *ctx, const float *x, float *state, const float 
 // RMSNorm row scale is applied once at the end.  Head-major packing makes
 // every group's weights a contiguous block, so no weight is read twice.
 // Workspace floats: x hi/lo 2Bd, qkv 3Bd, o hi/lo 2Bd, partial sums Bd, sumsq BH.
-size_t msr_decode_split_scratch_floats(int B, int d, int H) { return (size_t)B * (8 * (size_t)d + H); }
+// QKV split-K partial buffers of the transposed projection (kQkvPartials - 1
+// beyond the one the sequential layout already holds)
+constexpr int kQkvPartials = 4;
+size_t msr_decode_split_scratch_floats(int B, int d, int H) {
+  return (size_t)B * ((5 + 3 * kQkvPartials) * (size_t)d + H) + 64;
+}
+
+// Split count of the transposed QKV projection (weights as the 128-row
+// operand, the batch as one 128- or 256-wide tile), or 0 when the batch
+// does not fit one tile or is small enough for the direct form.
+static int qkv_trans_splits(const af_ctx *ctx, int B, int d) {
+  if (B <= 64 || B > 256 || d % 32 != 0) return 0;
+  const int mtiles = (3 * d + 127) / 128;
+  int sp = ctx->num_sms / mtiles;
+  const int nk = d / 32;
+  if (sp > nk / 4) sp = nk / 4;
+  if (sp > kQkvPartials) sp = kQkvPartials;
+  return sp < 1 ? 1 : sp;
+}
 
 namespace {
 __global__ void rowscale_kernel(const float *__restrict__ P, const float *__restrict__ sumsq, float *__restrict__ out,
@@ -132,14 +146,16 @@ int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const 
                                float eps, int B, int d, int H, float *out, float *scratch, cudaStream_t st,
                                const char *fn) {
   const int dh = d / H;
-  float *x_hi = scratch, *x_lo = x_hi + (size_t)B * d, *qkv = x_lo + (size_t)B * d;
-  float *o_hi = qkv + (size_t)B * 3 * d, *o_lo = o_hi + (size_t)B * d, *P = o_lo + (size_t)B * d;
+  float *x_hi = scratch, *x_lo = x_hi + (size_t)B * d;
+  float *o_hi = x_lo + (size_t)B * d, *o_lo = o_hi + (size_t)B * d, *P = o_lo + (size_t)B * d;
   float *sumsq = P + (size_t)B * d;
+  float *qkv = sumsq + (((size_t)B * H + 63) & ~size_t(63));  // kQkvPartials x [B][3d]
   const int64_t sbs = (int64_t)H * dh * dh;
   int G = ctx->decode_head_groups;
   if (G < 2 || H % G != 0 || G > af_ctx::kMaxSlices) G = 1;
   const int Hg = H / G, Ng = 3 * Hg * dh;
-  int rc = split_tf32(ctx, x, x_hi, x_lo, (int64_t)B * d, st, fn);
+  // the sequential step's W_o GEMM accumulates into out, zeroed here
+  int rc = split_tf32(ctx, x, x_hi, x_lo, (int64_t)B * d, st, fn, G == 1 ? out : nullptr);
   if (rc) return rc;
   auto qkv_gemm = [&](int g, cudaStream_t s) {
     GemmEpilogueArgs e;
@@ -154,13 +170,33 @@ int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const 
                                  sumsq, s, fn, 0, o_lo, g * Hg, Hg, 3 * (int64_t)dh);
   };
   if (G == 1) {
-    rc = qkv_gemm(0, st);
-    if (rc) return rc;
-    rc = retention(0, st);
+    const int nsp = qkv_trans_splits(ctx, B, d);
+    if (nsp > 0) {
+      // qkv^T = W_qkv . x^T: each weight tile is read by one CTA, split-K
+      // partials go to separate buffers that the retention kernel sums
+      GemmEpilogueArgs e;
+      e.out = qkv;
+      e.ldo = 3 * d;
+      e.trans = 1;
+      e.split_stride = (int64_t)B * 3 * d;
+      e.max_partials = kQkvPartials;
+      e.force_bn = B > 128 ? 256 : 128;
+      e.force_splits = nsp;
+      rc = tc_gemm_presplit(ctx, wq_hi, wq_lo, d, x_hi, x_lo, d, 3 * d, B, d, e, st, fn);
+      if (rc) return rc;
+      rc = launch_retention_step(ctx, state, sbs, gamma, qkv, qkv + dh, qkv + 2 * dh, 3 * (int64_t)d, o_hi, d, B, H,
+                                 dh, ret_norm_w, sumsq, st, fn, 0, o_lo, 0, H, 3 * (int64_t)dh, nsp,
+                                 (int64_t)B * 3 * d);
+    } else {
+      rc = qkv_gemm(0, st);
+      if (rc) return rc;
+      rc = retention(0, st);
+    }
     if (rc) return rc;
     GemmEpilogueArgs e2;
     e2.out = out;
     e2.ldo = d;
+    e2.accumulate = 1;  // into the zeroed out: split-K needs no memset
     e2.row_parts = sumsq;
     e2.nparts = H;
     e2.inv_d = 1.0f / (float)d;

@@ -23,6 +23,8 @@ namespace {
 struct HeadGroup {
   int h0, n;                // first head and number of heads in this launch
   int64_t qkv_head_stride;  // floats between consecutive heads' q (and k, v)
+  int nsplit;               // q/k/v are the sum of nsplit partial buffers (split-K GEMM output)
+  int64_t split_stride;     // floats between the partial buffers
 };
 
 template <int DH, int THREADS>
@@ -146,10 +148,22 @@ __global__ void __launch_bounds__(THREADS)
   const float *kh = k + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
   const float *vh = v + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
   for (int i = threadIdx.x; i < DH; i += THREADS) {
-    sk[i] = kh[i];
-    sq[i] = qh[i];
+    float kk = kh[i], qq = qh[i];
+    for (int z = 1; z < hg.nsplit; ++z) {
+      kk += kh[(size_t)z * hg.split_stride + i];
+      qq += qh[(size_t)z * hg.split_stride + i];
+    }
+    sk[i] = kk;
+    sq[i] = qq;
   }
-  const float4 vv = make_float4(vh[4 * cg], vh[4 * cg + 1], vh[4 * cg + 2], vh[4 * cg + 3]);
+  float4 vv = make_float4(vh[4 * cg], vh[4 * cg + 1], vh[4 * cg + 2], vh[4 * cg + 3]);
+  for (int z = 1; z < hg.nsplit; ++z) {
+    const float *vz = vh + (size_t)z * hg.split_stride + 4 * cg;
+    vv.x += vz[0];
+    vv.y += vz[1];
+    vv.z += vz[2];
+    vv.w += vz[3];
+  }
   const float g = gamma[h];
   __syncthreads();
   float *S = state + (size_t)b * state_bs + (size_t)h * DH * DH;
@@ -329,20 +343,22 @@ namespace af {
 int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const float *gamma, const float *q,
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs,
                           int batch, int H, int dh, const float *norm_w, float *sumsq, cudaStream_t st,
-                          const char *fn, int out_bf16, float *out_lo, int h0, int hn, int64_t qkv_hs) {
+                          const char *fn, int out_bf16, float *out_lo, int h0, int hn, int64_t qkv_hs, int nsplit,
+                          int64_t split_stride) {
   if (batch == 0) return AF_OK;
+  if (nsplit < 1) nsplit = 1;
   if (hn <= 0) {  // all heads, q/k/v head-contiguous
     h0 = 0;
     hn = H;
     qkv_hs = dh;
   }
-  const HeadGroup hgp{h0, hn, qkv_hs};
+  const HeadGroup hgp{h0, hn, qkv_hs, nsplit, split_stride};
   const bool all_heads = h0 == 0 && hn == H && qkv_hs == dh;
   const dim3 grid((unsigned)(batch * hn));
   if (out_bf16 && !(dh == 256 || dh == 128 || dh == 64) )
     return fail(AF_ERR_ARG, "%s: bf16 output needs head_dim 64, 128 or 256", fn);
   if (dh % 4 != 0 || dh > 1024 || state_bs % 4 != 0 || !aligned16(state)) {
-    if (norm_w || sumsq || !all_heads) return fail(AF_ERR_ARG, "%s: fused norm needs head_dim %% 4 == 0 and <= 1024", fn);
+    if (norm_w || sumsq || !all_heads || nsplit > 1) return fail(AF_ERR_ARG, "%s: fused norm needs head_dim %% 4 == 0 and <= 1024", fn);
     retention_step_scalar<<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, 1, H, dh);
     return launched(ctx, fn);
   }
@@ -366,7 +382,8 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
     retention_step_kernel<16, 64><<<grid, 64, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
                                                        norm_w, sumsq, out_bf16, out_lo, hgp);
   } else {
-    if (!all_heads) return fail(AF_ERR_ARG, "%s: head groups need head_dim 16..256 (power of two)", fn);
+    if (!all_heads || nsplit > 1)
+      return fail(AF_ERR_ARG, "%s: head groups and partial sums need head_dim 16..256 (power of two)", fn);
     const int ncg = dh / 4;
     int rgs = 256 / ncg;
     if (rgs < 1) rgs = 1;

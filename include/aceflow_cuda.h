@@ -195,8 +195,11 @@ int af_msr_decode_step_f32(af_ctx *ctx, const float *x, float *state, const floa
  * (af_set_option "decode_head_groups") the step runs as a pipeline over head
  * groups: one group's QKV projection overlapping the previous group's state
  * stream and the one before's W_o product.
+ * For 64 < batch <= 256 the QKV projection runs transposed (W_qkv . x^T:
+ * every weight tile read by one CTA) with split-K partial buffers that the
+ * state-stream kernel sums while it loads q, k, v.
  * head_dim 64/128/256, all pointers 16-byte aligned.
- * Workspace: batch*(8*d_model + num_heads) floats. */
+ * Workspace: batch*(17*d_model + num_heads) + 64 floats. */
 int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *state, const float *gamma,
                                  const float *w_qkv_hi, const float *w_qkv_lo, const float *w_o_hi,
                                  const float *w_o_lo, const float *ret_norm_w, float eps, int batch,

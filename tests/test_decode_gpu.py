@@ -235,7 +235,8 @@ def test_layers_cuda_match_reference_fixture(dev):
                    g["linear_out"]) < TOL
 
 
-@pytest.mark.parametrize("B,d,H,groups", [(256, 2048, 8, "4"), (256, 2048, 8, "1"), (5, 512, 2, "2"), (130, 1024, 8, "8")])
+@pytest.mark.parametrize("B,d,H,groups", [(256, 2048, 8, "4"), (256, 2048, 8, "1"), (5, 512, 2, "2"), (130, 1024, 8, "8"),
+                                           (130, 1024, 8, "1"), (100, 512, 4, "1"), (65, 256, 1, "1")])
 def test_msr_decode_step_split_weights_matches_oracle(dev, B, d, H, groups):
     """Head-major, tf32-split weights give the fp32 decode step, sequential
     (1 head group) or pipelined over head groups on three streams."""

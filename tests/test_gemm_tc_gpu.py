@@ -64,3 +64,22 @@ def test_unaligned_k_uses_simt_path(dev):
     x = torch.randn(5, 13, device=dev)
     w = torch.randn(7, 13, device=dev)
     assert rel_err(cuda_ops.linear(x, w).cpu().numpy(), (x.double() @ w.double().T).cpu().numpy()) < 1e-6
+
+
+@pytest.mark.parametrize("bn", ["96", "128", "64", "32"])
+@pytest.mark.parametrize("M,N,K", [(256, 6144, 2048), (200, 1000, 512), (1, 96, 64)])
+def test_presplit_gemm_every_tile_width(dev, bn, M, N, K, monkeypatch):
+    """The pre-split 3xTF32 GEMM (decode projections) at each tile width,
+    the 96-wide tile included, is fp32-accurate."""
+    from aceflow_b200 import cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g, device=dev)
+    w = 0.02 * torch.randn(N, K, generator=g, device=dev)
+    ref = (x.double() @ w.double().T).cpu().numpy()
+    monkeypatch.setenv("AF_GEMM_BN", bn)
+    y = cuda_ops.linear_f32_split(cuda_ops.split_tf32(x), cuda_ops.split_tf32(w))
+    torch.cuda.synchronize()
+    monkeypatch.delenv("AF_GEMM_BN")
+    assert rel_err(y.cpu().numpy(), ref) < 1e-5
+    _check(dev)
