@@ -220,6 +220,34 @@ def run_ours(args):
 
     from aceflow_b200 import _lib, cuda_ops
 
+    if args.only in ("prefill", "longctx", "stack"):
+        # one secondary workload alone (profiling runs); same objects as in the full line
+        peaks, _ = load_peaks()
+
+        def barrier1():
+            if world > 1:
+                dist.barrier()
+
+        def max1(v):
+            if world == 1:
+                return v
+            t = torch.tensor([v], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        if args.only == "prefill":
+            sec = bench_prefill(dev, args.prefill_passes, peaks)
+        elif args.only == "longctx":
+            sec = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier1, max1)
+        else:
+            sec = bench_stack(dev, peaks)
+        if rank == 0:
+            print(json.dumps({"section": args.only, **sec}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return 0
+
     d, H, B = D_MODEL, HEADS, STREAMS
     dh = d // H
     g = torch.Generator(device=dev)
@@ -573,6 +601,8 @@ def main():
     ap.add_argument("--no-stack", action="store_true", help="skip the 24-layer stack workload (N=1 only)")
     ap.add_argument("--prefill-passes", type=int, default=10)
     ap.add_argument("--no-longctx", action="store_true", help="skip the long-context head-sharded prefill")
+    ap.add_argument("--only", choices=["prefill", "longctx", "stack"], default=None,
+                    help="run one secondary workload alone and print its object (profiling)")
     ap.add_argument("--longctx-passes", type=int, default=5)
     args = ap.parse_args()
     if args.warmup < 3:
