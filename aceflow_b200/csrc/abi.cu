@@ -96,6 +96,8 @@ int af_cuda_init(int device, af_ctx **out) {
   }
   if (const char *env = getenv("AF_DECODE_SLICE_ROWS")) ctx->decode_slice_rows = atoi(env);
   if (const char *env = getenv("AF_DECODE_HEAD_GROUPS")) ctx->decode_head_groups = atoi(env);
+  if (const char *env = getenv("AF_SHARDED_HEAD_GROUPS")) ctx->sharded_head_groups = atoi(env);
+  if (const char *env = getenv("AF_COMM_RESERVE_SMS")) ctx->comm_reserve_sms = atoi(env);
   ctx->magic = kCtxMagic;
   *out = ctx;
   return AF_OK;
@@ -144,6 +146,12 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
     ctx->decode_head_groups = (int)value;
   } else if (!strcmp(name, "allow_split_k")) {
     ctx->allow_split_k = value != 0;
+  } else if (!strcmp(name, "sharded_head_groups")) {
+    if (value < 0 || value > af_ctx::kMaxSlices) return af::fail(AF_ERR_ARG, "af_set_option: sharded_head_groups 0..8");
+    ctx->sharded_head_groups = (int)value;
+  } else if (!strcmp(name, "comm_reserve_sms")) {
+    if (value < 0 || value > 64) return af::fail(AF_ERR_ARG, "af_set_option: comm_reserve_sms 0..64");
+    ctx->comm_reserve_sms = (int)value;
   } else if (!strcmp(name, "chunkwise_segments")) {
     if (value < 0 || value > 4096) return af::fail(AF_ERR_ARG, "af_set_option: chunkwise_segments 0..4096");
     ctx->chunk_segments = (int)value;

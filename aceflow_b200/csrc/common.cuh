@@ -33,6 +33,8 @@ struct af_ctx {
   // NCCL communicator of the head-sharded prefill (sharded_prefill.cu)
   void *comm = nullptr;
   int comm_nranks = 0, comm_rank = 0;
+  int sharded_head_groups = 0;  // head groups pipelined against the all-gather (0: auto; 1: one gather)
+  int comm_reserve_sms = 16;    // SMs the overlapped kernels leave to NCCL
 };
 
 constexpr uint32_t kCtxMagic = 0xACEF1011u;
@@ -85,6 +87,8 @@ struct GemmEpilogueArgs {
   int64_t split_stride = 0;  // split-K z stores its partial at out + z * split_stride (no atomics)
   int max_partials = 1;      // partial buffers available at out (split_stride != 0)
   int force_bn = 0, force_splits = 0;  // tile width / split count chosen by the caller (0: dispatch decides)
+  int scale_residual = 0;  // the row scale multiplies the residual too: out = (acc + residual) * scale
+  int max_ctas = 0;        // persistent kernel: at most this many CTAs (SMs left to a concurrent kernel); 0: all
 };
 
 bool tc_gemm_ok(const void *A, int64_t lda, const void *B, int64_t ldb, int K, bool fp32);

@@ -64,7 +64,28 @@ struct GemmEpilogue {
   // Split-K into separate partial buffers: split z stores (no atomics) at
   // out + z * split_stride; the consumer sums them.  0: one output.
   int64_t split_stride;
+  int scale_residual;      // the row scale multiplies the residual too: (acc + r) * scale
+  int res_vec;             // residual base 16-byte aligned and ldr a whole number of 16-byte units
 };
+
+// v[e] += r[e] * rs for the 16 columns n..n+15 of one row (vector loads when
+// the row segment is whole and aligned: each thread owns a different row, so
+// scalar loads would touch 32 lines per warp instruction 16 times over).
+__device__ __forceinline__ void add_residual16(float (&v)[16], const float *r, int n, int N, float rs, bool vec) {
+  if (vec && n + 16 <= N) {
+#pragma unroll
+    for (int e = 0; e < 16; e += 4) {
+      const float4 t = *reinterpret_cast<const float4 *>(r + e);
+      v[e] += t.x * rs;
+      v[e + 1] += t.y * rs;
+      v[e + 2] += t.z * rs;
+      v[e + 3] += t.w * rs;
+    }
+  } else {
+    for (int e = 0; e < 16; ++e)
+      if (n + e < N) v[e] += r[e] * rs;
+  }
+}
 
 // 1 / rms of one row from its partial sums of squares.
 __device__ __forceinline__ float row_scale(const GemmEpilogue &ep, int row, int M) {
@@ -180,11 +201,7 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
         if (first && ep.bias && n + e < N) v[e] += ep.bias[n + e];
       }
       if (ep.atomic) {
-        if (first && ep.residual) {
-          const float *r = ep.residual + (size_t)row * ep.ldr + n;
-          for (int e = 0; e < 16; ++e)
-            if (n + e < N) v[e] += r[e];
-        }
+        if (first && ep.residual) add_residual16(v, ep.residual + (size_t)row * ep.ldr + n, n, N, 1.f, ep.res_vec);
         float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + n;
         if (n + 16 <= N && ep.vec_ok) {
 #pragma unroll
@@ -195,12 +212,8 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
         }
         continue;
       }
-      if (ep.residual) {
-        const float *r = ep.residual + (size_t)row * ep.ldr + n;
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          if (n + e < N) v[e] += r[e];
-      }
+      if (ep.residual)
+        add_residual16(v, ep.residual + (size_t)row * ep.ldr + n, n, N, ep.scale_residual ? scale : 1.f, ep.res_vec);
       if (ep.out_bf16) {
         __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + n;
         if (n + 16 <= N && ep.vec_ok) {
@@ -594,7 +607,7 @@ int make_kmajor_map(CUtensorMap *map, const void *base, bool fp32, int rows, int
 
 template <int BN>
 int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
-                      const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
+                      const GemmEpilogue &ep, cudaStream_t st, const char *fn, int ep_max_ctas) {
   using C = TileCfg<BN, kBF16>;
   CUtensorMap ta, tb;
   int rc = make_kmajor_map(&ta, A, false, (K / ep.a_kb) * M, ep.a_kb, lda, C::BM, fn);
@@ -609,7 +622,8 @@ int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, in
     attr_done = true;
   }
   const int64_t total = (int64_t)((N + BN - 1) / BN) * ((M + C::BM - 1) / C::BM);
-  const int grid = (int)(total < ctx->num_sms ? total : ctx->num_sms);
+  const int cap = ep_max_ctas > 0 && ep_max_ctas < ctx->num_sms ? ep_max_ctas : ctx->num_sms;
+  const int grid = (int)(total < cap ? total : cap);
   umma_gemm_persistent_kernel<BN><<<grid, 192, C::SMEM, st>>>(ta, tb, M, N, K, ep, ctx->dev_err);
   return af::launched(ctx, fn);
 }
@@ -689,7 +703,8 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
   GemmEpilogue ep{a.out, a.ldo,      a.out_bf16, a.bias,   a.row_parts, a.nparts,   a.inv_d,
                   a.eps, a.residual, a.ldr,      a.swiglu, vec ? 1 : 0, 0,
                   a.a_kblock ? a.a_kblock : K, a.parts_block ? a.parts_block : (a.nparts > 0 ? a.nparts : 1),
-                  a.trans, a.split_stride};
+                  a.trans, a.split_stride, a.scale_residual,
+                  a.residual && af::aligned16(a.residual) && (a.ldr * 4) % 16 == 0 ? 1 : 0};
   if ((a.trans || a.split_stride) &&
       (a.swiglu || a.out_bf16 || a.bias || a.residual || a.row_parts || a.accumulate || a.a_kblock))
     return af::fail(AF_ERR_ARG, "%s: transposed / partial-buffer output is plain fp32 only", fn);
@@ -698,7 +713,7 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
   const int64_t sms = ctx->num_sms;
   constexpr int bk = MODE == kBF16 ? 64 : 32;
   const int nk = (K + bk - 1) / bk;
-  const bool can_split = !a.swiglu && !a.out_bf16 && ctx->allow_split_k;
+  const bool can_split = !a.swiglu && !a.out_bf16 && ctx->allow_split_k && !a.scale_residual;
   // Widest tile first (each A slice then feeds the most MMA work and is
   // re-read by the fewest CTAs; measured on B200: a 256x6144x2048 3xTF32
   // GEMM takes 54 us at BN=128 vs 92 us at BN=64).  Small-M GEMMs then fill
@@ -772,8 +787,8 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
   // large bf16 GEMMs (two or more waves of tiles): persistent kernel
   if (MODE == kBF16 && splits == 1 && !a.trans && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms &&
       !getenv("AF_GEMM_NO_PERSIST")) {
-    if (bn == 256) return launch_persistent<256>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
-    return launch_persistent<128>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+    if (bn == 256) return launch_persistent<256>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);
+    return launch_persistent<128>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);
   }
 #define AF_LAUNCH(BNV) return launch_tc<BNV, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn)
   switch (bn) {

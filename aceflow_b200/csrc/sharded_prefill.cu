@@ -74,6 +74,23 @@ int nccl_fail(ncclResult_t r, const char *fn, const char *what) {
 
 inline size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 
+// dst[n][(i * g + r) * dlg + c] = src[n][r * dl + i * dlg + c] in 16-byte
+// units (dlg8 = dlg / 8 bf16 per unit): W_o rows with their columns in the
+// K order of the gather buffers [G][g][N][dlg] (head group i, rank r).
+__global__ void gather_wo_cols_kernel(const uint4 *__restrict__ src, uint4 *__restrict__ dst, int G, int dl, int g,
+                                      int dlg8, int ld8, int dl8) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)dl * G * g * dlg8;
+  if (idx >= total) return;
+  const int c = (int)(idx % dlg8);
+  int64_t t = idx / dlg8;
+  const int rr = (int)(t % g);
+  t /= g;
+  const int i = (int)(t % G);
+  const int n = (int)(t / G);
+  dst[idx] = src[(size_t)n * ld8 + (size_t)rr * dl8 + (size_t)i * dlg8 + c];
+}
+
 }  // namespace
 
 namespace af {
@@ -144,54 +161,100 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
   if (B == 0 || T == 0) return AF_OK;
   const int Hl = H / g, dl = Hl * dh;
   const int64_t N = (int64_t)B * T;
-  const int parts = Hl * af::chunkwise_parts();
-  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, Hl, ctx->chunk_segments);
-  const size_t qkv_b = align256((size_t)N * 3 * dl * 2), o_b = align256((size_t)g * N * dl * 2),
-               ss_b = align256((size_t)g * N * parts * 4), seg_b = af::chunkwise_seg_state_bytes(B, Hl, pl);
+  // Head groups: the all-gather of group i runs on a side stream while group
+  // i+1 is projected and retained (the last group's gather stays exposed);
+  // one W_o GEMM then reads every group's gather buffer.  Needs per-group
+  // state views (one stream, or no state).  sharded_head_groups 0 = auto:
+  // 2 groups from 4 ranks up (below that the gather is short and the SMs left
+  // to it cost more than it hides).
+  int G = ctx->sharded_head_groups > 0 ? ctx->sharded_head_groups : (g >= 4 ? 2 : 1);
+  if (B > 1 && (state_in || state_out)) G = 1;
+  while (G > 1 && Hl % G != 0) --G;
+  if (G > af_ctx::kMaxSlices) G = af_ctx::kMaxSlices;
+  const int hg = Hl / G, dlg = hg * dh, P = hg * af::chunkwise_parts();
+  const int reserve = G > 1 && g > 1 ? ctx->comm_reserve_sms : 0;  // SMs left to the concurrent all-gather
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms - reserve, B, T, hg, ctx->chunk_segments);
+  const size_t qkv_b = align256((size_t)N * 3 * dlg * 2), o_b = align256((size_t)G * g * N * dlg * 2),
+               ss_b = align256((size_t)G * g * N * P * 4), seg_b = align256(af::chunkwise_seg_state_bytes(B, hg, pl)),
+               wo_b = G > 1 ? align256((size_t)dl * d * 2) : 0;
   void *ws = nullptr;
-  int rc = af::workspace(ctx, qkv_b + o_b + ss_b + seg_b, &ws, fn);
+  int rc = af::workspace(ctx, qkv_b + o_b + ss_b + seg_b + wo_b, &ws, fn);
   if (rc) return rc;
   uint8_t *base = static_cast<uint8_t *>(ws);
   uint16_t *qkv = reinterpret_cast<uint16_t *>(base);
-  uint16_t *o_all = reinterpret_cast<uint16_t *>(base + qkv_b);
-  float *ss_all = reinterpret_cast<float *>(base + qkv_b + o_b);
+  uint16_t *o_all = reinterpret_cast<uint16_t *>(base + qkv_b);             // [G][g][N][dlg]
+  float *ss_all = reinterpret_cast<float *>(base + qkv_b + o_b);            // [G][g][N][P]
   float *seg = seg_b ? reinterpret_cast<float *>(base + qkv_b + o_b + ss_b) : nullptr;
-  uint16_t *o_mine = o_all + (size_t)r * N * dl;
-  float *ss_mine = ss_all + (size_t)r * N * parts;
-  cudaStream_t st = af::stream_of(stream);
-  // 1. projection of this rank's heads
-  af::GemmEpilogueArgs e1;
-  e1.out = qkv;
-  e1.ldo = 3 * dl;
-  e1.out_bf16 = 1;
-  rc = af::tc_gemm(ctx, x, d, w_qkv_local, d, (int)N, 3 * dl, d, false, e1, st, fn);
-  if (rc) return rc;
-  // 2. retention of this rank's heads into its slot of the gather buffer
-  rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, Hl, gamma + (size_t)r * Hl, state_in, state_out, o_mine,
-                                    ret_norm_w + (size_t)r * dl, ss_mine, pl, seg, st, fn);
-  if (rc) return rc;
-  // 3. all-gather (in place) of head outputs and partial sums of squares
-  if (g > 1) {
-    ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
-    ncclResult_t nr = g_nccl.group_start();
-    if (nr == ncclSuccess) nr = g_nccl.all_gather(o_mine, o_all, (size_t)N * dl, ncclBfloat16, comm, st);
-    if (nr == ncclSuccess) nr = g_nccl.all_gather(ss_mine, ss_all, (size_t)N * parts, ncclFloat32, comm, st);
-    const ncclResult_t ne = g_nccl.group_end();
-    if (nr == ncclSuccess) nr = ne;
-    if (nr != ncclSuccess) return nccl_fail(nr, fn, "ncclAllGather");
+  uint16_t *wo_perm = G > 1 ? reinterpret_cast<uint16_t *>(base + qkv_b + o_b + ss_b + seg_b) : nullptr;
+  cudaStream_t st = af::stream_of(stream), cs = ctx->side[0];
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+  if (G > 1) {
+    // W_o rows with their columns in the gather buffers' K order
+    const int64_t vec = (int64_t)G * dl * g * (dlg / 8);
+    gather_wo_cols_kernel<<<(unsigned)((vec + 255) / 256), 256, 0, st>>>(
+        reinterpret_cast<const uint4 *>(w_o_rows), reinterpret_cast<uint4 *>(wo_perm), G, dl, g, dlg / 8, d / 8,
+        dl / 8);
+    rc = af::launched(ctx, fn);
+    if (rc) return rc;
   }
-  // 4. this rank's output columns: K-blocked gather buffer . W_o rows^T
-  af::GemmEpilogueArgs e2;
-  e2.out = out;
-  e2.ldo = dl;
-  e2.out_bf16 = out_bf16;
-  e2.row_parts = ss_all;
-  e2.nparts = g * parts;
-  e2.parts_block = parts;
-  e2.a_kblock = dl;
-  e2.inv_d = 1.0f / (float)d;
-  e2.eps = eps;
-  return af::tc_gemm(ctx, o_all, dl, w_o_rows, d, (int)N, dl, d, false, e2, st, fn);
+  for (int i = 0; i < G; ++i) {
+    // 1. projections of group i's heads: q, k, v column blocks of qkv [N][3*dlg]
+    for (int part = 0; part < 3; ++part) {
+      af::GemmEpilogueArgs e;
+      e.out = qkv + (size_t)part * dlg;
+      e.ldo = 3 * dlg;
+      e.out_bf16 = 1;
+      e.max_ctas = i > 0 ? ctx->num_sms - reserve : 0;
+      const uint16_t *wrows = w_qkv_local + ((size_t)part * dl + (size_t)i * dlg) * d;
+      rc = af::tc_gemm(ctx, x, d, wrows, d, (int)N, dlg, d, false, e, st, fn);
+      if (rc) return rc;
+    }
+    // 2. retention of group i into its slot of the gather buffer
+    uint16_t *o_grp = o_all + (size_t)i * g * N * dlg;
+    float *ss_grp = ss_all + (size_t)i * g * N * P;
+    const size_t st_off = (size_t)i * hg * dh * dh;  // one stream, or no state
+    rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, hg, gamma + (size_t)r * Hl + (size_t)i * hg,
+                                      state_in ? state_in + st_off : nullptr, state_out ? state_out + st_off : nullptr,
+                                      o_grp + (size_t)r * N * dlg, ret_norm_w + (size_t)r * dl + (size_t)i * dlg,
+                                      ss_grp + (size_t)r * N * P, pl, seg, st, fn);
+    if (rc) return rc;
+    // 3. all-gather (in place) of group i's outputs and partial sums of squares
+    if (g > 1) {
+      cudaStream_t as = G > 1 ? cs : st;
+      if (G > 1) {
+        AF_CUDA(cudaEventRecord(ctx->ev_a[i], st), fn);
+        AF_CUDA(cudaStreamWaitEvent(cs, ctx->ev_a[i], 0), fn);
+      }
+      ncclResult_t nr = g_nccl.group_start();
+      if (nr == ncclSuccess)
+        nr = g_nccl.all_gather(o_grp + (size_t)r * N * dlg, o_grp, (size_t)N * dlg, ncclBfloat16, comm, as);
+      if (nr == ncclSuccess)
+        nr = g_nccl.all_gather(ss_grp + (size_t)r * N * P, ss_grp, (size_t)N * P, ncclFloat32, comm, as);
+      const ncclResult_t ne = g_nccl.group_end();
+      if (nr == ncclSuccess) nr = ne;
+      if (nr != ncclSuccess) return nccl_fail(nr, fn, "ncclAllGather");
+      if (G > 1) AF_CUDA(cudaEventRecord(ctx->ev_b[i], cs), fn);
+    }
+  }
+  const bool waits = G > 1 && g > 1;  // gathers ran on the side stream
+  // 4. this rank's output columns: the gather buffers [G][g][N][dlg] as one
+  //    K-blocked operand . W_o rows (columns in the same K order)^T, 1/rms
+  //    per row in the epilogue
+  if (waits)
+    for (int i = 0; i < G; ++i) AF_CUDA(cudaStreamWaitEvent(st, ctx->ev_b[i], 0), fn);
+  af::GemmEpilogueArgs e;
+  e.out = out;
+  e.ldo = dl;
+  e.out_bf16 = out_bf16;
+  e.a_kblock = dlg;
+  e.row_parts = ss_all;
+  e.nparts = G * g * P;
+  e.parts_block = P;
+  e.inv_d = 1.0f / (float)d;
+  e.eps = eps;
+  rc = af::tc_gemm(ctx, o_all, dlg, G > 1 ? wo_perm : w_o_rows, d, (int)N, dl, d, false, e, st, fn);
+  if (rc) return rc;
+  return AF_OK;
 }
 
 }  // extern "C"

@@ -335,7 +335,8 @@ def linear_f32_split(x_split, w_split, bias: torch.Tensor | None = None) -> torc
 
 def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_sumsq: torch.Tensor | None = None,
               inv_d: float = 0.0, eps: float = 0.0, accumulate: bool = False, a_kblock: int = 0,
-              parts_block: int = 0) -> torch.Tensor:
+              parts_block: int = 0, bias: torch.Tensor | None = None,
+              residual: torch.Tensor | None = None) -> torch.Tensor:
     """out (+)= rowscale * A[M, K] . b[N, K]^T (af_gemm_bf16).
 
     a: bf16 2-D view with unit column stride.  Plain (a_kblock == 0): a is
@@ -343,7 +344,8 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_sumsq: to
     blocks [M, a_kblock] stacked (an all-gather of column slices).
     b: bf16 [N, K] view; out: fp32 [M, N] view.  rowscale from row_sumsq
     ([M, P] or, with parts_block, P/parts_block stacked blocks [M, parts_block])
-    as 1/sqrt(sum/d + eps) when given."""
+    as 1/sqrt(sum/d + eps) when given; bias [N] fp32 and residual (an fp32
+    [M, N] view, may be `out` itself) are added after the scale."""
     for n, t in (("a", a), ("b", b)):
         if t.dtype != BF16 or t.dim() != 2 or t.stride(1) != 1:
             raise ValueError(f"{n}: expected a 2-D bf16 view with unit column stride")
@@ -362,7 +364,14 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_sumsq: to
     if row_sumsq is not None:
         _need(row_sumsq, F32, "row_sumsq")
         P = row_sumsq.numel() // M
+    ldr = 0
+    if residual is not None:
+        if residual.dtype != F32 or residual.dim() != 2 or residual.stride(1) != 1 or tuple(residual.shape) != (M, N):
+            raise ValueError("residual: expected an fp32 [M, N] view with unit column stride")
+        ldr = residual.stride(0)
+    if bias is not None:
+        _need(bias, F32, "bias")
     _lib.call("af_gemm_bf16", _ctx(a), _p(a), a.stride(0), int(a_kblock), _p(b), b.stride(0), M, N, K, _p(out),
-              out.stride(0), 0, None, None, 0, _p(row_sumsq), P, int(parts_block), float(inv_d), float(eps),
-              int(accumulate), _stream(a))
+              out.stride(0), 0, _p(bias), _p(residual), ldr, _p(row_sumsq), P, int(parts_block), float(inv_d),
+              float(eps), int(accumulate), _stream(a))
     return out

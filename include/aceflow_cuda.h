@@ -65,7 +65,10 @@ int af_check_device(af_ctx *ctx, int *flags, int reset);
  *                              0 makes results bitwise reproducible run to run)
  *   "decode_slice_rows"  >= 0  batch slices of af_msr_decode_step_f32 (default 0: none)
  *   "chunkwise_segments" >= 0  sequence segments per stream in the chunkwise prefill
- *                              (default 0: enough to put one CTA on every SM; 1: none) */
+ *                              (default 0: enough to put one CTA on every SM; 1: none)
+ *   "sharded_head_groups" 0..8 head groups af_prefill_head_sharded pipelines against
+ *                              its all-gather (default 0: 2 from 4 ranks up, else 1)
+ *   "comm_reserve_sms"   0..64 SMs the overlapped kernels leave to the collective (default 16) */
 int af_set_option(af_ctx *ctx, const char *name, int64_t value);
 /* Number of this library's kernel launches issued through `ctx` so far. */
 int af_launch_count(af_ctx *ctx, int64_t *count);
@@ -343,7 +346,9 @@ int af_comm_destroy(af_ctx *ctx);
  *   out         [batch*T][dl] fp32 (or bf16 if out_bf16): its columns of
  *               the layer output.
  * One ncclAllGather of the head outputs (bf16) and of the per-row partial
- * sums of squares precedes the output projection.  Every rank must make the
+ * sums of squares precedes the output projection; with head groups
+ * (af_set_option "sharded_head_groups"; batch 1 or no state) each group's
+ * gather runs on a side stream under the next group's compute.  Every rank must make the
  * same call.  head_dim 256; H divisible by the rank count.  Workspace
  * batch*T*(6*dl + 2*d + 8*H) bytes plus segment states. */
 int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv_local,

@@ -83,3 +83,26 @@ def test_presplit_gemm_every_tile_width(dev, bn, M, N, K, monkeypatch):
     monkeypatch.delenv("AF_GEMM_BN")
     assert rel_err(y.cpu().numpy(), ref) < 1e-5
     _check(dev)
+
+
+@pytest.mark.parametrize("M,N,K,pad", [(300, 192, 256, 0), (129, 200, 128, 1), (4096, 512, 1024, 0)])
+def test_bf16_gemm_bias_residual_epilogue(dev, M, N, K, pad):
+    """Bias and residual in the epilogue, with the residual in vector
+    (aligned row stride) and scalar (odd row stride) form, and in place."""
+    from aceflow_b200 import cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g, device=dev).bfloat16()
+    b = (0.05 * torch.randn(N, K, generator=g, device=dev)).bfloat16()
+    bias = torch.randn(N, generator=g, device=dev)
+    base = torch.randn(M, N + pad, generator=g, device=dev)
+    res = base[:, :N]
+    ref = a.double() @ b.double().t() + bias.double() + res.double()
+    out = torch.empty(M, N, device=dev)
+    cuda_ops.gemm_bf16(a, b, out, bias=bias, residual=res)
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+    # in place: out is the residual
+    inplace = res.clone()
+    cuda_ops.gemm_bf16(a, b, inplace, bias=bias, residual=inplace)
+    assert rel_err(inplace.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+    _check(dev)

@@ -162,9 +162,10 @@ def test_gemm_bf16_kblocked_operand_and_blocked_parts(dev):
     assert rel_err(plain.cpu().numpy(), ref.cpu().numpy()) < 1e-5
 
 
-def test_head_sharded_prefill_single_rank(dev):
+@pytest.mark.parametrize("groups", [0, 2])
+def test_head_sharded_prefill_single_rank(dev, groups):
     """af_prefill_head_sharded on a 1-rank communicator equals the float64
-    layer (and af_msr_prefill_bf16)."""
+    layer (and af_msr_prefill_bf16), in one piece or as two head groups."""
     from aceflow_b200 import _lib, cuda_ops
     from aceflow_b200.sharded import HeadShardedPrefill
 
@@ -177,11 +178,13 @@ def test_head_sharded_prefill_single_rank(dev):
     wo = tb((0.02 * rng.standard_normal((d, d))).astype(np.float32))
     rw = torch.from_numpy((1 + 0.1 * rng.standard_normal(d)).astype(np.float32)).to(dev)
     sp = HeadShardedPrefill(wqkv, wo, rw, H, 1e-6)
+    _lib.set_option(0, "sharded_head_groups", groups)
     try:
         st = torch.empty(B, H, 256, 256, device=dev)
         out = sp(x, state_out=st)
         torch.cuda.synchronize()
     finally:
+        _lib.set_option(0, "sharded_head_groups", 0)
         sp.close()
     assert _lib.check_device(0) == 0
     f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731

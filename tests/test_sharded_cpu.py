@@ -72,9 +72,10 @@ def _inputs(B, T, H):
     return x, wqkv, wo, rw
 
 
-def _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, eps=1e-6):
+def _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, eps=1e-6, groups=1):
     """One rank's share of the layer in float64, step for step as
-    af_prefill_head_sharded lays it out."""
+    af_prefill_head_sharded lays it out (`groups` head groups, each gathered
+    separately, W_o summed over groups with the row scale applied last)."""
     from aceflow_b200.sharded import chunkwise_plan, head_range, shard_weights
     from oracle import retention_ref as R
 
@@ -105,19 +106,27 @@ def _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, eps=1e-6):
     o_w = o * rw[rank * dl:(rank + 1) * dl]
     # partial sums of squares per (head, 128-wide value slice): [N][Hl*2]
     ss = (o.reshape(N, Hl * 2, 128) ** 2).sum(-1)
-    # 3. all-gather: stacked by rank
-    o_all = gather(o_w)   # [world*N, dl]
-    ss_all = gather(ss)   # [world*N, Hl*2]
-    # 4. output columns of this rank: A(m, k) = o_all[(k // dl) * N + m, k % dl]
-    pb = Hl * 2
-    A = np.concatenate([o_all[r * N:(r + 1) * N] for r in range(world)], axis=1)
-    parts = np.concatenate([ss_all[r * N:(r + 1) * N] for r in range(world)], axis=1)
-    assert parts.shape[1] == world * pb
+    hg = Hl // groups
+    dlg, pb = hg * dh, hg * 2
+    acc = np.zeros((N, dl))
+    parts_all = []
+    for i in range(groups):
+        # 3. all-gather of group i: stacked by rank [world*N, dlg] and [world*N, pb]
+        o_all = gather(o_w[:, i * dlg:(i + 1) * dlg])
+        ss_all = gather(ss[:, i * pb:(i + 1) * pb])
+        # 4. A(m, k) = o_all[(k // dlg) * N + m, k % dlg]; W_o columns regrouped
+        #    to r' * dl + i * dlg + c for k = r' * dlg + c
+        A = np.concatenate([o_all[r * N:(r + 1) * N] for r in range(world)], axis=1)
+        cols = [r * dl + i * dlg + c for r in range(world) for c in range(dlg)]
+        acc += A @ wo_r[:, cols].T
+        parts_all += [ss_all[r * N:(r + 1) * N] for r in range(world)]
+    parts = np.concatenate(parts_all, axis=1)
+    assert parts.shape[1] == groups * world * pb
     scale = 1.0 / np.sqrt(parts.sum(1, keepdims=True) / d + eps)
-    return (scale * (A @ wo_r.T)).reshape(B, T, dl)
+    return (scale * acc).reshape(B, T, dl)
 
 
-def _worker(rank, world, port, B, T, H, outdir):
+def _worker(rank, world, port, B, T, H, outdir, groups):
     import datetime
 
     import torch.distributed as dist
@@ -132,14 +141,15 @@ def _worker(rank, world, port, B, T, H, outdir):
             return torch.cat(parts, 0).numpy()
 
         x, wqkv, wo, rw = _inputs(B, T, H)
-        out = _rank_layer(x, wqkv, wo, rw, H, world, rank, gather)
+        out = _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, groups=groups)
         np.save(os.path.join(outdir, f"out{rank}.npy"), out)
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_head_sharded_decomposition_two_gloo_ranks():
+@pytest.mark.parametrize("groups", [1, 2])
+def test_head_sharded_decomposition_two_gloo_ranks(groups):
     import torch.multiprocessing as mp
 
     from oracle import retention_ref as R
@@ -149,7 +159,7 @@ def test_head_sharded_decomposition_two_gloo_ranks():
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     with tempfile.TemporaryDirectory() as outdir:
-        mp.spawn(_worker, args=(WORLD, port, B, T, H, outdir), nprocs=WORLD, join=True)
+        mp.spawn(_worker, args=(WORLD, port, B, T, H, outdir, groups), nprocs=WORLD, join=True)
         out = np.concatenate([np.load(os.path.join(outdir, f"out{r}.npy")) for r in range(WORLD)], -1)
     x, wqkv, wo, rw = _inputs(B, T, H)
     wq, wk, wv = np.split(wqkv, 3)

@@ -25,10 +25,11 @@ def _inputs(B, T, H):
     return x, wqkv, wo, rw
 
 
-def _worker(rank, world, port, B, T, H, outdir):
+def _worker(rank, world, port, B, T, H, outdir, groups):
     import torch.distributed as dist
 
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["AF_SHARDED_HEAD_GROUPS"] = str(groups)  # read when the context is created
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=__import__("datetime").timedelta(seconds=120))
@@ -54,7 +55,8 @@ def _worker(rank, world, port, B, T, H, outdir):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_head_sharded_prefill_two_gpus():
+@pytest.mark.parametrize("groups", [0, 2])
+def test_head_sharded_prefill_two_gpus(groups):
     import socket
 
     import torch.multiprocessing as mp
@@ -66,7 +68,7 @@ def test_head_sharded_prefill_two_gpus():
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     with tempfile.TemporaryDirectory() as outdir:
-        mp.spawn(_worker, args=(WORLD, port, B, T, H, outdir), nprocs=WORLD, join=True)
+        mp.spawn(_worker, args=(WORLD, port, B, T, H, outdir, groups), nprocs=WORLD, join=True)
         outs = [np.load(os.path.join(outdir, f"out{r}.npy")) for r in range(WORLD)]
         states = [np.load(os.path.join(outdir, f"state{r}.npy")) for r in range(WORLD)]
     x, wqkv, wo, rw = _inputs(B, T, H)
