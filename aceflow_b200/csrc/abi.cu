@@ -146,6 +146,9 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
     ctx->decode_head_groups = (int)value;
   } else if (!strcmp(name, "allow_split_k")) {
     ctx->allow_split_k = value != 0;
+  } else if (!strcmp(name, "decode_transposed")) {
+    if (value < 0 || value > 15) return af::fail(AF_ERR_ARG, "af_set_option: decode_transposed 0..15");
+    ctx->decode_transposed = (int)value;
   } else if (!strcmp(name, "sharded_head_groups")) {
     if (value < 0 || value > af_ctx::kMaxSlices) return af::fail(AF_ERR_ARG, "af_set_option: sharded_head_groups 0..8");
     ctx->sharded_head_groups = (int)value;

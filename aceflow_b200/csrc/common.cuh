@@ -33,6 +33,8 @@ struct af_ctx {
   // NCCL communicator of the head-sharded prefill (sharded_prefill.cu)
   void *comm = nullptr;
   int comm_nranks = 0, comm_rank = 0;
+  // bf16 decode layer projections run transposed (bit 0 QKV, 1 W_o, 2 gate/up, 3 down)
+  int decode_transposed = 15;
   int sharded_head_groups = 0;  // head groups pipelined against the all-gather (0: auto; 1: one gather)
   int comm_reserve_sms = 16;    // SMs the overlapped kernels leave to NCCL
 };

@@ -77,6 +77,39 @@ __global__ void __launch_bounds__(256)
   for (int i = threadIdx.x; i < d; i += blockDim.x) y[off + i] = __float2bfloat16(row[i] * (inv * w[i]));
 }
 
+// The same for rows of d = 1024 * V4 floats, held in registers as float4s
+// (V4 per thread, 256 threads): one read of x, one write of y.
+template <int V4>
+__global__ void __launch_bounds__(256)
+    rmsnorm_to_bf16_reg_kernel(const float4 *__restrict__ x, const float4 *__restrict__ w, uint2 *__restrict__ y,
+                               float eps) {
+  constexpr int D4 = 256 * V4;
+  __shared__ float red[8];
+  const size_t off = (size_t)blockIdx.x * D4;
+  float4 a[V4];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < V4; ++i) {
+    a[i] = x[off + threadIdx.x + i * 256];
+    ss += a[i].x * a[i].x + a[i].y * a[i].y + a[i].z * a[i].z + a[i].w * a[i].w;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t += red[i];
+  const float inv = w ? 1.0f / sqrtf(t / (float)(4 * D4) + eps) : 1.f;
+#pragma unroll
+  for (int i = 0; i < V4; ++i) {
+    const int k = threadIdx.x + i * 256;
+    const float4 ww = w ? w[k] : make_float4(1.f, 1.f, 1.f, 1.f);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(a[i].x * (inv * ww.x), a[i].y * (inv * ww.y));
+    __nv_bfloat162 hi = __floats2bfloat162_rn(a[i].z * (inv * ww.z), a[i].w * (inv * ww.w));
+    y[off + k] = make_uint2(*reinterpret_cast<uint32_t *>(&lo), *reinterpret_cast<uint32_t *>(&hi));
+  }
+}
+
 // One CTA per row; ties resolve to the smallest index, NaN never wins (the
 // reference's strict `>` scan from index 0).
 __global__ void __launch_bounds__(512) argmax_rows_kernel(const float *__restrict__ logits, int V,
@@ -147,9 +180,17 @@ int af_rmsnorm_to_bf16(af_ctx *ctx, const float *x, const float *w, uint16_t *y,
   AF_REQUIRE(x && y, "af_rmsnorm_to_bf16", "null pointer");
   AF_REQUIRE(rows >= 0 && d > 0 && d <= 12288, "af_rmsnorm_to_bf16", "bad sizes rows=%d d=%d", rows, d);
   if (rows == 0) return AF_OK;
-  rmsnorm_to_bf16_kernel<<<rows, 256, (size_t)d * 4, af::stream_of(stream)>>>(x, w,
-                                                                             reinterpret_cast<__nv_bfloat16 *>(y),
-                                                                             d, eps);
+  cudaStream_t st = af::stream_of(stream);
+  const bool al = af::aligned16(x) && af::aligned16(y) && (w == nullptr || af::aligned16(w));
+  const float4 *x4 = reinterpret_cast<const float4 *>(x);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  uint2 *y4 = reinterpret_cast<uint2 *>(y);
+  if (al && d == 1024) rmsnorm_to_bf16_reg_kernel<1><<<rows, 256, 0, st>>>(x4, w4, y4, eps);
+  else if (al && d == 2048) rmsnorm_to_bf16_reg_kernel<2><<<rows, 256, 0, st>>>(x4, w4, y4, eps);
+  else if (al && d == 4096) rmsnorm_to_bf16_reg_kernel<4><<<rows, 256, 0, st>>>(x4, w4, y4, eps);
+  else if (al && d == 8192) rmsnorm_to_bf16_reg_kernel<8><<<rows, 256, 0, st>>>(x4, w4, y4, eps);
+  else
+    rmsnorm_to_bf16_kernel<<<rows, 256, (size_t)d * 4, st>>>(x, w, reinterpret_cast<__nv_bfloat16 *>(y), d, eps);
   return af::launched(ctx, fn);
 }
 
@@ -208,6 +249,31 @@ static int gemm(af_ctx *ctx, const void *A, const void *B, int M, int N, int K, 
 
 static size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 
+// Transposed decode projection: W[rows_w][K] as the 128-row operand, the
+// activations [batch][K] as one N tile (each weight tile is read by exactly
+// one CTA), split-K to fill the SMs.
+constexpr int kTransPartials = 4;
+static int trans_tile(int batch) {
+  int bn = 16;
+  while (bn < batch) bn *= 2;
+  return bn;
+}
+static int trans_splits(const af_ctx *ctx, int rows_w, int K, int max_splits) {
+  const int mt = (rows_w + 127) / 128;
+  int sp = ctx->num_sms / mt;
+  const int nk = (K + 63) / 64;
+  if (sp > nk / 2) sp = nk / 2;
+  if (sp > max_splits) sp = max_splits;
+  return sp < 1 ? 1 : sp;
+}
+static int gemm_t(af_ctx *ctx, const void *W, int rows_w, const void *X, int batch, int K, GemmEpilogueArgs e,
+                  int max_splits, cudaStream_t st, const char *fn) {
+  e.trans = 1;
+  e.force_bn = trans_tile(batch);
+  e.force_splits = max_splits > 1 ? trans_splits(ctx, rows_w, K, max_splits) : 1;
+  return tc_gemm(ctx, W, K, X, K, rows_w, batch, K, false, e, st, fn);
+}
+
 static int check_layer(const af_layer_weights *w, int B, int d, int H, int f, const char *fn) {
   if (!w || !w->w_qkv || !w->w_o || !w->w_gate_up || !w->w_down || !w->norm1 || !w->norm2 || !w->ret_norm)
     return fail(AF_ERR_ARG, "%s: null weight pointer", fn);
@@ -235,8 +301,11 @@ extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, i
              "bad state_batch_stride");
   if (B == 0) return AF_OK;
   const bool fp32 = !weights_bf16;
+  // bf16 weights, up to 256 streams: every projection runs transposed
+  const bool tr = !fp32 && B <= 256 && d % 64 == 0 && f % 64 == 0;
   const size_t ab = fp32 ? 4 : 2;  // activation bytes feeding the GEMMs
-  const size_t h_b = af::align256((size_t)B * d * ab), qkv_b = af::align256((size_t)B * 3 * d * 4),
+  const size_t h_b = af::align256((size_t)B * d * ab),
+               qkv_b = af::align256((size_t)(tr ? af::kTransPartials : 1) * B * 3 * d * 4),
                o_b = af::align256((size_t)B * d * ab), ss_b = af::align256((size_t)B * H * 4),
                hid_b = af::align256((size_t)B * f * ab);
   void *ws = nullptr;
@@ -249,6 +318,69 @@ extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, i
   float *ss = reinterpret_cast<float *>(p + h_b + qkv_b + o_b);
   void *hid = p + h_b + qkv_b + o_b + ss_b;
   cudaStream_t st = af::stream_of(stream);
+  if (tr) {
+    const int tm = ctx->decode_transposed;  // which projections run as W . x^T
+    // 1. h = bf16(RMSNorm1(x))
+    rc = af_rmsnorm_to_bf16(ctx, x, w->norm1, (uint16_t *)h, B, d, eps, stream);
+    if (rc) return rc;
+    // 2. qkv (transposed: split-K partial buffers, summed by the state stream)
+    int nsp = 1;
+    if (tm & 1) {
+      af::GemmEpilogueArgs e1;
+      e1.out = qkv;
+      e1.ldo = 3 * d;
+      e1.split_stride = (int64_t)B * 3 * d;
+      e1.max_partials = af::kTransPartials;
+      rc = af::gemm_t(ctx, w->w_qkv, 3 * d, h, B, d, e1, af::kTransPartials, st, fn);
+      nsp = af::trans_splits(ctx, 3 * d, d, af::kTransPartials);
+    } else {
+      rc = af::gemm(ctx, h, w->w_qkv, B, 3 * d, d, false, qkv, 0, nullptr, nullptr, 0, 0.f, 0.f, 0, st, fn);
+    }
+    if (rc) return rc;
+    // 3. state stream
+    rc = af::launch_retention_step(ctx, state, state_batch_stride, gamma, qkv, qkv + d, qkv + 2 * d, 3 * (int64_t)d,
+                                   (float *)o, d, B, H, dh, w->ret_norm, ss, st, fn, 1, nullptr, 0, 0, 0, nsp,
+                                   (int64_t)B * 3 * d);
+    if (rc) return rc;
+    // 4. x += diag(1/rms) (o*w) W_o^T (transposed: atomics over K splits, 1/rms per column)
+    if (tm & 2) {
+      af::GemmEpilogueArgs e2;
+      e2.out = x;
+      e2.ldo = d;
+      e2.accumulate = 1;
+      e2.row_parts = ss;
+      e2.nparts = H;
+      e2.inv_d = 1.0f / (float)d;
+      e2.eps = eps;
+      rc = af::gemm_t(ctx, w->w_o, d, o, B, d, e2, 8, st, fn);
+    } else {
+      rc = af::gemm(ctx, o, w->w_o, B, d, d, false, x, 0, x, ss, H, 1.0f / (float)d, eps, 0, st, fn);
+    }
+    if (rc) return rc;
+    // 5. h = bf16(RMSNorm2(x)); 6. hid = silu(g) * u
+    rc = af_rmsnorm_to_bf16(ctx, x, w->norm2, (uint16_t *)h, B, d, eps, stream);
+    if (rc) return rc;
+    if (tm & 4) {
+      af::GemmEpilogueArgs e3;
+      e3.out = hid;
+      e3.ldo = f;
+      e3.out_bf16 = 1;
+      e3.swiglu = 1;
+      rc = af::gemm_t(ctx, w->w_gate_up, 2 * f, h, B, d, e3, 1, st, fn);
+    } else {
+      rc = af::gemm(ctx, h, w->w_gate_up, B, 2 * f, d, false, hid, 1, nullptr, nullptr, 0, 0.f, 0.f, 1, st, fn);
+    }
+    if (rc) return rc;
+    // 7. x += hid W_down^T
+    if (tm & 8) {
+      af::GemmEpilogueArgs e4;
+      e4.out = x;
+      e4.ldo = d;
+      e4.accumulate = 1;
+      return af::gemm_t(ctx, w->w_down, d, hid, B, f, e4, 8, st, fn);
+    }
+    return af::gemm(ctx, hid, w->w_down, B, d, f, false, x, 0, x, nullptr, 0, 0.f, 0.f, 0, st, fn);
+  }
   if (fp32) rc = af::launch_rmsnorm_f32(ctx, x, nullptr, w->norm1, (float *)h, nullptr, B, d, eps, st, fn);
   else rc = af_rmsnorm_to_bf16(ctx, x, w->norm1, (uint16_t *)h, B, d, eps, stream);
   if (rc) return rc;

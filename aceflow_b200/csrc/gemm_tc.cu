@@ -144,7 +144,7 @@ __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__flo
 template <int BN, class Load16>
 __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load16, int row, bool row_ok, int n0,
                                            int N, bool ok, float scale, bool first) {
-  if (ep.swiglu) {
+  if (ep.swiglu && !ep.trans) {
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       float g[16], u[16];
@@ -177,16 +177,48 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
       }
     }
   } else if (ep.trans) {
-    float *o = reinterpret_cast<float *>(ep.out) + (size_t)blockIdx.z * ep.split_stride + row;
+    // Transposed tile: `row` is an output column (a weight row), the 16
+    // accumulator columns of a chunk are 16 output rows n..n+15 (batch rows).
+    // Lanes hold consecutive `row`s, so every store or atomic of one e is one
+    // coalesced 128-byte line.
+    const int lane = threadIdx.x & 31;
 #pragma unroll 1
     for (int c = 0; c < BN; c += 16) {
       float v[16];
       load16(c, v);
       const int n = n0 + c;
-      if (!ok || !row_ok || n >= N) continue;
+      if (ep.swiglu) {
+        // rows in groups of 16 gate then 16 up: lane l < 16 takes the up value
+        // of its hidden unit from lane l + 16
+        float u[16];
 #pragma unroll
-      for (int e = 0; e < 16; ++e)  // lanes hold consecutive rows: each store is one 128-byte line
-        if (n + e < N) o[(size_t)(n + e) * ep.ldo] = v[e] * scale;
+        for (int e = 0; e < 16; ++e) u[e] = __shfl_down_sync(0xffffffffu, v[e], 16);
+        if (!ok || !row_ok || n >= N || lane >= 16) continue;
+        const int j = ((row - lane) >> 1) + lane;  // hidden unit: 16 per 32-row group
+        __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + j;
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (n + e < N) {
+            const float gg = v[e];
+            o[(size_t)(n + e) * ep.ldo] = __float2bfloat16(gg / (1.0f + expf(-gg)) * u[e]);
+          }
+        continue;
+      }
+      // per-column 1/rms (output rows are streams): lane l computes column n + (l & 15)
+      float my_scale = 1.f;
+      if (ep.row_parts && n + (lane & 15) < N) my_scale = row_scale(ep, n + (lane & 15), N);
+      float cs[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) cs[e] = __shfl_sync(0xffffffffu, my_scale, e);
+      if (!ok || !row_ok || n >= N) continue;
+      float *o = reinterpret_cast<float *>(ep.out) + (size_t)blockIdx.z * ep.split_stride + row;
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (n + e < N) {
+          const float val = v[e] * cs[e];
+          if (ep.atomic) atomicAdd(o + (size_t)(n + e) * ep.ldo, val);
+          else o[(size_t)(n + e) * ep.ldo] = val;
+        }
     }
   } else {
 #pragma unroll 1
@@ -398,7 +430,7 @@ __global__ void __launch_bounds__(192, 1)
     const int row = m0 + q * 32 + lane;
     const bool row_ok = row < M;
     float scale = 1.f;
-    if (ep.row_parts && row_ok) scale = row_scale(ep, row, M);
+    if (ep.row_parts && row_ok && !ep.trans) scale = row_scale(ep, row, M);  // transposed: per column
     const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
     const int nacc = nk < C::NACC ? nk : C::NACC;  // accumulators that received products
     // Sum of the accumulators for 16 columns starting at `col` (warp-collective).
@@ -554,7 +586,7 @@ __global__ void __launch_bounds__(192, 1)
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < M;
       float scale = 1.f;
-      if (ep.row_parts && row_ok) scale = row_scale(ep, row, M);
+      if (ep.row_parts && row_ok && !ep.trans) scale = row_scale(ep, row, M);  // transposed: per column
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN);
       auto load16 = [&](int col, float (&v)[16]) {
         __syncwarp();
@@ -693,7 +725,7 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
   if (rc) return rc;
   if (M == 0 || N == 0) return AF_OK;
   const bool vec = af::aligned16(a.out) && (a.ldo * (a.out_bf16 ? 2 : 4)) % 16 == 0;
-  if (a.swiglu && (!vec || N % 32 != 0))
+  if (a.swiglu && !a.trans && (!vec || N % 32 != 0))
     return af::fail(AF_ERR_ARG, "%s: SwiGLU epilogue needs an aligned output and N %% 32 == 0", fn);
   constexpr int bk_elems = MODE == kBF16 ? 64 : 32;
   if (a.a_kblock && (a.a_kblock % bk_elems != 0 || K % a.a_kblock != 0 || lda < a.a_kblock))
@@ -705,9 +737,12 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
                   a.a_kblock ? a.a_kblock : K, a.parts_block ? a.parts_block : (a.nparts > 0 ? a.nparts : 1),
                   a.trans, a.split_stride, a.scale_residual,
                   a.residual && af::aligned16(a.residual) && (a.ldr * 4) % 16 == 0 ? 1 : 0};
-  if ((a.trans || a.split_stride) &&
-      (a.swiglu || a.out_bf16 || a.bias || a.residual || a.row_parts || a.accumulate || a.a_kblock))
-    return af::fail(AF_ERR_ARG, "%s: transposed / partial-buffer output is plain fp32 only", fn);
+  if (a.split_stride && (!a.trans || a.swiglu || a.out_bf16 || a.bias || a.residual || a.row_parts || a.accumulate ||
+                         a.a_kblock))
+    return af::fail(AF_ERR_ARG, "%s: partial buffers: transposed plain fp32 output only", fn);
+  if (a.trans && (a.bias || a.residual || a.a_kblock || a.scale_residual || (a.out_bf16 && !a.swiglu) ||
+                  (a.swiglu && (a.accumulate || !a.out_bf16 || M % 32 != 0))))
+    return af::fail(AF_ERR_ARG, "%s: unsupported transposed epilogue", fn);
   const int64_t mt = (M + 127) / 128;
   auto tiles = [&](int bn) { return mt * ((N + bn - 1) / bn); };
   const int64_t sms = ctx->num_sms;

@@ -375,3 +375,14 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_sumsq: to
               out.stride(0), 0, _p(bias), _p(residual), ldr, _p(row_sumsq), P, int(parts_block), float(inv_d),
               float(eps), int(accumulate), _stream(a))
     return out
+
+
+def rms_norm_to_bf16(x: torch.Tensor, w: torch.Tensor | None, eps: float) -> torch.Tensor:
+    """bf16(RMSNorm(x) * w) of fp32 rows [rows, d] (af_rmsnorm_to_bf16); w None: plain cast."""
+    _need(x, F32, "x")
+    if w is not None:
+        _need(w, F32, "w")
+    d = x.shape[-1]
+    y = torch.empty(x.shape, dtype=BF16, device=x.device)
+    _lib.call("af_rmsnorm_to_bf16", _ctx(x), _p(x), _p(w), _p(y), x.numel() // d, d, float(eps), _stream(x))
+    return y

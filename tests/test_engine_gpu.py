@@ -66,10 +66,15 @@ def test_forward_layer_fp32_matches_oracle(dev):
         assert rel_err(got, ref) < 1e-4
 
 
-@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
-def test_generate_matches_oracle(dev, dtype):
+@pytest.mark.parametrize("dtype,shape", [("float32", (2, 512, 2, 256, 300, 3, 20, 6)),
+                                         ("bfloat16", (2, 512, 2, 256, 300, 3, 20, 6)),
+                                         ("bfloat16", (1, 1024, 4, 512, 500, 64, 6, 3)),
+                                         ("bfloat16", (1, 1024, 4, 512, 500, 100, 4, 2))])
+def test_generate_matches_oracle(dev, dtype, shape):
+    """Prefill + greedy decode; bf16 weights with up to 256 streams take the
+    transposed decode projections (batch 3, 64, 100 -> tiles 16, 64, 128)."""
     bf16 = dtype == "bfloat16"
-    L, d, H, f, V, B, P, n = 2, 512, 2, 256, 300, 3, 20, 6
+    L, d, H, f, V, B, P, n = shape
     layers, emb = _model(L, d, f, V, 2, bf16)
     rng = np.random.default_rng(9)
     prompts = rng.integers(0, V, (B, P)).astype(np.int32)
@@ -116,3 +121,17 @@ def test_engine_validation(dev):
                                np.ones(64), np.ones(64))
     with pytest.raises(ValueError):
         eng.forward_layer(0, np.zeros(64, np.float32))  # weights not loaded
+
+
+@pytest.mark.parametrize("d", [1024, 2048, 4096, 8192, 512, 3000])
+@pytest.mark.parametrize("with_w", [True, False])
+def test_rmsnorm_to_bf16(dev, d, with_w):
+    from aceflow_b200 import cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(d)
+    x = torch.randn(5, d, generator=g, device=dev) * 3
+    w = (1 + 0.1 * torch.randn(d, generator=g, device=dev)) if with_w else None
+    y = cuda_ops.rms_norm_to_bf16(x, w, 1e-6)
+    xd = x.double()
+    ref = xd / torch.sqrt((xd * xd).mean(-1, keepdim=True) + 1e-6) * w.double() if with_w else xd
+    assert rel_err(y.float().cpu().numpy(), ref.cpu().numpy()) < 8e-3
