@@ -97,6 +97,7 @@ int af_cuda_init(int device, af_ctx **out) {
   if (const char *env = getenv("AF_DECODE_SLICE_ROWS")) ctx->decode_slice_rows = atoi(env);
   if (const char *env = getenv("AF_DECODE_HEAD_GROUPS")) ctx->decode_head_groups = atoi(env);
   if (const char *env = getenv("AF_SHARDED_HEAD_GROUPS")) ctx->sharded_head_groups = atoi(env);
+  if (const char *env = getenv("AF_PDL")) ctx->pdl = atoi(env) != 0;
   if (const char *env = getenv("AF_COMM_RESERVE_SMS")) ctx->comm_reserve_sms = atoi(env);
   ctx->magic = kCtxMagic;
   *out = ctx;
@@ -146,6 +147,8 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
     ctx->decode_head_groups = (int)value;
   } else if (!strcmp(name, "allow_split_k")) {
     ctx->allow_split_k = value != 0;
+  } else if (!strcmp(name, "pdl")) {
+    ctx->pdl = value != 0;
   } else if (!strcmp(name, "decode_transposed")) {
     if (value < 0 || value > 15) return af::fail(AF_ERR_ARG, "af_set_option: decode_transposed 0..15");
     ctx->decode_transposed = (int)value;

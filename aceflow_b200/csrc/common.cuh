@@ -9,6 +9,8 @@
 
 #include "../../include/aceflow_cuda.h"
 
+#include <utility>
+
 struct af_ctx {
   int device = 0;
   int num_sms = 0;
@@ -33,6 +35,7 @@ struct af_ctx {
   // NCCL communicator of the head-sharded prefill (sharded_prefill.cu)
   void *comm = nullptr;
   int comm_nranks = 0, comm_rank = 0;
+  int pdl = 1;  // decode chains use programmatic dependent launch
   // bf16 decode layer projections run transposed (bit 0 QKV, 1 W_o, 2 gate/up, 3 down)
   int decode_transposed = 15;
   int sharded_head_groups = 0;  // head groups pipelined against the all-gather (0: auto; 1: one gather)
@@ -89,6 +92,10 @@ struct GemmEpilogueArgs {
   int64_t split_stride = 0;  // split-K z stores its partial at out + z * split_stride (no atomics)
   int max_partials = 1;      // partial buffers available at out (split_stride != 0)
   int force_bn = 0, force_splits = 0;  // tile width / split count chosen by the caller (0: dispatch decides)
+  // Programmatic dependent launch: operand (1 = A, 2 = B) that does not depend
+  // on the previous kernel (the weights) and is prefetched before the wait;
+  // 0 = none.  pdl = launch with the attribute.
+  int pdl = 0, pre_operand = 0;
   int scale_residual = 0;  // the row scale multiplies the residual too: out = (acc + residual) * scale
   int max_ctas = 0;        // persistent kernel: at most this many CTAs (SMs left to a concurrent kernel); 0: all
 };
@@ -102,7 +109,10 @@ int tc_gemm_presplit(af_ctx *ctx, const float *A_hi, const float *A_lo, int64_t 
 // hi = tf32 part of src, lo = src - hi (exact); `zero` (n floats, may be
 // NULL) is cleared in the same pass.
 int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn,
-               float *zero = nullptr);
+               float *zero = nullptr, bool pdl = false);
+// bf16(RMSNorm(x) * w) rows (decoder.cu); pdl: programmatic dependent launch.
+int rmsnorm_to_bf16(af_ctx *ctx, const float *x, const float *w, uint16_t *y, int rows, int d, float eps,
+                    cudaStream_t st, const char *fn, bool pdl);
 
 // Chunkwise prefill (retention_chunkwise.cu).  A plan cuts each stream into
 // nseg segments of seg_len tokens (seg_len a multiple of the chunk length).
@@ -128,9 +138,28 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs, int batch, int H,
                           int dh, const float *norm_w, float *sumsq, cudaStream_t st, const char *fn, int out_bf16,
                           float *out_lo = nullptr, int h0 = 0, int hn = 0, int64_t qkv_hs = 0, int nsplit = 1,
-                          int64_t split_stride = 0);
+                          int64_t split_stride = 0, bool pdl = false);
 
 inline cudaStream_t stream_of(af_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Launches `kernel`, optionally as a programmatic dependent launch: it may
+// start while the previous kernel on the stream drains and must execute
+// griddep_wait() before it reads that kernel's results or writes anything.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 bool pdl, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -155,6 +184,10 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
   } while (0)
 
 // ------------------------------------------------------------------ device
+// Programmatic dependent launch: wait until the previous kernel on the
+// stream has completed and its memory is visible (a no-op otherwise).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float4 ld_stream(const float4 *p) {
   float4 v;
   asm volatile("ld.global.cs.v4.f32 {%0,%1,%2,%3}, [%4];"

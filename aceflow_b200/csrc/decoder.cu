@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(256)
   constexpr int D4 = 256 * V4;
   __shared__ float red[8];
   const size_t off = (size_t)blockIdx.x * D4;
+  griddep_wait();  // x comes from the kernel before (programmatic launch)
   float4 a[V4];
   float ss = 0.f;
 #pragma unroll
@@ -179,19 +180,7 @@ int af_rmsnorm_to_bf16(af_ctx *ctx, const float *x, const float *w, uint16_t *y,
   AF_ENTER(ctx, fn);
   AF_REQUIRE(x && y, "af_rmsnorm_to_bf16", "null pointer");
   AF_REQUIRE(rows >= 0 && d > 0 && d <= 12288, "af_rmsnorm_to_bf16", "bad sizes rows=%d d=%d", rows, d);
-  if (rows == 0) return AF_OK;
-  cudaStream_t st = af::stream_of(stream);
-  const bool al = af::aligned16(x) && af::aligned16(y) && (w == nullptr || af::aligned16(w));
-  const float4 *x4 = reinterpret_cast<const float4 *>(x);
-  const float4 *w4 = reinterpret_cast<const float4 *>(w);
-  uint2 *y4 = reinterpret_cast<uint2 *>(y);
-  if (al && d == 1024) rmsnorm_to_bf16_reg_kernel<1><<<rows, 256, 0, st>>>(x4, w4, y4, eps);
-  else if (al && d == 2048) rmsnorm_to_bf16_reg_kernel<2><<<rows, 256, 0, st>>>(x4, w4, y4, eps);
-  else if (al && d == 4096) rmsnorm_to_bf16_reg_kernel<4><<<rows, 256, 0, st>>>(x4, w4, y4, eps);
-  else if (al && d == 8192) rmsnorm_to_bf16_reg_kernel<8><<<rows, 256, 0, st>>>(x4, w4, y4, eps);
-  else
-    rmsnorm_to_bf16_kernel<<<rows, 256, (size_t)d * 4, st>>>(x, w, reinterpret_cast<__nv_bfloat16 *>(y), d, eps);
-  return af::launched(ctx, fn);
+  return af::rmsnorm_to_bf16(ctx, x, w, y, rows, d, eps, af::stream_of(stream), fn, false);
 }
 
 int af_argmax_rows(af_ctx *ctx, const float *logits, int rows, int V, int32_t *out, af_stream_t stream) {
@@ -227,6 +216,25 @@ int af_pack_gate_up(af_ctx *ctx, const void *src, void *dst, int f, int d, int e
 //   h = RMSNorm2(x); x += W_down (silu(g) * u),  [g|u] = h W_gate_up^T
 //                                  (SwiGLU in the gate/up GEMM epilogue)
 namespace af {
+int rmsnorm_to_bf16(af_ctx *ctx, const float *x, const float *w, uint16_t *y, int rows, int d, float eps,
+                    cudaStream_t st, const char *fn, bool pdl) {
+  if (rows == 0) return AF_OK;
+  const bool al = aligned16(x) && aligned16(y) && (w == nullptr || aligned16(w));
+  const float4 *x4 = reinterpret_cast<const float4 *>(x);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  uint2 *y4 = reinterpret_cast<uint2 *>(y);
+  pdl = pdl && ctx->pdl;
+  cudaError_t e = cudaSuccess;
+  const dim3 g(rows), b(256);
+  if (al && d == 1024) e = launch_kernel(rmsnorm_to_bf16_reg_kernel<1>, g, b, 0, st, pdl, x4, w4, y4, eps);
+  else if (al && d == 2048) e = launch_kernel(rmsnorm_to_bf16_reg_kernel<2>, g, b, 0, st, pdl, x4, w4, y4, eps);
+  else if (al && d == 4096) e = launch_kernel(rmsnorm_to_bf16_reg_kernel<4>, g, b, 0, st, pdl, x4, w4, y4, eps);
+  else if (al && d == 8192) e = launch_kernel(rmsnorm_to_bf16_reg_kernel<8>, g, b, 0, st, pdl, x4, w4, y4, eps);
+  else rmsnorm_to_bf16_kernel<<<rows, 256, (size_t)d * 4, st>>>(x, w, reinterpret_cast<__nv_bfloat16 *>(y), d, eps);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: launch: %s", fn, cudaGetErrorString(e));
+  return launched(ctx, fn);
+}
+
 int launch_rmsnorm_f32(af_ctx *ctx, const float *x, const float *res, const float *w, float *y, float *sum_out,
                        int rows, int d, float eps, cudaStream_t st, const char *fn);
 
@@ -320,8 +328,10 @@ extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, i
   cudaStream_t st = af::stream_of(stream);
   if (tr) {
     const int tm = ctx->decode_transposed;  // which projections run as W . x^T
-    // 1. h = bf16(RMSNorm1(x))
-    rc = af_rmsnorm_to_bf16(ctx, x, w->norm1, (uint16_t *)h, B, d, eps, stream);
+    // Every kernel of the chain is a programmatic dependent launch: the
+    // weight GEMMs stream their first weight tiles while the kernel before
+    // drains.  1. h = bf16(RMSNorm1(x))
+    rc = af::rmsnorm_to_bf16(ctx, x, w->norm1, (uint16_t *)h, B, d, eps, st, fn, true);
     if (rc) return rc;
     // 2. qkv (transposed: split-K partial buffers, summed by the state stream)
     int nsp = 1;
@@ -331,6 +341,8 @@ extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, i
       e1.ldo = 3 * d;
       e1.split_stride = (int64_t)B * 3 * d;
       e1.max_partials = af::kTransPartials;
+      e1.pdl = 1;
+      e1.pre_operand = 1;
       rc = af::gemm_t(ctx, w->w_qkv, 3 * d, h, B, d, e1, af::kTransPartials, st, fn);
       nsp = af::trans_splits(ctx, 3 * d, d, af::kTransPartials);
     } else {
@@ -340,7 +352,7 @@ extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, i
     // 3. state stream
     rc = af::launch_retention_step(ctx, state, state_batch_stride, gamma, qkv, qkv + d, qkv + 2 * d, 3 * (int64_t)d,
                                    (float *)o, d, B, H, dh, w->ret_norm, ss, st, fn, 1, nullptr, 0, 0, 0, nsp,
-                                   (int64_t)B * 3 * d);
+                                   (int64_t)B * 3 * d, true);
     if (rc) return rc;
     // 4. x += diag(1/rms) (o*w) W_o^T (transposed: atomics over K splits, 1/rms per column)
     if (tm & 2) {
@@ -352,13 +364,15 @@ extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, i
       e2.nparts = H;
       e2.inv_d = 1.0f / (float)d;
       e2.eps = eps;
+      e2.pdl = 1;
+      e2.pre_operand = 1;
       rc = af::gemm_t(ctx, w->w_o, d, o, B, d, e2, 8, st, fn);
     } else {
       rc = af::gemm(ctx, o, w->w_o, B, d, d, false, x, 0, x, ss, H, 1.0f / (float)d, eps, 0, st, fn);
     }
     if (rc) return rc;
     // 5. h = bf16(RMSNorm2(x)); 6. hid = silu(g) * u
-    rc = af_rmsnorm_to_bf16(ctx, x, w->norm2, (uint16_t *)h, B, d, eps, stream);
+    rc = af::rmsnorm_to_bf16(ctx, x, w->norm2, (uint16_t *)h, B, d, eps, st, fn, true);
     if (rc) return rc;
     if (tm & 4) {
       af::GemmEpilogueArgs e3;
@@ -366,6 +380,8 @@ extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, i
       e3.ldo = f;
       e3.out_bf16 = 1;
       e3.swiglu = 1;
+      e3.pdl = 1;
+      e3.pre_operand = 1;
       rc = af::gemm_t(ctx, w->w_gate_up, 2 * f, h, B, d, e3, 1, st, fn);
     } else {
       rc = af::gemm(ctx, h, w->w_gate_up, B, 2 * f, d, false, hid, 1, nullptr, nullptr, 0, 0.f, 0.f, 1, st, fn);
@@ -377,6 +393,8 @@ extern "C" int af_decoder_layer_decode(af_ctx *ctx, const af_layer_weights *w, i
       e4.out = x;
       e4.ldo = d;
       e4.accumulate = 1;
+      e4.pdl = 1;
+      e4.pre_operand = 1;
       return af::gemm_t(ctx, w->w_down, d, hid, B, f, e4, 8, st, fn);
     }
     return af::gemm(ctx, hid, w->w_down, B, d, f, false, x, 0, x, nullptr, 0, 0.f, 0.f, 0, st, fn);

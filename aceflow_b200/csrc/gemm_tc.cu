@@ -66,6 +66,7 @@ struct GemmEpilogue {
   int64_t split_stride;
   int scale_residual;      // the row scale multiplies the residual too: (acc + r) * scale
   int res_vec;             // residual base 16-byte aligned and ldr a whole number of 16-byte units
+  int pre_operand;         // 1 = A, 2 = B: loaded for the first ring slots before griddep_wait()
 };
 
 // v[e] += r[e] * rs for the 16 columns n..n+15 of one row (vector loads when
@@ -343,20 +344,38 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nk && !s_abort; ++kb) {
+      auto load_a = [&](int i, int kx) {
+        const int ka = kx % ep.a_kb, ma = m0 + (kx / ep.a_kb) * M;  // K-blocked A
+        tma_load_2d(stage_a(i), &tmA, &full[i], ka, ma);
+        if constexpr (C::PRE) tma_load_2d(lo_a(i, 0), &tmA2, &full[i], ka, ma);
+      };
+      auto load_b = [&](int i, int kx) {
+        tma_load_2d(stage_b(i), &tmB, &full[i], kx, n0);
+        if constexpr (C::PRE) tma_load_2d(lo_b(i, 0), &tmB2, &full[i], kx, n0);
+      };
+      // The operand that does not depend on the previous kernel (the
+      // weights) fills the free ring slots before the dependency wait; the
+      // other one follows it (always issued, so every slot's barrier completes).
+      const int pre = ep.pre_operand ? (nk < S ? nk : S) : 0;
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
+        if (ep.pre_operand == 1) load_a(kb, (kb_base + kb) * C::BK);
+        else load_b(kb, (kb_base + kb) * C::BK);
+      }
+      griddep_wait();
+      for (int kb = 0; kb < pre; ++kb) {
+        if (ep.pre_operand == 1) load_b(kb, (kb_base + kb) * C::BK);
+        else load_a(kb, (kb_base + kb) * C::BK);
+      }
+      int issued = pre;
+      for (int kb = pre; kb < nk && !s_abort; ++kb) {
         const int i = kb % S;
         const uint32_t ph = (kb / S) & 1;
         if (!mbar_wait(&empty[i], ph ^ 1)) { fail(); break; }
         const int kx = (kb_base + kb) * C::BK;
-        const int ka = kx % ep.a_kb, ma = m0 + (kx / ep.a_kb) * M;  // K-blocked A
         mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-        tma_load_2d(stage_a(i), &tmA, &full[i], ka, ma);
-        tma_load_2d(stage_b(i), &tmB, &full[i], kx, n0);
-        if constexpr (C::PRE) {
-          tma_load_2d(lo_a(i, 0), &tmA2, &full[i], ka, ma);
-          tma_load_2d(lo_b(i, 0), &tmB2, &full[i], kx, n0);
-        }
+        load_a(i, kx);
+        load_b(i, kx);
         issued = kb + 1;
       }
       // drain: every issued load has landed before this CTA may exit
@@ -426,6 +445,7 @@ __global__ void __launch_bounds__(192, 1)
     const bool ok = mbar_wait(accum, 0);
     if (!ok) fail();
     tc_fence_after();
+    griddep_wait();  // the epilogue reads row sums / residual and writes out
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = m0 + q * 32 + lane;
     const bool row_ok = row < M;
@@ -662,7 +682,7 @@ int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, in
 
 template <int BN, int MODE>
 int launch_tc(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void *B, const void *B2, int64_t ldb,
-              int M, int N, int K, int splits, const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
+              int M, int N, int K, int splits, const GemmEpilogue &ep, cudaStream_t st, const char *fn, bool pdl) {
   using C = TileCfg<BN, MODE>;
   CUtensorMap ta, tb, ta2, tb2;
   const bool fp32 = MODE != kBF16;
@@ -686,7 +706,9 @@ int launch_tc(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const voi
     attr_done = true;
   }
   const dim3 grid((N + BN - 1) / BN, (M + C::BM - 1) / C::BM, splits);
-  umma_gemm_kernel<BN, MODE><<<grid, 192, C::SMEM, st>>>(ta, tb, ta2, tb2, M, N, K, ep, ctx->dev_err);
+  const cudaError_t e = af::launch_kernel(umma_gemm_kernel<BN, MODE>, grid, dim3(192), C::SMEM, st, pdl, ta, tb, ta2,
+                                          tb2, M, N, K, ep, ctx->dev_err);
+  if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: launch: %s", fn, cudaGetErrorString(e));
   return af::launched(ctx, fn);
 }
 
@@ -706,6 +728,7 @@ __global__ void split_tf32_kernel(const float *__restrict__ src, float *__restri
 // of the same step accumulates into.
 __global__ void split_tf32_vec_kernel(const float4 *__restrict__ src, float4 *__restrict__ hi, float4 *__restrict__ lo,
                                       float4 *__restrict__ zero, int64_t n4) {
+  griddep_wait();  // programmatic launch: the previous kernel may still read `zero`
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     const float4 x = src[i];
     const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
@@ -736,7 +759,11 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
                   a.eps, a.residual, a.ldr,      a.swiglu, vec ? 1 : 0, 0,
                   a.a_kblock ? a.a_kblock : K, a.parts_block ? a.parts_block : (a.nparts > 0 ? a.nparts : 1),
                   a.trans, a.split_stride, a.scale_residual,
-                  a.residual && af::aligned16(a.residual) && (a.ldr * 4) % 16 == 0 ? 1 : 0};
+                  a.residual && af::aligned16(a.residual) && (a.ldr * 4) % 16 == 0 ? 1 : 0, 0};
+  // programmatic dependent launch (non-persistent kernels only; split-K with a
+  // memset before it is launched normally)
+  bool pdl = a.pdl && ctx->pdl;
+  ep.pre_operand = pdl ? a.pre_operand : 0;
   if (a.split_stride && (!a.trans || a.swiglu || a.out_bf16 || a.bias || a.residual || a.row_parts || a.accumulate ||
                          a.a_kblock))
     return af::fail(AF_ERR_ARG, "%s: partial buffers: transposed plain fp32 output only", fn);
@@ -815,6 +842,8 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
     if (a.residual == a.out) {
       ep.residual = nullptr;  // out already holds the residual: every split adds its partial into it
     } else {
+      pdl = false;
+      ep.pre_operand = 0;
       cudaError_t e = cudaMemsetAsync(a.out, 0, (size_t)M * a.ldo * 4, st);
       if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: zeroing the split-K output: %s", fn, cudaGetErrorString(e));
     }
@@ -825,7 +854,8 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
     if (bn == 256) return launch_persistent<256>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);
     return launch_persistent<128>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);
   }
-#define AF_LAUNCH(BNV) return launch_tc<BNV, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn)
+#define AF_LAUNCH(BNV) \
+  return launch_tc<BNV, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn, pdl)
   switch (bn) {
     case 256:
       if constexpr (MODE != kTF32S) AF_LAUNCH(256);
@@ -876,16 +906,16 @@ int tc_gemm_presplit(af_ctx *ctx, const float *A_hi, const float *A_lo, int64_t 
 }
 
 int split_tf32(af_ctx *ctx, const float *src, float *hi, float *lo, int64_t n, cudaStream_t st, const char *fn,
-               float *zero) {
+               float *zero, bool pdl) {
   if (n == 0) return AF_OK;
   if (n % 4 == 0 && aligned16(src) && aligned16(hi) && aligned16(lo) && (!zero || aligned16(zero))) {
     const int64_t n4 = n / 4;
     int64_t blocks = (n4 + 255) / 256;
     if (blocks > (int64_t)ctx->num_sms * 8) blocks = (int64_t)ctx->num_sms * 8;
-    split_tf32_vec_kernel<<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const float4 *>(src),
-                                                            reinterpret_cast<float4 *>(hi),
-                                                            reinterpret_cast<float4 *>(lo),
-                                                            reinterpret_cast<float4 *>(zero), n4);
+    const cudaError_t e = launch_kernel(split_tf32_vec_kernel, dim3((unsigned)blocks), dim3(256), 0, st, pdl && ctx->pdl,
+                                        reinterpret_cast<const float4 *>(src), reinterpret_cast<float4 *>(hi),
+                                        reinterpret_cast<float4 *>(lo), reinterpret_cast<float4 *>(zero), n4);
+    if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: launch: %s", fn, cudaGetErrorString(e));
     return launched(ctx, fn);
   }
   if (zero) AF_CUDA(cudaMemsetAsync(zero, 0, (size_t)n * sizeof(float), st), fn);

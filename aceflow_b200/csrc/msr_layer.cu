@@ -155,7 +155,7 @@ int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const 
   if (G < 2 || H % G != 0 || G > af_ctx::kMaxSlices) G = 1;
   const int Hg = H / G, Ng = 3 * Hg * dh;
   // the sequential step's W_o GEMM accumulates into out, zeroed here
-  int rc = split_tf32(ctx, x, x_hi, x_lo, (int64_t)B * d, st, fn, G == 1 ? out : nullptr);
+  int rc = split_tf32(ctx, x, x_hi, x_lo, (int64_t)B * d, st, fn, G == 1 ? out : nullptr, G == 1);
   if (rc) return rc;
   auto qkv_gemm = [&](int g, cudaStream_t s) {
     GemmEpilogueArgs e;
@@ -182,11 +182,13 @@ int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const 
       e.max_partials = kQkvPartials;
       e.force_bn = B > 128 ? 256 : 128;
       e.force_splits = nsp;
+      e.pdl = 1;  // programmatic dependent launches: weight tiles stream while the split kernel drains
+      e.pre_operand = 1;
       rc = tc_gemm_presplit(ctx, wq_hi, wq_lo, d, x_hi, x_lo, d, 3 * d, B, d, e, st, fn);
       if (rc) return rc;
       rc = launch_retention_step(ctx, state, sbs, gamma, qkv, qkv + dh, qkv + 2 * dh, 3 * (int64_t)d, o_hi, d, B, H,
                                  dh, ret_norm_w, sumsq, st, fn, 0, o_lo, 0, H, 3 * (int64_t)dh, nsp,
-                                 (int64_t)B * 3 * d);
+                                 (int64_t)B * 3 * d, true);
     } else {
       rc = qkv_gemm(0, st);
       if (rc) return rc;
@@ -197,6 +199,8 @@ int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const 
     e2.out = out;
     e2.ldo = d;
     e2.accumulate = 1;  // into the zeroed out: split-K needs no memset
+    e2.pdl = 1;
+    e2.pre_operand = 2;  // W_o (B) does not depend on the state stream
     e2.row_parts = sumsq;
     e2.nparts = H;
     e2.inv_d = 1.0f / (float)d;

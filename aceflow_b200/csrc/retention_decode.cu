@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(THREADS)
   const float *qh = q + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
   const float *kh = k + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
   const float *vh = v + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
+  griddep_wait();  // q, k, v come from the kernel before (programmatic launch)
   for (int i = threadIdx.x; i < DH; i += THREADS) {
     float kk = kh[i], qq = qh[i];
     for (int z = 1; z < hg.nsplit; ++z) {
@@ -344,7 +345,7 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
                           const float *k, const float *v, int64_t qs, float *out, int64_t out_rs,
                           int batch, int H, int dh, const float *norm_w, float *sumsq, cudaStream_t st,
                           const char *fn, int out_bf16, float *out_lo, int h0, int hn, int64_t qkv_hs, int nsplit,
-                          int64_t split_stride) {
+                          int64_t split_stride, bool pdl) {
   if (batch == 0) return AF_OK;
   if (nsplit < 1) nsplit = 1;
   if (hn <= 0) {  // all heads, q/k/v head-contiguous
@@ -367,8 +368,10 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
   if (out_lo && (!aligned16(out_lo) || !(dh == 256 || dh == 128 || dh == 64)))
     return fail(AF_ERR_ARG, "%s: split output needs head_dim 64, 128 or 256 and an aligned buffer", fn);
   if (fast && dh == 256) {
-    retention_step_kernel<256, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
-                                                          norm_w, sumsq, out_bf16, out_lo, hgp);
+    const cudaError_t e = launch_kernel(retention_step_kernel<256, 256>, grid, dim3(256), 0, st, pdl && ctx->pdl, state,
+                                        state_bs, gamma, q, k, v, qs, out, out_rs, H, norm_w, sumsq, out_bf16, out_lo,
+                                        hgp);
+    if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: launch: %s", fn, cudaGetErrorString(e));
   } else if (fast && dh == 128) {
     retention_step_kernel<128, 256><<<grid, 256, 0, st>>>(state, state_bs, gamma, q, k, v, qs, out, out_rs, H,
                                                           norm_w, sumsq, out_bf16, out_lo, hgp);
