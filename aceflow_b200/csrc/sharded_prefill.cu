@@ -164,10 +164,10 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
   // Head groups: the all-gather of group i runs on a side stream while group
   // i+1 is projected and retained (the last group's gather stays exposed);
   // one W_o GEMM then reads every group's gather buffer.  Needs per-group
-  // state views (one stream, or no state).  sharded_head_groups 0 = auto:
-  // 2 groups from 4 ranks up (below that the gather is short and the SMs left
-  // to it cost more than it hides).
-  int G = ctx->sharded_head_groups > 0 ? ctx->sharded_head_groups : (g >= 4 ? 2 : 1);
+  // state views (one stream, or no state).  sharded_head_groups 0 = auto = 1:
+  // measured on B200 at T=65536, d=4096, the overlap did not pay (8 GPUs
+  // 2.151 vs 2.165 ms, 4 GPUs 3.267 vs 3.175 ms with 2 groups).
+  int G = ctx->sharded_head_groups > 0 ? ctx->sharded_head_groups : 1;
   if (B > 1 && (state_in || state_out)) G = 1;
   while (G > 1 && Hl % G != 0) --G;
   if (G > af_ctx::kMaxSlices) G = af_ctx::kMaxSlices;

@@ -67,7 +67,7 @@ int af_check_device(af_ctx *ctx, int *flags, int reset);
  *   "chunkwise_segments" >= 0  sequence segments per stream in the chunkwise prefill
  *                              (default 0: enough to put one CTA on every SM; 1: none)
  *   "sharded_head_groups" 0..8 head groups af_prefill_head_sharded pipelines against
- *                              its all-gather (default 0: 2 from 4 ranks up, else 1)
+ *                              its all-gather (default 0 = 1: measured not to pay)
  *   "comm_reserve_sms"   0..64 SMs the overlapped kernels leave to the collective (default 16)
  *   "decode_transposed"  0..15 bf16 af_decoder_layer_decode projections computed as
  *                              W . x^T (bit 0 QKV, 1 W_o, 2 gate/up, 3 down; default 15)
