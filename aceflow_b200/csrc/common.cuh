@@ -36,6 +36,7 @@ struct af_ctx {
   void *comm = nullptr;
   int comm_nranks = 0, comm_rank = 0;
   int pdl = 1;  // decode chains use programmatic dependent launch
+  int gemm_pair = 1;  // large bf16 GEMMs on CTA pairs (cta_group::2, 256 x 256 tiles)
   // bf16 decode layer projections run transposed (bit 0 QKV, 1 W_o, 2 gate/up, 3 down)
   int decode_transposed = 15;
   int sharded_head_groups = 0;  // head groups pipelined against the all-gather (0: auto; 1: one gather)

@@ -626,6 +626,178 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// Persistent bf16 GEMM on CTA pairs (cta_group::2): a cluster of two CTAs
+// on the two SMs of a TPC computes 256 x 256 tiles.  Each CTA loads its own
+// 128 rows of A and 128 rows of B per K slice (32 KB per stage, so a stage
+// carries a third fewer bytes per MMA flop than a 128 x 256 tile on one SM);
+// the rank-0 CTA issues the MMAs, whose accumulator rows land in each CTA's
+// own TMEM (two 256-column buffers: one tile's epilogue overlaps the next
+// tile's MMAs).  Barriers:
+//   full[i]  (rank 0)  both CTAs' TMA bytes of stage i landed
+//   empty[i] (each)    the MMAs reading stage i retired (commit to both CTAs)
+//   accf[b]  (each)    accumulator b holds a finished tile (commit to both)
+//   acce[b]  (rank 0)  both CTAs' epilogues (256 threads) read accumulator b
+struct PairCfg {
+  static constexpr int BM = 256, BN = 256, HALF = 128, BK = 64;
+  static constexpr int A_BYTES = HALF * 128, B_BYTES = HALF * 128, STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM_LIMIT = 227 * 1024 - 64;
+  static constexpr int STAGES = (SMEM_LIMIT - 1024 - 256) / STAGE_BYTES;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  static_assert(STAGES >= 2 && 2 * STAGES + 5 <= 32, "ring depth / barrier block");
+};
+
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
+                          int N, int K, GemmEpilogue ep, int *err) {
+  using C = PairCfg;
+  constexpr int S = C::STAGES;
+  constexpr uint32_t TM_COLS = 512;  // two 256-column accumulators
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * C::STAGE_BYTES);
+  uint64_t *full = bars, *empty = bars + S;
+  uint64_t *accf = bars + 2 * S, *acce = bars + 2 * S + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 4);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const int n_tiles = (N + C::BN - 1) / C::BN, m_tiles = (M + C::BM - 1) / C::BM;
+  const int total = n_tiles * m_tiles;
+  const int nk = (K + C::BK - 1) / C::BK;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 256);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist and their TMEM is allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto stage_a = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES; };
+  auto stage_b = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES + C::A_BYTES; };
+  auto fail = [&]() {
+    s_abort = 1;
+    atomicOr(err, 1 << AF_ERR_TIMEOUT);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;  // K slices issued, over all tiles
+      for (int t = cid; t < total && !s_abort; t += ncl) {
+        const int m0 = (t / n_tiles) * C::BM + (int)rank * C::HALF, n0 = (t % n_tiles) * C::BN + (int)rank * C::HALF;
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int i = g % S;
+          if (!mbar_wait(&empty[i], ((g / S) & 1) ^ 1)) { fail(); break; }
+          if (rank == 0) mbar_arrive_expect_tx(&full[i], 2 * C::STAGE_BYTES);
+          const uint32_t fb = mapa_shared(&full[i], 0);
+          const int kx = kb * C::BK;
+          tma_load_2d_pair(stage_a(i), &tmA, fb, kx % ep.a_kb, m0 + (kx / ep.a_kb) * M);
+          tma_load_2d_pair(stage_b(i), &tmB, fb, kx, n0);
+        }
+      }
+      if (rank == 0) {
+        for (int x = g - S < 0 ? 0 : g - S; x < g; ++x)  // both CTAs' loads still in flight
+          if (!mbar_wait(&full[x % S], (x / S) & 1)) { fail(); break; }
+      } else if (s_abort) {
+        // this CTA's loads complete the other CTA's barriers: give them time to land
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 100000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0) {
+      constexpr uint32_t idesc = idesc_f32acc(kFmtBF16, C::BM, C::BN);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int t = cid; t < total && ok; t += ncl, ++it) {
+        const int b = it & 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&acce[b], ((it >> 1) & 1) ^ 1));
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * C::BN);
+        for (int kb = 0; kb < nk; ++kb, ++g) {
+          const int i = g % S;
+          ok = __all_sync(0xffffffffu, mbar_wait(&full[i], (g / S) & 1));
+          if (!ok || __any_sync(0xffffffffu, s_abort != 0)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint64_t da = sdesc_k_sw128(stage_a(i)), db = sdesc_k_sw128(stage_b(i));
+#pragma unroll
+            for (int k = 0; k < C::BK / 16; ++k) {
+              const uint64_t off = (uint64_t)(k * 32) >> 4;
+              umma_bf16_pair(acc, da + off, db + off, idesc, (kb | k) != 0);
+            }
+            umma_commit_pair(mapa_shared(&empty[i], 0));
+            umma_commit_pair(mapa_shared(&empty[i], 1));
+          }
+          __syncwarp();
+        }
+        if (lane == 0 && ok) {
+          umma_commit_pair(mapa_shared(&accf[b], 0));
+          umma_commit_pair(mapa_shared(&accf[b], 1));
+        }
+        __syncwarp();
+      }
+      if (!ok && lane == 0) fail();
+    }
+  } else {
+    const int q = warp & 3;
+    int it = 0;
+    for (int t = cid; t < total; t += ncl, ++it) {
+      const int b = it & 1;
+      const bool ok = mbar_wait(&accf[b], (it >> 1) & 1);
+      if (!ok) {
+        fail();
+        break;
+      }
+      tc_fence_after();
+      const int m0 = (t / n_tiles) * C::BM, n0 = (t % n_tiles) * C::BN;
+      const int row = m0 + (int)rank * C::HALF + q * 32 + lane;
+      const bool row_ok = row < M;
+      float scale = 1.f;
+      if (ep.row_parts && row_ok) scale = row_scale(ep, row, M);
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * C::BN);
+      auto load16 = [&](int col, float (&v)[16]) {
+        __syncwarp();
+        tmem_ld16(tbase + col, v);
+        tmem_wait_ld();
+      };
+      store_tile<C::BN>(ep, load16, row, row_ok, n0, N, true, scale, true);
+      tc_fence_before();
+      if (rank == 0) mbar_arrive(&acce[b]);
+      else mbar_arrive_cluster(mapa_shared(&acce[b], 0));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA frees TMEM or exits while the pair's MMAs may touch it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, TM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -677,6 +849,40 @@ int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, in
   const int cap = ep_max_ctas > 0 && ep_max_ctas < ctx->num_sms ? ep_max_ctas : ctx->num_sms;
   const int grid = (int)(total < cap ? total : cap);
   umma_gemm_persistent_kernel<BN><<<grid, 192, C::SMEM, st>>>(ta, tb, M, N, K, ep, ctx->dev_err);
+  return af::launched(ctx, fn);
+}
+
+int launch_pair(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
+                const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
+  using C = PairCfg;
+  CUtensorMap ta, tb;
+  int rc = make_kmajor_map(&ta, A, false, (K / ep.a_kb) * M, ep.a_kb, lda, C::HALF, fn);
+  if (rc) return rc;
+  rc = make_kmajor_map(&tb, B, false, N, K, ldb, C::HALF, fn);
+  if (rc) return rc;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(umma_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)C::SMEM);
+    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
+    attr_done = true;
+  }
+  const int64_t total = (int64_t)((N + C::BN - 1) / C::BN) * ((M + C::BM - 1) / C::BM);
+  const int pairs = (int)(total < ctx->num_sms / 2 ? total : ctx->num_sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_kernel, ta, tb, M, N, K, ep, ctx->dev_err);
+  if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: pair launch: %s", fn, cudaGetErrorString(e));
   return af::launched(ctx, fn);
 }
 
@@ -851,6 +1057,8 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
   // large bf16 GEMMs (two or more waves of tiles): persistent kernel
   if (MODE == kBF16 && splits == 1 && !a.trans && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms &&
       !getenv("AF_GEMM_NO_PERSIST")) {
+    if (bn == 256 && ctx->gemm_pair && !a.max_ctas && M >= 256 && N >= 256)
+      return launch_pair(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
     if (bn == 256) return launch_persistent<256>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);
     return launch_persistent<128>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);
   }

@@ -106,3 +106,34 @@ def test_bf16_gemm_bias_residual_epilogue(dev, M, N, K, pad):
     cuda_ops.gemm_bf16(a, b, inplace, bias=bias, residual=inplace)
     assert rel_err(inplace.cpu().numpy(), ref.cpu().numpy()) < 1e-5
     _check(dev)
+
+
+@pytest.mark.parametrize("M,N,K", [(8192, 2048, 2048), (8292, 2112, 1000)])
+def test_bf16_gemm_cta_pair_matches_fp64(dev, M, N, K):
+    """Large bf16 GEMMs run on CTA pairs (cta_group::2, 256 x 256 tiles):
+    ragged M, N, K, with bias, residual and the 1/rms row scale, equal to the
+    fp64 product and to the one-SM persistent kernel."""
+    from aceflow_b200 import _lib, cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g, device=dev).bfloat16()
+    b = (0.05 * torch.randn(N, K, generator=g, device=dev)).bfloat16()
+    bias = torch.randn(N, generator=g, device=dev)
+    res = torch.randn(M, N, generator=g, device=dev)
+    parts = torch.rand(M, 3, generator=g, device=dev) * 10
+    scale = 1.0 / torch.sqrt(parts.double().sum(1, keepdim=True) / K + 1e-6)
+    ref = (a.double() @ b.double().t()) * scale + bias.double() + res.double()
+    out = torch.empty(M, N, device=dev)
+    cuda_ops.gemm_bf16(a, b, out, parts, inv_d=1.0 / K, eps=1e-6, bias=bias, residual=res)
+    torch.cuda.synchronize()
+    _check(dev)
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+    _lib.set_option(0, "gemm_pair", 0)
+    try:
+        one = torch.empty(M, N, device=dev)
+        cuda_ops.gemm_bf16(a, b, one, parts, inv_d=1.0 / K, eps=1e-6, bias=bias, residual=res)
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_option(0, "gemm_pair", 1)
+    assert rel_err(out.cpu().numpy(), one.cpu().numpy()) < 1e-6
+    _check(dev)
