@@ -19,9 +19,11 @@
 //   output  O^T = S^T Q_c^T         M=128 N=64  K=256  A = bf16(S^T) K-major (written)
 //              + V_c^T P'^T                       K=64   A = V_c MN-major (TMA), B = P' (written)
 //   update  S^T += Vs^T K_c        M=128 N=256 K=64   A = decay-scaled V (written), B = K_c MN-major
-// Warp roles (192 threads): warp 0 TMA producer; warp 1 TMEM allocator and
-// single-thread tcgen05.mma issuer; warps 2-5 math (TMEM ld/st, decay masks
-// generated in registers, bf16 operand tiles, output + RMSNorm partials).
+// Warp roles (320 threads): warp 0 TMA producer; warp 1 TMEM allocator and
+// single-thread tcgen05.mma issuer; warps 2-9 math (TMEM ld/st, decay masks
+// generated in registers, bf16 operand tiles, output + RMSNorm partials):
+// two warps per TMEM lane quadrant, each taking half of the columns of every
+// step, so the per-chunk chain of TMEM round trips is split in two.
 //
 // Inputs come straight from the bf16 QKV projection [B*T][3d] through one
 // 3-D tensor map (d_model fastest, then T, then B) so the T edge zero-fills.
@@ -118,15 +120,17 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
       : "memory");
 }
 
-__device__ __forceinline__ void math_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+constexpr int MATH_THREADS = 256;  // warps 2-9
 
-// Named barrier over the 128 math threads that also ORs a predicate, so every
+__device__ __forceinline__ void math_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Named barrier over the 256 math threads that also ORs a predicate, so every
 // participant leaves with the same answer (s_abort may change concurrently).
 __device__ __forceinline__ bool math_sync_or(bool pred) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      "bar.red.or.pred q, 1, 256, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
       : "r"((uint32_t)pred)
       : "memory");
@@ -134,7 +138,7 @@ __device__ __forceinline__ bool math_sync_or(bool pred) {
 }
 
 template <bool STATE_ONLY>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(320, 1)
     retention_chunkwise_kernel(const __grid_constant__ CUtensorMap tm, ChunkParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -163,10 +167,10 @@ __global__ void __launch_bounds__(192, 1)
     s_abort = 0;
     mbar_init(bar_load, 1);
     mbar_init(bar_sc, 1);
-    mbar_init(bar_math, 128);
+    mbar_init(bar_math, MATH_THREADS);
     mbar_init(bar_o, 1);
     mbar_init(bar_upd, 1);
-    mbar_init(bar_out, 128);
+    mbar_init(bar_out, MATH_THREADS);
     fence_barrier_init();
     prefetch_tmap(&tm);
   }
@@ -286,15 +290,16 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ math warps
-    const int q = warp & 3;
-    const int mt = threadIdx.x - 64;   // 0..127
+    const int q = warp & 3;            // TMEM lane quadrant
+    const int half = (warp - 2) >> 2;  // which half of the columns this warp takes
+    const int mt = threadIdx.x - 64;   // 0..255
     const int v = q * 32 + lane;       // TMEM lane of this thread = value index in the slice
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     // initial state S^T[v][k] = S[k][v]
     {
       const float *sin = (!STATE_ONLY && p.state_in) ? p.state_in + ((size_t)bsh * DH) * DH + slice * VS + v : nullptr;
 #pragma unroll 1
-      for (int k0 = 0; k0 < DH; k0 += 16) {
+      for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 16) {
         float x[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) x[j] = sin ? sin[(size_t)(k0 + j) * DH] : 0.f;
@@ -313,7 +318,7 @@ __global__ void __launch_bounds__(192, 1)
         if (!ok) s_abort = 1;
         if (ok) {
 #pragma unroll 2
-          for (int i = mt; i < V_BYTES / 16; i += 128) {
+          for (int i = mt; i < V_BYTES / 16; i += MATH_THREADS) {
             const int off = i * 16;
             const int j = (off % BOX) / 128;
             const float sc = j < L ? gpow[L - 1 - j] * tail : 0.f;
@@ -344,7 +349,7 @@ __global__ void __launch_bounds__(192, 1)
       // (a) S_op = bf16(S^T) (K-major [v][k]); S^T *= gamma^L in TMEM
       const float gL = gpow[L];
 #pragma unroll 1
-      for (int k0 = 0; k0 < DH; k0 += 64) {  // 64 columns per TMEM round trip
+      for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 64) {  // 64 columns per TMEM round trip
         float x[64];
         __syncwarp();
 #pragma unroll
@@ -369,7 +374,7 @@ __global__ void __launch_bounds__(192, 1)
       if (!ok) s_abort = 1;
       if (ok) {
 #pragma unroll 2
-        for (int i = mt; i < V_BYTES / 16; i += 128) {
+        for (int i = mt; i < V_BYTES / 16; i += MATH_THREADS) {
           const int off = i * 16;
           const int j = (off % BOX) / 128;  // token row of this 16-byte chunk
           const float sc = j < L ? gpow[L - 1 - j] : 0.f;
@@ -383,24 +388,28 @@ __global__ void __launch_bounds__(192, 1)
           *reinterpret_cast<uint4 *>(sm + VT_OFF + off) = raw;
         }
       }
-      // (c) P'[i][j] = Sc[i][j] * gamma^-(j+1) for j <= i (rows i = 16q + lane, lanes < 16)
+      // (c) P'[i][j] = Sc[i][j] * gamma^-(j+1) for j <= i (rows i = 16q + lane,
+      //     lanes < 16; this warp's half of the columns j)
       ok = ok && mbar_wait(bar_sc, c & 1);
       if (!ok) s_abort = 1;
       if (ok) {
         tc_fence_after();
         const int i = q * 16 + lane;
-        float x[C];
+        constexpr int CH = C / 2;
+        const int j0 = half * CH;
+        float x[CH];
         __syncwarp();
 #pragma unroll
-        for (int u = 0; u < C / 16; ++u) tmem_ld16(tmem + lane_base + TM_SC + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+        for (int u = 0; u < CH / 16; ++u)
+          tmem_ld16(tmem + lane_base + TM_SC + j0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
         tmem_wait_ld();
         if (lane < 16) {
 #pragma unroll
-          for (int j = 0; j < C; ++j) x[j] = (j <= i) ? x[j] * ginv[j] : 0.f;
+          for (int j = 0; j < CH; ++j) x[j] = (j0 + j <= i) ? x[j] * ginv[j0 + j] : 0.f;
 #pragma unroll
-          for (int c16 = 0; c16 < C / 8; ++c16) {
+          for (int c16 = 0; c16 < CH / 8; ++c16) {
             const float *y = x + 8 * c16;
-            *reinterpret_cast<uint4 *>(sm + P_OFF + sw128(i, c16)) =
+            *reinterpret_cast<uint4 *>(sm + P_OFF + sw128(i, j0 / 8 + c16)) =
                 make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
           }
         }
@@ -416,25 +425,28 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const int col = h * DH + slice * VS + v;
       const float wv = p.norm_w ? p.norm_w[col] : 1.f;
-      __nv_bfloat16 *orow = p.out + ((size_t)b * p.T + t0) * d + col;
-      float x[C];
+      constexpr int CH = C / 2;  // this warp's half of the chunk's tokens
+      const int i0 = half * CH;
+      __nv_bfloat16 *orow = p.out + ((size_t)b * p.T + t0 + i0) * d + col;
+      float x[CH];
       __syncwarp();
 #pragma unroll
-      for (int u = 0; u < C / 16; ++u) tmem_ld16(tmem + lane_base + TM_O + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+      for (int u = 0; u < CH / 16; ++u)
+        tmem_ld16(tmem + lane_base + TM_O + i0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar_out);  // O^T is in registers: the next chunk's MMAs may overwrite it
 #pragma unroll
-      for (int i = 0; i < C; ++i) {
-        x[i] *= gpow[i + 1];
-        if (i < L) orow[(size_t)i * d] = __float2bfloat16(x[i] * wv);
+      for (int i = 0; i < CH; ++i) {
+        x[i] *= gpow[i0 + i + 1];
+        if (i0 + i < L) orow[(size_t)i * d] = __float2bfloat16(x[i] * wv);
         x[i] *= x[i];
       }
       // column sums of o^2 over the warp's 32 values of v: recursive halving
-      // (lane l ends with tokens 2l and 2l+1), 62 shuffles for 64 tokens
-      static_assert(C == 64, "the halving schedule below is written for 64 tokens");
+      // (lane l ends with token i0 + l), 31 shuffles for 32 tokens
+      static_assert(C == 64, "the halving schedule below is written for 2 x 32 tokens");
 #pragma unroll
-      for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+      for (int o = 16, n = 16; o >= 1; o >>= 1, n >>= 1) {
         const bool up = lane & o;
 #pragma unroll
         for (int j = 0; j < n; ++j) {
@@ -443,8 +455,7 @@ __global__ void __launch_bounds__(192, 1)
           x[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
         }
       }
-      red[q * C + 2 * lane] = x[0];
-      red[q * C + 2 * lane + 1] = x[1];
+      red[q * C + i0 + lane] = x[0];
       math_sync();
       if (p.sumsq && mt < L) {
         const float s2 = red[mt] + red[C + mt] + red[2 * C + mt] + red[3 * C + mt];
@@ -463,7 +474,7 @@ __global__ void __launch_bounds__(192, 1)
         const size_t sidx = STATE_ONLY ? (size_t)bsh : (size_t)(b * p.H + h);
         float *so = p.state_out + (sidx * DH) * DH + slice * VS + v;
 #pragma unroll 1
-        for (int k0 = 0; k0 < DH; k0 += 16) {
+        for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 16) {
           float x[16];
           __syncwarp();
           tmem_ld16(tmem + lane_base + TM_S + k0, x);
@@ -516,7 +527,7 @@ int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const ChunkParams &p, c
     if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
     attr = true;
   }
-  retention_chunkwise_kernel<SO><<<p.B * p.nseg * p.H * NSL, 192, SMEM, st>>>(tm, p);
+  retention_chunkwise_kernel<SO><<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, SMEM, st>>>(tm, p);
   return af::launched(ctx, fn);
 }
 
