@@ -140,40 +140,51 @@ struct TileCfg {
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
 // Epilogue of one 128 x BN tile for the calling warp's 32 rows: reads the
-// accumulator through load16 (warp-collective TMEM loads), applies row scale,
-// bias, residual or SwiGLU, and stores (or atomically adds, for split-K).
-template <int BN, class Load16>
-__device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load16, int row, bool row_ok, int n0,
-                                           int N, bool ok, float scale, bool first) {
+// accumulator through load16 (warp-collective TMEM loads; wait_ld() waits for
+// the loads issued so far, so up to 64 columns are in flight per round trip),
+// applies row scale, bias, residual or SwiGLU, and stores (or atomically adds,
+// for split-K).
+template <int BN, class Load16, class WaitLd>
+__device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load16, WaitLd &&wait_ld, int row,
+                                           bool row_ok, int n0, int N, bool ok, float scale, bool first) {
   if (ep.swiglu && !ep.trans) {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float g[16], u[16];
-      load16(c, g);
-      load16(c + 16, u);
-      const int nout = (n0 + c) / 2;  // first output column of this group
-      if (ok && row_ok && n0 + c + 32 <= N) {
-        float hh[16];
+    for (int c0 = 0; c0 < BN; c0 += 64) {
+      float gu[4][16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const float gg = g[e] * scale, uu = u[e] * scale;
-          hh[e] = gg / (1.0f + expf(-gg)) * uu;
-        }
-        if (ep.out_bf16) {
-          __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + nout;
-          uint32_t pk[8];
+      for (int u = 0; u < 4; ++u)
+        if (c0 + 16 * u < BN) load16(c0 + 16 * u, gu[u]);
+      wait_ld();
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            __nv_bfloat162 b2 = __floats2bfloat162_rn(hh[2 * e], hh[2 * e + 1]);
-            pk[e] = *reinterpret_cast<uint32_t *>(&b2);
+      for (int pr = 0; pr < 2; ++pr) {
+        const int c = c0 + 32 * pr;
+        if (c >= BN) break;
+        const float(&g)[16] = gu[2 * pr];
+        const float(&u)[16] = gu[2 * pr + 1];
+        const int nout = (n0 + c) / 2;  // first output column of this group
+        if (ok && row_ok && n0 + c + 32 <= N) {
+          float hh[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float gg = g[e] * scale, uu = u[e] * scale;
+            hh[e] = gg / (1.0f + expf(-gg)) * uu;
           }
-          reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-        } else {
-          float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + nout;
+          if (ep.out_bf16) {
+            __nv_bfloat16 *o = reinterpret_cast<__nv_bfloat16 *>(ep.out) + (size_t)row * ep.ldo + nout;
+            uint32_t pk[8];
 #pragma unroll
-          for (int e = 0; e < 16; e += 4)
-            *reinterpret_cast<float4 *>(o + e) = make_float4(hh[e], hh[e + 1], hh[e + 2], hh[e + 3]);
+            for (int e = 0; e < 8; ++e) {
+              __nv_bfloat162 b2 = __floats2bfloat162_rn(hh[2 * e], hh[2 * e + 1]);
+              pk[e] = *reinterpret_cast<uint32_t *>(&b2);
+            }
+            reinterpret_cast<uint4 *>(o)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            reinterpret_cast<uint4 *>(o)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          } else {
+            float *o = reinterpret_cast<float *>(ep.out) + (size_t)row * ep.ldo + nout;
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+              *reinterpret_cast<float4 *>(o + e) = make_float4(hh[e], hh[e + 1], hh[e + 2], hh[e + 3]);
+          }
         }
       }
     }
@@ -187,6 +198,7 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
     for (int c = 0; c < BN; c += 16) {
       float v[16];
       load16(c, v);
+      wait_ld();
       const int n = n0 + c;
       if (ep.swiglu) {
         // rows in groups of 16 gate then 16 up: lane l < 16 takes the up value
@@ -222,12 +234,9 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
         }
     }
   } else {
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      float v[16];
-      load16(c, v);
-      const int n = n0 + c;
-      if (!ok || !row_ok || n >= N) continue;
+    // one 16-column chunk: scale, bias, residual, store / atomic add
+    auto emit16 = [&](float(&v)[16], int n) {
+      if (!ok || !row_ok || n >= N) return;
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
         v[e] *= scale;
@@ -243,7 +252,7 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
         } else {
           for (int e = 0; e < 16 && n + e < N; ++e) atomicAdd(o + e, v[e]);
         }
-        continue;
+        return;
       }
       if (ep.residual)
         add_residual16(v, ep.residual + (size_t)row * ep.ldr + n, n, N, ep.scale_residual ? scale : 1.f, ep.res_vec);
@@ -271,6 +280,17 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
           for (int e = 0; e < 16 && n + e < N; ++e) o[e] = v[e];
         }
       }
+    };
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 64) {
+      float vv[4][16];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (c0 + 16 * u < BN) load16(c0 + 16 * u, vv[u]);
+      wait_ld();
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (c0 + 16 * u < BN) emit16(vv[u], n0 + c0 + 16 * u);
     }
   }
 }
@@ -457,7 +477,7 @@ __global__ void __launch_bounds__(192, 1)
     auto load16 = [&](int col, float (&v)[16]) {
       __syncwarp();
       tmem_ld16(tbase + col, v);
-      if constexpr (TF32X3) {
+      if constexpr (TF32X3) {  // sums the accumulators (waits inside)
         float w[16];
         tmem_ld16(tbase + (uint32_t)(C::NACC * BN) + col, w);
         tmem_wait_ld();
@@ -471,11 +491,12 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int e = 0; e < 16; ++e) v[e] += w[e];
         }
-      } else {
-        tmem_wait_ld();
       }
     };
-    store_tile<BN>(ep, load16, row, row_ok, n0, N, ok, scale, blockIdx.z == 0);
+    auto wait_ld = [&]() {
+      if constexpr (!TF32X3) tmem_wait_ld();
+    };
+    store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, ok, scale, blockIdx.z == 0);
   }
   tc_fence_before();
   __syncthreads();
@@ -611,9 +632,9 @@ __global__ void __launch_bounds__(192, 1)
       auto load16 = [&](int col, float (&v)[16]) {
         __syncwarp();
         tmem_ld16(tbase + col, v);
-        tmem_wait_ld();
       };
-      store_tile<BN>(ep, load16, row, row_ok, n0, N, true, scale, true);
+      auto wait_ld = [&]() { tmem_wait_ld(); };
+      store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, true, scale, true);
       tc_fence_before();
       mbar_arrive(&acce[b]);
     }
@@ -781,9 +802,9 @@ __global__ void __launch_bounds__(192, 1)
       auto load16 = [&](int col, float (&v)[16]) {
         __syncwarp();
         tmem_ld16(tbase + col, v);
-        tmem_wait_ld();
       };
-      store_tile<C::BN>(ep, load16, row, row_ok, n0, N, true, scale, true);
+      auto wait_ld = [&]() { tmem_wait_ld(); };
+      store_tile<C::BN>(ep, load16, wait_ld, row, row_ok, n0, N, true, scale, true);
       tc_fence_before();
       if (rank == 0) mbar_arrive(&acce[b]);
       else mbar_arrive_cluster(mapa_shared(&acce[b], 0));
