@@ -33,6 +33,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 D_MODEL, HEADS, STREAMS = 2048, 8, 256
+# DRAM bytes (read + write) of one state-stream launch at this workload,
+# measured with ncu (profiles/retention_step_kernel_decode_b256_d2048.md)
+STATE_KERNEL_TRAFFIC = 555.808e6 + 483.676e6
 EPS = 1e-6
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
@@ -332,7 +335,10 @@ def run_ours(args):
                    "eps": EPS},
         "roofline": {"bound": "hbm", "kernel": "retention_step_kernel<256,256>", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
-                     "peak_source": peak_kind, "traffic": None, "kernel_ms": kernel_ms,
+                     "peak_source": peak_kind, "traffic": STATE_KERNEL_TRAFFIC,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
+                                       "profiles/retention_step_kernel_decode_b256_d2048.md",
+                     "kernel_ms": kernel_ms,
                      "algorithmic_bytes_per_launch": kbytes,
                      "step_bytes": step_bytes,
                      "step_frac": step_bytes / (ms_step / 1e3) / 1e9 / peaks["hbm_gbs"]},
