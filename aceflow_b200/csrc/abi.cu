@@ -99,6 +99,7 @@ int af_cuda_init(int device, af_ctx **out) {
   if (const char *env = getenv("AF_SHARDED_HEAD_GROUPS")) ctx->sharded_head_groups = atoi(env);
   if (const char *env = getenv("AF_PDL")) ctx->pdl = atoi(env) != 0;
   if (const char *env = getenv("AF_GEMM_PAIR")) ctx->gemm_pair = atoi(env) != 0;
+  if (const char *env = getenv("AF_DECODE_PAIRS")) ctx->decode_pairs = atoi(env) != 0;
   if (const char *env = getenv("AF_COMM_RESERVE_SMS")) ctx->comm_reserve_sms = atoi(env);
   ctx->magic = kCtxMagic;
   *out = ctx;
@@ -148,6 +149,8 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
     ctx->decode_head_groups = (int)value;
   } else if (!strcmp(name, "allow_split_k")) {
     ctx->allow_split_k = value != 0;
+  } else if (!strcmp(name, "decode_pairs")) {
+    ctx->decode_pairs = value != 0;
   } else if (!strcmp(name, "gemm_pair")) {
     ctx->gemm_pair = value != 0;
   } else if (!strcmp(name, "pdl")) {

@@ -37,6 +37,7 @@ struct af_ctx {
   int comm_nranks = 0, comm_rank = 0;
   int pdl = 1;  // decode chains use programmatic dependent launch
   int gemm_pair = 1;  // large bf16 GEMMs on CTA pairs (cta_group::2, 256 x 256 tiles)
+  int decode_pairs = 1;  // decode-step projections on CTA pairs (256-row tiles)
   // bf16 decode layer projections run transposed (bit 0 QKV, 1 W_o, 2 gate/up, 3 down)
   int decode_transposed = 15;
   int sharded_head_groups = 0;  // head groups pipelined against the all-gather (0: auto; 1: one gather)
@@ -97,6 +98,7 @@ struct GemmEpilogueArgs {
   // on the previous kernel (the weights) and is prefetched before the wait;
   // 0 = none.  pdl = launch with the attribute.
   int pdl = 0, pre_operand = 0;
+  int pair = 0;  // run on CTA pairs (256-row tiles; width and splits from force_bn / force_splits)
   int scale_residual = 0;  // the row scale multiplies the residual too: out = (acc + residual) * scale
   int max_ctas = 0;        // persistent kernel: at most this many CTAs (SMs left to a concurrent kernel); 0: all
 };

@@ -819,6 +819,201 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// One 256 x BN output tile per CTA pair (cta_group::2), split-K over
+// gridDim.z: the decode-sized bf16 and pre-split 3xTF32 products.  Each CTA
+// loads its own 128 rows of A and BN/2 rows of B per K slice, so the operand
+// that every tile shares (the activations of a transposed projection, or the
+// weights of a direct one) is fetched half per CTA: fewer bytes per SM per
+// MMA flop than a 128 x BN tile on one SM.  Barriers as in the persistent
+// pair kernel, one tile: full[i] on rank 0, empty[i] and accf on both CTAs.
+template <int BN, int MODE>
+struct PairSplitCfg {
+  static constexpr bool TF32X3 = MODE != kBF16;
+  static constexpr int HALF = 128, BNH = BN / 2;
+  static constexpr int ELEM = TF32X3 ? 4 : 2, BK = 128 / ELEM, UK = 32 / ELEM;
+  static constexpr int A_BYTES = HALF * 128, B_BYTES = BNH * 128, RAW = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = TF32X3 ? 2 * RAW : RAW;  // hi and lo parts for 3xTF32
+  static constexpr int SMEM_LIMIT = 227 * 1024 - 64;
+  static constexpr int STAGES_FIT = (SMEM_LIMIT - 1024 - 256) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT < 12 ? STAGES_FIT : 12;
+  static constexpr int ACC_COLS = (TF32X3 ? 2 : 1) * BN;  // accumulator (+ correction terms)
+  static constexpr int TMEM_COLS =
+      ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128 : ACC_COLS <= 256 ? 256 : 512;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  static_assert(MODE == kBF16 || MODE == kTF32P, "bf16 or pre-split tf32");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "pair N");
+  static_assert(ACC_COLS <= 512 && STAGES >= 2 && 2 * STAGES + 2 <= 32, "TMEM / ring / barrier block");
+};
+
+template <int BN, int MODE>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_pair_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                                int M, int N, int K, GemmEpilogue ep, int *err) {
+  using C = PairSplitCfg<BN, MODE>;
+  constexpr bool TF32X3 = C::TF32X3;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (size_t)S * C::STAGE_BYTES);
+  uint64_t *full = bars, *empty = bars + S, *accf = bars + 2 * S;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 1);
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int m0 = (int)(blockIdx.x >> 1) * 256 + (int)rank * C::HALF;  // this CTA's A rows
+  const int n0 = blockIdx.y * BN, nb0 = n0 + (int)rank * C::BNH;       // the tile's N, this CTA's B rows
+  const int nk_all = (K + C::BK - 1) / C::BK;
+  const int kb_base = (int)(((int64_t)blockIdx.z * nk_all) / gridDim.z);
+  const int nk = (int)(((int64_t)(blockIdx.z + 1) * nk_all) / gridDim.z) - kb_base;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(accf, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if constexpr (TF32X3) {
+      prefetch_tmap(&tmA2);
+      prefetch_tmap(&tmB2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist and their TMEM is allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto stage = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES; };
+  auto fail = [&]() {
+    s_abort = 1;
+    atomicOr(err, 1 << AF_ERR_TIMEOUT);
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      auto load_a = [&](int i, int kx) {
+        const uint32_t fb = mapa_shared(&full[i], 0);
+        const int ka = kx % ep.a_kb, ma = m0 + (kx / ep.a_kb) * M;
+        tma_load_2d_pair(stage(i), &tmA, fb, ka, ma);
+        if constexpr (TF32X3) tma_load_2d_pair(stage(i) + C::RAW, &tmA2, fb, ka, ma);
+      };
+      auto load_b = [&](int i, int kx) {
+        const uint32_t fb = mapa_shared(&full[i], 0);
+        tma_load_2d_pair(stage(i) + C::A_BYTES, &tmB, fb, kx, nb0);
+        if constexpr (TF32X3) tma_load_2d_pair(stage(i) + C::RAW + C::A_BYTES, &tmB2, fb, kx, nb0);
+      };
+      // operand independent of the previous kernel first (programmatic launch)
+      const int pre = ep.pre_operand ? (nk < S ? nk : S) : 0;
+      for (int kb = 0; kb < pre; ++kb) {
+        if (rank == 0) mbar_arrive_expect_tx(&full[kb], 2 * C::STAGE_BYTES);
+        if (ep.pre_operand == 1) load_a(kb, (kb_base + kb) * C::BK);
+        else load_b(kb, (kb_base + kb) * C::BK);
+      }
+      griddep_wait();
+      for (int kb = 0; kb < pre; ++kb) {
+        if (ep.pre_operand == 1) load_b(kb, (kb_base + kb) * C::BK);
+        else load_a(kb, (kb_base + kb) * C::BK);
+      }
+      for (int kb = pre; kb < nk && !s_abort; ++kb) {
+        const int i = kb % S;
+        if (!mbar_wait(&empty[i], ((kb / S) & 1) ^ 1)) { fail(); break; }
+        if (rank == 0) mbar_arrive_expect_tx(&full[i], 2 * C::STAGE_BYTES);
+        const int kx = (kb_base + kb) * C::BK;
+        load_a(i, kx);
+        load_b(i, kx);
+      }
+      if (rank == 0) {
+        for (int kb = nk - S < 0 ? 0 : nk - S; kb < nk; ++kb)  // both CTAs' loads still in flight
+          if (!mbar_wait(&full[kb % S], (kb / S) & 1)) { fail(); break; }
+      } else if (s_abort) {
+        const uint64_t t0 = globaltimer();  // this CTA's loads complete the other CTA's barriers
+        while (globaltimer() - t0 < 100000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (rank == 0) {
+      constexpr uint32_t idesc = idesc_f32acc(TF32X3 ? kFmtTF32 : kFmtBF16, 256, BN);
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int i = kb % S;
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[i], (kb / S) & 1));
+        if (!ok || __any_sync(0xffffffffu, s_abort != 0)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint64_t da = sdesc_k_sw128(stage(i)), db = sdesc_k_sw128(stage(i) + C::A_BYTES);
+#pragma unroll
+          for (int k = 0; k < C::BK / C::UK; ++k) {
+            const uint64_t off = (uint64_t)(k * 32) >> 4;
+            if constexpr (TF32X3) {
+              const uint64_t dal = sdesc_k_sw128(stage(i) + C::RAW), dbl = sdesc_k_sw128(stage(i) + C::RAW + C::A_BYTES);
+              umma_tf32_pair(tmem, da + off, db + off, idesc, (kb | k) != 0);
+              umma_tf32_pair(tmem + BN, da + off, dbl + off, idesc, (kb | k) != 0);
+              umma_tf32_pair(tmem + BN, dal + off, db + off, idesc, 1);
+            } else {
+              umma_bf16_pair(tmem, da + off, db + off, idesc, (kb | k) != 0);
+            }
+          }
+          umma_commit_pair(mapa_shared(&empty[i], 0));
+          umma_commit_pair(mapa_shared(&empty[i], 1));
+        }
+        __syncwarp();
+      }
+      if (lane == 0) {
+        if (!ok) fail();
+        umma_commit_pair(mapa_shared(accf, 0));  // also on failure, so the epilogues do not wait out
+        umma_commit_pair(mapa_shared(accf, 1));
+      }
+      __syncwarp();
+    }
+  } else {
+    const bool ok = mbar_wait(accf, 0);
+    if (!ok) fail();
+    tc_fence_after();
+    griddep_wait();  // the epilogue reads row sums / residual and writes out
+    const int q = warp & 3;
+    const int row = m0 + q * 32 + lane;
+    const bool row_ok = row < M;
+    float scale = 1.f;
+    if (ep.row_parts && row_ok && !ep.trans) scale = row_scale(ep, row, M);
+    const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16);
+    auto load16 = [&](int col, float (&v)[16]) {
+      __syncwarp();
+      tmem_ld16(tbase + col, v);
+      if constexpr (TF32X3) {  // accumulator + correction terms
+        float w[16];
+        tmem_ld16(tbase + (uint32_t)BN + col, w);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] += w[e];
+      }
+    };
+    auto wait_ld = [&]() {
+      if constexpr (!TF32X3) tmem_wait_ld();
+    };
+    store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, ok && !s_abort, scale, blockIdx.z == 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA frees TMEM or exits while the pair's MMAs may touch it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  }
+}
+
 // ------------------------------------------------------------------ host
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -870,6 +1065,52 @@ int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, in
   const int cap = ep_max_ctas > 0 && ep_max_ctas < ctx->num_sms ? ep_max_ctas : ctx->num_sms;
   const int grid = (int)(total < cap ? total : cap);
   umma_gemm_persistent_kernel<BN><<<grid, 192, C::SMEM, st>>>(ta, tb, M, N, K, ep, ctx->dev_err);
+  return af::launched(ctx, fn);
+}
+
+template <int BN, int MODE>
+int launch_pair_split(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void *B, const void *B2,
+                      int64_t ldb, int M, int N, int K, int splits, const GemmEpilogue &ep, cudaStream_t st,
+                      const char *fn, bool pdl) {
+  using C = PairSplitCfg<BN, MODE>;
+  const bool fp32 = MODE != kBF16;
+  CUtensorMap ta, tb, ta2, tb2;
+  int rc = make_kmajor_map(&ta, A, fp32, (K / ep.a_kb) * M, ep.a_kb, lda, C::HALF, fn);
+  if (rc) return rc;
+  rc = make_kmajor_map(&tb, B, fp32, N, K, ldb, C::BNH, fn);
+  if (rc) return rc;
+  ta2 = ta;
+  tb2 = tb;
+  if (MODE == kTF32P) {
+    rc = make_kmajor_map(&ta2, A2, true, (K / ep.a_kb) * M, ep.a_kb, lda, C::HALF, fn);
+    if (rc) return rc;
+    rc = make_kmajor_map(&tb2, B2, true, N, K, ldb, C::BNH, fn);
+    if (rc) return rc;
+  }
+  static bool attr_done = false;  // per template instance
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(umma_gemm_pair_split_kernel<BN, MODE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
+    attr_done = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * ((M + 255) / 256), (N + BN - 1) / BN, splits);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_split_kernel<BN, MODE>, ta, tb, ta2, tb2, M, N, K, ep,
+                                           ctx->dev_err);
+  if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: pair launch: %s", fn, cudaGetErrorString(e));
   return af::launched(ctx, fn);
 }
 
@@ -1076,12 +1317,27 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
     }
   }
   // large bf16 GEMMs (two or more waves of tiles): persistent kernel
-  if (MODE == kBF16 && splits == 1 && !a.trans && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms &&
+  if (MODE == kBF16 && splits == 1 && !a.trans && !a.pair && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms &&
       !getenv("AF_GEMM_NO_PERSIST")) {
     if (bn == 256 && ctx->gemm_pair && !a.max_ctas && M >= 256 && N >= 256)
       return launch_pair(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
     if (bn == 256) return launch_persistent<256>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);
     return launch_persistent<128>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);
+  }
+  if (a.pair && (MODE == kBF16 || MODE == kTF32P) && M > 128) {
+    // CTA pairs: 256-row tiles (the caller chose width and splits)
+    if constexpr (MODE == kBF16 || MODE == kTF32P) {
+      switch (bn) {
+        case 256:
+          return launch_pair_split<256, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn, pdl);
+        case 128:
+          return launch_pair_split<128, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn, pdl);
+        case 64:
+          return launch_pair_split<64, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn, pdl);
+        default:
+          break;
+      }
+    }
   }
 #define AF_LAUNCH(BNV) \
   return launch_tc<BNV, MODE>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn, pdl)

@@ -184,6 +184,7 @@ int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const 
       e.force_splits = nsp;
       e.pdl = 1;  // programmatic dependent launches: weight tiles stream while the split kernel drains
       e.pre_operand = 1;
+      e.pair = ctx->decode_pairs;  // CTA pairs: each CTA fetches half of the activation tile
       rc = tc_gemm_presplit(ctx, wq_hi, wq_lo, d, x_hi, x_lo, d, 3 * d, B, d, e, st, fn);
       if (rc) return rc;
       rc = launch_retention_step(ctx, state, sbs, gamma, qkv, qkv + dh, qkv + 2 * dh, 3 * (int64_t)d, o_hi, d, B, H,
@@ -201,6 +202,7 @@ int msr_decode_step_split_impl(af_ctx *ctx, const float *x, float *state, const 
     e2.accumulate = 1;  // into the zeroed out: split-K needs no memset
     e2.pdl = 1;
     e2.pre_operand = 2;  // W_o (B) does not depend on the state stream
+    // (W_o on CTA pairs measured slower, 25.9 vs 24.3 us: 16 K slices per split are too few to repay the pair)
     e2.row_parts = sumsq;
     e2.nparts = H;
     e2.inv_d = 1.0f / (float)d;
