@@ -20,14 +20,17 @@
 //              + V_c^T P'^T                       K=64   A = V_c MN-major (TMA), B = P' (written)
 //   update  S^T += Vs^T K_c        M=128 N=256 K=64   A = decay-scaled V (written), B = K_c MN-major
 // Warp roles (320 threads): warp 0 TMA producer; warp 1 TMEM allocator and
-// single-thread tcgen05.mma issuer; warps 2-9 math (TMEM ld/st, decay masks
+// single-thread tcgen05.mma issuer (the state term of O is issued as soon as
+// the bf16 state operand is written, before the decay mask is ready); warps
+// 2-9 math (TMEM ld/st, decay masks
 // generated in registers, bf16 operand tiles, output + RMSNorm partials):
 // two warps per TMEM lane quadrant, each taking half of the columns of every
 // step, so the per-chunk chain of TMEM round trips is split in two.
 //
 // Inputs come straight from the bf16 QKV projection [B*T][3d] through one
 // 3-D tensor map (d_model fastest, then T, then B) so the T edge zero-fills.
-// Outputs: O * ret_norm_w as bf16 [B*T][d] (the A operand of the W_o GEMM),
+// Outputs: O * ret_norm_w as bf16 [B*T][d] (the A operand of the W_o GEMM;
+// staged in shared memory and written by TMA stores, one per 64 x 64 box),
 // per-row partial sums of O^2 (the GEMM applies 1/rms per row), and the
 // final state in the decode layout [B][H][k][v] fp32.
 //
@@ -61,8 +64,10 @@ constexpr int V_OFF = K_OFF + K_BYTES, V_BYTES = C * VS * 2;  // 2 boxes [64 tok
 constexpr int SOP_OFF = V_OFF + V_BYTES, SOP_BYTES = VS * DH * 2;  // 4 K-slices [128 v x 64 k], 16 KB each
 constexpr int P_OFF = SOP_OFF + SOP_BYTES, P_BYTES = C * C * 2;    // [64 i x 64 j]
 constexpr int VT_OFF = P_OFF + P_BYTES, VT_BYTES = V_BYTES;         // decay-scaled V, V's layout
-constexpr int TILE_BYTES = VT_OFF + VT_BYTES;                       // 168 KB
-// tail: 6 mbarriers + TMEM slot (64 B), gamma^n (C+1), gamma^-(j+1) (C), [4][C] partials
+// output staging for the TMA store, two buffers of two [64 tok x 64 v] bf16 halves
+constexpr int OST_OFF = VT_OFF + VT_BYTES, OST_HALF = C * 64 * 2, OST_BYTES = 2 * 2 * OST_HALF;
+constexpr int TILE_BYTES = OST_OFF + OST_BYTES;                     // 200 KB
+// tail: 7 mbarriers + TMEM slot (64 B), gamma^n (C+1), gamma^-(j+1) (C), [4][C] partials
 constexpr size_t TAIL_BYTES = 64 + 4 * ((C + 1) + C + 4 * C);
 constexpr size_t SMEM = 1024 + TILE_BYTES + ((TAIL_BYTES + 255) / 256) * 256;
 constexpr int BOX = 64 * 64 * 2;  // one TMA box: 64 rows x 128 bytes
@@ -122,6 +127,19 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
 
 constexpr int MATH_THREADS = 256;  // warps 2-9
 
+// TMA store of a [64 x 64] bf16 box from shared memory (bulk group).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void math_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
 // Named barrier over the 256 math threads that also ORs a predicate, so every
@@ -139,13 +157,14 @@ __device__ __forceinline__ bool math_sync_or(bool pred) {
 
 template <bool STATE_ONLY>
 __global__ void __launch_bounds__(320, 1)
-    retention_chunkwise_kernel(const __grid_constant__ CUtensorMap tm, ChunkParams p) {
+    retention_chunkwise_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_out,
+                               ChunkParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + TILE_BYTES);
   uint64_t *bar_load = bars + 0, *bar_sc = bars + 1, *bar_math = bars + 2, *bar_o = bars + 3, *bar_upd = bars + 4,
-           *bar_out = bars + 5;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 6);
+           *bar_out = bars + 5, *bar_sop = bars + 6;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 7);
   float *gpow = reinterpret_cast<float *>(bars + 8);   // gamma^n, n = 0..C
   float *ginv = gpow + (C + 1);                        // gamma^-(j+1), j = 0..C-1
   float *red = ginv + C;                               // [4][C] per-warp partial sums
@@ -171,8 +190,10 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(bar_o, 1);
     mbar_init(bar_upd, 1);
     mbar_init(bar_out, MATH_THREADS);
+    mbar_init(bar_sop, MATH_THREADS);
     fence_barrier_init();
     prefetch_tmap(&tm);
+    if (!STATE_ONLY) prefetch_tmap(&tm_out);
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + C + 1) {
     const int n = threadIdx.x - 64;
@@ -254,13 +275,14 @@ __global__ void __launch_bounds__(320, 1)
         umma_commit(bar_sc);
       }
       __syncwarp();
-      ok = mbar_wait(bar_math, c & 1);
+      // O^T = bf16(S^T) . Q^T (K = 256 keys) as soon as the state operand is
+      // written: it overlaps the math warps' decay mask and scaled V
+      ok = mbar_wait(bar_sop, c & 1);
       if (ok && c > 0) ok = mbar_wait(bar_out, (c - 1) & 1);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
       tc_fence_after();
       if (lane == 0) {
-        // O^T = bf16(S^T) . Q^T  (K = 256 keys)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
 #pragma unroll
@@ -269,6 +291,13 @@ __global__ void __launch_bounds__(320, 1)
             const uint64_t db = sdesc_k_sw128(sm + Q_OFF + kk * BOX) + ((k * 32) >> 4);
             umma_bf16(tmem + TM_O, da, db, id_inter, (kk | k) != 0);
           }
+      }
+      __syncwarp();
+      ok = mbar_wait(bar_math, c & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
+      tc_fence_after();
+      if (lane == 0) {
         //     + V^T . P'^T  (K = 64 tokens)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -369,6 +398,9 @@ __global__ void __launch_bounds__(320, 1)
         for (int u = 0; u < 4; ++u) tmem_st16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
       }
       tmem_wait_st();
+      fence_proxy_async_smem();  // S_op (generic stores) before the MMAs that read it
+      tc_fence_before();
+      mbar_arrive(bar_sop);
       // (b) Vs = diag(gamma^(L-1-j)) V, same swizzled layout as V
       ok = mbar_wait(bar_load, c & 1);
       if (!ok) s_abort = 1;
@@ -427,7 +459,9 @@ __global__ void __launch_bounds__(320, 1)
       const float wv = p.norm_w ? p.norm_w[col] : 1.f;
       constexpr int CH = C / 2;  // this warp's half of the chunk's tokens
       const int i0 = half * CH;
-      __nv_bfloat16 *orow = p.out + ((size_t)b * p.T + t0 + i0) * d + col;
+      // staging buffer of this chunk: [v / 64][token][v % 64] bf16
+      __nv_bfloat16 *ost = reinterpret_cast<__nv_bfloat16 *>(sm + OST_OFF + (c & 1) * 2 * OST_HALF +
+                                                             (v >> 6) * OST_HALF) + (v & 63);
       float x[CH];
       __syncwarp();
 #pragma unroll
@@ -439,7 +473,7 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
       for (int i = 0; i < CH; ++i) {
         x[i] *= gpow[i0 + i + 1];
-        if (i0 + i < L) orow[(size_t)i * d] = __float2bfloat16(x[i] * wv);
+        ost[(i0 + i) * 64] = __float2bfloat16(x[i] * wv);
         x[i] *= x[i];
       }
       // column sums of o^2 over the warp's 32 values of v: recursive halving
@@ -456,12 +490,22 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       red[q * C + i0 + lane] = x[0];
+      fence_proxy_async_smem();  // staged output before the TMA store reads it
       math_sync();
+      if (mt == 0) {
+        // the chunk's [64 tok x 128 v] output: two boxes; rows past T are clipped
+        const uint8_t *src = sm + OST_OFF + (c & 1) * 2 * OST_HALF;
+        tma_store_3d(&tm_out, src, col - v, t0, b);
+        tma_store_3d(&tm_out, src + OST_HALF, col - v + 64, t0, b);
+        bulk_commit();
+        bulk_wait_read<1>();  // the other buffer (chunk c-1's store) is free for chunk c+1
+      }
       if (p.sumsq && mt < L) {
         const float s2 = red[mt] + red[C + mt] + red[2 * C + mt] + red[3 * C + mt];
         p.sumsq[((size_t)b * p.T + t0 + mt) * (p.H * NSL) + h * NSL + slice] = s2;
       }
     }
+    if (!STATE_ONLY && mt == 0) bulk_wait_all();  // the output stores have completed
     // final state: S[k][v] = S^T[v][k] (segment end states in the state pass,
     // else the last segment's state)
     const bool aborted = math_sync_or(s_abort != 0);
@@ -519,7 +563,8 @@ __global__ void seg_scan_kernel(float4 *__restrict__ states, const float4 *__res
 PFN_cuTensorMapEncodeTiled_v12000 g_encode3 = nullptr;
 
 template <bool SO>
-int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const ChunkParams &p, cudaStream_t st, const char *fn) {
+int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const CUtensorMap &tm_out, const ChunkParams &p,
+                     cudaStream_t st, const char *fn) {
   static bool attr = false;  // per instance
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(retention_chunkwise_kernel<SO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -527,7 +572,7 @@ int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const ChunkParams &p, c
     if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
     attr = true;
   }
-  retention_chunkwise_kernel<SO><<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, SMEM, st>>>(tm, p);
+  retention_chunkwise_kernel<SO><<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, SMEM, st>>>(tm, tm_out, p);
   return af::launched(ctx, fn);
 }
 
@@ -580,9 +625,21 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: tensor map encode failed (%d)", fn, (int)r);
+  // output [B][T][d] bf16 for the TMA stores: [64 tok x 64 v] boxes, the T edge clipped per stream
+  CUtensorMap tm_out = tm;
+  if (out) {
+    cuuint64_t odims[3] = {(cuuint64_t)d, (cuuint64_t)T, (cuuint64_t)B};
+    cuuint64_t ostrides[2] = {(cuuint64_t)d * 2, (cuuint64_t)T * d * 2};
+    cuuint32_t obox[3] = {64, (cuuint32_t)C, 1};
+    r = g_encode3(&tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, odims, ostrides, obox, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: output tensor map encode failed (%d)", fn, (int)r);
+  }
   ChunkParams p{B,       T,         H,       pl.nseg, pl.seg_len, gamma, state_in, state_out,
                 reinterpret_cast<__nv_bfloat16 *>(out), norm_w, sumsq, ctx->dev_err};
-  if (pl.nseg == 1) return launch_chunkwise<false>(ctx, tm, p, st, fn);
+  if (!out) return fail(AF_ERR_ARG, "%s: output is NULL", fn);
+  if (pl.nseg == 1) return launch_chunkwise<false>(ctx, tm, tm_out, p, st, fn);
   // 1. segment end states from zero
   ChunkParams ps = p;
   ps.state_in = nullptr;
@@ -590,7 +647,7 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   ps.out = nullptr;
   ps.norm_w = nullptr;
   ps.sumsq = nullptr;
-  int rc = launch_chunkwise<true>(ctx, tm, ps, st, fn);
+  int rc = launch_chunkwise<true>(ctx, tm, tm, ps, st, fn);
   if (rc) return rc;
   // 2. states before each segment
   const int64_t n4 = (int64_t)B * H * (DH * DH / 4);
@@ -601,7 +658,7 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   if (rc) return rc;
   // 3. the full pass from each segment's state
   p.state_in = seg_states;
-  return launch_chunkwise<false>(ctx, tm, p, st, fn);
+  return launch_chunkwise<false>(ctx, tm, tm_out, p, st, fn);
 }
 
 int chunkwise_head_dim() { return DH; }
