@@ -67,8 +67,13 @@ constexpr int VT_OFF = P_OFF + P_BYTES, VT_BYTES = V_BYTES;         // decay-sca
 // output staging for the TMA store, two buffers of two [64 tok x 64 v] bf16 halves
 constexpr int OST_OFF = VT_OFF + VT_BYTES, OST_HALF = C * 64 * 2, OST_BYTES = 2 * 2 * OST_HALF;
 constexpr int TILE_BYTES = OST_OFF + OST_BYTES;                     // 200 KB
-// tail: 7 mbarriers + TMEM slot (64 B), gamma^n (C+1), gamma^-(j+1) (C), [4][C] partials
-constexpr size_t TAIL_BYTES = 64 + 4 * ((C + 1) + C + 4 * C);
+// The state-only pass keeps a ring of SO_NS slots (K, V, decay-scaled V) in
+// the same space, so its loads run two chunks ahead of its update MMAs.
+constexpr int SO_SLOT = K_BYTES + 2 * V_BYTES, SO_NS = 3;
+static_assert(SO_NS * SO_SLOT <= TILE_BYTES, "state-pass ring");
+// tail: 24 mbarrier words (the TMEM slot in the last), gamma^n (C+1),
+// gamma^-(j+1) (C), [4][C] partials
+constexpr size_t TAIL_BYTES = 24 * 8 + 4 * ((C + 1) + C + 4 * C);
 constexpr size_t SMEM = 1024 + TILE_BYTES + ((TAIL_BYTES + 255) / 256) * 256;
 constexpr int BOX = 64 * 64 * 2;  // one TMA box: 64 rows x 128 bytes
 
@@ -164,8 +169,10 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + TILE_BYTES);
   uint64_t *bar_load = bars + 0, *bar_sc = bars + 1, *bar_math = bars + 2, *bar_o = bars + 3, *bar_upd = bars + 4,
            *bar_out = bars + 5, *bar_sop = bars + 6;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 7);
-  float *gpow = reinterpret_cast<float *>(bars + 8);   // gamma^n, n = 0..C
+  // state-only pass: per ring slot, loads landed / scaled V written / update done
+  uint64_t *bar_lds = bars + 8, *bar_mts = bars + 11, *bar_ups = bars + 14;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 23);
+  float *gpow = reinterpret_cast<float *>(bars + 24);  // gamma^n, n = 0..C
   float *ginv = gpow + (C + 1);                        // gamma^-(j+1), j = 0..C-1
   float *red = ginv + C;                               // [4][C] per-warp partial sums
   __shared__ volatile int s_abort;
@@ -191,6 +198,11 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(bar_upd, 1);
     mbar_init(bar_out, MATH_THREADS);
     mbar_init(bar_sop, MATH_THREADS);
+    for (int i = 0; i < SO_NS; ++i) {
+      mbar_init(&bar_lds[i], 1);
+      mbar_init(&bar_mts[i], MATH_THREADS);
+      mbar_init(&bar_ups[i], 1);
+    }
     fence_barrier_init();
     prefetch_tmap(&tm);
     if (!STATE_ONLY) prefetch_tmap(&tm_out);
@@ -215,7 +227,26 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    if (lane == 0 && STATE_ONLY) {
+      // ring of SO_NS slots: slot c % SO_NS is reused once chunk c - SO_NS's update retired
+      int issued = 0;
+      for (int c = 0; c < nch && !s_abort; ++c) {
+        const int sl = c % SO_NS;
+        if (c >= SO_NS && !mbar_wait(&bar_ups[sl], ((c / SO_NS) - 1) & 1)) { fail(); break; }
+        const int t0 = tb + c * C;
+        uint8_t *base = sm + sl * SO_SLOT;
+        mbar_arrive_expect_tx(&bar_lds[sl], K_BYTES + V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tma_load_3d(base + kk * BOX, &tm, &bar_lds[sl], d + h * DH + kk * 64, t0, b);
+#pragma unroll
+        for (int vb = 0; vb < 2; ++vb)
+          tma_load_3d(base + K_BYTES + vb * BOX, &tm, &bar_lds[sl], 2 * d + h * DH + slice * VS + vb * 64, t0, b);
+        issued = c + 1;
+      }
+      for (int c = issued - SO_NS < 0 ? 0 : issued - SO_NS; c < issued; ++c)  // loads still in flight
+        if (!mbar_wait(&bar_lds[c % SO_NS], (c / SO_NS) & 1)) { fail(); break; }
+    } else if (lane == 0) {
       int issued = 0;
       for (int c = 0; c < nch && !s_abort; ++c) {
         if (c > 0 && !mbar_wait(bar_upd, (c - 1) & 1)) { fail(); break; }
@@ -242,18 +273,20 @@ __global__ void __launch_bounds__(320, 1)
     if constexpr (STATE_ONLY) {
       // only the update: S^T += Vs^T . K once the math warps wrote Vs
       for (int c = 0; c < nch; ++c) {
-        bool ok = mbar_wait(bar_math, c & 1);
+        const int sl = c % SO_NS;
+        uint8_t *base = sm + sl * SO_SLOT;
+        bool ok = mbar_wait(&bar_mts[sl], (c / SO_NS) & 1);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
         tc_fence_after();
         if (lane == 0) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t da = sdesc_mn_sw128(sm + VT_OFF + k * 2048, BOX);
-            const uint64_t db = sdesc_mn_sw128(sm + K_OFF + k * 2048, BOX);
+            const uint64_t da = sdesc_mn_sw128(base + K_BYTES + V_BYTES + k * 2048, BOX);
+            const uint64_t db = sdesc_mn_sw128(base + k * 2048, BOX);
             umma_bf16(tmem + TM_S, da, db, id_upd, 1);
           }
-          umma_commit(bar_upd);
+          umma_commit(&bar_ups[sl]);
         }
         __syncwarp();
       }
@@ -343,7 +376,9 @@ __global__ void __launch_bounds__(320, 1)
         const int t0 = tb + c * C;
         const int L = min(C, te - t0);
         const float tail = exp2f((float)(te - t0 - L) * lg);  // gamma^(tokens after this chunk)
-        bool ok = mbar_wait(bar_load, c & 1);
+        const int sl = c % SO_NS;
+        uint8_t *base = sm + sl * SO_SLOT;
+        bool ok = mbar_wait(&bar_lds[sl], (c / SO_NS) & 1);
         if (!ok) s_abort = 1;
         if (ok) {
 #pragma unroll 2
@@ -351,19 +386,19 @@ __global__ void __launch_bounds__(320, 1)
             const int off = i * 16;
             const int j = (off % BOX) / 128;
             const float sc = j < L ? gpow[L - 1 - j] * tail : 0.f;
-            uint4 raw = *reinterpret_cast<const uint4 *>(sm + V_OFF + off);
+            uint4 raw = *reinterpret_cast<const uint4 *>(base + K_BYTES + off);
             __nv_bfloat162 *e = reinterpret_cast<__nv_bfloat162 *>(&raw);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               float2 f = __bfloat1622float2(e[u]);
               e[u] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
             }
-            *reinterpret_cast<uint4 *>(sm + VT_OFF + off) = raw;
+            *reinterpret_cast<uint4 *>(base + K_BYTES + V_BYTES + off) = raw;
           }
         }
         fence_proxy_async_smem();
         tc_fence_before();
-        mbar_arrive(bar_math);
+        mbar_arrive(&bar_mts[sl]);
         if (math_sync_or(s_abort != 0)) break;
       }
     } else
@@ -510,8 +545,13 @@ __global__ void __launch_bounds__(320, 1)
     // else the last segment's state)
     const bool aborted = math_sync_or(s_abort != 0);
     const bool write_state = p.state_out && (STATE_ONLY || s == p.nseg - 1);
+    // the last chunk's update MMAs (in the state pass: on its ring slot's barrier)
+    auto wait_last_update = [&]() {
+      if constexpr (STATE_ONLY) return mbar_wait(&bar_ups[(nch - 1) % SO_NS], ((nch - 1) / SO_NS) & 1);
+      else return mbar_wait(bar_upd, (nch - 1) & 1);
+    };
     if (!aborted && write_state) {
-      bool ok = mbar_wait(bar_upd, (nch - 1) & 1);
+      bool ok = wait_last_update();
       if (!ok) s_abort = 1;
       if (!math_sync_or(s_abort != 0)) {
         tc_fence_after();
@@ -528,7 +568,7 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
     } else if (!aborted && nch > 0) {
-      if (!mbar_wait(bar_upd, (nch - 1) & 1)) s_abort = 1;  // last MMAs retired before TMEM is freed
+      if (!wait_last_update()) s_abort = 1;  // last MMAs retired before TMEM is freed
     }
   }
   tc_fence_before();
