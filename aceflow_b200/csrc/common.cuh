@@ -9,6 +9,7 @@
 
 #include "../../include/aceflow_cuda.h"
 
+#include <atomic>
 #include <utility>
 
 struct af_ctx {
@@ -144,6 +145,19 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
                           int64_t split_stride = 0, bool pdl = false);
 
 inline cudaStream_t stream_of(af_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Raises a kernel's dynamic shared-memory limit on the context's device,
+// once per device (the attribute is per device; `done` is the call site's
+// device bitmask - setting it twice is harmless, so the check may race).
+inline int smem_attr(af_ctx *ctx, const void *kernel, size_t bytes, std::atomic<unsigned long long> &done,
+                     const char *fn) {
+  const unsigned long long bit = 1ull << (ctx->device & 63);
+  if (done.load(std::memory_order_relaxed) & bit) return AF_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: shared-memory attribute: %s", fn, cudaGetErrorString(e));
+  done.fetch_or(bit, std::memory_order_relaxed);
+  return AF_OK;
+}
 
 // Launches `kernel`, optionally as a programmatic dependent launch: it may
 // start while the previous kernel on the stream drains and must execute

@@ -1054,13 +1054,10 @@ int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, in
   if (rc) return rc;
   rc = make_kmajor_map(&tb, B, false, N, K, ldb, BN, fn);
   if (rc) return rc;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(umma_gemm_persistent_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::SMEM);
-    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
-    attr_done = true;
-  }
+  static std::atomic<unsigned long long> attr_devices{0};
+  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_persistent_kernel<BN>), C::SMEM,
+                              attr_devices, fn))
+    return arc;
   const int64_t total = (int64_t)((N + BN - 1) / BN) * ((M + C::BM - 1) / C::BM);
   const int cap = ep_max_ctas > 0 && ep_max_ctas < ctx->num_sms ? ep_max_ctas : ctx->num_sms;
   const int grid = (int)(total < cap ? total : cap);
@@ -1087,13 +1084,10 @@ int launch_pair_split(af_ctx *ctx, const void *A, const void *A2, int64_t lda, c
     rc = make_kmajor_map(&tb2, B2, true, N, K, ldb, C::BNH, fn);
     if (rc) return rc;
   }
-  static bool attr_done = false;  // per template instance
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(umma_gemm_pair_split_kernel<BN, MODE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
-    attr_done = true;
-  }
+  static std::atomic<unsigned long long> attr_devices{0};
+  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_pair_split_kernel<BN, MODE>), C::SMEM,
+                              attr_devices, fn))
+    return arc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * ((M + 255) / 256), (N + BN - 1) / BN, splits);
   cfg.blockDim = dim3(192);
@@ -1122,13 +1116,9 @@ int launch_pair(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t 
   if (rc) return rc;
   rc = make_kmajor_map(&tb, B, false, N, K, ldb, C::HALF, fn);
   if (rc) return rc;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(umma_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)C::SMEM);
-    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
-    attr_done = true;
-  }
+  static std::atomic<unsigned long long> attr_devices{0};
+  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_pair_kernel), C::SMEM, attr_devices, fn))
+    return arc;
   const int64_t total = (int64_t)((N + C::BN - 1) / C::BN) * ((M + C::BM - 1) / C::BM);
   const int pairs = (int)(total < ctx->num_sms / 2 ? total : ctx->num_sms / 2);
   cudaLaunchConfig_t cfg = {};
@@ -1166,13 +1156,10 @@ int launch_tc(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const voi
     rc = make_kmajor_map(&tb2, B2, true, N, K, ldb, BN, fn);
     if (rc) return rc;
   }
-  static bool attr_done = false;  // per template instance
-  if (!attr_done) {
-    cudaError_t e =
-        cudaFuncSetAttribute(umma_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: smem attribute: %s", fn, cudaGetErrorString(e));
-    attr_done = true;
-  }
+  static std::atomic<unsigned long long> attr_devices{0};
+  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_kernel<BN, MODE>), C::SMEM,
+                              attr_devices, fn))
+    return arc;
   const dim3 grid((N + BN - 1) / BN, (M + C::BM - 1) / C::BM, splits);
   const cudaError_t e = af::launch_kernel(umma_gemm_kernel<BN, MODE>, grid, dim3(192), C::SMEM, st, pdl, ta, tb, ta2,
                                           tb2, M, N, K, ep, ctx->dev_err);

@@ -605,13 +605,10 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode3 = nullptr;
 template <bool SO>
 int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const CUtensorMap &tm_out, const ChunkParams &p,
                      cudaStream_t st, const char *fn) {
-  static bool attr = false;  // per instance
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(retention_chunkwise_kernel<SO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)SMEM);
-    if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-    attr = true;
-  }
+  static std::atomic<unsigned long long> attr_devices{0};
+  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(retention_chunkwise_kernel<SO>), SMEM,
+                              attr_devices, fn))
+    return arc;
   retention_chunkwise_kernel<SO><<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, SMEM, st>>>(tm, tm_out, p);
   return af::launched(ctx, fn);
 }
