@@ -100,6 +100,10 @@ int af_cuda_init(int device, af_ctx **out) {
   if (const char *env = getenv("AF_PDL")) ctx->pdl = atoi(env) != 0;
   if (const char *env = getenv("AF_GEMM_PAIR")) ctx->gemm_pair = atoi(env) != 0;
   if (const char *env = getenv("AF_DECODE_PAIRS")) ctx->decode_pairs = atoi(env) != 0;
+  if (const char *env = getenv("AF_GEMM_PRODUCERS")) {
+    const int v = atoi(env);
+    if (v >= 1 && v <= 4) ctx->gemm_producers = v;
+  }
   if (const char *env = getenv("AF_COMM_RESERVE_SMS")) ctx->comm_reserve_sms = atoi(env);
   ctx->magic = kCtxMagic;
   *out = ctx;
@@ -153,6 +157,9 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
     ctx->decode_pairs = value != 0;
   } else if (!strcmp(name, "gemm_pair")) {
     ctx->gemm_pair = value != 0;
+  } else if (!strcmp(name, "gemm_producers")) {
+    if (value < 1 || value > 4) return af::fail(AF_ERR_ARG, "af_set_option: gemm_producers must be 1..4");
+    ctx->gemm_producers = (int)value;
   } else if (!strcmp(name, "pdl")) {
     ctx->pdl = value != 0;
   } else if (!strcmp(name, "decode_transposed")) {

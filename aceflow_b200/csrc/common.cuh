@@ -39,6 +39,7 @@ struct af_ctx {
   int pdl = 1;  // decode chains use programmatic dependent launch
   int gemm_pair = 1;  // large bf16 GEMMs on CTA pairs (cta_group::2, 256 x 256 tiles)
   int decode_pairs = 1;  // decode-step projections on CTA pairs (256-row tiles)
+  int gemm_producers = 1;  // TMA producer threads per tensor-core GEMM CTA (1..4)
   // bf16 decode layer projections run transposed (bit 0 QKV, 1 W_o, 2 gate/up, 3 down)
   int decode_transposed = 15;
   int sharded_head_groups = 0;  // head groups pipelined against the all-gather (0: auto; 1: one gather)

@@ -101,16 +101,63 @@ __device__ __forceinline__ float row_scale(const GemmEpilogue &ep, int row, int 
 
 constexpr int kBF16 = 0, kTF32S = 1, kTF32P = 2;
 
-template <int BN, int MODE>
+// TMA producers.  One thread issuing a K slice's loads and waiting for a
+// ring slot sustains about 3.5 M slices per second whatever their size (16 to
+// 64 KB; measured on B200), so the GEMMs below may spread the slices over np
+// producer threads: lane 0 of warp 0 and of the np - 1 warps after the six
+// fixed ones (TMA, MMA, four epilogue warps).  Producer p issues the K slices
+// g = p (mod np); every slot is still handed over by its own full / empty
+// barriers, so the MMA thread consumes the slices in order.
+constexpr int kMaxProducers = 4;
+constexpr int kMaxGemmThreads = 32 * (5 + kMaxProducers);
+__host__ __device__ __forceinline__ int gemm_threads(int np) { return 32 * (5 + np); }
+__device__ __forceinline__ int num_producers() { return (int)(blockDim.x >> 5) - 5; }
+__device__ __forceinline__ bool is_producer_warp(int warp) { return warp == 0 || warp >= 6; }
+__device__ __forceinline__ int producer_id(int warp) { return warp == 0 ? 0 : warp - 5; }
+// At most S producers take part: a producer waits for slot g % S with a
+// parity wait, which is exact only while that slot's empty barrier is at most
+// one phase behind, i.e. slice g - 2S has been consumed.  The producer's own
+// previous slice g - np was issued after slice g - np - S was consumed, which
+// covers g - 2S when np <= S.
+__device__ __forceinline__ int active_producers(int S) {
+  const int n = num_producers();
+  return n < S ? n : S;
+}
+// first g >= from with g = p (mod np)
+__device__ __forceinline__ int first_owned(int from, int p, int np) { return from + ((p - from % np) + np) % np; }
+// Before the CTA exits, every load a producer issued has landed.  Normal
+// end: its own slices among the last S (no later slice reuses their slots,
+// so each parity wait is exact).  After an abort with one producer, the last
+// S slices it issued; with several, other producers may have refilled those
+// slots, so it waits a fixed 100 us for the copies in flight instead.
+template <class Fail>
+__device__ __forceinline__ void drain_producer(uint64_t *full, int S, int n, int issued, int p, int np, bool aborted,
+                                               Fail &&fail) {
+  if (!aborted || np == 1) {
+    const int end = aborted ? issued : n;
+    for (int g = first_owned(end - S < 0 ? 0 : end - S, p, np); g < end; g += np)
+      if (!sm100::mbar_wait(&full[g % S], (g / S) & 1)) {
+        fail();
+        return;
+      }
+  } else {
+    const uint64_t t0 = sm100::globaltimer();
+    while (sm100::globaltimer() - t0 < 100000ull) {
+    }
+  }
+}
+
+template <int BN, int MODE, int KS = 1>
 struct TileCfg {
   static constexpr bool TF32X3 = MODE != kBF16;
   static constexpr bool PRE = MODE == kTF32P;
   static constexpr int BM = 128;
   static constexpr int ELEM = TF32X3 ? 4 : 2;
-  static constexpr int BK = 128 / ELEM;          // one 128-byte swizzle row per K slice
+  static constexpr int BK = KS * 128 / ELEM;     // K per stage: KS 128-byte swizzle rows (K slices)
   static constexpr int UK = 32 / ELEM;           // K per tcgen05.mma (32 bytes)
-  static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int A_SLICE = BM * 128, B_SLICE = BN * 128;
+  static constexpr int A_BYTES = KS * A_SLICE;
+  static constexpr int B_BYTES = KS * B_SLICE;
   static constexpr int RAW_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGE_BYTES = PRE ? 2 * RAW_BYTES : RAW_BYTES;  // one TMA ring stage
   // kTF32S: two split slots (lo parts) double-buffer the converter -> MMA
@@ -131,6 +178,7 @@ struct TileCfg {
       ACC_COLS <= 32 ? 32 : ACC_COLS <= 64 ? 64 : ACC_COLS <= 128 ? 128 : ACC_COLS <= 256 ? 256 : 512;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (size_t)LO_SLOTS * RAW_BYTES + 256;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
+  static_assert(KS == 1 || MODE == kBF16, "several K slices per stage: bf16 only");
   static_assert(ACC_COLS <= 512, "TMEM columns");
   static_assert(STAGES >= 2, "pipeline depth");
   static_assert(1024 + (size_t)STAGES * STAGE_BYTES + (size_t)LO_SLOTS * RAW_BYTES + 256 <= (size_t)SMEM_LIMIT,
@@ -295,12 +343,12 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
   }
 }
 
-template <int BN, int MODE>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, int MODE, int KS>
+__global__ void __launch_bounds__(kMaxGemmThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, int M, int N,
                      int K, GemmEpilogue ep, int *err) {
-  using C = TileCfg<BN, MODE>;
+  using C = TileCfg<BN, MODE, KS>;
   constexpr bool TF32X3 = C::TF32X3;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -362,33 +410,43 @@ __global__ void __launch_bounds__(192, 1)
     atomicOr(err, 1 << AF_ERR_TIMEOUT);
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (is_producer_warp(warp)) {
+    if (lane == 0 && producer_id(warp) < active_producers(S)) {
+      // producer p issues the K slices kb = p (mod np)
+      const int np = active_producers(S), p = producer_id(warp);
       auto load_a = [&](int i, int kx) {
         const int ka = kx % ep.a_kb, ma = m0 + (kx / ep.a_kb) * M;  // K-blocked A
-        tma_load_2d(stage_a(i), &tmA, &full[i], ka, ma);
-        if constexpr (C::PRE) tma_load_2d(lo_a(i, 0), &tmA2, &full[i], ka, ma);
+        if constexpr (KS > 1) {  // KS slices in one 3-D copy (K blocks are multiples of BK)
+          tma_load_3d(stage_a(i), &tmA, &full[i], 0, ma, ka / 64);
+        } else {
+          tma_load_2d(stage_a(i), &tmA, &full[i], ka, ma);
+          if constexpr (C::PRE) tma_load_2d(lo_a(i, 0), &tmA2, &full[i], ka, ma);
+        }
       };
       auto load_b = [&](int i, int kx) {
-        tma_load_2d(stage_b(i), &tmB, &full[i], kx, n0);
-        if constexpr (C::PRE) tma_load_2d(lo_b(i, 0), &tmB2, &full[i], kx, n0);
+        if constexpr (KS > 1) {
+          tma_load_3d(stage_b(i), &tmB, &full[i], 0, n0, kx / 64);
+        } else {
+          tma_load_2d(stage_b(i), &tmB, &full[i], kx, n0);
+          if constexpr (C::PRE) tma_load_2d(lo_b(i, 0), &tmB2, &full[i], kx, n0);
+        }
       };
       // The operand that does not depend on the previous kernel (the
       // weights) fills the free ring slots before the dependency wait; the
       // other one follows it (always issued, so every slot's barrier completes).
       const int pre = ep.pre_operand ? (nk < S ? nk : S) : 0;
-      for (int kb = 0; kb < pre; ++kb) {
+      for (int kb = p; kb < pre; kb += np) {
         mbar_arrive_expect_tx(&full[kb], C::STAGE_BYTES);
         if (ep.pre_operand == 1) load_a(kb, (kb_base + kb) * C::BK);
         else load_b(kb, (kb_base + kb) * C::BK);
       }
       griddep_wait();
-      for (int kb = 0; kb < pre; ++kb) {
+      for (int kb = p; kb < pre; kb += np) {
         if (ep.pre_operand == 1) load_b(kb, (kb_base + kb) * C::BK);
         else load_a(kb, (kb_base + kb) * C::BK);
       }
-      int issued = pre;
-      for (int kb = pre; kb < nk && !s_abort; ++kb) {
+      int issued = pre;  // K slices [0, issued) are this producer's share issued so far
+      for (int kb = first_owned(pre, p, np); kb < nk && !s_abort; kb += np) {
         const int i = kb % S;
         const uint32_t ph = (kb / S) & 1;
         if (!mbar_wait(&empty[i], ph ^ 1)) { fail(); break; }
@@ -398,9 +456,7 @@ __global__ void __launch_bounds__(192, 1)
         load_b(i, kx);
         issued = kb + 1;
       }
-      // drain: every issued load has landed before this CTA may exit
-      for (int kb = issued - S < 0 ? 0 : issued - S; kb < issued; ++kb)
-        if (!mbar_wait(&full[kb % S], (kb / S) & 1)) { fail(); break; }
+      drain_producer(full, S, nk, issued, p, np, s_abort != 0, fail);
     }
   } else if (warp == 1) {
     constexpr uint32_t idesc = idesc_f32acc(TF32X3 ? kFmtTF32 : kFmtBF16, C::BM, BN);
@@ -415,19 +471,23 @@ __global__ void __launch_bounds__(192, 1)
       if (__any_sync(0xffffffffu, s_abort != 0)) break;
       tc_fence_after();
       if (lane == 0) {
-        const uint64_t da = sdesc_k_sw128(stage_a(i)), db = sdesc_k_sw128(stage_b(i));
 #pragma unroll
-        for (int k = 0; k < C::BK / C::UK; ++k) {
-          const uint64_t off = (uint64_t)(k * 32) >> 4;  // 32 bytes along K inside the swizzle row
-          if constexpr (TF32X3) {
-            const uint64_t dal = sdesc_k_sw128(lo_a(i, j)), dbl = sdesc_k_sw128(lo_b(i, j));
-            const uint32_t acc = tmem + (uint32_t)((kb % C::NACC) * BN);
-            const uint32_t corr = tmem + (uint32_t)(C::NACC * BN);
-            umma_tf32(acc, da + off, db + off, idesc, (kb >= C::NACC || k > 0) ? 1u : 0u);
-            umma_tf32(corr, da + off, dbl + off, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            umma_tf32(corr, dal + off, db + off, idesc, 1);
-          } else {
-            umma_bf16(tmem, da + off, db + off, idesc, (kb | k) != 0);
+        for (int sl = 0; sl < KS; ++sl) {
+          const uint64_t da = sdesc_k_sw128(stage_a(i) + sl * C::A_SLICE),
+                         db = sdesc_k_sw128(stage_b(i) + sl * C::B_SLICE);
+#pragma unroll
+          for (int k = 0; k < 128 / 32; ++k) {
+            const uint64_t off = (uint64_t)(k * 32) >> 4;  // 32 bytes along K inside the swizzle row
+            if constexpr (TF32X3) {
+              const uint64_t dal = sdesc_k_sw128(lo_a(i, j)), dbl = sdesc_k_sw128(lo_b(i, j));
+              const uint32_t acc = tmem + (uint32_t)((kb % C::NACC) * BN);
+              const uint32_t corr = tmem + (uint32_t)(C::NACC * BN);
+              umma_tf32(acc, da + off, db + off, idesc, (kb >= C::NACC || k > 0) ? 1u : 0u);
+              umma_tf32(corr, da + off, dbl + off, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              umma_tf32(corr, dal + off, db + off, idesc, 1);
+            } else {
+              umma_bf16(tmem, da + off, db + off, idesc, (kb | sl | k) != 0);
+            }
           }
         }
         umma_commit(&empty[i]);
@@ -511,7 +571,7 @@ __global__ void __launch_bounds__(192, 1)
 // TMEM accumulators so the epilogue of one tile overlaps the MMAs of the
 // next.  The TMA ring and its phases run continuously across tiles.
 template <int BN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kMaxGemmThreads, 1)
     umma_gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                 int M, int N, int K, GemmEpilogue ep, int *err) {
   using C = TileCfg<BN, kBF16>;
@@ -561,23 +621,24 @@ __global__ void __launch_bounds__(192, 1)
     atomicOr(err, 1 << AF_ERR_TIMEOUT);
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
-      int g = 0;  // k slices issued so far, over all tiles
-      for (int t = blockIdx.x; t < total && !s_abort; t += gridDim.x) {
+  if (is_producer_warp(warp)) {
+    if (lane == 0 && producer_id(warp) < active_producers(S)) {
+      const int np = active_producers(S), p = producer_id(warp);  // producer p: slices g = p (mod np)
+      const int my_tiles = blockIdx.x < total ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+      const int g_end = my_tiles * nk;  // K slices of this CTA over all its tiles
+      int issued = 0;
+      for (int g = p; g < g_end && !s_abort; g += np) {
+        const int t = (int)blockIdx.x + (g / nk) * (int)gridDim.x, kb = g % nk;
         const int m0 = (t / n_tiles) * C::BM, n0 = (t % n_tiles) * BN;
-        for (int kb = 0; kb < nk; ++kb, ++g) {
-          const int i = g % S;
-          if (!mbar_wait(&empty[i], ((g / S) & 1) ^ 1)) { fail(); break; }
-          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-          const int kx = kb * C::BK;
-          tma_load_2d(stage_a(i), &tmA, &full[i], kx % ep.a_kb, m0 + (kx / ep.a_kb) * M);
-          tma_load_2d(stage_b(i), &tmB, &full[i], kb * C::BK, n0);
-        }
-        if (s_abort) break;
+        const int i = g % S;
+        if (!mbar_wait(&empty[i], ((g / S) & 1) ^ 1)) { fail(); break; }
+        mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+        const int kx = kb * C::BK;
+        tma_load_2d(stage_a(i), &tmA, &full[i], kx % ep.a_kb, m0 + (kx / ep.a_kb) * M);
+        tma_load_2d(stage_b(i), &tmB, &full[i], kb * C::BK, n0);
+        issued = g + 1;
       }
-      for (int x = g - S < 0 ? 0 : g - S; x < g; ++x)  // drain the loads still in flight
-        if (!mbar_wait(&full[x % S], (x / S) & 1)) { fail(); break; }
+      drain_producer(full, S, g_end, issued, p, np, s_abort != 0, fail);
     }
   } else if (warp == 1) {
     constexpr uint32_t idesc = idesc_f32acc(kFmtBF16, C::BM, BN);
@@ -658,19 +719,28 @@ __global__ void __launch_bounds__(192, 1)
 //   empty[i] (each)    the MMAs reading stage i retired (commit to both CTAs)
 //   accf[b]  (each)    accumulator b holds a finished tile (commit to both)
 //   acce[b]  (rank 0)  both CTAs' epilogues (256 threads) read accumulator b
+//
+// A ring stage holds KS consecutive 64-element K slices (KS = 2 when K allows:
+// one 3-D TMA copy per operand and stage).  Each stage costs the MMA thread a
+// barrier wait and a commit per CTA, about 200 ns measured on B200 against
+// 70 ns per 256 x 256 x 16 MMA, so two slices per stage (8 MMAs) amortise
+// them twice as well as one.
+template <int KS>
 struct PairCfg {
-  static constexpr int BM = 256, BN = 256, HALF = 128, BK = 64;
-  static constexpr int A_BYTES = HALF * 128, B_BYTES = HALF * 128, STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BM = 256, BN = 256, HALF = 128, BK = 64 * KS;  // K elements per stage
+  static constexpr int SLICE = HALF * 128;                            // one K slice of 128 rows
+  static constexpr int A_BYTES = KS * SLICE, B_BYTES = KS * SLICE, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SMEM_LIMIT = 227 * 1024 - 64;
   static constexpr int STAGES = (SMEM_LIMIT - 1024 - 256) / STAGE_BYTES;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
   static_assert(STAGES >= 2 && 2 * STAGES + 5 <= 32, "ring depth / barrier block");
 };
 
-__global__ void __launch_bounds__(192, 1)
+template <int KS>
+__global__ void __launch_bounds__(kMaxGemmThreads, 1)
     umma_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
                           int N, int K, GemmEpilogue ep, int *err) {
-  using C = PairCfg;
+  using C = PairCfg<KS>;
   constexpr int S = C::STAGES;
   constexpr uint32_t TM_COLS = 512;  // two 256-column accumulators
   extern __shared__ uint8_t smem_raw[];
@@ -718,24 +788,31 @@ __global__ void __launch_bounds__(192, 1)
     atomicOr(err, 1 << AF_ERR_TIMEOUT);
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
-      int g = 0;  // K slices issued, over all tiles
-      for (int t = cid; t < total && !s_abort; t += ncl) {
+  if (is_producer_warp(warp)) {
+    if (lane == 0 && producer_id(warp) < active_producers(S)) {
+      const int np = active_producers(S), p = producer_id(warp);  // producer p: slices g = p (mod np)
+      const int my_tiles = cid < total ? (total - 1 - cid) / ncl + 1 : 0;
+      const int g_end = my_tiles * nk;  // K slices of this pair over all its tiles
+      int issued = 0;
+      for (int g = p; g < g_end && !s_abort; g += np) {
+        const int t = cid + (g / nk) * ncl, kb = g % nk;
         const int m0 = (t / n_tiles) * C::BM + (int)rank * C::HALF, n0 = (t % n_tiles) * C::BN + (int)rank * C::HALF;
-        for (int kb = 0; kb < nk; ++kb, ++g) {
-          const int i = g % S;
-          if (!mbar_wait(&empty[i], ((g / S) & 1) ^ 1)) { fail(); break; }
-          if (rank == 0) mbar_arrive_expect_tx(&full[i], 2 * C::STAGE_BYTES);
-          const uint32_t fb = mapa_shared(&full[i], 0);
-          const int kx = kb * C::BK;
+        const int i = g % S;
+        if (!mbar_wait(&empty[i], ((g / S) & 1) ^ 1)) { fail(); break; }
+        if (rank == 0) mbar_arrive_expect_tx(&full[i], 2 * C::STAGE_BYTES);
+        const uint32_t fb = mapa_shared(&full[i], 0);
+        const int kx = kb * C::BK;
+        if constexpr (KS == 1) {
           tma_load_2d_pair(stage_a(i), &tmA, fb, kx % ep.a_kb, m0 + (kx / ep.a_kb) * M);
           tma_load_2d_pair(stage_b(i), &tmB, fb, kx, n0);
+        } else {  // KS slices per copy: K blocks of A are multiples of BK (host check)
+          tma_load_3d_pair(stage_a(i), &tmA, fb, 0, m0 + (kx / ep.a_kb) * M, (kx % ep.a_kb) / 64);
+          tma_load_3d_pair(stage_b(i), &tmB, fb, 0, n0, kx / 64);
         }
+        issued = g + 1;
       }
       if (rank == 0) {
-        for (int x = g - S < 0 ? 0 : g - S; x < g; ++x)  // both CTAs' loads still in flight
-          if (!mbar_wait(&full[x % S], (x / S) & 1)) { fail(); break; }
+        drain_producer(full, S, g_end, issued, p, np, s_abort != 0, fail);  // both CTAs' loads
       } else if (s_abort) {
         // this CTA's loads complete the other CTA's barriers: give them time to land
         const uint64_t t0 = globaltimer();
@@ -763,11 +840,14 @@ __global__ void __launch_bounds__(192, 1)
           }
           tc_fence_after();
           if (lane == 0) {
-            const uint64_t da = sdesc_k_sw128(stage_a(i)), db = sdesc_k_sw128(stage_b(i));
 #pragma unroll
-            for (int k = 0; k < C::BK / 16; ++k) {
-              const uint64_t off = (uint64_t)(k * 32) >> 4;
-              umma_bf16_pair(acc, da + off, db + off, idesc, (kb | k) != 0);
+            for (int sl = 0; sl < KS; ++sl) {
+              const uint64_t da = sdesc_k_sw128(stage_a(i) + sl * C::SLICE), db = sdesc_k_sw128(stage_b(i) + sl * C::SLICE);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const uint64_t off = (uint64_t)(k * 32) >> 4;
+                umma_bf16_pair(acc, da + off, db + off, idesc, (kb | sl | k) != 0);
+              }
             }
             umma_commit_pair(mapa_shared(&empty[i], 0));
             umma_commit_pair(mapa_shared(&empty[i], 1));
@@ -846,7 +926,7 @@ struct PairSplitCfg {
 };
 
 template <int BN, int MODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kMaxGemmThreads, 1)
     umma_gemm_pair_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                 const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                                 int M, int N, int K, GemmEpilogue ep, int *err) {
@@ -898,8 +978,9 @@ __global__ void __launch_bounds__(192, 1)
     atomicOr(err, 1 << AF_ERR_TIMEOUT);
   };
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (is_producer_warp(warp)) {
+    if (lane == 0 && producer_id(warp) < active_producers(S)) {
+      const int np = active_producers(S), p = producer_id(warp);  // producer p: K slices kb = p (mod np)
       auto load_a = [&](int i, int kx) {
         const uint32_t fb = mapa_shared(&full[i], 0);
         const int ka = kx % ep.a_kb, ma = m0 + (kx / ep.a_kb) * M;
@@ -913,27 +994,28 @@ __global__ void __launch_bounds__(192, 1)
       };
       // operand independent of the previous kernel first (programmatic launch)
       const int pre = ep.pre_operand ? (nk < S ? nk : S) : 0;
-      for (int kb = 0; kb < pre; ++kb) {
+      for (int kb = p; kb < pre; kb += np) {
         if (rank == 0) mbar_arrive_expect_tx(&full[kb], 2 * C::STAGE_BYTES);
         if (ep.pre_operand == 1) load_a(kb, (kb_base + kb) * C::BK);
         else load_b(kb, (kb_base + kb) * C::BK);
       }
       griddep_wait();
-      for (int kb = 0; kb < pre; ++kb) {
+      for (int kb = p; kb < pre; kb += np) {
         if (ep.pre_operand == 1) load_b(kb, (kb_base + kb) * C::BK);
         else load_a(kb, (kb_base + kb) * C::BK);
       }
-      for (int kb = pre; kb < nk && !s_abort; ++kb) {
+      int issued = pre;
+      for (int kb = first_owned(pre, p, np); kb < nk && !s_abort; kb += np) {
         const int i = kb % S;
         if (!mbar_wait(&empty[i], ((kb / S) & 1) ^ 1)) { fail(); break; }
         if (rank == 0) mbar_arrive_expect_tx(&full[i], 2 * C::STAGE_BYTES);
         const int kx = (kb_base + kb) * C::BK;
         load_a(i, kx);
         load_b(i, kx);
+        issued = kb + 1;
       }
       if (rank == 0) {
-        for (int kb = nk - S < 0 ? 0 : nk - S; kb < nk; ++kb)  // both CTAs' loads still in flight
-          if (!mbar_wait(&full[kb % S], (kb / S) & 1)) { fail(); break; }
+        drain_producer(full, S, nk, issued, p, np, s_abort != 0, fail);  // both CTAs' loads
       } else if (s_abort) {
         const uint64_t t0 = globaltimer();  // this CTA's loads complete the other CTA's barriers
         while (globaltimer() - t0 < 100000ull) {
@@ -1015,6 +1097,12 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ------------------------------------------------------------------ host
+// Threads of a GEMM CTA: the six fixed warps and one more warp per extra
+// TMA producer (the option, capped at the ring depth).
+int block_threads(const af_ctx *ctx, int stages) {
+  return gemm_threads(ctx->gemm_producers < stages ? ctx->gemm_producers : stages);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int get_encoder(const char *fn) {
@@ -1061,7 +1149,8 @@ int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, in
   const int64_t total = (int64_t)((N + BN - 1) / BN) * ((M + C::BM - 1) / C::BM);
   const int cap = ep_max_ctas > 0 && ep_max_ctas < ctx->num_sms ? ep_max_ctas : ctx->num_sms;
   const int grid = (int)(total < cap ? total : cap);
-  umma_gemm_persistent_kernel<BN><<<grid, 192, C::SMEM, st>>>(ta, tb, M, N, K, ep, ctx->dev_err);
+  umma_gemm_persistent_kernel<BN><<<grid, block_threads(ctx, C::STAGES), C::SMEM, st>>>(ta, tb, M, N, K, ep,
+                                                                                       ctx->dev_err);
   return af::launched(ctx, fn);
 }
 
@@ -1090,7 +1179,7 @@ int launch_pair_split(af_ctx *ctx, const void *A, const void *A2, int64_t lda, c
     return arc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * ((M + 255) / 256), (N + BN - 1) / BN, splits);
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(block_threads(ctx, C::STAGES));
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
@@ -1108,22 +1197,46 @@ int launch_pair_split(af_ctx *ctx, const void *A, const void *A2, int64_t lda, c
   return af::launched(ctx, fn);
 }
 
-int launch_pair(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
-                const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
-  using C = PairCfg;
+// K-major 3-D view of a bf16 matrix for stages of KS K slices: {64 elements,
+// rows, K / 64 slices}, strides {row pitch, 128 bytes}; box {64, box_rows, KS}.
+int make_kslices_map(CUtensorMap *map, const void *base, int rows, int K, int64_t ld, int box_rows, int ks,
+                     const char *fn) {
+  cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(K / 64)};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, 128};
+  cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)ks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return af::fail(AF_ERR_ARG, "%s: cuTensorMapEncodeTiled (3-D) failed (%d)", fn, (int)r);
+  return AF_OK;
+}
+
+template <int KS>
+int launch_pair_ks(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
+                   const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
+  using C = PairCfg<KS>;
   CUtensorMap ta, tb;
-  int rc = make_kmajor_map(&ta, A, false, (K / ep.a_kb) * M, ep.a_kb, lda, C::HALF, fn);
-  if (rc) return rc;
-  rc = make_kmajor_map(&tb, B, false, N, K, ldb, C::HALF, fn);
+  int rc;
+  if constexpr (KS == 1) {
+    rc = make_kmajor_map(&ta, A, false, (K / ep.a_kb) * M, ep.a_kb, lda, C::HALF, fn);
+    if (rc) return rc;
+    rc = make_kmajor_map(&tb, B, false, N, K, ldb, C::HALF, fn);
+  } else {
+    rc = make_kslices_map(&ta, A, (K / ep.a_kb) * M, ep.a_kb, lda, C::HALF, KS, fn);
+    if (rc) return rc;
+    rc = make_kslices_map(&tb, B, N, K, ldb, C::HALF, KS, fn);
+  }
   if (rc) return rc;
   static std::atomic<unsigned long long> attr_devices{0};
-  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_pair_kernel), C::SMEM, attr_devices, fn))
+  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_pair_kernel<KS>), C::SMEM, attr_devices,
+                              fn))
     return arc;
   const int64_t total = (int64_t)((N + C::BN - 1) / C::BN) * ((M + C::BM - 1) / C::BM);
   const int pairs = (int)(total < ctx->num_sms / 2 ? total : ctx->num_sms / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(block_threads(ctx, C::STAGES));
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1133,20 +1246,38 @@ int launch_pair(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_kernel, ta, tb, M, N, K, ep, ctx->dev_err);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_kernel<KS>, ta, tb, M, N, K, ep, ctx->dev_err);
   if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: pair launch: %s", fn, cudaGetErrorString(e));
   return af::launched(ctx, fn);
 }
 
-template <int BN, int MODE>
-int launch_tc(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void *B, const void *B2, int64_t ldb,
-              int M, int N, int K, int splits, const GemmEpilogue &ep, cudaStream_t st, const char *fn, bool pdl) {
-  using C = TileCfg<BN, MODE>;
+// Two K slices per stage when every stage's slices lie in one K block of A
+// (K a multiple of 64; K blocks, if any, multiples of 128); AF_GEMM_KS=1
+// forces one.
+int launch_pair(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
+                const GemmEpilogue &ep, cudaStream_t st, const char *fn) {
+  bool two = K % 64 == 0 && (ep.a_kb == K || ep.a_kb % 128 == 0);
+  if (const char *e = getenv("AF_GEMM_KS")) two = two && atoi(e) != 1;
+  if (two) return launch_pair_ks<2>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+  return launch_pair_ks<1>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
+}
+
+template <int BN, int MODE, int KS>
+int launch_tc_ks(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void *B, const void *B2, int64_t ldb,
+                 int M, int N, int K, int splits, const GemmEpilogue &ep, cudaStream_t st, const char *fn, bool pdl) {
+  using C = TileCfg<BN, MODE, KS>;
   CUtensorMap ta, tb, ta2, tb2;
   const bool fp32 = MODE != kBF16;
-  int rc = make_kmajor_map(&ta, A, fp32, (K / ep.a_kb) * M, ep.a_kb, lda, C::BM, fn);
-  if (rc) return rc;
-  rc = make_kmajor_map(&tb, B, fp32, N, K, ldb, BN, fn);
+  int rc;
+  if constexpr (KS > 1) {
+    rc = make_kslices_map(&ta, A, (K / ep.a_kb) * M, ep.a_kb, lda, C::BM, KS, fn);
+    if (rc) return rc;
+    rc = make_kslices_map(&tb, B, N, K, ldb, BN, KS, fn);
+  } else {
+    rc = make_kmajor_map(&ta, A, fp32, (K / ep.a_kb) * M, ep.a_kb, lda, C::BM, fn);
+    if (rc) return rc;
+    rc = make_kmajor_map(&tb, B, fp32, N, K, ldb, BN, fn);
+  }
   if (rc) return rc;
   ta2 = ta;
   tb2 = tb;
@@ -1157,14 +1288,30 @@ int launch_tc(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const voi
     if (rc) return rc;
   }
   static std::atomic<unsigned long long> attr_devices{0};
-  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_kernel<BN, MODE>), C::SMEM,
+  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_kernel<BN, MODE, KS>), C::SMEM,
                               attr_devices, fn))
     return arc;
   const dim3 grid((N + BN - 1) / BN, (M + C::BM - 1) / C::BM, splits);
-  const cudaError_t e = af::launch_kernel(umma_gemm_kernel<BN, MODE>, grid, dim3(192), C::SMEM, st, pdl, ta, tb, ta2,
-                                          tb2, M, N, K, ep, ctx->dev_err);
+  const cudaError_t e =
+      af::launch_kernel(umma_gemm_kernel<BN, MODE, KS>, grid, dim3(block_threads(ctx, C::STAGES)), C::SMEM, st, pdl,
+                        ta, tb, ta2, tb2, M, N, K, ep, ctx->dev_err);
   if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: launch: %s", fn, cudaGetErrorString(e));
   return af::launched(ctx, fn);
+}
+
+// bf16 tiles up to 128 wide take two K slices per stage (half the MMA
+// thread's barrier waits and commits per MMA) when K is a multiple of 64, K
+// blocks of A are multiples of 128 and every split keeps at least one stage;
+// AF_GEMM_KS=1 forces one slice.
+template <int BN, int MODE>
+int launch_tc(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void *B, const void *B2, int64_t ldb,
+              int M, int N, int K, int splits, const GemmEpilogue &ep, cudaStream_t st, const char *fn, bool pdl) {
+  if constexpr (MODE == kBF16 && BN <= 128) {
+    bool two = K % 64 == 0 && (ep.a_kb == K || ep.a_kb % 128 == 0) && splits <= (K + 127) / 128;
+    if (const char *e = getenv("AF_GEMM_KS")) two = two && atoi(e) != 1;
+    if (two) return launch_tc_ks<BN, MODE, 2>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn, pdl);
+  }
+  return launch_tc_ks<BN, MODE, 1>(ctx, A, A2, lda, B, B2, ldb, M, N, K, splits, ep, st, fn, pdl);
 }
 
 // Splits the fp32 array src into an exact tf32 part and the remainder.

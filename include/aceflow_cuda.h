@@ -73,7 +73,8 @@ int af_check_device(af_ctx *ctx, int *flags, int reset);
  *                              W . x^T (bit 0 QKV, 1 W_o, 2 gate/up, 3 down; default 15)
  *   "pdl"                0/1   decode chains as programmatic dependent launches (default 1)
  *   "gemm_pair"          0/1   large bf16 GEMMs on CTA pairs, 256 x 256 tiles (default 1)
- *   "decode_pairs"       0/1   the decode step's projections on CTA pairs (default 1) */
+ *   "decode_pairs"       0/1   the decode step's projections on CTA pairs (default 1)
+ *   "gemm_producers"     1..4  TMA producer threads per tensor-core GEMM CTA (default 1) */
 int af_set_option(af_ctx *ctx, const char *name, int64_t value);
 /* Number of this library's kernel launches issued through `ctx` so far. */
 int af_launch_count(af_ctx *ctx, int64_t *count);

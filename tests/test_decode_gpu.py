@@ -297,3 +297,36 @@ def test_msr_decode_step_split_pairs_option(dev, pairs):
     finally:
         _lib.set_option(0, "decode_pairs", 1)
     assert _lib.check_device(0) == 0
+
+
+@pytest.mark.parametrize("groups", [1, 4])
+def test_msr_decode_step_split_four_producers(dev, groups):
+    """Decode step with four TMA producer threads per GEMM CTA, sequential and
+    over four head groups on three streams (the 3xTF32 GEMMs there have a
+    3-stage ring, so the producer count is capped at 3): equal to the oracle."""
+    from aceflow_b200 import _lib, cuda_ops
+
+    B, d, H = 256, 2048, 8
+    rng = np.random.default_rng(91)
+    dh = d // H
+    w_qkv = (0.02 * rng.standard_normal((3 * d, d))).astype(np.float32)
+    w_o = (0.02 * rng.standard_normal((d, d))).astype(np.float32)
+    ret_w = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    gamma = R.gammas(H)
+    wq_s, wo_s = cuda_ops.prepare_decode_weights(T(w_qkv, dev), T(w_o, dev), H)
+    st = np.zeros((B, H, dh, dh), np.float32)
+    st_d = torch.zeros(B, H, dh, dh, device=dev)
+    _lib.set_option(0, "gemm_producers", 4)
+    _lib.set_option(0, "decode_head_groups", groups)
+    try:
+        for s in range(2):
+            x = rng.standard_normal((B, d)).astype(np.float32)
+            ref = cpu_ref.msr_decode_step(x, st, gamma, w_qkv, w_o, ret_w, 1e-6)
+            out = cuda_ops.msr_decode_step_split(T(x, dev), st_d, T(gamma, dev), wq_s, wo_s, T(ret_w, dev), 1e-6)
+            torch.cuda.synchronize()
+            assert rel_err(out.cpu().numpy(), ref) < TOL, s
+            assert rel_err(st_d.cpu().numpy(), st) < TOL, s
+    finally:
+        _lib.set_option(0, "gemm_producers", 1)
+        _lib.set_option(0, "decode_head_groups", 1)
+    assert _lib.check_device(0) == 0

@@ -137,3 +137,79 @@ def test_bf16_gemm_cta_pair_matches_fp64(dev, M, N, K):
         _lib.set_option(0, "gemm_pair", 1)
     assert rel_err(out.cpu().numpy(), one.cpu().numpy()) < 1e-6
     _check(dev)
+
+
+@pytest.mark.parametrize("producers", [2, 4])
+def test_gemm_producer_threads_same_result(dev, producers):
+    """TMA loads spread over several producer threads (af_set_option
+    "gemm_producers") feed the MMAs the same K slices in the same order: the
+    CTA-pair GEMM (no split-K) is bit-identical, the split-K ones (atomic
+    adds in any order) and the pre-split decode GEMM agree to fp32 rounding.
+    Kernels whose ring is shallower than the producer count (3 stages for
+    3xTF32 tiles of 128 columns) cap it."""
+    from aceflow_b200 import _lib, cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(producers)
+    cases = []
+    for M, N, K in [(8192, 2048, 2048), (300, 200, 136), (64, 11264, 2048)]:
+        a = torch.randn(M, K, generator=g, device=dev).bfloat16()
+        b = (0.05 * torch.randn(N, K, generator=g, device=dev)).bfloat16()
+        cases.append((a, b))
+    x = torch.randn(256, 2048, generator=g, device=dev)
+    w = 0.02 * torch.randn(6144, 2048, generator=g, device=dev)
+    xs, ws = cuda_ops.split_tf32(x), cuda_ops.split_tf32(w)
+
+    def run():
+        outs = []
+        for a, b in cases:
+            o = torch.empty(a.shape[0], b.shape[0], device=dev)
+            cuda_ops.gemm_bf16(a, b, o)
+            outs.append(o)
+        outs.append(cuda_ops.linear_f32_split(xs, ws))
+        torch.cuda.synchronize()
+        return outs
+
+    ref = run()
+    _lib.set_option(0, "gemm_producers", producers)
+    try:
+        got = run()
+    finally:
+        _lib.set_option(0, "gemm_producers", 1)
+    assert torch.equal(ref[0], got[0])
+    for r, o in zip(ref[1:], got[1:]):
+        assert rel_err(o.cpu().numpy(), r.cpu().numpy()) < 1e-6
+    _check(dev)
+
+
+@pytest.mark.parametrize("bn", ["16", "32", "64", "128"])
+@pytest.mark.parametrize("M,N,K", [(64, 11264, 2048), (300, 200, 192), (1000, 96, 4096)])
+def test_bf16_two_k_slices_per_stage(dev, bn, M, N, K, monkeypatch):
+    """bf16 tiles up to 128 wide load two 64-element K slices per ring stage
+    with one 3-D TMA copy per operand (K a multiple of 64): the MMAs run in
+    the same order as with one slice per stage, so without split-K the two
+    are bit-identical, and both equal the fp64 product."""
+    from aceflow_b200 import cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g, device=dev).bfloat16()
+    b = (0.05 * torch.randn(N, K, generator=g, device=dev)).bfloat16()
+    ref = (a.double() @ b.double().t()).cpu().numpy()
+    monkeypatch.setenv("AF_GEMM_BN", bn)
+    monkeypatch.setenv("AF_GEMM_SPLITS", "1")
+    outs = []
+    for ks in ("2", "1"):
+        monkeypatch.setenv("AF_GEMM_KS", ks)
+        o = torch.empty(M, N, device=dev)
+        cuda_ops.gemm_bf16(a, b, o)
+        torch.cuda.synchronize()
+        outs.append(o)
+    assert torch.equal(outs[0], outs[1])
+    assert rel_err(outs[0].cpu().numpy(), ref) < 1e-5
+    # split-K over two-slice stages (atomics): fp32 rounding of the partial sums
+    monkeypatch.setenv("AF_GEMM_KS", "2")
+    monkeypatch.setenv("AF_GEMM_SPLITS", "3")
+    o = torch.empty(M, N, device=dev)
+    cuda_ops.gemm_bf16(a, b, o)
+    torch.cuda.synchronize()
+    assert rel_err(o.cpu().numpy(), ref) < 1e-5
+    _check(dev)
