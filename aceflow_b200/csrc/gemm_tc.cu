@@ -67,7 +67,13 @@ struct GemmEpilogue {
   int scale_residual;      // the row scale multiplies the residual too: (acc + r) * scale
   int res_vec;             // residual base 16-byte aligned and ldr a whole number of 16-byte units
   int pre_operand;         // 1 = A, 2 = B: loaded for the first ring slots before griddep_wait()
+  // Tile written through shared memory by TMA (the ring, free once the
+  // accumulator is complete), see store_tile_staged: 0 = no, kStageTrans =
+  // transposed plain store [BN][128] (partial buffers: z = split), kStageAdd
+  // = row-major reduce-add into out, 128-byte-swizzled 32-column boxes.
+  int staged;
 };
+constexpr int kStageTrans = 1, kStageAdd = 2;
 
 // v[e] += r[e] * rs for the 16 columns n..n+15 of one row (vector loads when
 // the row segment is whole and aligned: each thread owns a different row, so
@@ -343,11 +349,83 @@ __device__ __forceinline__ void store_tile(const GemmEpilogue &ep, Load16 &&load
   }
 }
 
+// Bulk tensor stores from shared memory (bulk async-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+// Element-wise f32 add of a shared-memory box into global memory (performed
+// at L2; replaces per-thread atomics of a split-K or accumulating epilogue).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_wait_all() {
+  asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Barrier over the four epilogue warps (2..5).
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Epilogue through shared memory: the calling warp's 32 rows of a 128 x BN
+// accumulator tile are written to `stg` (the free TMA ring) and one thread
+// stores the tile with TMA.
+//   kStageTrans: element (row, n) at stg[n * 128 + row] (lanes: consecutive
+//     rows, conflict-free); one 3-D store {row, n, split} of the [BN][128]
+//     box: the transposed product, or its split's partial buffer.
+//   kStageAdd: 32-column boxes [128 rows][32 cols] one after another, each
+//     128-byte swizzled (16-byte chunk c of row r at chunk c ^ (r & 7), so the
+//     lanes' float4 writes spread over the banks); the row scale is applied
+//     and each box is added into out by a TMA reduce-add.
+// Rows and columns past the output are dropped by the tensor map bounds.
+template <int BN, class Load16, class WaitLd>
+__device__ __forceinline__ void store_tile_staged(const GemmEpilogue &ep, const CUtensorMap *tmO, Load16 &&load16,
+                                                  WaitLd &&wait_ld, float *stg, int r, int m0, int n0, int z,
+                                                  bool ok, float scale) {
+  if (ep.staged == kStageTrans) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      load16(c, v);
+      wait_ld();
+#pragma unroll
+      for (int e = 0; e < 16; ++e) stg[(c + e) * 128 + r] = v[e];
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      load16(c, v);
+      wait_ld();
+      uint8_t *box = reinterpret_cast<uint8_t *>(stg) + (c / 32) * (128 * 128) + r * 128;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int chunk = ((c % 32) / 4 + u) ^ (r & 7);
+        *reinterpret_cast<float4 *>(box + chunk * 16) =
+            make_float4(v[4 * u] * scale, v[4 * u + 1] * scale, v[4 * u + 2] * scale, v[4 * u + 3] * scale);
+      }
+    }
+  }
+  fence_proxy_async_smem();  // generic-proxy writes before the bulk copy reads them
+  epilogue_sync();
+  if (threadIdx.x == 64 && ok) {
+    if (ep.staged == kStageTrans) {
+      tma_store_3d(tmO, stg, m0, n0, z);
+    } else {
+#pragma unroll 1
+      for (int j = 0; j < BN / 32; ++j)
+        tma_reduce_add_2d(tmO, reinterpret_cast<uint8_t *>(stg) + j * (128 * 128), n0 + 32 * j, m0);
+    }
+    bulk_commit_wait_all();  // shared memory is read (and the writes issued) before the CTA exits
+  }
+}
+
 template <int BN, int MODE, int KS>
 __global__ void __launch_bounds__(kMaxGemmThreads, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, int M, int N,
-                     int K, GemmEpilogue ep, int *err) {
+                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                     const __grid_constant__ CUtensorMap tmO, int M, int N, int K, GemmEpilogue ep, int *err) {
   using C = TileCfg<BN, MODE, KS>;
   constexpr bool TF32X3 = C::TF32X3;
   constexpr int S = C::STAGES;
@@ -556,7 +634,11 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
     auto wait_ld = [&]() {
       if constexpr (!TF32X3) tmem_wait_ld();
     };
-    store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, ok, scale, blockIdx.z == 0);
+    if (ep.staged)
+      store_tile_staged<BN>(ep, &tmO, load16, wait_ld, reinterpret_cast<float *>(smem), q * 32 + lane, m0, n0,
+                            blockIdx.z, ok && !s_abort, scale);
+    else
+      store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, ok, scale, blockIdx.z == 0);
   }
   tc_fence_before();
   __syncthreads();
@@ -929,7 +1011,8 @@ template <int BN, int MODE>
 __global__ void __launch_bounds__(kMaxGemmThreads, 1)
     umma_gemm_pair_split_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                                 const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                                int M, int N, int K, GemmEpilogue ep, int *err) {
+                                const __grid_constant__ CUtensorMap tmO, int M, int N, int K, GemmEpilogue ep,
+                                int *err) {
   using C = PairSplitCfg<BN, MODE>;
   constexpr bool TF32X3 = C::TF32X3;
   constexpr int S = C::STAGES;
@@ -1085,7 +1168,11 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
     auto wait_ld = [&]() {
       if constexpr (!TF32X3) tmem_wait_ld();
     };
-    store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, ok && !s_abort, scale, blockIdx.z == 0);
+    if (ep.staged)
+      store_tile_staged<BN>(ep, &tmO, load16, wait_ld, reinterpret_cast<float *>(smem), q * 32 + lane, m0, n0,
+                            blockIdx.z, ok && !s_abort, scale);
+    else
+      store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, ok && !s_abort, scale, blockIdx.z == 0);
   }
   tc_fence_before();
   __syncthreads();
@@ -1132,6 +1219,34 @@ int make_kmajor_map(CUtensorMap *map, const void *base, bool fp32, int rows, int
   if (r != CUDA_SUCCESS) return af::fail(AF_ERR_ARG, "%s: cuTensorMapEncodeTiled failed (%d)", fn, (int)r);
   return AF_OK;
 }
+
+// Tensor map of the output for a staged epilogue (store_tile_staged).
+int make_staged_out_map(CUtensorMap *map, const GemmEpilogue &ep, int M, int N, int splits, int BN, const char *fn) {
+  CUresult r;
+  if (ep.staged == kStageTrans) {
+    const int64_t zs = ep.split_stride ? ep.split_stride : ep.ldo * (int64_t)N;
+    cuuint64_t dims[3] = {(cuuint64_t)M, (cuuint64_t)N, (cuuint64_t)(ep.split_stride ? splits : 1)};
+    cuuint64_t strides[2] = {(cuuint64_t)ep.ldo * 4, (cuuint64_t)zs * 4};
+    cuuint32_t box[3] = {128, (cuuint32_t)BN, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ep.out, dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)ep.ldo * 4};
+    cuuint32_t box[2] = {32, 128};
+    cuuint32_t estr[2] = {1, 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ep.out, dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
+  if (r != CUDA_SUCCESS) return af::fail(AF_ERR_ARG, "%s: output tensor map failed (%d)", fn, (int)r);
+  return AF_OK;
+}
+
+// Bytes of shared memory a staged epilogue of a 128 x BN tile needs.
+constexpr size_t staged_bytes(int BN) { return (size_t)128 * BN * 4; }
 
 template <int BN>
 int launch_persistent(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64_t ldb, int M, int N, int K,
@@ -1191,8 +1306,17 @@ int launch_pair_split(af_ctx *ctx, const void *A, const void *A2, int64_t lda, c
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_split_kernel<BN, MODE>, ta, tb, ta2, tb2, M, N, K, ep,
-                                           ctx->dev_err);
+  CUtensorMap to = ta;
+  GemmEpilogue epx = ep;
+  // the ring must hold the staged tile; reduce-adds go in 32-column boxes
+  if ((size_t)C::STAGES * C::STAGE_BYTES < staged_bytes(BN) || (epx.staged == kStageAdd && BN % 32 != 0))
+    epx.staged = 0;
+  if (epx.staged) {
+    rc = make_staged_out_map(&to, epx, M, N, splits, BN, fn);
+    if (rc) return rc;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_split_kernel<BN, MODE>, ta, tb, ta2, tb2, to, M, N, K,
+                                           epx, ctx->dev_err);
   if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: pair launch: %s", fn, cudaGetErrorString(e));
   return af::launched(ctx, fn);
 }
@@ -1287,6 +1411,15 @@ int launch_tc_ks(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const 
     rc = make_kmajor_map(&tb2, B2, true, N, K, ldb, BN, fn);
     if (rc) return rc;
   }
+  CUtensorMap to = ta;
+  GemmEpilogue epx = ep;
+  // the ring must hold the staged tile; reduce-adds go in 32-column boxes
+  if ((size_t)C::STAGES * C::STAGE_BYTES < staged_bytes(BN) || (epx.staged == kStageAdd && BN % 32 != 0))
+    epx.staged = 0;
+  if (epx.staged) {
+    rc = make_staged_out_map(&to, epx, M, N, splits, BN, fn);
+    if (rc) return rc;
+  }
   static std::atomic<unsigned long long> attr_devices{0};
   if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(umma_gemm_kernel<BN, MODE, KS>), C::SMEM,
                               attr_devices, fn))
@@ -1294,7 +1427,7 @@ int launch_tc_ks(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const 
   const dim3 grid((N + BN - 1) / BN, (M + C::BM - 1) / C::BM, splits);
   const cudaError_t e =
       af::launch_kernel(umma_gemm_kernel<BN, MODE, KS>, grid, dim3(block_threads(ctx, C::STAGES)), C::SMEM, st, pdl,
-                        ta, tb, ta2, tb2, M, N, K, ep, ctx->dev_err);
+                        ta, tb, ta2, tb2, to, M, N, K, epx, ctx->dev_err);
   if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: launch: %s", fn, cudaGetErrorString(e));
   return af::launched(ctx, fn);
 }
@@ -1449,6 +1582,14 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
       cudaError_t e = cudaMemsetAsync(a.out, 0, (size_t)M * a.ldo * 4, st);
       if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: zeroing the split-K output: %s", fn, cudaGetErrorString(e));
     }
+  }
+  // Epilogue through shared memory and TMA (umma_gemm_kernel and the pair
+  // split kernel): transposed plain stores (partial buffers) and row-major
+  // accumulation without bias or residual.  AF_GEMM_NO_STAGE=1 turns it off.
+  const bool out_ok = af::aligned16(a.out) && (a.ldo * 4) % 16 == 0 && (a.split_stride * 4) % 16 == 0;
+  if (out_ok && !a.out_bf16 && !a.swiglu && !getenv("AF_GEMM_NO_STAGE")) {
+    if (a.trans && !ep.atomic && !a.row_parts) ep.staged = kStageTrans;
+    else if (!a.trans && ep.atomic && !ep.residual && !a.bias) ep.staged = kStageAdd;
   }
   // large bf16 GEMMs (two or more waves of tiles): persistent kernel
   if (MODE == kBF16 && splits == 1 && !a.trans && !a.pair && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms &&

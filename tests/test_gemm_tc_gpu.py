@@ -213,3 +213,41 @@ def test_bf16_two_k_slices_per_stage(dev, bn, M, N, K, monkeypatch):
     torch.cuda.synchronize()
     assert rel_err(o.cpu().numpy(), ref) < 1e-5
     _check(dev)
+
+
+@pytest.mark.parametrize("M,N,K,bn,splits", [(256, 2048, 2048, "128", "4"), (300, 200, 512, "64", "3"),
+                                             (130, 1000, 1024, "32", "2")])
+def test_staged_reduce_add_epilogue(dev, M, N, K, bn, splits, monkeypatch):
+    """Split-K partial products added into the output by TMA reduce-adds of
+    128-byte-swizzled shared-memory boxes (ragged M and N clipped by the
+    tensor map), with and without the 1/rms row scale, equal to the per-thread
+    atomics and to fp64."""
+    from aceflow_b200 import cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(M + N)
+    x = torch.randn(M, K, generator=g, device=dev)
+    w = 0.02 * torch.randn(N, K, generator=g, device=dev)
+    parts = torch.rand(M, 4, generator=g, device=dev) * 10
+    scale = 1.0 / torch.sqrt(parts.double().sum(1, keepdim=True) / K + 1e-6)
+    xs, ws = cuda_ops.split_tf32(x), cuda_ops.split_tf32(w)
+    ref = (x.double() @ w.double().T).cpu().numpy()
+    monkeypatch.setenv("AF_GEMM_BN", bn)
+    monkeypatch.setenv("AF_GEMM_SPLITS", splits)
+    outs = []
+    for no_stage in (False, True):
+        if no_stage:
+            monkeypatch.setenv("AF_GEMM_NO_STAGE", "1")
+        y = cuda_ops.linear_f32_split(xs, ws)
+        torch.cuda.synchronize()
+        outs.append(y.cpu().numpy())
+    assert rel_err(outs[0], ref) < 1e-5
+    assert rel_err(outs[0], outs[1]) < 1e-6
+    monkeypatch.delenv("AF_GEMM_NO_STAGE")
+    ab = x.bfloat16()
+    bb = w.bfloat16()
+    o = torch.empty(M, N, device=dev)
+    cuda_ops.gemm_bf16(ab, bb, o, parts, inv_d=1.0 / K, eps=1e-6)
+    torch.cuda.synchronize()
+    ref2 = (ab.double() @ bb.double().t() * scale).cpu().numpy()
+    assert rel_err(o.cpu().numpy(), ref2) < 1e-5
+    _check(dev)
