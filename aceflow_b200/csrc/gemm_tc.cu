@@ -70,10 +70,11 @@ struct GemmEpilogue {
   // Tile written through shared memory by TMA (the ring, free once the
   // accumulator is complete), see store_tile_staged: 0 = no, kStageTrans =
   // transposed plain store [BN][128] (partial buffers: z = split), kStageAdd
-  // = row-major reduce-add into out, 128-byte-swizzled 32-column boxes.
+  // = row-major reduce-add into out, 128-byte-swizzled 32-column boxes,
+  // kStageTransAdd = transposed reduce-add of the [BN][128] box.
   int staged;
 };
-constexpr int kStageTrans = 1, kStageAdd = 2;
+constexpr int kStageTrans = 1, kStageAdd = 2, kStageTransAdd = 3, kStageSwiGLU = 4;
 
 // v[e] += r[e] * rs for the 16 columns n..n+15 of one row (vector loads when
 // the row segment is whole and aligned: each thread owns a different row, so
@@ -355,6 +356,11 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void 
                "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
 // Element-wise f32 add of a shared-memory box into global memory (performed
 // at L2; replaces per-thread atomics of a split-K or accumulating epilogue).
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const void *src, int x, int y) {
@@ -374,6 +380,11 @@ __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;
 //   kStageTrans: element (row, n) at stg[n * 128 + row] (lanes: consecutive
 //     rows, conflict-free); one 3-D store {row, n, split} of the [BN][128]
 //     box: the transposed product, or its split's partial buffer.
+//   kStageTransAdd: the same box with the per-column 1/rms (columns are
+//     streams) applied, added into out by one 2-D TMA reduce-add {row, n}.
+//   kStageSwiGLU: transposed SwiGLU (rows in groups of 16 gate then 16 up):
+//     h = silu(gate) * up as bf16 at [n][hidden], hidden = m0/2 + 0..63, one
+//     2-D store of the [BN][64] box.
 //   kStageAdd: 32-column boxes [128 rows][32 cols] one after another, each
 //     128-byte swizzled (16-byte chunk c of row r at chunk c ^ (r & 7), so the
 //     lanes' float4 writes spread over the banks); the row scale is applied
@@ -382,13 +393,37 @@ __device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;
 template <int BN, class Load16, class WaitLd>
 __device__ __forceinline__ void store_tile_staged(const GemmEpilogue &ep, const CUtensorMap *tmO, Load16 &&load16,
                                                   WaitLd &&wait_ld, float *stg, int r, int m0, int n0, int z,
-                                                  bool ok, float scale) {
-  if (ep.staged == kStageTrans) {
+                                                  int N, bool ok, float scale) {
+  if (ep.staged == kStageSwiGLU) {
+    const int lane = threadIdx.x & 31;
+    __nv_bfloat16 *hb = reinterpret_cast<__nv_bfloat16 *>(stg) + (r - lane) / 2 + lane;  // hidden unit of lane < 16
 #pragma unroll 1
     for (int c = 0; c < BN; c += 16) {
       float v[16];
       load16(c, v);
       wait_ld();
+      float u[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) u[e] = __shfl_down_sync(0xffffffffu, v[e], 16);
+      if (lane < 16) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) hb[(c + e) * 64] = __float2bfloat16(v[e] / (1.0f + expf(-v[e])) * u[e]);
+      }
+    }
+  } else if (ep.staged == kStageTrans || ep.staged == kStageTransAdd) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      load16(c, v);
+      wait_ld();
+      if (ep.staged == kStageTransAdd && ep.row_parts) {
+        // per-column 1/rms: lane l computes column n0 + c + (l & 15)
+        const int col = n0 + c + (lane & 15);
+        const float my_scale = col < N ? row_scale(ep, col, N) : 1.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) v[e] *= __shfl_sync(0xffffffffu, my_scale, e);
+      }
 #pragma unroll
       for (int e = 0; e < 16; ++e) stg[(c + e) * 128 + r] = v[e];
     }
@@ -412,6 +447,10 @@ __device__ __forceinline__ void store_tile_staged(const GemmEpilogue &ep, const 
   if (threadIdx.x == 64 && ok) {
     if (ep.staged == kStageTrans) {
       tma_store_3d(tmO, stg, m0, n0, z);
+    } else if (ep.staged == kStageTransAdd) {
+      tma_reduce_add_2d(tmO, stg, m0, n0);
+    } else if (ep.staged == kStageSwiGLU) {
+      tma_store_2d(tmO, stg, m0 / 2, n0);
     } else {
 #pragma unroll 1
       for (int j = 0; j < BN / 32; ++j)
@@ -636,7 +675,7 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
     };
     if (ep.staged)
       store_tile_staged<BN>(ep, &tmO, load16, wait_ld, reinterpret_cast<float *>(smem), q * 32 + lane, m0, n0,
-                            blockIdx.z, ok && !s_abort, scale);
+                            blockIdx.z, N, ok && !s_abort, scale);
     else
       store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, ok, scale, blockIdx.z == 0);
   }
@@ -1170,7 +1209,7 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
     };
     if (ep.staged)
       store_tile_staged<BN>(ep, &tmO, load16, wait_ld, reinterpret_cast<float *>(smem), q * 32 + lane, m0, n0,
-                            blockIdx.z, ok && !s_abort, scale);
+                            blockIdx.z, N, ok && !s_abort, scale);
     else
       store_tile<BN>(ep, load16, wait_ld, row, row_ok, n0, N, ok && !s_abort, scale, blockIdx.z == 0);
   }
@@ -1230,6 +1269,22 @@ int make_staged_out_map(CUtensorMap *map, const GemmEpilogue &ep, int M, int N, 
     cuuint32_t box[3] = {128, (cuuint32_t)BN, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ep.out, dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (ep.staged == kStageSwiGLU) {
+    cuuint64_t dims[2] = {(cuuint64_t)(M / 2), (cuuint64_t)N};
+    cuuint64_t strides[1] = {(cuuint64_t)ep.ldo * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)BN};
+    cuuint32_t estr[2] = {1, 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, ep.out, dims, strides, box, estr,
+                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else if (ep.staged == kStageTransAdd) {
+    cuuint64_t dims[2] = {(cuuint64_t)M, (cuuint64_t)N};
+    cuuint64_t strides[1] = {(cuuint64_t)ep.ldo * 4};
+    cuuint32_t box[2] = {128, (cuuint32_t)BN};
+    cuuint32_t estr[2] = {1, 1};
+    r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ep.out, dims, strides, box, estr,
                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   } else {
@@ -1587,8 +1642,12 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
   // split kernel): transposed plain stores (partial buffers) and row-major
   // accumulation without bias or residual.  AF_GEMM_NO_STAGE=1 turns it off.
   const bool out_ok = af::aligned16(a.out) && (a.ldo * 4) % 16 == 0 && (a.split_stride * 4) % 16 == 0;
+  if (af::aligned16(a.out) && (a.ldo * 2) % 16 == 0 && a.trans && a.swiglu && a.out_bf16 && !a.row_parts &&
+      !ep.atomic && M % 128 == 0 && !getenv("AF_GEMM_NO_STAGE"))
+    ep.staged = kStageSwiGLU;
   if (out_ok && !a.out_bf16 && !a.swiglu && !getenv("AF_GEMM_NO_STAGE")) {
     if (a.trans && !ep.atomic && !a.row_parts) ep.staged = kStageTrans;
+    else if (a.trans && ep.atomic) ep.staged = kStageTransAdd;
     else if (!a.trans && ep.atomic && !ep.residual && !a.bias) ep.staged = kStageAdd;
   }
   // large bf16 GEMMs (two or more waves of tiles): persistent kernel
