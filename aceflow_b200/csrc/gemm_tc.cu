@@ -74,7 +74,7 @@ struct GemmEpilogue {
   // kStageTransAdd = transposed reduce-add of the [BN][128] box.
   int staged;
 };
-constexpr int kStageTrans = 1, kStageAdd = 2, kStageTransAdd = 3, kStageSwiGLU = 4;
+constexpr int kStageTrans = 1, kStageAdd = 2, kStageTransAdd = 3, kStageSwiGLU = 4, kStagePair = 5;
 
 // v[e] += r[e] * rs for the 16 columns n..n+15 of one row (vector loads when
 // the row segment is whole and aligned: each thread owns a different row, so
@@ -368,6 +368,12 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *map, const 
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_but_one() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_commit_wait_all() {
   asm volatile("cp.async.bulk.commit_group;\n\tcp.async.bulk.wait_group 0;" ::: "memory");
 }
@@ -853,14 +859,20 @@ struct PairCfg {
   static constexpr int A_BYTES = KS * SLICE, B_BYTES = KS * SLICE, STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SMEM_LIMIT = 227 * 1024 - 64;
   static constexpr int STAGES = (SMEM_LIMIT - 1024 - 256) / STAGE_BYTES;
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+  // Epilogue staging (output through TMA stores), when it fits beside the
+  // ring: 8 KB per epilogue warp.
+  static constexpr int STG_WARP = 8192;
+  static constexpr int STG_BYTES =
+      1024 + STAGES * STAGE_BYTES + 1024 + 4 * STG_WARP <= SMEM_LIMIT ? 4 * STG_WARP : 0;
+  static constexpr size_t STG_OFF = (size_t)STAGES * STAGE_BYTES + 1024;  // after the barrier block
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + (STG_BYTES ? 1024 + STG_BYTES : 256);
   static_assert(STAGES >= 2 && 2 * STAGES + 5 <= 32, "ring depth / barrier block");
 };
 
 template <int KS>
 __global__ void __launch_bounds__(kMaxGemmThreads, 1)
-    umma_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, int M,
-                          int N, int K, GemmEpilogue ep, int *err) {
+    umma_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          const __grid_constant__ CUtensorMap tmO, int M, int N, int K, GemmEpilogue ep, int *err) {
   using C = PairCfg<KS>;
   constexpr int S = C::STAGES;
   constexpr uint32_t TM_COLS = 512;  // two 256-column accumulators
@@ -1005,11 +1017,90 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
         tmem_ld16(tbase + col, v);
       };
       auto wait_ld = [&]() { tmem_wait_ld(); };
-      store_tile<C::BN>(ep, load16, wait_ld, row, row_ok, n0, N, true, scale, true);
+      if (C::STG_BYTES && ep.staged == kStagePair) {
+        // The tile through this warp's 8 KB staging buffer and TMA stores, per
+        // 64 columns: fp32 as two 128-byte-swizzled [32 rows x 32 cols] boxes
+        // (the whole buffer), bf16 as one [32 x 64] box (alternating halves).
+        // Chunk c of row r sits at chunk c ^ (r & 7), so the lanes' 16-byte
+        // writes spread over the banks.
+        uint8_t *buf = smem + C::STG_OFF + q * C::STG_WARP;
+        const int row0 = m0 + (int)rank * C::HALF + q * 32;
+#pragma unroll 1
+        for (int c0 = 0; c0 < C::BN; c0 += 64) {
+          float vv[4][16];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) load16(c0 + 16 * u, vv[u]);
+          wait_ld();
+          if (ep.out_bf16) {
+            uint8_t *box = buf + ((c0 >> 6) & 1) * 4096;
+            if (lane == 0) bulk_wait_read_but_one();  // the store that last read this half is done
+            __syncwarp();
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int n = n0 + c0 + 16 * u;
+              uint32_t pk[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                float x0 = vv[u][2 * e] * scale, x1 = vv[u][2 * e + 1] * scale;
+                if (ep.bias) {
+                  x0 += n + 2 * e < N ? ep.bias[n + 2 * e] : 0.f;
+                  x1 += n + 2 * e + 1 < N ? ep.bias[n + 2 * e + 1] : 0.f;
+                }
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(x0, x1);
+                pk[e] = *reinterpret_cast<uint32_t *>(&b2);
+              }
+              uint8_t *line = box + lane * 128;
+              *reinterpret_cast<uint4 *>(line + (((2 * u) ^ (lane & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              *reinterpret_cast<uint4 *>(line + (((2 * u + 1) ^ (lane & 7)) * 16)) =
+                  make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmO, box, n0 + c0, row0);
+              bulk_commit();
+            }
+            continue;
+          }
+          if (lane == 0) bulk_wait_read_all();  // the buffer's previous stores have read it
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int n = n0 + c0 + 16 * u;
+            uint8_t *box = buf + (u >> 1) * 4096 + lane * 128;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              float4 f;
+              f.x = vv[u][4 * k] * scale;
+              f.y = vv[u][4 * k + 1] * scale;
+              f.z = vv[u][4 * k + 2] * scale;
+              f.w = vv[u][4 * k + 3] * scale;
+              if (ep.bias) {
+                const int c = n + 4 * k;
+                f.x += c < N ? ep.bias[c] : 0.f;
+                f.y += c + 1 < N ? ep.bias[c + 1] : 0.f;
+                f.z += c + 2 < N ? ep.bias[c + 2] : 0.f;
+                f.w += c + 3 < N ? ep.bias[c + 3] : 0.f;
+              }
+              *reinterpret_cast<float4 *>(box + ((((u & 1) * 4 + k) ^ (lane & 7)) * 16)) = f;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmO, buf, n0 + c0, row0);
+            tma_store_2d(&tmO, buf + 4096, n0 + c0 + 32, row0);
+            bulk_commit();
+          }
+        }
+      } else {
+        store_tile<C::BN>(ep, load16, wait_ld, row, row_ok, n0, N, true, scale, true);
+      }
       tc_fence_before();
       if (rank == 0) mbar_arrive(&acce[b]);
       else mbar_arrive_cluster(mapa_shared(&acce[b], 0));
     }
+    if (C::STG_BYTES && ep.staged == kStagePair && lane == 0) bulk_wait_all();  // stores done before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -1425,7 +1516,26 @@ int launch_pair_ks(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_kernel<KS>, ta, tb, M, N, K, ep, ctx->dev_err);
+  // fp32 or bf16 output without residual: epilogue through shared memory
+  // and TMA stores (AF_GEMM_NO_STAGE=1 turns it off)
+  CUtensorMap to = ta;
+  GemmEpilogue epx = ep;
+  epx.staged = 0;
+  const int ob = ep.out_bf16 ? 2 : 4;
+  if (C::STG_BYTES && !ep.trans && !ep.atomic && !ep.swiglu && !ep.residual && af::aligned16(ep.out) &&
+      (ep.ldo * ob) % 16 == 0 && !getenv("AF_GEMM_NO_STAGE")) {
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)ep.ldo * ob};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / ob), 32};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r =
+        g_encode(&to, ep.out_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ep.out,
+                 dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return af::fail(AF_ERR_ARG, "%s: output tensor map failed (%d)", fn, (int)r);
+    epx.staged = kStagePair;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_kernel<KS>, ta, tb, to, M, N, K, epx, ctx->dev_err);
   if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: pair launch: %s", fn, cudaGetErrorString(e));
   return af::launched(ctx, fn);
 }

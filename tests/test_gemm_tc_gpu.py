@@ -251,3 +251,43 @@ def test_staged_reduce_add_epilogue(dev, M, N, K, bn, splits, monkeypatch):
     ref2 = (ab.double() @ bb.double().t() * scale).cpu().numpy()
     assert rel_err(o.cpu().numpy(), ref2) < 1e-5
     _check(dev)
+
+
+@pytest.mark.parametrize("M,N,K", [(8292, 2112, 2048), (4096, 768, 4096)])
+def test_pair_gemm_staged_store_epilogue(dev, M, N, K, monkeypatch):
+    """CTA-pair GEMM with fp32 and bf16 output written through
+    128-byte-swizzled shared-memory boxes and TMA stores (two K slices per
+    stage leave room for 8 KB per epilogue warp): ragged M and N, bias and
+    1/rms row scale: every element written, equal to the per-thread stores
+    up to rounding and to fp64."""
+    from aceflow_b200 import cuda_ops
+
+    g = torch.Generator(device=dev).manual_seed(M + N)
+    a = torch.randn(M, K, generator=g, device=dev).bfloat16()
+    b = (0.05 * torch.randn(N, K, generator=g, device=dev)).bfloat16()
+    bias = torch.randn(N, generator=g, device=dev)
+    parts = torch.rand(M, 2, generator=g, device=dev) * 10
+    scale = 1.0 / torch.sqrt(parts.double().sum(1, keepdim=True) / K + 1e-6)
+    ref = ((a.double() @ b.double().t()) * scale + bias.double()).cpu().numpy()
+    outs = []
+    for no_stage in (False, True):
+        if no_stage:
+            monkeypatch.setenv("AF_GEMM_NO_STAGE", "1")
+        o = torch.full((M, N), float("nan"), device=dev)
+        cuda_ops.gemm_bf16(a, b, o, parts, inv_d=1.0 / K, eps=1e-6, bias=bias)
+        torch.cuda.synchronize()
+        outs.append(o)
+    assert torch.isfinite(outs[0]).all()  # every element written (the buffer started as NaN)
+    assert rel_err(outs[0].cpu().numpy(), outs[1].cpu().numpy()) < 1e-6  # same products, FMA contraction aside
+    assert rel_err(outs[0].cpu().numpy(), ref) < 1e-5
+    # bf16 output: one [32 x 64] box per 64 columns, double-buffered
+    monkeypatch.delenv("AF_GEMM_NO_STAGE")
+    yb = cuda_ops.linear_bf16(a, b, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    monkeypatch.setenv("AF_GEMM_NO_STAGE", "1")
+    yb2 = cuda_ops.linear_bf16(a, b, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert torch.isfinite(yb.float()).all()
+    assert rel_err(yb.float().cpu().numpy(), yb2.float().cpu().numpy()) < 1e-2
+    assert rel_err(yb.float().cpu().numpy(), (a.double() @ b.double().t()).cpu().numpy()) < 1e-2
+    _check(dev)
