@@ -74,7 +74,8 @@ struct GemmEpilogue {
   // kStageTransAdd = transposed reduce-add of the [BN][128] box.
   int staged;
 };
-constexpr int kStageTrans = 1, kStageAdd = 2, kStageTransAdd = 3, kStageSwiGLU = 4, kStagePair = 5;
+constexpr int kStageTrans = 1, kStageAdd = 2, kStageTransAdd = 3, kStageSwiGLU = 4, kStagePair = 5,
+              kStagePairAdd = 6;  // pair kernel: TMA store / TMA reduce-add into out (in-place residual)
 
 // v[e] += r[e] * rs for the 16 columns n..n+15 of one row (vector loads when
 // the row segment is whole and aligned: each thread owns a different row, so
@@ -1017,7 +1018,7 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
         tmem_ld16(tbase + col, v);
       };
       auto wait_ld = [&]() { tmem_wait_ld(); };
-      if (C::STG_BYTES && ep.staged == kStagePair) {
+      if (C::STG_BYTES && (ep.staged == kStagePair || ep.staged == kStagePairAdd)) {
         // The tile through this warp's 8 KB staging buffer and TMA stores, per
         // 64 columns: fp32 as two 128-byte-swizzled [32 rows x 32 cols] boxes
         // (the whole buffer), bf16 as one [32 x 64] box (alternating halves).
@@ -1088,8 +1089,13 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmO, buf, n0 + c0, row0);
-            tma_store_2d(&tmO, buf + 4096, n0 + c0 + 32, row0);
+            if (ep.staged == kStagePairAdd) {  // out holds the residual: add the tile into it
+              tma_reduce_add_2d(&tmO, buf, n0 + c0, row0);
+              tma_reduce_add_2d(&tmO, buf + 4096, n0 + c0 + 32, row0);
+            } else {
+              tma_store_2d(&tmO, buf, n0 + c0, row0);
+              tma_store_2d(&tmO, buf + 4096, n0 + c0 + 32, row0);
+            }
             bulk_commit();
           }
         }
@@ -1100,7 +1106,7 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
       if (rank == 0) mbar_arrive(&acce[b]);
       else mbar_arrive_cluster(mapa_shared(&acce[b], 0));
     }
-    if (C::STG_BYTES && ep.staged == kStagePair && lane == 0) bulk_wait_all();  // stores done before exit
+    if (C::STG_BYTES && ep.staged && lane == 0) bulk_wait_all();  // stores done before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -1522,7 +1528,10 @@ int launch_pair_ks(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64
   GemmEpilogue epx = ep;
   epx.staged = 0;
   const int ob = ep.out_bf16 ? 2 : 4;
-  if (C::STG_BYTES && !ep.trans && !ep.atomic && !ep.swiglu && !ep.residual && af::aligned16(ep.out) &&
+  // a residual that is the output itself (x += ...) becomes a TMA reduce-add
+  const bool in_place = ep.residual && (const void *)ep.residual == ep.out && ep.ldr == ep.ldo && !ep.out_bf16 &&
+                        !ep.scale_residual;
+  if (C::STG_BYTES && !ep.trans && !ep.atomic && !ep.swiglu && (!ep.residual || in_place) && af::aligned16(ep.out) &&
       (ep.ldo * ob) % 16 == 0 && !getenv("AF_GEMM_NO_STAGE")) {
     cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
     cuuint64_t strides[1] = {(cuuint64_t)ep.ldo * ob};
@@ -1533,7 +1542,7 @@ int launch_pair_ks(af_ctx *ctx, const void *A, int64_t lda, const void *B, int64
                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return af::fail(AF_ERR_ARG, "%s: output tensor map failed (%d)", fn, (int)r);
-    epx.staged = kStagePair;
+    epx.staged = in_place ? kStagePairAdd : kStagePair;
   }
   const cudaError_t e = cudaLaunchKernelEx(&cfg, umma_gemm_pair_kernel<KS>, ta, tb, to, M, N, K, epx, ctx->dev_err);
   if (e != cudaSuccess) return af::fail(AF_ERR_CUDA, "%s: pair launch: %s", fn, cudaGetErrorString(e));

@@ -258,8 +258,9 @@ def test_pair_gemm_staged_store_epilogue(dev, M, N, K, monkeypatch):
     """CTA-pair GEMM with fp32 and bf16 output written through
     128-byte-swizzled shared-memory boxes and TMA stores (two K slices per
     stage leave room for 8 KB per epilogue warp): ragged M and N, bias and
-    1/rms row scale: every element written, equal to the per-thread stores
-    up to rounding and to fp64."""
+    1/rms row scale, and an in-place residual added by TMA reduce-adds:
+    every element written, equal to the per-thread stores up to rounding and
+    to fp64."""
     from aceflow_b200 import cuda_ops
 
     g = torch.Generator(device=dev).manual_seed(M + N)
@@ -280,8 +281,21 @@ def test_pair_gemm_staged_store_epilogue(dev, M, N, K, monkeypatch):
     assert torch.isfinite(outs[0]).all()  # every element written (the buffer started as NaN)
     assert rel_err(outs[0].cpu().numpy(), outs[1].cpu().numpy()) < 1e-6  # same products, FMA contraction aside
     assert rel_err(outs[0].cpu().numpy(), ref) < 1e-5
+    # in place (x += ...): the output holds the residual; the staged tile is
+    # added into it by TMA reduce-adds
+    res = torch.randn(M, N, generator=g, device=dev)
+    inplace = []
+    for no_stage in (True, False):
+        if not no_stage:
+            monkeypatch.delenv("AF_GEMM_NO_STAGE")
+        o = res.clone()
+        cuda_ops.gemm_bf16(a, b, o, parts, inv_d=1.0 / K, eps=1e-6, bias=bias, residual=o)
+        torch.cuda.synchronize()
+        inplace.append(o)
+    ref_ip = ref + res.double().cpu().numpy()
+    assert rel_err(inplace[1].cpu().numpy(), ref_ip) < 1e-5
+    assert rel_err(inplace[1].cpu().numpy(), inplace[0].cpu().numpy()) < 1e-6
     # bf16 output: one [32 x 64] box per 64 columns, double-buffered
-    monkeypatch.delenv("AF_GEMM_NO_STAGE")
     yb = cuda_ops.linear_bf16(a, b, out_dtype=torch.bfloat16)
     torch.cuda.synchronize()
     monkeypatch.setenv("AF_GEMM_NO_STAGE", "1")
