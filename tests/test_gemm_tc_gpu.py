@@ -305,3 +305,26 @@ def test_pair_gemm_staged_store_epilogue(dev, M, N, K, monkeypatch):
     assert rel_err(yb.float().cpu().numpy(), yb2.float().cpu().numpy()) < 1e-2
     assert rel_err(yb.float().cpu().numpy(), (a.double() @ b.double().t()).cpu().numpy()) < 1e-2
     _check(dev)
+
+
+@pytest.mark.parametrize("kb", [256, 64])
+def test_pair_gemm_kblocked_operand(dev, kb):
+    """CTA-pair GEMM reading A as stacked K blocks [K/kb][M][kb] (the
+    head-sharded prefill's all-gathered outputs): K blocks that are multiples
+    of 128 take two-slice stages with 3-D copies, others one slice; both
+    equal the plain product."""
+    from aceflow_b200 import cuda_ops
+
+    M, N, K = 8192, 2560, 1024
+    g = torch.Generator(device=dev).manual_seed(kb)
+    a = torch.randn(M, K, generator=g, device=dev).bfloat16()
+    b = (0.05 * torch.randn(N, K, generator=g, device=dev)).bfloat16()
+    a_blk = torch.cat([a[:, i * kb:(i + 1) * kb] for i in range(K // kb)], 0).contiguous()
+    out = torch.empty(M, N, device=dev)
+    cuda_ops.gemm_bf16(a_blk, b, out, a_kblock=kb)
+    ref = torch.empty(M, N, device=dev)
+    cuda_ops.gemm_bf16(a, b, ref)
+    torch.cuda.synchronize()
+    assert rel_err(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+    assert rel_err(out.cpu().numpy(), (a.double() @ b.double().t()).cpu().numpy()) < 1e-5
+    _check(dev)
