@@ -66,6 +66,7 @@ SIGNATURES = {
     "af_rmsnorm_to_bf16": [_vp, _vp, _vp, _vp, _i, _i, _f, _vp],
     "af_argmax_rows": [_vp, _vp, _i, _i, _vp, _vp],
     "af_lm_head_argmax": [_vp, _vp, _vp, _f, _vp, _i, _i, _i, _i, _vp, _vp, _vp],
+    "af_sample_rows": [_vp, _vp, _i, _i, _vp, _i64, _i, _f, _i, _f, _f, _vp, _vp, _vp],
 }
 _RESTYPE = {"af_last_error": ctypes.c_char_p}
 

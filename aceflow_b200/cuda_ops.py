@@ -386,3 +386,30 @@ def rms_norm_to_bf16(x: torch.Tensor, w: torch.Tensor | None, eps: float) -> tor
     y = torch.empty(x.shape, dtype=BF16, device=x.device)
     _lib.call("af_rmsnorm_to_bf16", _ctx(x), _p(x), _p(w), _p(y), x.numel() // d, d, float(eps), _stream(x))
     return y
+
+
+def sample_rows(logits: torch.Tensor, uniforms: torch.Tensor | None = None, context: torch.Tensor | None = None,
+                temperature: float = 0.7, top_k: int = 40, top_p: float = 0.9,
+                repetition_penalty: float = 1.2) -> torch.Tensor:
+    """One token per row of logits [rows, vocab] fp32 (af_sample_rows, the
+    reference's sample_token_from_logits).  uniforms [rows] fp32 in [0, 1)
+    stand in for the reference's random draws (required unless
+    temperature <= 1e-4); context [rows, L] int32 holds each row's recent
+    ids for the repetition penalty (-1 pads)."""
+    _need(logits, F32, "logits")
+    if logits.dim() != 2:
+        raise ValueError("logits must be [rows, vocab]")
+    rows, V = logits.shape
+    if uniforms is not None:
+        _need(uniforms, F32, "uniforms")
+        if uniforms.numel() != rows:
+            raise ValueError("uniforms must hold one value per row")
+    ctx_ptr, stride, clen = None, 0, 0
+    if context is not None and context.numel():
+        if context.dtype != torch.int32 or context.dim() != 2 or context.shape[0] != rows or context.stride(1) != 1:
+            raise ValueError("context must be an int32 [rows, L] tensor with unit column stride")
+        ctx_ptr, stride, clen = _p(context), context.stride(0), context.shape[1]
+    out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    _lib.call("af_sample_rows", _ctx(logits), _p(logits), rows, V, ctx_ptr, int(stride), int(clen), float(temperature),
+              int(top_k), float(top_p), float(repetition_penalty), _p(uniforms), _p(out), _stream(logits))
+    return out

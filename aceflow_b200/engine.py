@@ -232,15 +232,58 @@ class AceEngine:
         return res[0] if self.batch == 1 and np.asarray(q_seq).ndim == 1 else res
 
     # ---------------------------------------------------------------- generation
-    def _check_generate(self, temperature, repetition_penalty):
+    def _check_generate(self):
         if self.embedding is None:
             raise ValueError("Embedding table not loaded.")
         for i, L in enumerate(self.layers):
             if L is None:
                 raise ValueError(f"Layer {i} weights are not loaded.")
-        if temperature > 1e-4 or repetition_penalty != 1.0:
-            raise NotImplementedError("only greedy decoding (temperature <= 1e-4, repetition_penalty 1.0) runs on "
-                                      "the GPU engine")
+
+    # ---------------------------------------------------------------- sampling
+    PENALTY_WINDOW = 60  # generate_stream_internal penalises the last 60 ids (cpu/mod.rs:739)
+
+    def _logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """logits [rows, vocab] = head . RMSNorm_final(hidden) (project_logits)."""
+        rows = hidden.shape[0]
+        head = self.lm_head if self.lm_head is not None else self.embedding
+        bf = int(self._wdt == torch.bfloat16)
+        logits = torch.empty(rows, self.vocab_size, device=self.device)
+        toks = torch.empty(rows, dtype=torch.int32, device=self.device)
+        fn = self.final_norm
+        _lib.call("af_lm_head_argmax", self._ctx(), hidden.data_ptr(), None if fn is None else fn.data_ptr(),
+                  float(self.eps), head.data_ptr(), bf, rows, self.vocab_size, self._d, logits.data_ptr(),
+                  toks.data_ptr(), self._stream())
+        return logits
+
+    @staticmethod
+    def _uniform(uniform):
+        return float(np.random.random()) if uniform is None else float(uniform)
+
+    def sample_token_from_logits(self, logits, context_tokens, temperature: float = 0.7, top_k: int = 40,
+                                 top_p: float = 0.9, repetition_penalty: float = 1.2, uniform=None) -> int:
+        """AceEngine.sample_token_from_logits (cpu/mod.rs:404-420, sampler.rs:104-180)
+        on the GPU.  `uniform` in [0, 1) is the random draw (the reference
+        takes it from a clock-seeded generator); None draws one from numpy's
+        global generator."""
+        lt = torch.as_tensor(_f32(logits).reshape(1, -1)).to(self.device)
+        ctx = np.asarray(list(context_tokens), np.int64)
+        ctx = np.where((ctx >= 0) & (ctx < lt.shape[1]), ctx, -1).astype(np.int32).reshape(1, -1)
+        ct = torch.as_tensor(ctx).to(self.device) if ctx.size else None
+        u = torch.tensor([self._uniform(uniform)], dtype=torch.float32, device=self.device)
+        return int(cuda_ops.sample_rows(lt, u, ct, temperature, top_k, top_p, repetition_penalty).cpu()[0])
+
+    def sample_next_token(self, hidden_state, context_tokens, temperature: float = 0.7, top_k: int = 40,
+                          top_p: float = 0.9, repetition_penalty: float = 1.2, uniform=None) -> int:
+        """AceEngine.sample_next_token (cpu/mod.rs:349-394): final RMSNorm,
+        LM head (the tied embedding unless one was loaded), then
+        sample_token_from_logits."""
+        self._check_generate()
+        h = _f32(hidden_state).reshape(-1)
+        if h.size != self._d:
+            raise ValueError(f"hidden_state length {h.size} must match d_model {self._d}")
+        logits = self._logits(torch.as_tensor(h.reshape(1, -1)).to(self.device))
+        return self.sample_token_from_logits(logits.cpu().numpy()[0], context_tokens, temperature, top_k, top_p,
+                                             repetition_penalty, uniform)
 
     def prefill_device(self, x: torch.Tensor, T: int) -> None:
         """All layers over a [batch*T, d] fp32 device tensor of prompt
@@ -276,13 +319,21 @@ class AceEngine:
                   float(self.eps), head.data_ptr(), bf, B, V, d, logits.data_ptr(), toks.data_ptr(), st)
 
     def generate_batch(self, prompts, max_new_tokens: int, stop_at_eos: bool = False, teacher=None,
-                       return_logits: bool = False, use_graph: bool = False, timing: dict | None = None):
-        """Greedy generation for `batch` streams: prompts [batch, P] ids.
-        Returns tokens [batch, max_new_tokens] (-1 after a stream stopped at
-        EOS id 2 when stop_at_eos) and optionally the logits per step.
-        `teacher` [batch, max_new_tokens] feeds given ids instead of the
-        argmax (for parity checks)."""
-        self._check_generate(0.0, 1.0)
+                       return_logits: bool = False, use_graph: bool = False, timing: dict | None = None,
+                       temperature: float = 0.0, top_k: int = 40, top_p: float = 0.9,
+                       repetition_penalty: float = 1.0, uniforms=None, seed: int | None = None):
+        """Generation for `batch` streams: prompts [batch, P] ids.  Returns
+        tokens [batch, max_new_tokens] (-1 after a stream stopped at EOS id 2
+        when stop_at_eos) and optionally the logits per step.  `teacher`
+        [batch, max_new_tokens] feeds given ids instead of the drawn ones (for
+        parity checks).  Greedy by default; with temperature > 1e-4 or a
+        repetition penalty each step runs sample_token_from_logits on the GPU
+        (af_sample_rows) over the last 60 ids of prompt + output, as
+        generate_stream_internal does (cpu/mod.rs:739-746), with draws from
+        `uniforms` [batch, max_new_tokens] in [0, 1), else from a torch
+        generator seeded with `seed`."""
+        self._check_generate()
+        sampling = temperature > 1e-4 or repetition_penalty != 1.0
         pr = torch.as_tensor(np.asarray(prompts, np.int32)).to(self.device)
         B, P = pr.shape
         if B != self.batch:
@@ -310,11 +361,30 @@ class AceEngine:
         fn = self.final_norm
         teach = None if teacher is None else torch.as_tensor(np.asarray(teacher, np.int32)).to(self.device)
         alive = torch.ones(B, dtype=torch.bool, device=self.device)
-        if use_graph and teacher is None and not return_logits and not stop_at_eos:
+        if use_graph and teacher is None and not return_logits and not stop_at_eos and not sampling:
             return self._generate_graph(cur, logits, toks, out, head, bf, max_new_tokens, timing)
+        if sampling:
+            # ids seen so far per stream (prompt, then outputs) for the penalty window
+            seen = torch.empty(B, P + max_new_tokens, dtype=torch.int32, device=self.device)
+            seen[:, :P] = pr
+            if uniforms is not None:
+                uni = torch.as_tensor(np.asarray(uniforms, np.float32).reshape(B, max_new_tokens)).to(self.device)
+            else:
+                gen = torch.Generator(device=self.device)
+                gen.manual_seed(int(seed) if seed is not None else int(np.random.randint(1 << 31)))
+                uni = torch.rand(B, max_new_tokens, generator=gen, device=self.device)
         for s in range(max_new_tokens):
             _lib.call("af_lm_head_argmax", self._ctx(), cur.data_ptr(), None if fn is None else fn.data_ptr(),
                       float(self.eps), head.data_ptr(), bf, B, V, d, logits.data_ptr(), toks.data_ptr(), st)
+            if sampling:
+                n_seen = P + s
+                w0 = max(0, n_seen - self.PENALTY_WINDOW)
+                win = seen[:, w0:n_seen]
+                ur = uni[:, s].contiguous()
+                _lib.call("af_sample_rows", self._ctx(), logits.data_ptr(), B, V, win.data_ptr() if n_seen else None,
+                          seen.stride(0), n_seen - w0, float(temperature), int(top_k), float(top_p),
+                          float(repetition_penalty), ur.data_ptr(), toks.data_ptr(), st)
+                seen[:, n_seen] = toks
             out[:, s] = torch.where(alive, toks, torch.full_like(toks, -1))
             if return_logits:
                 all_logits.append(logits.clone())
@@ -373,13 +443,17 @@ class AceEngine:
         return out.cpu().numpy()
 
     def generate_stream(self, prompt_tokens: Sequence[int], max_new_tokens: int, temperature: float = 0.7,
-                        top_k: int = 40, top_p: float = 0.9, repetition_penalty: float = 1.2) -> List[int]:
+                        top_k: int = 40, top_p: float = 0.9, repetition_penalty: float = 1.2,
+                        seed: int | None = None) -> List[int]:
         """AceEngine.generate_stream (cpu/mod.rs:454-484) for a one-stream
-        engine: greedy only; stops after EOS id 2 like the reference."""
-        self._check_generate(temperature, repetition_penalty)
+        engine: the reference's sampling (or greedy at temperature <= 1e-4
+        without penalty); stops after EOS id 2 like the reference.  `seed`
+        fixes the draws (the reference seeds from the clock)."""
+        self._check_generate()
         if self.batch != 1:
             raise ValueError("generate_stream drives one stream; use generate_batch")
-        toks = self.generate_batch([list(prompt_tokens)], max_new_tokens, stop_at_eos=True)[0]
+        toks = self.generate_batch([list(prompt_tokens)], max_new_tokens, stop_at_eos=True, temperature=temperature,
+                                   top_k=top_k, top_p=top_p, repetition_penalty=repetition_penalty, seed=seed)[0]
         res = []
         for t in toks:
             if t < 0:

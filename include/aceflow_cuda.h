@@ -329,6 +329,25 @@ int af_lm_head_argmax(af_ctx *ctx, const float *x, const float *final_norm, floa
                       const void *table, int table_bf16, int batch, int vocab, int d,
                       float *logits, int32_t *tokens, af_stream_t stream);
 
+/* tokens[r] = one draw from row r of logits [rows][vocab] (fp32), as
+ * sample_token_from_logits (aceflow-core/src/cpu/sampler.rs:104-180):
+ * repetition penalty over the distinct in-range tokens of row r's context
+ * (apply_repetition_penalty, sampler.rs:83-102): context_tokens[r *
+ * context_stride + 0 .. context_len) (ids < 0 or >= vocab are skipped, so -1
+ * pads shorter contexts; context_len 0: none), then greedy when
+ * temperature <= 1e-4, else logits /
+ * max(temperature, 1e-5), the top_k largest (0 = all), a softmax over them,
+ * the sorted prefix through the first place where the running sum exceeds
+ * top_p, and the first item of that prefix where the running sum reaches
+ * uniforms[r] * (its mass).  uniforms [rows] in [0, 1) take the place of the
+ * reference's clock-seeded generator (sampler.rs:8-35); they may be NULL
+ * when greedy.  Equal logits are ordered by lowest index.  logits is not
+ * modified; vocab <= AF_SAMPLE_MAX_VOCAB. */
+#define AF_SAMPLE_MAX_VOCAB 50000
+int af_sample_rows(af_ctx *ctx, const float *logits, int rows, int vocab, const int32_t *context_tokens,
+                   int64_t context_stride, int context_len, float temperature, int top_k, float top_p,
+                   float repetition_penalty, const float *uniforms, int32_t *out, af_stream_t stream);
+
 /* ------------------------------------------------------- multi-GPU prefill
  * One process per GPU.  Rank 0 creates an id with af_comm_unique_id, the
  * ranks share it out of band (torch.distributed, MPI, a file), then every

@@ -186,6 +186,70 @@ def greedy_token(logits: np.ndarray, context=(), repetition_penalty: float = 1.0
     return int(np.argmax(logits))
 
 
+def sample_token(logits: np.ndarray, context=(), temperature: float = 0.7, top_k: int = 40, top_p: float = 0.9,
+                 repetition_penalty: float = 1.2, u: float = 0.5, detail: bool = False):
+    """sample_token_from_logits, aceflow-core/src/cpu/sampler.rs:104-180, in
+    float32 with the reference's sequential sums, the uniform variate u in
+    [0, 1) given (the reference draws it from a clock-seeded generator,
+    sampler.rs:8-35,169).  Steps: repetition penalty (sampler.rs:83-102);
+    greedy at temperature <= 1e-4; logits * (1 / max(temperature, 1e-5));
+    candidates in descending order, the first top_k when 0 < top_k < n;
+    softmax normalised by the sequential exp sum; the prefix through the
+    first place where the running probability exceeds top_p (top_p < 1);
+    the first kept item whose running sum reaches u * (sum of kept).  Equal
+    logits are ordered by lowest index (the reference's unstable sorts leave
+    that order unspecified).
+
+    detail=True returns (token, margin): the smallest distance, relative to
+    1, between the draw or top_p and a running-sum boundary that decides the
+    result (0 for greedy) - results with a tiny margin depend on rounding."""
+    logits = np.array(logits, dtype=F32, copy=True)
+    n = logits.size
+    if n == 0:
+        return (0, 1.0) if detail else 0
+    if repetition_penalty != 1.0 and len(context):
+        for tok in dict.fromkeys(int(t) for t in context):
+            if 0 <= tok < n:
+                val = logits[tok]
+                logits[tok] = val / F32(repetition_penalty) if val > 0 else val * F32(repetition_penalty)
+    if temperature <= 1e-4:
+        best = 0
+        for i in range(1, n):
+            if logits[i] > logits[best]:
+                best = i
+        return (best, 1.0) if detail else best
+    inv_t = F32(1.0) / max(F32(temperature), F32(1e-5))
+    logits = (logits * inv_t).astype(F32)
+    order = np.lexsort((np.arange(n), -logits.astype(np.float64)))
+    if 0 < top_k < n:
+        order = order[:top_k]
+    vals = logits[order]
+    ex = np.exp((vals - vals[0]).astype(F32)).astype(F32)
+    exp_sum = np.cumsum(ex, dtype=F32)[-1]
+    probs = (ex * (F32(1.0) / max(exp_sum, F32(1e-12)))).astype(F32)
+    margin = 1.0
+    cutoff = len(order)
+    if top_p < 1.0:
+        cum = np.cumsum(probs, dtype=F32)
+        over = np.nonzero(cum > F32(top_p))[0]
+        if over.size:
+            cutoff = int(over[0]) + 1
+            margin = min(margin, abs(float(cum[cutoff - 1]) - top_p))
+            if cutoff >= 2:
+                margin = min(margin, abs(float(cum[cutoff - 2]) - top_p))
+        cutoff = max(1, min(cutoff, len(order)))
+    cum = np.cumsum(probs[:cutoff], dtype=F32)
+    total = cum[-1]
+    sample = F32(F32(u) * total)
+    hit = np.nonzero(sample <= cum)[0]
+    pos = int(hit[0]) if hit.size else 0
+    margin = min(margin, abs(float(cum[pos]) - float(sample)))
+    if pos >= 1:
+        margin = min(margin, abs(float(sample) - float(cum[pos - 1])))
+    tok = int(order[pos])
+    return (tok, margin) if detail else tok
+
+
 def msr_recurrent_step(x_t, state, gamma, w_qkv, w_o, ret_norm_w, eps=1e-6):
     """One recurrent decode step of the Python MultiScaleRetention module for a
     batch of independent streams.

@@ -106,8 +106,41 @@ def test_generate_stream_api(dev):
         if t == 2:
             break
     assert out == exp
-    with pytest.raises(NotImplementedError):
-        eng.generate_stream([1], 2)  # default temperature 0.7: sampling is not on the GPU path
+    # the reference's defaults (temperature 0.7, top_k 40, top_p 0.9, penalty 1.2) sample on the
+    # GPU; a seed makes the draws repeatable
+    eng.reset_memory()
+    a1 = eng.generate_stream([1, 5], 4, seed=11)
+    eng.reset_memory()
+    a2 = eng.generate_stream([1, 5], 4, seed=11)
+    assert a1 == a2 and 1 <= len(a1) <= 4 and all(0 <= t < V for t in a1)
+
+
+def test_generate_sampling_matches_oracle(dev):
+    """Sampled generation (temperature, top-k, top-p, repetition penalty over
+    the last 60 ids of prompt + output): each step's token is the oracle's
+    sample_token on that step's logits, context window and draw (rows whose
+    draw lies within rounding of a boundary are not compared)."""
+    from oracle import retention_ref as R
+
+    L, d, H, f, V, B, P, n = 1, 256, 2, 96, 300, 3, 58, 6
+    layers, emb = _model(L, d, f, V, 9, False)
+    eng = _engine(layers, emb, H, B, "float32", 1e-5)
+    rng = np.random.default_rng(2)
+    prompts = rng.integers(3, V, (B, P)).astype(np.int32)
+    uni = rng.random((B, n)).astype(np.float32)
+    t, k, p, rp = 0.8, 20, 0.9, 1.3
+    toks, logits = eng.generate_batch(prompts, n, return_logits=True, temperature=t, top_k=k, top_p=p,
+                                      repetition_penalty=rp, uniforms=uni)
+    compared = 0
+    for b in range(B):
+        seen = list(prompts[b])
+        for s_ in range(n):
+            want, margin = R.sample_token(logits[b, s_], seen[-60:], t, k, p, rp, float(uni[b, s_]), detail=True)
+            if margin >= 1e-4:
+                compared += 1
+                assert toks[b, s_] == want, (b, s_, toks[b, s_], want)
+            seen.append(int(toks[b, s_]))
+    assert compared >= B * n * 3 // 4
 
 
 def test_engine_validation(dev):

@@ -68,6 +68,29 @@ def test_kat_dot():
     assert abs(cpu_ref.lib().oref_dot_product(cpu_ref._p(a), cpu_ref._p(b), 17) - ref) < 1e-4
 
 
+def test_kat_sampler_restatement():
+    """The full sampler restatement against the reference's tests
+    (sampler.rs:187-197) and hand-worked cases of sampler.rs:130-179."""
+    assert R.sample_token([1.0, 3.0, 2.0], [], 0.0, 0, 1.0, 1.0) == 1
+    assert R.sample_token([1.0, 3.0, 2.0], [1], 0.0, 0, 1.0, 10.0) == 2
+    # logits ln 1, ln 2, ln 3, ln 4 at temperature 1: probabilities .1 .2 .3 .4
+    lg = np.log(np.array([1.0, 2.0, 3.0, 4.0], np.float32))
+    # sorted 3, 2, 1, 0 with running sums .4 .7 .9 1.0
+    assert [R.sample_token(lg, (), 1.0, 0, 1.0, 1.0, u) for u in (0.0, 0.39, 0.41, 0.69, 0.71, 0.89, 0.91)] == \
+        [3, 3, 2, 2, 1, 1, 0]
+    # top_k 2 keeps 3, 2 (renormalised 4/7, 3/7); top_p 0.5 keeps 3, 2 (.7 is the first sum > .5),
+    # top_p 0.3 keeps only 3
+    assert R.sample_token(lg, (), 1.0, 2, 1.0, 1.0, 0.56) == 3
+    assert R.sample_token(lg, (), 1.0, 2, 1.0, 1.0, 0.58) == 2
+    assert R.sample_token(lg, (), 1.0, 0, 0.5, 1.0, 0.99) == 2
+    assert R.sample_token(lg, (), 1.0, 0, 0.3, 1.0, 0.99) == 3
+    # penalty 2 on token 3 (once, though listed twice): ln4 / 2 = ln2, so 1 and 3
+    # tie at ln 2; probabilities 3/8 (token 2), 2/8, 2/8, 1/8 with the tie in
+    # index order: a draw at 0.5 lands on token 1, at 0.7 on token 3
+    assert R.sample_token(lg, [3, 3], 1.0, 0, 1.0, 2.0, 0.5) == 1
+    assert R.sample_token(lg, [3, 3], 1.0, 0, 1.0, 2.0, 0.7) == 3
+
+
 def test_kat_greedy_sampler():
     # aceflow-core/src/cpu/sampler.rs:187-197
     assert R.greedy_token([1.0, 3.0, 2.0], [], 1.0) == 1
