@@ -239,6 +239,35 @@ class AceEngine:
             if L is None:
                 raise ValueError(f"Layer {i} weights are not loaded.")
 
+    def get_embedding(self, token_id: int) -> np.ndarray:
+        """AceEngine.get_embedding (cpu/mod.rs:285-304): the embedding row of
+        token_id as float32."""
+        if self.embedding is None:
+            raise ValueError("Embedding table is not loaded.")
+        if not 0 <= int(token_id) < self.vocab_size:
+            raise ValueError(f"token_id {token_id} out of vocabulary bounds (vocab_size: {self.vocab_size})")
+        return self.embedding[int(token_id)].float().cpu().numpy()
+
+    def _rmsnorm_dev(self, x, weights, eps):
+        xv, wv = _f32(x).reshape(-1), _f32(weights).reshape(-1)
+        if xv.size != wv.size:
+            raise ValueError(f"x length {xv.size} must match weights length {wv.size}")
+        y = cuda_ops.rms_norm(torch.as_tensor(xv.reshape(1, -1)).to(self.device),
+                              torch.as_tensor(wv).to(self.device), float(self.eps if eps is None else eps))
+        return y.cpu().numpy().reshape(-1)
+
+    def rmsnorm(self, x, weights, eps=None) -> np.ndarray:
+        """AceEngine.rmsnorm (cpu/mod.rs:306-327, norm.rs:6-59) on the GPU;
+        eps defaults to the engine's."""
+        return self._rmsnorm_dev(x, weights, eps)
+
+    def rmsnorm_inplace(self, x: np.ndarray, weights, eps=None) -> None:
+        """AceEngine.rmsnorm_inplace (cpu/mod.rs:329-347): x (a float32 numpy
+        vector) is overwritten with its RMSNorm."""
+        if not isinstance(x, np.ndarray) or x.dtype != np.float32 or x.ndim != 1:
+            raise TypeError("x must be a 1-D float32 numpy array")
+        x[...] = self._rmsnorm_dev(x, weights, eps)
+
     # ---------------------------------------------------------------- sampling
     PENALTY_WINDOW = 60  # generate_stream_internal penalises the last 60 ids (cpu/mod.rs:739)
 

@@ -143,6 +143,30 @@ def test_generate_sampling_matches_oracle(dev):
     assert compared >= B * n * 3 // 4
 
 
+def test_embedding_and_rmsnorm_methods(dev):
+    """get_embedding, rmsnorm and rmsnorm_inplace (cpu/mod.rs:285-347)
+    against the oracle's rmsnorm_core restatement."""
+    from oracle import retention_ref as R
+
+    L, d, H, f, V = 1, 256, 2, 64, 30
+    layers, emb = _model(L, d, f, V, 6, False)
+    eng = _engine(layers, emb, H, 1, "float32", 1e-5)
+    assert np.array_equal(eng.get_embedding(7), emb[7])
+    with pytest.raises(ValueError):
+        eng.get_embedding(V)
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal(d).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    ref = R.rmsnorm_core(x, w, 1e-5)
+    assert rel_err(eng.rmsnorm(x, w), ref) < 1e-5
+    assert rel_err(eng.rmsnorm(x, w, eps=1e-2), R.rmsnorm_core(x, w, 1e-2)) < 1e-5
+    y = x.copy()
+    eng.rmsnorm_inplace(y, w)
+    assert rel_err(y, ref) < 1e-5
+    with pytest.raises(ValueError):
+        eng.rmsnorm(x, w[:10])
+
+
 def test_engine_validation(dev):
     from aceflow_b200.engine import AceEngine
 
