@@ -68,6 +68,44 @@ class AceEngine:
     def reset_memory(self) -> None:
         self.states.zero_()
 
+    # Retention state save/restore (no reference counterpart: AceEngine only
+    # resets it, cpu/mod.rs:115-117).  Layout [layer][stream][head][k][v], fp32.
+    def get_state(self) -> np.ndarray:
+        """A host copy of every layer's retention state."""
+        return self.states.cpu().numpy()
+
+    def set_state(self, state) -> None:
+        """Replace the retention state (same shape as get_state's)."""
+        st = torch.as_tensor(_f32(state))
+        if tuple(st.shape) != tuple(self.states.shape):
+            raise ValueError(f"state shape {tuple(st.shape)} must be {tuple(self.states.shape)}")
+        self.states.copy_(st.to(self.device))
+
+    def save_state(self, path: str, metadata: dict | None = None) -> int:
+        """Write the retention state to an MTF file (one tensor per layer,
+        "state.<layer>"); returns the file size."""
+        from .io import mtf
+
+        meta = {"num_layers": self.num_layers, "batch": self.batch, "num_heads": self._h, "head_dim": self._dh}
+        meta.update(metadata or {})
+        return mtf.save_mtf(path, {f"state.{i}": self.states[i] for i in range(self.num_layers)}, metadata=meta)
+
+    def load_state(self, path: str) -> None:
+        """Read a state written by save_state straight into device memory."""
+        from .io import mtf
+
+        names = [f"state.{i}" for i in range(self.num_layers)]
+        with mtf.MtfReader(path) as r:
+            missing = [n for n in names if n not in r]
+            if missing:
+                raise ValueError(f"state file lacks {missing[0]}")
+            for n in names:
+                if tuple(r.tensors[n]["shape"]) != tuple(self.states.shape[1:]):
+                    raise ValueError(f"{n} has shape {r.tensors[n]['shape']}, expected {list(self.states.shape[1:])}")
+            dev = r.load_to_device(self.device, names)
+        for i, n in enumerate(names):
+            self.states[i].copy_(dev[n])
+
     def _dev(self, a, dtype=None) -> torch.Tensor:
         if isinstance(a, torch.Tensor):  # already a tensor (e.g. generated on the device)
             return a.detach().to(self.device, dtype or torch.float32).contiguous()

@@ -167,6 +167,30 @@ def test_embedding_and_rmsnorm_methods(dev):
         eng.rmsnorm(x, w[:10])
 
 
+def test_state_save_restore(dev, tmp_path):
+    """The retention state saved mid-generation (to a host array and to an
+    MTF file) and restored gives the same continuation."""
+    L, d, H, f, V, B = 2, 256, 2, 64, 60, 2
+    layers, emb = _model(L, d, f, V, 12, False)
+    eng = _engine(layers, emb, H, B, "float32", 1e-5)
+    prompts = np.array([[3, 9, 4], [7, 1, 8]], np.int32)
+    eng.generate_batch(prompts, 3)
+    snap = eng.get_state()
+    p = str(tmp_path / "state.mtf")
+    eng.save_state(p)
+    want = eng.generate_batch(prompts, 4)
+    eng.reset_memory()
+    assert not eng.get_state().any()
+    eng.set_state(snap)
+    assert np.array_equal(eng.generate_batch(prompts, 4), want)
+    eng.reset_memory()
+    eng.load_state(p)
+    assert np.array_equal(eng.get_state(), snap)
+    assert np.array_equal(eng.generate_batch(prompts, 4), want)
+    with pytest.raises(ValueError):
+        eng.set_state(snap[:1])
+
+
 def test_engine_validation(dev):
     from aceflow_b200.engine import AceEngine
 
