@@ -173,6 +173,8 @@ class MtfReader:
         pinned = [torch.empty(max(cap, 1), dtype=torch.uint8, pin_memory=True) for _ in range(2)]
         done = [None, None]
         side = torch.cuda.Stream(dev)
+        cur = torch.cuda.current_stream(dev)
+        side.wait_stream(cur)
         out: Dict[str, torch.Tensor] = {}
         with torch.cuda.stream(side):
             for i, n in enumerate(names):
@@ -191,7 +193,9 @@ class MtfReader:
                 done[j] = ev
                 t = d.view(_TORCH.get(code, torch.float32)).reshape(tuple(meta["shape"]))
                 out[n] = t.to(dtype) if dtype is not None and t.dtype != dtype else t
-        torch.cuda.current_stream(dev).wait_stream(side)
+        cur.wait_stream(side)
+        for t in out.values():
+            t.record_stream(cur)  # allocated on the side stream, used on the caller's
         for ev in done:
             if ev is not None:
                 ev.synchronize()  # pinned buffers are released on return
