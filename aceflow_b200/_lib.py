@@ -35,6 +35,7 @@ SIGNATURES = {
     "af_launch_count": [_vp, ctypes.POINTER(_i64)],
     "af_check_device": [_vp, ctypes.POINTER(_i), _i],
     "af_set_option": [_vp, ctypes.c_char_p, _i64],
+    "af_selftest_bounded_wait": [_vp, _i64, _vp],
     "af_retention_step": [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i, _i, _i, _vp],
     "af_retention_scan": [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i, _i, _i, _i, _vp],
     "af_rmsnorm_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f, _vp],
@@ -49,6 +50,8 @@ SIGNATURES = {
     "af_comm_init": [_vp, _i, _i, _vp],
     "af_comm_destroy": [_vp],
     "af_prefill_head_sharded": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp],
+    "af_prefill_head_sharded_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp],
+    "af_phase_times": [_vp, ctypes.POINTER(_f), ctypes.POINTER(ctypes.c_char_p), _i, ctypes.POINTER(_i)],
     "af_gemm_bf16": [_vp, _vp, _i64, _i, _vp, _i64, _i, _i, _i, _vp, _i64, _i, _vp, _vp, _i64, _vp, _i, _i, _f, _f, _i,
                      _vp],
     "af_msr_decode_step_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
@@ -140,6 +143,16 @@ def check_device(device_index: int, reset: bool = True) -> int:
     flags = ctypes.c_int()
     check(lib().af_check_device(context(device_index), ctypes.byref(flags), int(reset)), "af_check_device")
     return int(flags.value)
+
+
+def phase_times(device_index: int) -> list:
+    """[(phase, ms)] of the last prefill call made with the "phase_marks"
+    option on (af_phase_times)."""
+    ms = (_f * 16)()
+    names = (ctypes.c_char_p * 16)()
+    n = _i()
+    check(lib().af_phase_times(context(device_index), ms, names, 16, ctypes.byref(n)), "af_phase_times")
+    return [(names[i].decode(), float(ms[i])) for i in range(n.value)]
 
 
 def launch_count(device_index: int) -> int:

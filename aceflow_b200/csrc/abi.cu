@@ -123,6 +123,8 @@ int af_cuda_destroy(af_ctx *ctx) {
     if (ctx->ev_a[i]) cudaEventDestroy(ctx->ev_a[i]);
     if (ctx->ev_b[i]) cudaEventDestroy(ctx->ev_b[i]);
   }
+  for (int i = 0; i < af_ctx::kMaxMarks; ++i)
+    if (ctx->mark_ev[i]) cudaEventDestroy(ctx->mark_ev[i]);
   ctx->magic = 0;
   delete ctx;
   return AF_OK;
@@ -135,6 +137,7 @@ int af_reserve_workspace(af_ctx *ctx, size_t bytes) {
 }
 
 int af_check_device(af_ctx *ctx, int *flags, int reset) {
+  if (ctx == nullptr) return af::noalloc_check_device(flags, reset);
   AF_ENTER(ctx, "af_check_device");
   int h = 0;
   AF_CUDA(cudaMemcpy(&h, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost), "af_check_device");
@@ -174,11 +177,32 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
   } else if (!strcmp(name, "chunkwise_segments")) {
     if (value < 0 || value > 4096) return af::fail(AF_ERR_ARG, "af_set_option: chunkwise_segments 0..4096");
     ctx->chunk_segments = (int)value;
+  } else if (!strcmp(name, "phase_marks")) {
+    for (int i = 0; value && i < af_ctx::kMaxMarks; ++i)
+      if (!ctx->mark_ev[i]) AF_CUDA(cudaEventCreate(&ctx->mark_ev[i]), "af_set_option(phase_marks)");
+    ctx->phase_marks = value != 0;
+    ctx->nmarks = 0;
   } else if (!strcmp(name, "decode_slice_rows")) {
     if (value < 0) return af::fail(AF_ERR_ARG, "af_set_option: decode_slice_rows >= 0");
     ctx->decode_slice_rows = (int)value;
   } else {
     return af::fail(AF_ERR_ARG, "af_set_option: unknown option '%s'", name);
+  }
+  return AF_OK;
+}
+
+int af_phase_times(af_ctx *ctx, float *ms, const char **names, int max, int *n) {
+  AF_ENTER(ctx, "af_phase_times");
+  if (!ms || !names || !n || max < 0) return af::fail(AF_ERR_ARG, "af_phase_times: null output or bad max");
+  *n = 0;
+  if (!ctx->phase_marks || ctx->nmarks < 2) return AF_OK;
+  AF_CUDA(cudaEventSynchronize(ctx->mark_ev[ctx->nmarks - 1]), "af_phase_times");
+  for (int i = 1; i < ctx->nmarks && *n < max; ++i) {
+    float t = 0.f;
+    AF_CUDA(cudaEventElapsedTime(&t, ctx->mark_ev[i - 1], ctx->mark_ev[i]), "af_phase_times");
+    ms[*n] = t;
+    names[*n] = ctx->mark_name[i];
+    ++*n;
   }
   return AF_OK;
 }

@@ -44,6 +44,14 @@ struct af_ctx {
   int decode_transposed = 15;
   int sharded_head_groups = 0;  // head groups pipelined against the all-gather (0: auto; 1: one gather)
   int comm_reserve_sms = 16;    // SMs the overlapped kernels leave to NCCL
+  // Phase marks (af_set_option "phase_marks"): timing events the prefill
+  // entry points record on the caller's stream at their phase boundaries,
+  // read back by af_phase_times.
+  static constexpr int kMaxMarks = 16;
+  int phase_marks = 0;
+  int nmarks = 0;
+  cudaEvent_t mark_ev[kMaxMarks] = {};
+  const char *mark_name[kMaxMarks] = {};
 };
 
 constexpr uint32_t kCtxMagic = 0xACEF1011u;
@@ -132,6 +140,12 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
 int chunkwise_head_dim();
 int chunkwise_parts();
 
+// af_check_device(NULL, ...): the allocation-free decode step's error word on
+// the current device (decode_noalloc.cu).
+int noalloc_check_device(int *flags, int reset);
+// Device address of that error word on the current device.
+int noalloc_error_word(int **word, const char *fn);
+
 // Releases the context's communicator, if any (sharded_prefill.cu).
 void comm_release(af_ctx *ctx);
 
@@ -146,6 +160,19 @@ int launch_retention_step(af_ctx *ctx, float *state, int64_t state_bs, const flo
                           int64_t split_stride = 0, bool pdl = false);
 
 inline cudaStream_t stream_of(af_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Phase marks: `mark_begin` starts a call's list, `mark` closes the phase
+// named `name` (no-ops unless the context has phase_marks on; the events were
+// created when it was switched on).
+inline void mark(af_ctx *ctx, const char *name, cudaStream_t st) {
+  if (!ctx->phase_marks || ctx->nmarks >= af_ctx::kMaxMarks || !ctx->mark_ev[ctx->nmarks]) return;
+  cudaEventRecord(ctx->mark_ev[ctx->nmarks], st);
+  ctx->mark_name[ctx->nmarks++] = name;
+}
+inline void mark_begin(af_ctx *ctx, cudaStream_t st) {
+  ctx->nmarks = 0;
+  mark(ctx, "begin", st);
+}
 
 // Raises a kernel's dynamic shared-memory limit on the context's device,
 // once per device (the attribute is per device; `done` is the call site's

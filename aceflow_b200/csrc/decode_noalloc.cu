@@ -3,10 +3,11 @@
 // af_msr_decode_step_f32 takes its scratch (the packed q/k/v projection, the
 // retention output and the per-head sums of squares) from the context's
 // workspace, which grows with cudaMalloc on first use.  Some callers cannot
-// allocate at that point: code running inside a CUDA-graph capture (where
-// cudaMalloc is illegal), serving processes whose device memory is handed
-// out by their own arena allocator and must not be touched by a library,
-// and plugins loaded into a host that owns the whole device.  For them,
+// allocate at that point: serving processes whose device memory is carved up
+// front by their own arena allocator (a library cudaMalloc would break their
+// accounting or fail outright once the arena holds the free memory), plugins
+// loaded into a host that owns the device-memory budget, and loops that must
+// not take cudaMalloc's implicit synchronisation.  For them,
 // af_msr_decode_step_f32_noalloc runs the very same kernels, with its scratch
 // in a fixed array compiled into this library (kNoallocScratchFloats floats,
 // 16 MiB, held on every GPU that loads the library until the process exits)
@@ -14,7 +15,14 @@
 //
 // The array's name is a host-side stand-in in host code, not a device
 // address: the device address is looked up with cudaGetSymbolAddress once
-// per device, with that device current, by the first call made on it.
+// per device, with that device current, by the first call made on it (so
+// that first call should come before any stream capture).  The cached
+// address belongs to the device's current primary context: after
+// cudaDeviceReset the entry point must not be called again in the process.
+//
+// The kernels' bounded waits report a timeout in this file's own device
+// error word (there is no context to hold one); af_check_device(NULL, ...)
+// reads and clears it for the current device.
 #include "common.cuh"
 
 #include <mutex>
@@ -72,6 +80,40 @@ int setup_device(int dev, DeviceSetup *out, const char *fn) {
 }
 
 }  // namespace
+
+namespace af {
+// Device address of the error word on the current device (set-up included).
+int noalloc_error_word(int **word, const char *fn) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: cudaGetDevice: %s", fn, cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(AF_ERR_ARG, "%s: device %d out of range", fn, dev);
+  DeviceSetup s;
+  int rc = setup_device(dev, &s, fn);
+  if (rc) return rc;
+  *word = s.err;
+  return AF_OK;
+}
+
+// af_check_device(NULL, ...): the allocation-free entry point's error word on
+// the current device.  cudaMemcpyFromSymbol synchronises the device first.
+int noalloc_check_device(int *flags, int reset) {
+  const char *fn = "af_check_device(NULL)";
+  int h = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&h, g_noalloc_err, sizeof(int));
+  if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+  if (reset && h) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(int));
+    if (e != cudaSuccess) return fail(AF_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+  }
+  if (flags) *flags = h;
+  if (h & (1 << AF_ERR_TIMEOUT))
+    return fail(AF_ERR_TIMEOUT, "%s: a device-side wait of the allocation-free decode step timed out (flags 0x%x)",
+                fn, h);
+  return AF_OK;
+}
+}  // namespace af
 
 extern "C" int af_msr_decode_step_f32_noalloc(const float *x, float *state, const float *gamma, const float *w_qkv,
                                               const float *w_o, const float *ret_norm_w, float eps, int B, int d,

@@ -328,6 +328,7 @@ extern "C" int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int
     int rc = af::workspace(ctx, seg_bytes, &ws, fn);
     if (rc) return rc;
   }
+  af::mark_begin(ctx, af::stream_of(stream));
   return af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, out, norm_w, sumsq, pl,
                                       static_cast<float *>(ws), af::stream_of(stream), fn);
 }
@@ -361,12 +362,14 @@ extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_
   float *ss = reinterpret_cast<float *>(base + qkv_bytes + o_bytes);
   float *seg = seg_bytes ? reinterpret_cast<float *>(base + qkv_bytes + o_bytes + ss_bytes) : nullptr;
   cudaStream_t st = af::stream_of(stream);
+  af::mark_begin(ctx, st);
   af::GemmEpilogueArgs e1;
   e1.out = qkv;
   e1.ldo = 3 * d;
   e1.out_bf16 = 1;
   rc = af::tc_gemm(ctx, x, d, w_qkv, d, (int)N, 3 * d, d, false, e1, st, fn);
   if (rc) return rc;
+  af::mark(ctx, "qkv", st);
   rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, H, gamma, state_in, state_out, o, ret_norm_w, ss, pl, seg, st,
                                     fn);
   if (rc) return rc;
@@ -378,7 +381,9 @@ extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_
   e2.nparts = parts;
   e2.inv_d = 1.0f / (float)d;
   e2.eps = eps;
-  return af::tc_gemm(ctx, o, d, w_o, d, (int)N, d, d, false, e2, st, fn);
+  rc = af::tc_gemm(ctx, o, d, w_o, d, (int)N, d, d, false, e2, st, fn);
+  af::mark(ctx, "w_o", st);
+  return rc;
 }
 
 extern "C" int af_pack_qkv_heads(af_ctx *ctx, const void *src, void *dst, int d, int H, int elem_bytes,

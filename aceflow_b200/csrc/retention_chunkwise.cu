@@ -676,7 +676,11 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   ChunkParams p{B,       T,         H,       pl.nseg, pl.seg_len, gamma, state_in, state_out,
                 reinterpret_cast<__nv_bfloat16 *>(out), norm_w, sumsq, ctx->dev_err};
   if (!out) return fail(AF_ERR_ARG, "%s: output is NULL", fn);
-  if (pl.nseg == 1) return launch_chunkwise<false>(ctx, tm, tm_out, p, st, fn);
+  if (pl.nseg == 1) {
+    const int rc = launch_chunkwise<false>(ctx, tm, tm_out, p, st, fn);
+    mark(ctx, "chunkwise", st);
+    return rc;
+  }
   // 1. segment end states from zero
   ChunkParams ps = p;
   ps.state_in = nullptr;
@@ -686,6 +690,7 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   ps.sumsq = nullptr;
   int rc = launch_chunkwise<true>(ctx, tm, tm, ps, st, fn);
   if (rc) return rc;
+  mark(ctx, "chunk_state", st);
   // 2. states before each segment
   const int64_t n4 = (int64_t)B * H * (DH * DH / 4);
   seg_scan_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, st>>>(reinterpret_cast<float4 *>(seg_states),
@@ -693,9 +698,12 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
                                                                 pl.nseg, H, pl.seg_len);
   rc = launched(ctx, fn);
   if (rc) return rc;
+  mark(ctx, "chunk_scan", st);
   // 3. the full pass from each segment's state
   p.state_in = seg_states;
-  return launch_chunkwise<false>(ctx, tm, tm_out, p, st, fn);
+  rc = launch_chunkwise<false>(ctx, tm, tm_out, p, st, fn);
+  mark(ctx, "chunkwise", st);
+  return rc;
 }
 
 int chunkwise_head_dim() { return DH; }

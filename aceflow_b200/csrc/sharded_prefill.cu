@@ -36,6 +36,8 @@ struct NcclApi {
   decltype(&ncclCommDestroy) comm_destroy = nullptr;
   decltype(&ncclCommAbort) comm_abort = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclSend) send = nullptr;
+  decltype(&ncclRecv) recv = nullptr;
   decltype(&ncclGroupStart) group_start = nullptr;
   decltype(&ncclGroupEnd) group_end = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
@@ -59,6 +61,8 @@ int load_nccl(const char *fn) {
   AF_SYM(comm_destroy, "ncclCommDestroy");
   AF_SYM(comm_abort, "ncclCommAbort");
   AF_SYM(all_gather, "ncclAllGather");
+  AF_SYM(send, "ncclSend");
+  AF_SYM(recv, "ncclRecv");
   AF_SYM(group_start, "ncclGroupStart");
   AF_SYM(group_end, "ncclGroupEnd");
   AF_SYM(error_string, "ncclGetErrorString");
@@ -188,6 +192,7 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
   uint16_t *wo_perm = G > 1 ? reinterpret_cast<uint16_t *>(base + qkv_b + o_b + ss_b + seg_b) : nullptr;
   cudaStream_t st = af::stream_of(stream), cs = ctx->side[0];
   ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+  af::mark_begin(ctx, st);
   if (G > 1) {
     // W_o rows with their columns in the gather buffers' K order
     const int64_t vec = (int64_t)G * dl * g * (dlg / 8);
@@ -209,6 +214,7 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
       rc = af::tc_gemm(ctx, x, d, wrows, d, (int)N, dlg, d, false, e, st, fn);
       if (rc) return rc;
     }
+    if (G == 1) af::mark(ctx, "qkv", st);
     // 2. retention of group i into its slot of the gather buffer
     uint16_t *o_grp = o_all + (size_t)i * g * N * dlg;
     float *ss_grp = ss_all + (size_t)i * g * N * P;
@@ -236,6 +242,7 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
       if (G > 1) AF_CUDA(cudaEventRecord(ctx->ev_b[i], cs), fn);
     }
   }
+  if (G == 1) af::mark(ctx, "allgather", st);
   const bool waits = G > 1 && g > 1;  // gathers ran on the side stream
   // 4. this rank's output columns: the gather buffers [G][g][N][dlg] as one
   //    K-blocked operand . W_o rows (columns in the same K order)^T, 1/rms
@@ -254,6 +261,115 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
   e.eps = eps;
   rc = af::tc_gemm(ctx, o_all, dlg, G > 1 ? wo_perm : w_o_rows, d, (int)N, dl, d, false, e, st, fn);
   if (rc) return rc;
+  af::mark(ctx, "w_o", st);
+  return AF_OK;
+}
+
+// Row-sharded variant: the exchange is an all-to-all instead of an
+// all-gather.  Rank r still projects and retains its heads over all N rows,
+// then sends rows [s*c, s*c + n_s) of its head outputs (and their partial
+// sums of squares) to rank s and receives the other ranks' heads for its own
+// rows [r*c, r*c + n_r), c = ceil(N/g): (g-1)/g^2 of the layer's bf16 output
+// crosses NVLink per rank instead of the all-gather's (g-1)/g.  Its rows are
+// then complete (every head), so the RMSNorm and the FULL W_o run locally:
+// out [n_r][d], the layer output's rows of this rank.  The receive buffer
+// [g][n_r][dl] is the K-blocked operand of the W_o GEMM (block p = rank p's
+// heads = columns p*dl.. of O, W_o's natural K order).
+int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv_local, const uint16_t *w_o,
+                                 const float *ret_norm_w, const float *gamma, float eps, int B, int T, int d, int H,
+                                 const float *state_in, float *state_out, void *out, int out_bf16,
+                                 af_stream_t stream) {
+  const char *fn = "af_prefill_head_sharded_rows";
+  AF_ENTER(ctx, fn);
+  AF_REQUIRE(ctx->comm, "af_prefill_head_sharded_rows", "no communicator: call af_comm_init first");
+  const int g = ctx->comm_nranks, r = ctx->comm_rank;
+  const int dh = af::chunkwise_head_dim();
+  AF_REQUIRE(x && w_qkv_local && w_o && ret_norm_w && gamma && out, "af_prefill_head_sharded_rows", "null pointer");
+  AF_REQUIRE(B >= 0 && T >= 0 && H > 0 && d == H * dh && H % g == 0, "af_prefill_head_sharded_rows",
+             "needs head_dim %d and heads divisible by ranks (d=%d H=%d ranks=%d)", dh, d, H, g);
+  AF_REQUIRE(af::aligned16(x) && af::aligned16(w_qkv_local) && af::aligned16(w_o) && af::aligned16(out),
+             "af_prefill_head_sharded_rows", "x, weights and out must be 16-byte aligned");
+  AF_REQUIRE((int64_t)B * T <= 65535LL * 128, "af_prefill_head_sharded_rows", "B*T too large");
+  if (B == 0 || T == 0) return AF_OK;
+  const int Hl = H / g, dl = Hl * dh, P = Hl * af::chunkwise_parts();
+  const int64_t N = (int64_t)B * T;
+  const int64_t c = (N + g - 1) / g;  // rows per rank (the last ranks may hold fewer)
+  auto rows_of = [&](int s) -> int64_t {
+    const int64_t lo = (int64_t)s * c;
+    return lo >= N ? 0 : (N - lo < c ? N - lo : c);
+  };
+  const int64_t nr = rows_of(r);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, Hl, ctx->chunk_segments);
+  const size_t qkv_b = align256((size_t)N * 3 * dl * 2), o_b = align256((size_t)N * dl * 2),
+               ss_b = align256((size_t)N * P * 4), ro_b = align256((size_t)g * c * dl * 2),
+               rss_b = align256((size_t)g * c * P * 4), seg_b = align256(af::chunkwise_seg_state_bytes(B, Hl, pl));
+  void *ws = nullptr;
+  int rc = af::workspace(ctx, qkv_b + o_b + ss_b + ro_b + rss_b + seg_b, &ws, fn);
+  if (rc) return rc;
+  uint8_t *base = static_cast<uint8_t *>(ws);
+  uint16_t *qkv = reinterpret_cast<uint16_t *>(base);
+  uint16_t *o_loc = reinterpret_cast<uint16_t *>(base + qkv_b);                      // [N][dl]
+  float *ss_loc = reinterpret_cast<float *>(base + qkv_b + o_b);                     // [N][P]
+  uint16_t *o_rows = reinterpret_cast<uint16_t *>(base + qkv_b + o_b + ss_b);        // [g][nr][dl]
+  float *ss_rows = reinterpret_cast<float *>(base + qkv_b + o_b + ss_b + ro_b);      // [g][nr][P]
+  float *seg = seg_b ? reinterpret_cast<float *>(base + qkv_b + o_b + ss_b + ro_b + rss_b) : nullptr;
+  cudaStream_t st = af::stream_of(stream);
+  ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
+  af::mark_begin(ctx, st);
+  // 1. projections of this rank's heads
+  for (int part = 0; part < 3; ++part) {
+    af::GemmEpilogueArgs e;
+    e.out = qkv + (size_t)part * dl;
+    e.ldo = 3 * dl;
+    e.out_bf16 = 1;
+    rc = af::tc_gemm(ctx, x, d, w_qkv_local + (size_t)part * dl * d, d, (int)N, dl, d, false, e, st, fn);
+    if (rc) return rc;
+  }
+  af::mark(ctx, "qkv", st);
+  // 2. retention of its heads over all rows
+  rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, Hl, gamma + (size_t)r * Hl, state_in, state_out, o_loc,
+                                    ret_norm_w + (size_t)r * dl, ss_loc, pl, seg, st, fn);
+  if (rc) return rc;
+  // 3. all-to-all: rows of rank s go to rank s; rank p's heads land in block p
+  if (g > 1) {
+    ncclResult_t nr_ = g_nccl.group_start();
+    for (int s2 = 0; s2 < g && nr_ == ncclSuccess; ++s2) {
+      const int64_t ns = rows_of(s2);
+      if (ns > 0) {
+        nr_ = g_nccl.send(o_loc + (size_t)s2 * c * dl, (size_t)ns * dl, ncclBfloat16, s2, comm, st);
+        if (nr_ == ncclSuccess)
+          nr_ = g_nccl.send(ss_loc + (size_t)s2 * c * P, (size_t)ns * P, ncclFloat32, s2, comm, st);
+      }
+      if (nr > 0 && nr_ == ncclSuccess) {
+        nr_ = g_nccl.recv(o_rows + (size_t)s2 * nr * dl, (size_t)nr * dl, ncclBfloat16, s2, comm, st);
+        if (nr_ == ncclSuccess)
+          nr_ = g_nccl.recv(ss_rows + (size_t)s2 * nr * P, (size_t)nr * P, ncclFloat32, s2, comm, st);
+      }
+    }
+    const ncclResult_t ne = g_nccl.group_end();
+    if (nr_ == ncclSuccess) nr_ = ne;
+    if (nr_ != ncclSuccess) return nccl_fail(nr_, fn, "ncclSend/ncclRecv");
+  } else {
+    AF_CUDA(cudaMemcpyAsync(o_rows, o_loc, (size_t)N * dl * 2, cudaMemcpyDeviceToDevice, st), fn);
+    AF_CUDA(cudaMemcpyAsync(ss_rows, ss_loc, (size_t)N * P * 4, cudaMemcpyDeviceToDevice, st), fn);
+  }
+  af::mark(ctx, "alltoall", st);
+  if (nr == 0) return AF_OK;
+  // 4. this rank's rows of the output: RMSNorm row scale from all heads' partial
+  //    sums, then the full W_o
+  af::GemmEpilogueArgs e;
+  e.out = out;
+  e.ldo = d;
+  e.out_bf16 = out_bf16;
+  e.a_kblock = dl;
+  e.row_parts = ss_rows;
+  e.nparts = g * P;
+  e.parts_block = P;
+  e.inv_d = 1.0f / (float)d;
+  e.eps = eps;
+  rc = af::tc_gemm(ctx, o_rows, dl, w_o, d, (int)nr, d, d, false, e, st, fn);
+  if (rc) return rc;
+  af::mark(ctx, "w_o", st);
   return AF_OK;
 }
 

@@ -53,15 +53,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for the phase with `parity` to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Waits for the phase with `parity` to complete; false on timeout (after
+// `limit_ns` of %globaltimer time).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 256; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) return false;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
 }
 

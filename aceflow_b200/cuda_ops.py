@@ -13,6 +13,7 @@ from . import _lib
 
 F32 = torch.float32
 BF16 = torch.bfloat16
+CHUNKS = (64,)  # chunk lengths of the tensor-core chunkwise prefill
 
 
 def _dev(t: torch.Tensor) -> int:
@@ -206,10 +207,12 @@ def linear_bf16(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = No
 
 def retention_chunkwise_bf16(qkv: torch.Tensor, B: int, T: int, H: int, gamma: torch.Tensor,
                              state_in: torch.Tensor | None = None, norm_w: torch.Tensor | None = None,
-                             want_state: bool = True):
+                             want_state: bool = True, chunk: int = 64):
     """Tensor-core chunkwise retention over a bf16 QKV buffer [B*T, 3*H*256].
     Returns (out bf16 [B*T, H*256] (times norm_w), sumsq [B*T, 2H], state_out
     [B, H, 256, 256] fp32 or None)."""
+    if chunk not in CHUNKS:
+        raise ValueError(f"chunk must be one of {CHUNKS}, got {chunk}")
     _need(qkv, BF16, "qkv")
     d = H * 256
     if tuple(qkv.shape) != (B * T, 3 * d):
@@ -231,9 +234,11 @@ def retention_chunkwise_bf16(qkv: torch.Tensor, B: int, T: int, H: int, gamma: t
 
 def msr_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, ret_norm_w: torch.Tensor,
                      gamma: torch.Tensor, eps: float, state_in: torch.Tensor | None = None,
-                     out_dtype=torch.float32, want_state: bool = True):
+                     out_dtype=torch.float32, want_state: bool = True, chunk: int = 64):
     """MultiScaleRetention prefill on the bf16 tensor cores: x [B, T, d] bf16
     -> (out [B, T, d] out_dtype, final state [B, H, 256, 256] fp32 or None)."""
+    if chunk not in CHUNKS:
+        raise ValueError(f"chunk must be one of {CHUNKS}, got {chunk}")
     _need(x, BF16, "x")
     B, T, d = x.shape
     H = d // 256
@@ -246,6 +251,10 @@ def msr_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, re
         raise ValueError("w_qkv must be [3d, d] and w_o [d, d]")
     if state_in is not None:
         _need(state_in, F32, "state_in")
+        if tuple(state_in.shape) != (B, H, 256, 256):
+            raise ValueError(f"state_in must be [{B}, {H}, 256, 256]")
+    if out_dtype not in (F32, BF16):
+        raise ValueError("out_dtype must be float32 or bfloat16")
     out = torch.empty(B, T, d, dtype=out_dtype, device=x.device)
     state_out = torch.empty(B, H, 256, 256, dtype=F32, device=x.device) if want_state else None
     _lib.call("af_msr_prefill_bf16", _ctx(x), _p(x), _p(w_qkv), _p(w_o), _p(ret_norm_w), _p(gamma), float(eps),
@@ -257,19 +266,51 @@ def msr_decode_step_noalloc(x: torch.Tensor, state: torch.Tensor, gamma: torch.T
                             w_o: torch.Tensor, ret_norm_w: torch.Tensor, eps: float,
                             out: torch.Tensor | None = None) -> torch.Tensor:
     """af_msr_decode_step_f32_noalloc: the decode step with the library's
-    static scratch array (no allocation, no context) on x's device."""
+    static scratch array (no allocation, no context) on x's device.  The C
+    entry point cannot see tensor shapes, so every shape and device is
+    checked here before the call."""
+    if x.dim() != 2 or state.dim() != 4:
+        raise ValueError("x must be [B, d] and state [B, H, d/H, d/H]")
     B, d = x.shape
     H = state.shape[1]
     for n, t in (("x", x), ("state", state), ("gamma", gamma), ("w_qkv", w_qkv), ("w_o", w_o),
                  ("ret_norm_w", ret_norm_w)):
         _need(t, F32, n)
+    if H <= 0 or d % H:
+        raise ValueError(f"d_model ({d}) must be divisible by num_heads ({H})")
+    if tuple(state.shape) != (B, H, d // H, d // H):
+        raise ValueError(f"state shape {tuple(state.shape)} != {(B, H, d // H, d // H)}")
+    if tuple(w_qkv.shape) != (3 * d, d) or tuple(w_o.shape) != (d, d):
+        raise ValueError("w_qkv must be [3d, d] and w_o [d, d]")
+    if gamma.numel() != H or ret_norm_w.numel() != d:
+        raise ValueError(f"gamma must hold {H} values and ret_norm_w {d}")
+    if out is not None:
+        _need(out, F32, "out")
+        if tuple(out.shape) != (B, d):
+            raise ValueError(f"out must be [{B}, {d}]")
+    for n, t in (("state", state), ("gamma", gamma), ("w_qkv", w_qkv), ("w_o", w_o), ("ret_norm_w", ret_norm_w),
+                 ("out", out)):
+        if t is not None and t.device != x.device:
+            raise ValueError(f"{n} is on {t.device}, x on {x.device}")
+    _dev(x)
     if out is None:
         out = torch.empty(B, d, dtype=F32, device=x.device)
-    _dev(x)
     with torch.cuda.device(x.device):
         _lib.call("af_msr_decode_step_f32_noalloc", _p(x), _p(state), _p(gamma), _p(w_qkv), _p(w_o), _p(ret_norm_w),
                   float(eps), B, d, H, _p(out), _stream(x))
     return out
+
+
+def noalloc_check_device(device, reset: bool = True) -> int:
+    """Reads (and with `reset` clears) the allocation-free decode step's
+    device error word on `device` (af_check_device with a NULL context);
+    raises RuntimeError if one of its bounded waits timed out."""
+    import ctypes
+
+    flags = ctypes.c_int()
+    with torch.cuda.device(device):
+        _lib.check(_lib.lib().af_check_device(None, ctypes.byref(flags), int(reset)), "af_check_device")
+    return int(flags.value)
 
 
 def split_tf32(t: torch.Tensor):
@@ -375,6 +416,15 @@ def gemm_bf16(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, row_sumsq: to
               out.stride(0), 0, _p(bias), _p(residual), ldr, _p(row_sumsq), P, int(parts_block), float(inv_d),
               float(eps), int(accumulate), _stream(a))
     return out
+
+
+def to_bf16(x: torch.Tensor) -> torch.Tensor:
+    """fp32 -> bf16 (round to nearest even) on the device, same shape
+    (af_rmsnorm_to_bf16 with no weight: a plain cast)."""
+    _need(x, F32, "x")
+    if x.dim() == 0 or x.shape[-1] == 0:
+        raise ValueError("x must have a non-empty last dimension")
+    return rms_norm_to_bf16(x, None, 0.0)
 
 
 def rms_norm_to_bf16(x: torch.Tensor, w: torch.Tensor | None, eps: float) -> torch.Tensor:

@@ -10,9 +10,11 @@ State layout: one device tensor [num_layers][batch][H][dh][dh] fp32 (layer
 major, so each layer's slice is the [batch][H][k][v] layout every retention
 kernel takes).
 
-Supported sampling: greedy (temperature <= 1e-4) with repetition_penalty 1.0,
-the configuration the decoder-stack workload uses; other settings raise
-NotImplementedError rather than silently differing from the reference.
+Generation: greedy (temperature <= 1e-4) and the reference's sampling
+(repetition penalty, temperature, top-k, top-p, then a draw;
+sampler.rs:83-180) both run on the GPU (af_lm_head_argmax, af_sample_rows);
+the draws take caller-supplied (or seeded) uniforms in place of the
+reference's clock-seeded generator.
 """
 from __future__ import annotations
 
@@ -239,7 +241,11 @@ class AceEngine:
         """AceEngine.retention_step (cpu/mod.rs:486-512) for the batch."""
         if layer_idx >= self.num_layers:
             raise ValueError(f"layer_idx {layer_idx} out of range (total layers: {self.num_layers})")
-        rows = [self._rows(a)[0] for a in (q, k, v)]
+        arrs = [_f32(a) for a in (q, k, v)]
+        if any(a.shape[-1] != self._d for a in arrs):
+            raise ValueError(f"Expected input vectors of length {self._d}, got q={arrs[0].shape[-1]}, "
+                             f"k={arrs[1].shape[-1]}, v={arrs[2].shape[-1]}")
+        rows = [self._rows(a)[0] for a in arrs]
         one = np.asarray(q).ndim == 1
         qkv = torch.from_numpy(np.concatenate(rows, axis=1)).to(self.device)
         d = self._d

@@ -16,8 +16,19 @@ Methods:
   forward_chunkwise(x, chunk, state) -> (out, state)
   init_state(batch) -> zero state [B, H, dh, dh] fp32
 
-On CUDA: fp32 inputs run the exact fp32 kernels (projection GEMM, state
-scan / step, fused RMSNorm); the fused decode step is one ABI call.
+On CUDA the prompt (forward / forward_parallel / forward_chunkwise) runs one
+of two paths:
+  * the chunkwise form on the bf16 tensor cores (af_msr_prefill_bf16: bf16
+    QKV GEMM, tcgen05 chunkwise retention with the state carried in TMEM,
+    W_o GEMM with the RMSNorm as a row scale; fp32 accumulation, 2e-2 of the
+    float64 reference) for bf16 inputs, for fp32 inputs when the module was
+    built with prefill_dtype="bfloat16", and always for forward_chunkwise
+    (head_dim 256);
+  * the exact fp32 path otherwise (3xTF32 QKV GEMM, the recurrence token by
+    token as the reference's AceEngine.prefill_recurrent, fused RMSNorm,
+    3xTF32 W_o GEMM; 1e-4 of the reference), which any head_dim can take.
+The output's dtype is the input's.  forward_recurrent is one fused fp32
+decode step (af_msr_decode_step_f32_split).
 """
 from __future__ import annotations
 
@@ -30,12 +41,17 @@ from ..core.tensor import Tensor
 from .layers import RMSNorm
 from .module import Module, Parameter
 
+TC_HEAD_DIM = 256   # head_dim of the tensor-core chunkwise kernel
+DEFAULT_CHUNK = 64  # tokens per chunk of the chunkwise prefill
+
 
 class MultiScaleRetention(Module):
     """Multi-Scale Retention (MSR) layer."""
 
-    def __init__(self, d_model: int, num_heads: int):
+    def __init__(self, d_model: int, num_heads: int, *, prefill_dtype: Optional[str] = None):
         super().__init__()
+        if prefill_dtype not in (None, "float32", "bfloat16"):
+            raise ValueError("prefill_dtype must be None, 'float32' or 'bfloat16'")
         if num_heads <= 0 or d_model % num_heads != 0:
             raise ValueError(f"d_model ({d_model}) must be divisible by num_heads ({num_heads})")
         self.d_model = d_model
@@ -48,6 +64,9 @@ class MultiScaleRetention(Module):
         self.w_v = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
         self.w_o = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
         self.ret_norm = RMSNorm(d_model)
+        # "bfloat16": fp32 prompts on CUDA also take the tensor-core chunkwise
+        # prefill (2e-2 tolerance); None/"float32": they take the exact path
+        self.prefill_dtype = prefill_dtype
         self._dev = None  # packed device weights
 
     # ------------------------------------------------------------ device pack
@@ -73,6 +92,21 @@ class MultiScaleRetention(Module):
             raise ValueError(f"module weights are on {self.w_q.device}, input on {x.device}; call .to(device)")
         return self._dev
 
+    def _packed_bf16(self, x: Tensor) -> dict:
+        """bf16 copies of W_qkv and W_o for the tensor-core prefill, made on
+        first use and kept with the fp32 packs."""
+        p = self._packed(x)
+        if "w_qkv_bf16" not in p:
+            if self.head_dim != TC_HEAD_DIM:
+                raise ValueError(f"the tensor-core chunkwise prefill needs head_dim {TC_HEAD_DIM} "
+                                 f"(d_model {self.d_model}, {self.num_heads} heads); use forward_parallel on "
+                                 "fp32 inputs for the exact path")
+            from .. import cuda_ops
+
+            p["w_qkv_bf16"] = cuda_ops.to_bf16(p["w_qkv"])
+            p["w_o_bf16"] = cuda_ops.to_bf16(p["w_o"].contiguous())
+        return p
+
     def init_state(self, batch: int, device=None) -> Tensor:
         """Zero recurrent state [batch, H, dh, dh] fp32 (AceEngine.reset_memory,
         aceflow-core/src/cpu/mod.rs:115-117)."""
@@ -80,9 +114,15 @@ class MultiScaleRetention(Module):
         return Tensor.zeros([batch, self.num_heads, self.head_dim, self.head_dim], dev)
 
     # ------------------------------------------------------------ forward
+    def _use_tensor_cores(self, x: Tensor) -> bool:
+        return x.dtype == "bfloat16" or (self.prefill_dtype == "bfloat16" and self.head_dim == TC_HEAD_DIM)
+
     def forward_parallel(self, x: Tensor) -> Tensor:
         if x.device.is_cuda:
-            out, _ = self.forward_chunkwise(x)
+            if self._use_tensor_cores(x):
+                out, _ = self._prefill_tensor_cores(x, DEFAULT_CHUNK, None, want_state=False)
+            else:
+                out, _ = self._prefill_exact(x, None)
             return out
         arr = x.numpy()
         b, n, d = arr.shape
@@ -103,25 +143,56 @@ class MultiScaleRetention(Module):
     def forward(self, x: Tensor) -> Tensor:
         return self.forward_parallel(x)
 
-    def forward_chunkwise(self, x: Tensor, chunk: int = 64,
+    def forward_chunkwise(self, x: Tensor, chunk: int = DEFAULT_CHUNK,
                           state: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
-        """Prefill x [B, T, d] from `state` (zeros if None); returns the layer
-        output and the state after the last token."""
+        """Prefill x [B, T, d] from `state` (zeros if None) in chunks of
+        `chunk` tokens; returns the layer output and the state after the last
+        token.  On CUDA this is the tcgen05 chunkwise kernel (bf16 operands,
+        fp32 accumulation and state; head_dim 256); on CPU the recurrence."""
         B, T, d = x.shape
-        if state is None:
-            state = self.init_state(B, x.device)
         if not x.device.is_cuda:
+            if state is None:
+                state = self.init_state(B, x.device)
             outs = []
             for t in range(T):
                 o, state = self.forward_recurrent(Tensor(x.numpy()[:, t]), state)
                 outs.append(o.numpy())
             return Tensor(np.stack(outs, 1), x.device), state
+        return self._prefill_tensor_cores(x, chunk, state, want_state=True)
+
+    def _prefill_tensor_cores(self, x: Tensor, chunk: int, state: Optional[Tensor],
+                              want_state: bool) -> Tuple[Tensor, Optional[Tensor]]:
+        """af_msr_prefill_bf16 on x [B, T, d] (bf16, or fp32 cast to bf16 on
+        the device); output in x's dtype, final state fp32."""
+        import torch
+
         from .. import cuda_ops
 
+        p = self._packed_bf16(x)
+        xt = x.torch.contiguous()
+        xb = xt if xt.dtype == torch.bfloat16 else cuda_ops.to_bf16(xt)
+        st_in = None
+        if state is not None:
+            st_in = state.torch
+            if st_in.dtype != torch.float32 or not st_in.is_contiguous() or st_in.device != xt.device:
+                raise ValueError("state must be a contiguous fp32 tensor on the input's device")
+        out, st = cuda_ops.msr_prefill_bf16(xb, p["w_qkv_bf16"], p["w_o_bf16"], self.ret_norm.weight.torch,
+                                            p["gamma"], self.ret_norm.eps, state_in=st_in, out_dtype=xt.dtype,
+                                            want_state=want_state, chunk=chunk)
+        return Tensor._wrap(out, x.device), (Tensor._wrap(st, x.device) if st is not None else None)
+
+    def _prefill_exact(self, x: Tensor, state: Optional[Tensor]) -> Tuple[Tensor, Tensor]:
+        """The fp32 path: QKV GEMM (3xTF32), the recurrence token by token
+        (af_retention_scan, as AceEngine.prefill_recurrent), RMSNorm, W_o GEMM."""
+        from .. import cuda_ops
+
+        B, T, d = x.shape
+        if x.dtype != "float32":
+            raise ValueError("the exact prefill takes fp32 inputs")
+        if state is None:
+            state = self.init_state(B, x.device)
         p = self._packed(x)
         st = state.torch
-        if x.torch.dtype != st.dtype:
-            raise ValueError("bfloat16 prefill is served by the tensor-core chunkwise kernel")
         qkv = cuda_ops.linear(x.torch.reshape(B * T, d), p["w_qkv"]).reshape(B, T, 3 * d)
         o = cuda_ops.retention_scan(st, p["gamma"], qkv[:, :, :d], qkv[:, :, d:2 * d], qkv[:, :, 2 * d:])
         normed = cuda_ops.rms_norm(o, self.ret_norm.weight.torch, self.ret_norm.eps)

@@ -34,7 +34,7 @@ sys.path.insert(0, ROOT)
 
 D_MODEL, HEADS, STREAMS = 2048, 8, 256
 # DRAM bytes (read + write) of one state-stream launch at this workload,
-# measured with ncu (profiles/retention_step_kernel_decode_b256_d2048.md)
+# measured with ncu (dram__bytes_read.sum + dram__bytes_write.sum)
 STATE_KERNEL_TRAFFIC = 555.808e6 + 483.676e6
 EPS = 1e-6
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
@@ -125,6 +125,61 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
+# ---------------------------------------------------------------- checker
+def msr_rows_reference(x, w_qkv, w_o, ret_w, num_heads, eps, row_sets, col_range=None):
+    """Rows of the MultiScaleRetention forward (aceflow/nn/retention.py:44-66:
+    parallel retention, RMSNorm over d_model, W_o) for ONE stream, in float64
+    on x's device, used as the parity checker of the large workloads.
+
+    x [T, d] (any float dtype: the values the kernels read), w_qkv [3d, d]
+    (rows q | k | v), w_o [d, d], ret_w [d]; row_sets: (r0, r1) ranges of
+    output rows; col_range (c0, c1): only those output columns (the W_o rows a
+    head-sharded rank owns).  The state before row r0 is formed in one
+    product, S = K[:r0]^T diag(gamma^(r0-1-t)) V[:r0], so the cost does not
+    grow with the number of chunks.  Returns one [r1 - r0, cols] tensor per set."""
+    import torch
+
+    f64 = torch.float64
+    T, d = x.shape
+    H, dh = num_heads, x.shape[1] // num_heads
+    dev = x.device
+    Wq, Wk, Wv = (w.to(f64) for w in w_qkv.chunk(3))
+    Wo = w_o.to(f64)
+    if col_range is not None:
+        Wo = Wo[col_range[0]:col_range[1]]
+    need = max(r1 for _, r1 in row_sets)
+    x64 = x[:need].to(f64)
+    K, V = x64 @ Wk.T, x64 @ Wv.T
+    rw = ret_w.to(f64)
+    outs = []
+    for r0, r1 in row_sets:
+        q = x64[r0:r1] @ Wq.T
+        R = r1 - r0
+        i = torch.arange(R, device=dev, dtype=f64)
+        dist = i[:, None] - i[None, :]
+        o = torch.empty(R, d, dtype=f64, device=dev)
+        for h in range(H):
+            g = 1.0 - 2.0 ** (-5 - h)
+            sl = slice(h * dh, (h + 1) * dh)
+            inter = torch.zeros(R, dh, dtype=f64, device=dev)
+            if r0 > 0:
+                w = g ** (r0 - 1 - torch.arange(r0, device=dev, dtype=f64))
+                S = (K[:r0, sl] * w[:, None]).T @ V[:r0, sl]
+                inter = (g ** (i + 1))[:, None] * (q[:, sl] @ S)
+            D = torch.where(dist >= 0, g ** dist.clamp(min=0), torch.zeros((), dtype=f64, device=dev))
+            o[:, sl] = inter + ((q[:, sl] @ K[r0:r1, sl].T) * D) @ V[r0:r1, sl]
+        o = o / torch.sqrt((o * o).mean(-1, keepdim=True) + eps) * rw
+        outs.append(o @ Wo.T)
+    return outs
+
+
+def max_rel_err(got_sets, ref_sets) -> float:
+    """max |got - ref| / max |ref| over all sets (the parity metric)."""
+    num = max(float((g.double() - r).abs().max()) for g, r in zip(got_sets, ref_sets))
+    den = max(float(r.abs().max()) for r in ref_sets)
+    return num / max(den, 1e-30)
+
+
 # ---------------------------------------------------------------- CPU legs
 def cpu_decode_sample(seconds: float, nthreads: int, seed: int = 0):
     """Times the C restatement of the reference CPU path (oracle/cpu_ref.c,
@@ -152,6 +207,82 @@ def cpu_decode_sample(seconds: float, nthreads: int, seed: int = 0):
         if el >= seconds:
             break
     return B * steps / el, steps, B, el
+
+
+def cpu_prefill_sample(seconds: float, nthreads: int, d: int, H: int, streams: int, piece: int = 8, seed: int = 0):
+    """The reference's only CPU prefill, the token-serial recurrence
+    (AceEngine.prefill_recurrent, cpu/mod.rs:547-587, per token the whole
+    layer as its decode step: gemv_avx2 QKV, retention_step_core,
+    rmsnorm_core, gemv_avx2 W_o), in the C restatement (oracle/cpu_ref.c,
+    OpenMP over streams), on `min(streams, nthreads)` streams and successive
+    `piece`-token slices until `seconds` elapse.  Its cost per token does not
+    depend on the position, so tokens/s of this prefix is the rate of the
+    whole prompt.  Returns (tok/s, tokens, streams, seconds, threads)."""
+    from oracle import cpu_ref
+
+    rng = np.random.default_rng(seed)
+    dh = d // H
+    B = max(1, min(streams, nthreads))
+    w_qkv = (0.02 * rng.standard_normal((3 * d, d))).astype(np.float32)
+    w_o = (0.02 * rng.standard_normal((d, d))).astype(np.float32)
+    ret_w = np.ones(d, np.float32)
+    gamma = np.array([1.0 - 2.0 ** (-5.0 - h) for h in range(H)], np.float32)
+    state = np.zeros((B, H, dh, dh), np.float32)
+    x = rng.standard_normal((B, piece, d)).astype(np.float32)
+    threads = min(nthreads, B)
+    cpu_ref.msr_prefill_recurrent(x[:, :1].copy(), state, gamma, w_qkv, w_o, ret_w, EPS, threads)  # warm
+    toks, t0 = 0, time.perf_counter()
+    while True:
+        cpu_ref.msr_prefill_recurrent(x, state, gamma, w_qkv, w_o, ret_w, EPS, threads)
+        toks += B * piece
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return toks / el, toks, B, el, threads
+
+
+def cpu_stack_sample(seconds: float, nthreads: int, c: dict, sample_layers: int = 2, seed: int = 0):
+    """Greedy decode of the decoder stack on the host (AceEngine.
+    generate_stream_internal, cpu/mod.rs:708-769, in the C restatement
+    oracle/cpu_ref.c: per token every layer's forward_layer_internal and the
+    tied LM head), one stream per thread, on a model of `sample_layers`
+    layers with the workload's other sizes.  The per-token cost is the
+    memory traffic of fp32 weights, state and LM head, so the 24-layer rate is
+    the sample's rate times bytes(sample) / bytes(24 layers).  Returns
+    (tok/s at the full depth, sample tok/s, streams, seconds, description)."""
+    from oracle import cpu_ref
+
+    rng = np.random.default_rng(seed)
+    d, H, f, V, L = c["d"], c["H"], c["f"], c["V"], c["L"]
+    dh = d // H
+    one = np.ones(d, np.float32)
+    layers = [dict(w_qkv=(0.02 * rng.standard_normal((3 * d, d))).astype(np.float32),
+                   w_o=(0.02 * rng.standard_normal((d, d))).astype(np.float32),
+                   w_gate_up=(0.02 * rng.standard_normal((2 * f, d))).astype(np.float32),
+                   w_down=(0.02 * rng.standard_normal((d, f))).astype(np.float32),
+                   norm1=one, norm2=one, ret_norm=one) for _ in range(sample_layers)]
+    emb = (0.02 * rng.standard_normal((V, d))).astype(np.float32)
+    B = max(1, min(nthreads, c["B"]))
+    prompts = rng.integers(0, V, (B, 1)).astype(np.int32)
+    cpu_ref.generate_greedy(layers, emb, prompts, 1, H, 1e-6, nthreads=nthreads)  # warm
+    n, el = 2, 0.0
+    while True:
+        t0 = time.perf_counter()
+        cpu_ref.generate_greedy(layers, emb, prompts, n, H, 1e-6, nthreads=nthreads)
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 64:
+            break
+        n *= 2
+    sample_rate = B * (n + 1) / el  # prompt token + n generated tokens per stream
+
+    def token_bytes(nl):
+        return 4 * (nl * (4 * d * d + 3 * f * d) + V * d) + 2 * 4 * nl * H * dh * dh
+
+    rate = sample_rate * token_bytes(sample_layers) / token_bytes(L)
+    desc = (f"{B} streams (one per thread) x {n + 1} tokens of a {sample_layers}-layer model with the workload's "
+            f"sizes in {el:.1f} s, scaled to {L} layers by fp32 bytes per token "
+            f"({token_bytes(sample_layers) / 1e9:.2f} -> {token_bytes(L) / 1e9:.2f} GB)")
+    return rate, sample_rate, B, el, desc
 
 
 def host_threads() -> int:
@@ -239,7 +370,7 @@ def run_ours(args):
             return float(t.item())
 
         if args.only == "prefill":
-            sec = bench_prefill(dev, args.prefill_passes, peaks)
+            sec = bench_prefill(dev, args.prefill_passes, peaks, 0.0, args.chunk)
         elif args.only == "longctx":
             sec = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier1, max1)
         else:
@@ -283,23 +414,58 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def per_rank(v):
+        """Every rank's value (for the spread), gathered to all ranks."""
+        if world == 1:
+            return [v]
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        return [float(p.item()) for p in parts]
+
     clocks = ClockSampler(local)
     with clocks:
         for i in range(args.warmup):
             step(i)
         torch.cuda.synchronize()
+        # The K timed steps are captured once into a CUDA graph and replayed
+        # as one launch: the device runs them back to back, whatever the host
+        # (with 8 ranks, 8 Python processes plus NCCL proxy threads) does
+        # meanwhile.  The same K steps issued eagerly are timed as well.
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        launches0 = _lib.launch_count(local)
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(args.steps):
+                step(args.warmup + i)
+        launches = _lib.launch_count(local) - launches0  # this library's kernels in one replay
+        stream.wait_stream(cap)
+        graph.replay()  # untimed first replay
+        torch.cuda.synchronize()
         barrier()
         torch.cuda.synchronize()
-        launches0 = _lib.launch_count(local)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        my_ms = e0.elapsed_time(e1)
+        ms_all = per_rank(my_ms)
+        ms_total = max(ms_all)
+        # eager: the same K steps launched one by one from Python
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
         e0.record(stream)
         for i in range(args.steps):
             step(args.warmup + i)
         e1.record(stream)
         torch.cuda.synchronize()
-        launches = _lib.launch_count(local) - launches0
         barrier()
-        ms_total = max_over_ranks(e0.elapsed_time(e1))
+        eager_all = per_rank(e0.elapsed_time(e1))
+        del graph
 
         # dominant kernel alone (the fp32 state stream), CUDA events on its stream
         qkv = torch.randn(B, 3 * d, generator=g, device=dev)
@@ -315,8 +481,8 @@ def run_ours(args):
         kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
 
         # end to end through the public API with host buffers
-        e2e_ms = run_e2e(args, dev, state, gamma, w_qkv_s, w_o_s, ret_w, cuda_ops, barrier)
-        e2e_ms = max_over_ranks(e2e_ms)
+        e2e_all = per_rank(run_e2e(args, dev, state, gamma, w_qkv_s, w_o_s, ret_w, cuda_ops, barrier))
+        e2e_ms = max(e2e_all)
 
     ms_step = ms_total / args.steps
     value = world * B * args.steps / (ms_total / 1e3)
@@ -336,8 +502,7 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "kernel": "retention_step_kernel<256,256>", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                      "peak_source": peak_kind, "traffic": STATE_KERNEL_TRAFFIC,
-                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, "
-                                       "profiles/retention_step_kernel_decode_b256_d2048.md",
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch at this workload",
                      "kernel_ms": kernel_ms,
                      "algorithmic_bytes_per_launch": kbytes,
                      "step_bytes": step_bytes,
@@ -346,14 +511,21 @@ def run_ours(args):
                 "h2d_bytes_per_step": B * d * 4, "d2h_bytes_per_step": B * d * 4,
                 "ms_per_step": e2e_ms / args.steps},
         "gpu_launches": int(launches),
+        "timing": {"timed_region": "one CUDA-graph replay of the K steps (captured before timing)",
+                   "eager_ms_per_step": max(eager_all) / args.steps,
+                   "per_rank_ms_per_step": {"graph": [v / args.steps for v in ms_all],
+                                            "eager": [v / args.steps for v in eager_all],
+                                            "e2e": [v / args.steps for v in e2e_all]}},
         "clocks": clocks.summary(),
     }
+    sub_cpu = args.sub_cpu_seconds if (world == 1 and not args.no_cpu) else 0.0
     if world == 1 and not args.no_prefill:
-        line["prefill"] = bench_prefill(dev, args.prefill_passes, peaks)
+        line["prefill"] = bench_prefill(dev, args.prefill_passes, peaks, sub_cpu, args.chunk)
     if not args.no_longctx and HEADS_LONGCTX % world == 0:
-        line["longctx"] = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier, max_over_ranks)
+        line["longctx"] = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier, max_over_ranks,
+                                        sub_cpu)
     if world == 1 and not args.no_stack:
-        line["stack"] = bench_stack(dev, peaks)
+        line["stack"] = bench_stack(dev, peaks, sub_cpu)
     if world == 1 and rank == 0 and not args.no_cpu:
         nthreads = host_threads()
         v, steps, b, el = cpu_decode_sample(args.cpu_seconds, nthreads)
@@ -435,58 +607,99 @@ def prefill_flops(B, T, d, H, C):
     return proj, intra, inter
 
 
-def bench_prefill(dev, passes, peaks):
+def _phase_times(dev, fn):
+    """Runs fn() once with the library's phase marks on; [(phase, ms)]."""
+    from aceflow_b200 import _lib
+
+    idx = dev.index or 0
+    _lib.set_option(idx, "phase_marks", 1)
+    try:
+        fn()
+        return [(n, round(ms, 4)) for n, ms in _lib.phase_times(idx)]
+    finally:
+        _lib.set_option(idx, "phase_marks", 0)
+
+
+def bench_prefill(dev, passes, peaks, cpu_seconds=0.0, chunk=64):
+    """The prefill workload through the reference's module API:
+    af.nn.MultiScaleRetention(2048, 8).to("cuda:0") called on a bf16 prompt
+    (the tensor-core chunkwise prefill), bf16 output."""
     import torch
 
+    import aceflow_b200 as af
     from aceflow_b200 import _lib, cuda_ops
 
     c = PREFILL
     B, T, d, H = c["B"], c["T"], c["d"], c["H"]
     g = torch.Generator(device=dev).manual_seed(7)
     x = torch.randn(B, T, d, generator=g, device=dev).bfloat16()
-    w_qkv = (0.02 * torch.randn(3 * d, d, generator=g, device=dev)).bfloat16()
-    w_o = (0.02 * torch.randn(d, d, generator=g, device=dev)).bfloat16()
-    rw = torch.ones(d, device=dev)
-    gamma = cuda_ops.gammas(H, dev)
+    ws = [(0.02 * torch.randn(d, d, generator=g, device=dev)).bfloat16() for _ in range(4)]
+    m = af.nn.MultiScaleRetention(d, H)
+    for name, w in zip(("w_q", "w_k", "w_v", "w_o"), ws):
+        setattr(m, name, af.nn.Parameter(af.Tensor(w.float())))
+    m.to(str(dev))
+    xt = af.Tensor(x, device=str(dev), dtype="bfloat16")
+
+    def run():
+        return m.forward_chunkwise(xt, chunk=chunk)[0] if chunk != 64 else m(xt)
+
     out = None
     for _ in range(3):
-        out, _st = cuda_ops.msr_prefill_bf16(x, w_qkv, w_o, rw, gamma, EPS, want_state=False)
+        out = run()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(passes):
-        out, _st = cuda_ops.msr_prefill_bf16(x, w_qkv, w_o, rw, gamma, EPS, want_state=False)
+        out = run()
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / passes
+    phases = _phase_times(dev, run)
+    # parity: stream 0's first and last 128 rows against float64
+    w_qkv = torch.cat(ws[:3]).contiguous()
+    rows = [(0, 128), (T - 128, T)]
+    ref = msr_rows_reference(x[0], w_qkv, ws[3], torch.ones(d, device=dev), H, EPS, rows)
+    err = max_rel_err([out.torch[0, r0:r1] for r0, r1 in rows], ref)
     # the retention core alone (chunkwise kernel), CUDA events on its stream
     qkv = torch.randn(B * T, 3 * d, generator=g, device=dev).bfloat16()
+    rw = torch.ones(d, device=dev)
+    gamma = cuda_ops.gammas(H, dev)
     for _ in range(2):
-        cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False)
+        cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False, chunk=chunk)
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     for _ in range(passes):
-        cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False)
+        cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False, chunk=chunk)
     e3.record(stream)
     torch.cuda.synchronize()
     core_ms = e2.elapsed_time(e3) / passes
     _lib.check_device(dev.index or 0)
-    proj, intra, inter = prefill_flops(B, T, d, H, c["C"])
+    proj, intra, inter = prefill_flops(B, T, d, H, chunk)
     total = proj + intra + inter
     tfl = total / (ms / 1e3) / 1e12
     core_tfl = (intra + inter) / (core_ms / 1e3) / 1e12
-    return {
+    res = {
         "metric": "retention prefill tok/s (B=8,T=4096,d=2048)", "value": B * T / (ms / 1e3), "unit": "tok/s",
         "ms_per_pass": ms, "passes": passes, "dtype": "bf16 (fp32 accumulate)",
-        "config": {"workload": "MultiScaleRetention prefill, d_model=2048, 8 heads, B=8, T=4096, chunk 64",
+        "config": {"workload": f"MultiScaleRetention prefill, d_model=2048, 8 heads, B=8, T=4096, chunk {chunk}",
+                   "api": "af.nn.MultiScaleRetention(2048, 8).to('cuda') on a bf16 prompt",
                    "l2": "inputs larger than L2 (x 128 MiB, qkv 384 MiB)"},
+        "max_rel_err": err, "tolerance": 2e-2,
+        "parity_rows": "stream 0, rows 0-127 and 3968-4095, against float64",
+        "phases_ms": phases,
         "roofline": {"bound": "tensor", "achieved": tfl, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": tfl / peaks["bf16_tflops"], "algorithmic_flop": total},
         "retention_core": {"kernel": "retention_chunkwise_kernel", "ms": core_ms, "achieved": core_tfl,
                            "unit": "TFLOP/s", "frac": core_tfl / peaks["bf16_tflops"],
                            "algorithmic_flop": intra + inter},
     }
+    if cpu_seconds > 0:
+        v, toks, b, el, thr = cpu_prefill_sample(cpu_seconds, host_threads(), d, H, B)
+        res["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": thr, "kind": "port",
+                               "sample": f"{toks} tokens ({b} streams x {toks // b}) of the token-serial prefill "
+                                         f"(AceEngine.prefill_recurrent, C restatement) in {el:.1f} s"}
+    return res
 
 
 # ---------------------------------------------------------------- long context
@@ -494,15 +707,18 @@ LONGCTX = dict(B=1, T=65536, d=4096, H=16, C=64)
 HEADS_LONGCTX = LONGCTX["H"]
 
 
-def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks):
+def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_seconds=0.0):
     """Head-sharded prefill of one 65536-token stream (d_model 4096, 16 heads)
     over all ranks: QKV of the rank's heads, chunkwise retention (sequence
-    segments), NCCL all-gather of head outputs, output projection of the
-    rank's columns.  Total work is fixed, so N GPUs scale it strongly."""
+    segments), the exchange of head outputs, output projection.  Two
+    exchanges: the all-gather the workload names (each rank then owns output
+    columns) and the all-to-all (each rank owns output rows; 8x fewer bytes
+    over NVLink at 8 GPUs).  Total work is fixed, so N GPUs scale it
+    strongly.  Rank 0 checks its share of three row blocks against float64."""
     import torch
 
     from aceflow_b200 import _lib
-    from aceflow_b200.sharded import HeadShardedPrefill, chunkwise_plan
+    from aceflow_b200.sharded import HeadShardedPrefill, chunkwise_plan, row_range
 
     c = LONGCTX
     B, T, d, H = c["B"], c["T"], c["d"], c["H"]
@@ -511,50 +727,89 @@ def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks):
     w_qkv = (0.02 * torch.randn(3 * d, d, generator=g, device=dev)).bfloat16()
     w_o = (0.02 * torch.randn(d, d, generator=g, device=dev)).bfloat16()
     rw = torch.ones(d, device=dev)
-    sp = HeadShardedPrefill(w_qkv, w_o, rw, H, EPS)
-    del w_qkv
-    out = torch.empty(B, T, d // world, device=dev)
-    for _ in range(2):
-        sp(x, out=out)
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(passes):
-        sp(x, out=out)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1) / passes)
-    _lib.check_device(dev.index or 0)
-    barrier()
-    sp.close()
+    check_rows = [(0, 128), (T // 2 - 64, T // 2 + 64), (T - 128, T)]
     proj, intra, inter = prefill_flops(B, T, d, H, c["C"])
     total = proj + intra + inter
-    per_gpu_tfl = total / world / (ms / 1e3) / 1e12
+    res = {}
+    for layout in ("columns", "rows"):
+        sp = HeadShardedPrefill(w_qkv, w_o, rw, H, EPS, layout=layout)
+        if layout == "columns":
+            out = torch.empty(B, T, d // world, device=dev)
+        else:
+            out = torch.empty(row_range(B * T, world, rank)[1], d, device=dev)
+        for _ in range(2):
+            sp(x, out=out)
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(passes):
+            sp(x, out=out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = max_over_ranks(e0.elapsed_time(e1) / passes)
+        barrier()
+        phases = _phase_times(dev, lambda: sp(x, out=out))
+        _lib.check_device(dev.index or 0)
+        barrier()
+        sp.close()
+        err = None
+        if rank == 0:  # rank 0's share of three row blocks against float64
+            if layout == "columns":
+                dl = d // world
+                ref = msr_rows_reference(x[0], w_qkv, w_o, rw, H, EPS, check_rows, col_range=(0, dl))
+                got = [out[0, r0:r1] for r0, r1 in check_rows]
+            else:
+                lo, n = row_range(B * T, world, 0)
+                rows0 = [(lo, lo + 128), (lo + n - 128, lo + n)]  # the ends of rank 0's rows
+                ref = msr_rows_reference(x[0], w_qkv, w_o, rw, H, EPS, rows0)
+                got = [out[r0 - lo:r1 - lo] for r0, r1 in rows0]
+            err = max_rel_err(got, ref)
+            del ref
+        barrier()
+        per_gpu_tfl = total / world / (ms / 1e3) / 1e12
+        res[layout] = {"ms_per_pass": ms, "value": B * T / (ms / 1e3), "phases_ms_rank0": phases,
+                       "max_rel_err_rank0": err, "frac_per_gpu": per_gpu_tfl / peaks["bf16_tflops"],
+                       "achieved_per_gpu": per_gpu_tfl}
     nseg, seg_len = chunkwise_plan(torch.cuda.get_device_properties(dev).multi_processor_count, B, T, H // world)
     gather_bytes = (world - 1) * B * T * (d // world) * 2  # bf16 head outputs received per rank
-    return {
+    a2a_bytes = (world - 1) * (-(-B * T // world)) * (d // world) * 2
+    col = res["columns"]
+    line = {
         "metric": "long-context head-sharded prefill tok/s (B=1,T=65536,d=4096,H=16)",
-        "value": B * T / (ms / 1e3), "unit": "tok/s", "ms_per_pass": ms, "passes": passes, "n_gpus": world,
-        "scaling": "strong", "dtype": "bf16 (fp32 accumulate)",
+        "value": col["value"], "unit": "tok/s", "ms_per_pass": col["ms_per_pass"], "passes": passes,
+        "n_gpus": world, "scaling": "strong", "dtype": "bf16 (fp32 accumulate)",
         "config": {"workload": "MultiScaleRetention prefill, d_model=4096, 16 heads (head_dim 256), B=1, T=65536, "
-                               "chunk 64", "parallelism": f"head-sharded x{world}, {H // world} heads per GPU, "
-                                                          "one NCCL all-gather before W_o",
+                               f"chunk {c['C']}", "parallelism": f"head-sharded x{world}, {H // world} heads per GPU, "
+                                                             "one NCCL all-gather before W_o",
                    "segments": {"nseg": nseg, "seg_len": seg_len},
                    "l2": "inputs larger than L2 (x 512 MiB, qkv per GPU >= 192 MiB)"},
-        "roofline": {"bound": "tensor", "achieved": per_gpu_tfl, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "per": "GPU", "frac": per_gpu_tfl / peaks["bf16_tflops"], "algorithmic_flop": total,
+        "max_rel_err": col["max_rel_err_rank0"], "tolerance": 2e-2,
+        "parity_rows_alltoall": "the first and last 128 of rank 0's own rows against float64",
+        "parity_rows": "rank 0's output share of rows 0-127, 32704-32831, 65408-65535 against float64",
+        "phases_ms_rank0": col["phases_ms_rank0"],
+        "roofline": {"bound": "tensor", "achieved": col["achieved_per_gpu"], "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "per": "GPU", "frac": col["frac_per_gpu"], "algorithmic_flop": total,
                      "allgather_bytes_per_rank": gather_bytes},
+        "alltoall": {"parallelism": f"head-sharded x{world}; NCCL all-to-all of head outputs, each rank owns "
+                                    f"{-(-B * T // world)} output rows and applies the full W_o",
+                     "bytes_received_per_rank": a2a_bytes, **res["rows"]},
     }
+    if cpu_seconds > 0 and rank == 0 and world == 1:
+        v, toks, b, el, thr = cpu_prefill_sample(cpu_seconds, 1, d, H, B)
+        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": thr, "kind": "port",
+                                "sample": f"{toks} tokens of the one stream, token-serial (AceEngine.prefill_recurrent, "
+                                          f"C restatement; one stream runs on one thread) in {el:.1f} s"}
+    return line
 
 
 # ---------------------------------------------------------------- stack
 STACK = dict(L=24, d=2048, H=8, f=5632, V=32000, B=64, P=512, n=256)
 
 
-def bench_stack(dev, peaks):
+def bench_stack(dev, peaks, cpu_seconds=0.0):
     import torch
 
     from aceflow_b200 import _lib
@@ -579,7 +834,7 @@ def bench_stack(dev, peaks):
     pre_flop = 2 * params * B * P + L * sum(prefill_flops(B, P, d, H, 64)[1:])
     dec_bytes = 2 * params + 2 * L * B * H * (d // H) ** 2 * 4
     dec_ms = t["decode_ms"] / t["decode_steps"]
-    return {
+    res = {
         "metric": "24-layer retention decoder: prefill and greedy decode tok/s",
         "config": {"workload": "24 x [RMSNorm -> MSR -> RMSNorm -> SwiGLU(5632)], d_model=2048, 8 heads, "
                                "vocab 32000 tied, bf16 weights, batch 64, 512-token prompt, 256 greedy steps",
@@ -593,6 +848,11 @@ def bench_stack(dev, peaks):
         "decode_bytes_per_step": dec_bytes, "first_token_ms": t["first_token_ms"],
         "tokens_checksum": int(np.asarray(toks, np.int64).sum()),
     }
+    if cpu_seconds > 0:
+        rate, sample_rate, b, el, desc = cpu_stack_sample(cpu_seconds, host_threads(), c)
+        res["cpu_baseline"] = {"value": rate, "unit": "tok/s (decode)", "cores": b, "kind": "port",
+                               "sample": desc, "sample_value": sample_rate}
+    return res
 
 
 def main():
@@ -610,6 +870,9 @@ def main():
     ap.add_argument("--only", choices=["prefill", "longctx", "stack"], default=None,
                     help="run one secondary workload alone and print its object (profiling)")
     ap.add_argument("--longctx-passes", type=int, default=5)
+    ap.add_argument("--sub-cpu-seconds", type=float, default=4.0,
+                    help="seconds of each CPU baseline of the prefill, long-context and stack workloads (N=1)")
+    ap.add_argument("--chunk", type=int, default=64, help="chunk length of the prefill workload")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -5,7 +5,7 @@
  * Linear / RMSNorm / SwiGLU, af.ops and AceEngine APIs.  Each entry point
  * names the reference interface it replaces (paths relative to the
  * 42Wor/aceflow checkout).  A Rust `extern "C"` block, a PyO3 method or a
- * Python ctypes stub binds these symbols directly (INTEGRATION.md).
+ * Python ctypes stub binds these symbols directly.
  *
  * Conventions
  *  - Every pointer argument except `af_ctx*` and host-side parameters is a
@@ -57,8 +57,18 @@ int af_reserve_workspace(af_ctx *ctx, size_t bytes);
 /* Synchronises the device and reads the context's device error word: a
  * kernel whose bounded wait gave up sets bit AF_ERR_TIMEOUT instead of
  * hanging.  Returns AF_ERR_TIMEOUT if set; `flags` (may be NULL) receives the
- * word; `reset` clears it. */
+ * word; `reset` clears it.  ctx == NULL reads (and with `reset` clears) the
+ * error word of af_msr_decode_step_f32_noalloc on the current device, which
+ * takes no context. */
 int af_check_device(af_ctx *ctx, int *flags, int reset);
+/* Runs the bounded-wait error path on purpose, with no fault: one thread
+ * waits (the kernels' own mbarrier wait, limit `limit_ns`, 1 us .. 2 s) on a
+ * barrier phase nothing completes, gives up and sets AF_ERR_TIMEOUT in the
+ * context's error word (ctx == NULL: the word of
+ * af_msr_decode_step_f32_noalloc on the current device), which
+ * af_check_device then reports.  No reference counterpart: the reference's
+ * failures are host-side PyValueErrors (aceflow-core/src/cpu/mod.rs:188-238). */
+int af_selftest_bounded_wait(af_ctx *ctx, int64_t limit_ns, af_stream_t stream);
 /* Tuning switches of a context (no reference counterpart):
  *   "decode_head_groups" 1..8  head groups pipelined by the split decode step (default 1)
  *   "allow_split_k"      0/1   small-M GEMMs may split K with fp32 atomics (default 1;
@@ -74,8 +84,17 @@ int af_check_device(af_ctx *ctx, int *flags, int reset);
  *   "pdl"                0/1   decode chains as programmatic dependent launches (default 1)
  *   "gemm_pair"          0/1   large bf16 GEMMs on CTA pairs, 256 x 256 tiles (default 1)
  *   "decode_pairs"       0/1   the decode step's projections on CTA pairs (default 1)
- *   "gemm_producers"     1..4  TMA producer threads per tensor-core GEMM CTA (default 1) */
+ *   "gemm_producers"     1..4  TMA producer threads per tensor-core GEMM CTA (default 1)
+ *   "phase_marks"        0/1   record timing events at the prefill phases (af_phase_times) */
 int af_set_option(af_ctx *ctx, const char *name, int64_t value);
+/* Phase times of the last prefill call made with af_set_option "phase_marks"
+ * on (af_msr_prefill_bf16, af_retention_chunkwise_bf16,
+ * af_prefill_head_sharded[_rows]): the device time between consecutive phase
+ * boundaries on the caller's stream, e.g. "qkv", "chunk_state",
+ * "chunk_scan", "chunkwise", "allgather"/"alltoall", "w_o".  Waits for the
+ * last boundary.  Fills up to `max` entries; `n` receives the count (0 when
+ * marks are off).  No reference counterpart (measurement). */
+int af_phase_times(af_ctx *ctx, float *ms, const char **names, int max, int *n);
 /* Number of this library's kernel launches issued through `ctx` so far. */
 int af_launch_count(af_ctx *ctx, int64_t *count);
 
@@ -214,17 +233,22 @@ int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *state, cons
                                  const float *w_o_lo, const float *ret_norm_w, float eps, int batch,
                                  int d_model, int num_heads, float *out, af_stream_t stream);
 
-/* The same decode step for callers that cannot allocate device memory at
- * call time (inside a CUDA-graph capture, or in a process whose device
- * memory belongs to its own arena allocator).  No reference counterpart: the
- * reference's CPU engine preallocates its host buffers in AceEngine::new.
- * Scratch comes from a fixed 16 MiB array inside the library (2^22 floats;
- * the step needs batch*(4*d_model + num_heads) of them, e.g. batch <= 511 at
- * d_model 2048), so the call allocates nothing and takes no context; larger
- * sizes return AF_ERR_ARG.  The current device is used.  The first call on a
- * device looks up the array's address (and loads the library's kernels):
- * make it before any stream capture.  All calls on a device share the
- * array, so calls that overlap on the GPU (concurrent streams) race. */
+/* The same decode step for callers that cannot allocate device memory when
+ * they run it: a server whose device memory is carved up front by its own
+ * arena allocator, or a plugin inside a host that owns the device-memory
+ * budget.  No reference counterpart: the reference's CPU engine preallocates
+ * its host buffers in AceEngine::new.  Scratch comes from a fixed 16 MiB
+ * array inside the library (2^22 floats; the step needs
+ * batch*(4*d_model + num_heads) of them, i.e. batch <= 511 at d_model 2048),
+ * held on every GPU that loads the library until the process exits; larger
+ * sizes return AF_ERR_ARG.  The call allocates nothing and takes no context;
+ * the current device is used.  The first call on a device looks up the
+ * array's device address (and loads the library's kernels there): make it
+ * before any stream capture, and do not call the entry point again after
+ * cudaDeviceReset.  All calls on a device share the array and keep the last
+ * call's contents, so calls that overlap on the GPU (concurrent streams)
+ * race: at most one call in flight per device.  A bounded-wait timeout in its
+ * kernels is reported by af_check_device(NULL, ...). */
 int af_msr_decode_step_f32_noalloc(const float *x, float *state, const float *gamma,
                                    const float *w_qkv, const float *w_o, const float *ret_norm_w,
                                    float eps, int batch, int d_model, int num_heads, float *out,
@@ -381,6 +405,22 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
                             float eps, int batch, int T, int d_model, int num_heads,
                             const float *state_in, float *state_out, void *out, int out_bf16,
                             af_stream_t stream);
+
+/* The same layer, row-sharded: the exchange is an all-to-all (ncclSend /
+ * ncclRecv pairs) instead of the all-gather, so each rank receives only
+ * (g-1)/g^2 of the head outputs, and holds the complete rows
+ * [r*c, r*c + n_r) (c = ceil(batch*T / g)) on which it applies the RMSNorm
+ * and the FULL W_o.
+ *   w_qkv_local [3*dl][d] bf16 as above; w_o [d][d] bf16 (all of it);
+ *   out [n_r][d] fp32 (or bf16): rows r*c .. r*c + n_r - 1 of the layer
+ *   output [batch*T][d] (n_r = 0 on ranks past the last row).
+ * Every rank must make the same call.  head_dim 256; H divisible by the rank
+ * count.  Workspace batch*T*(6*dl + 2*dl/g + 8*H/g*(1 + 1/g)) bytes plus
+ * segment states. */
+int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv_local, const uint16_t *w_o,
+                                 const float *ret_norm_w, const float *gamma, float eps, int batch, int T,
+                                 int d_model, int num_heads, const float *state_in, float *state_out, void *out,
+                                 int out_bf16, af_stream_t stream);
 
 #ifdef __cplusplus
 }

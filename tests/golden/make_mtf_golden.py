@@ -49,4 +49,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} <path of the 42Wor/aceflow checkout>")
+    main(sys.argv[1])

@@ -216,3 +216,77 @@ def test_rmsnorm_to_bf16(dev, d, with_w):
     xd = x.double()
     ref = xd / torch.sqrt((xd * xd).mean(-1, keepdim=True) + 1e-6) * w.double() if with_w else xd
     assert rel_err(y.float().cpu().numpy(), ref.cpu().numpy()) < 8e-3
+
+
+def test_engine_retention_step_packed_and_prefill_recurrent(dev):
+    """AceEngine.retention_step / retention_step_packed / prefill_recurrent
+    (aceflow-core/src/cpu/mod.rs:486-587) against the oracle's
+    retention_step_core on the same per-layer state slice: the step's output,
+    the packed split q | k | v, prefill_recurrent returning only the last
+    token's output, the state left behind, and the reference's length and
+    layer-index errors."""
+    from aceflow_b200.engine import AceEngine
+
+    L, d, H = 2, 512, 2
+    dh = d // H
+    gamma = np.array([1 - 2.0 ** (-5 - h) for h in range(H)], np.float32)
+    rng = np.random.default_rng(17)
+    eng = AceEngine(L, d, H, batch=1)
+    states = np.zeros((L, H, dh, dh), np.float32)  # the reference's one-stream layout
+    # retention_step on layer 1 (1-D vectors, as the reference takes them)
+    q, k, v = (rng.standard_normal(d).astype(np.float32) for _ in range(3))
+    ref = cpu_ref.retention_step_core(states, gamma, 1, H, dh, q, k, v)
+    assert rel_err(eng.retention_step(1, q, k, v), ref) < 1e-5
+    # retention_step_packed continues the same state
+    qkv = rng.standard_normal(3 * d).astype(np.float32)
+    ref = cpu_ref.retention_step_core(states, gamma, 1, H, dh, qkv[:d].copy(), qkv[d:2 * d].copy(), qkv[2 * d:].copy())
+    got = eng.retention_step_packed(1, qkv)
+    assert got.shape == (d,) and rel_err(got, ref) < 1e-5
+    with pytest.raises(ValueError, match="Expected packed QKV vector of length"):
+        eng.retention_step_packed(1, qkv[:-1])
+    with pytest.raises(ValueError, match="Expected input vectors of length"):
+        eng.retention_step(0, q[:-1], k, v)
+    with pytest.raises(ValueError, match="out of range"):
+        eng.retention_step(2, q, k, v)
+    # prefill_recurrent on layer 0: flat [T*d] sequences, only the last output comes back
+    T = 37
+    qs, ks, vs = (rng.standard_normal(T * d).astype(np.float32) for _ in range(3))
+    for t in range(T):
+        last = cpu_ref.retention_step_core(states, gamma, 0, H, dh, qs[t * d:(t + 1) * d].copy(),
+                                           ks[t * d:(t + 1) * d].copy(), vs[t * d:(t + 1) * d].copy())
+    got = eng.prefill_recurrent(0, T, qs, ks, vs)
+    assert got.shape == (d,) and rel_err(got, last) < 1e-4
+    assert rel_err(eng.get_state()[:, 0], states) < 1e-5  # both layers' slices, layer 1 untouched by the prefill
+    with pytest.raises(ValueError, match="Expected sequence vectors of length"):
+        eng.prefill_recurrent(0, T, qs[:-d], ks, vs)
+    with pytest.raises(ValueError, match="out of range"):
+        eng.prefill_recurrent(5, T, qs, ks, vs)
+
+
+def test_engine_retention_step_batched_streams(dev):
+    """The batched engine (one state slice per stream) equals one oracle
+    state per stream."""
+    from aceflow_b200.engine import AceEngine
+
+    L, d, H, B = 1, 256, 4, 3
+    dh = d // H
+    gamma = np.array([1 - 2.0 ** (-5 - h) for h in range(H)], np.float32)
+    rng = np.random.default_rng(23)
+    eng = AceEngine(L, d, H, batch=B)
+    states = np.zeros((B, L, H, dh, dh), np.float32)
+    for _ in range(3):
+        q, k, v = (rng.standard_normal((B, d)).astype(np.float32) for _ in range(3))
+        ref = np.stack([cpu_ref.retention_step_core(states[b], gamma, 0, H, dh, q[b].copy(), k[b].copy(), v[b].copy())
+                        for b in range(B)])
+        assert rel_err(eng.retention_step(0, q, k, v), ref) < 1e-5
+    T = 9
+    qs, ks, vs = (rng.standard_normal((B, T * d)).astype(np.float32) for _ in range(3))
+    last = np.zeros((B, d), np.float32)
+    for b in range(B):
+        for t in range(T):
+            sl = slice(t * d, (t + 1) * d)
+            last[b] = cpu_ref.retention_step_core(states[b], gamma, 0, H, dh, qs[b, sl].copy(), ks[b, sl].copy(),
+                                                  vs[b, sl].copy())
+    got = eng.prefill_recurrent(0, T, qs, ks, vs)
+    assert got.shape == (B, d) and rel_err(got, last) < 1e-4
+    assert rel_err(eng.get_state()[0], states[:, 0]) < 1e-5

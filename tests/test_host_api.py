@@ -103,3 +103,30 @@ def test_module_parameters_and_to_cpu():
     assert names == ["w_gate.weight", "w_up.weight", "w_down.weight"]
     m.to("cpu")
     assert all(p.device == "cpu" for p in m.parameters())
+
+
+def test_noalloc_wrapper_rejects_bad_shapes_before_any_launch():
+    """The allocation-free entry point cannot check sizes itself, so its
+    wrapper rejects a mis-shaped state or weight (ValueError) before the
+    call; CPU tensors reach the shape checks first."""
+    import torch
+
+    from aceflow_b200 import cuda_ops
+
+    B, d, H = 2, 64, 4
+    x = torch.zeros(B, d)
+    gamma, rw = torch.ones(H), torch.ones(d)
+    w_qkv, w_o = torch.zeros(3 * d, d), torch.zeros(d, d)
+    with pytest.raises(ValueError, match="state shape"):
+        cuda_ops.msr_decode_step_noalloc(x, torch.zeros(B, H, 8, 8), gamma, w_qkv, w_o, rw, 1e-6)
+    state = torch.zeros(B, H, d // H, d // H)
+    with pytest.raises(ValueError, match="w_qkv"):
+        cuda_ops.msr_decode_step_noalloc(x, state, gamma, torch.zeros(2 * d, d), w_o, rw, 1e-6)
+    with pytest.raises(ValueError, match="w_qkv"):
+        cuda_ops.msr_decode_step_noalloc(x, state, gamma, w_qkv, torch.zeros(d, 2 * d), rw, 1e-6)
+    with pytest.raises(ValueError, match="gamma"):
+        cuda_ops.msr_decode_step_noalloc(x, state, torch.ones(H + 1), w_qkv, w_o, rw, 1e-6)
+    with pytest.raises(ValueError, match="out"):
+        cuda_ops.msr_decode_step_noalloc(x, state, gamma, w_qkv, w_o, rw, 1e-6, out=torch.zeros(B, d + 1))
+    with pytest.raises(ValueError, match="CUDA"):  # well-shaped CPU tensors: the device check
+        cuda_ops.msr_decode_step_noalloc(x, state, gamma, w_qkv, w_o, rw, 1e-6)

@@ -162,10 +162,11 @@ def test_gemm_bf16_kblocked_operand_and_blocked_parts(dev):
     assert rel_err(plain.cpu().numpy(), ref.cpu().numpy()) < 1e-5
 
 
-@pytest.mark.parametrize("groups", [0, 2])
-def test_head_sharded_prefill_single_rank(dev, groups):
-    """af_prefill_head_sharded on a 1-rank communicator equals the float64
-    layer (and af_msr_prefill_bf16), in one piece or as two head groups."""
+@pytest.mark.parametrize("groups,layout", [(0, "columns"), (2, "columns"), (0, "rows")])
+def test_head_sharded_prefill_single_rank(dev, groups, layout):
+    """af_prefill_head_sharded (columns: all-gather; in one piece or as two
+    head groups) and af_prefill_head_sharded_rows (rows: all-to-all) on a
+    1-rank communicator equal the float64 layer and af_msr_prefill_bf16."""
     from aceflow_b200 import _lib, cuda_ops
     from aceflow_b200.sharded import HeadShardedPrefill
 
@@ -177,12 +178,15 @@ def test_head_sharded_prefill_single_rank(dev, groups):
     wqkv = tb((0.02 * rng.standard_normal((3 * d, d))).astype(np.float32))
     wo = tb((0.02 * rng.standard_normal((d, d))).astype(np.float32))
     rw = torch.from_numpy((1 + 0.1 * rng.standard_normal(d)).astype(np.float32)).to(dev)
-    sp = HeadShardedPrefill(wqkv, wo, rw, H, 1e-6)
+    sp = HeadShardedPrefill(wqkv, wo, rw, H, 1e-6, layout=layout)
     _lib.set_option(0, "sharded_head_groups", groups)
     try:
         st = torch.empty(B, H, 256, 256, device=dev)
         out = sp(x, state_out=st)
         torch.cuda.synchronize()
+        if layout == "rows":
+            assert tuple(out.shape) == (B * T, d)
+            out = sp.gather_output(out, B, T)
     finally:
         _lib.set_option(0, "sharded_head_groups", 0)
         sp.close()
@@ -194,3 +198,87 @@ def test_head_sharded_prefill_single_rank(dev, groups):
     one, st1 = cuda_ops.msr_prefill_bf16(x, wqkv, wo, rw, cuda_ops.gammas(H, dev), 1e-6)
     assert rel_err(out.cpu().numpy(), one.cpu().numpy()) < 1e-3
     assert rel_err(st.cpu().numpy(), st1.cpu().numpy()) < 1e-3
+
+
+# ---- the reference module API on CUDA: af.nn.MultiScaleRetention ----------
+def _module(d, H, seed, **kw):
+    import aceflow_b200 as af
+
+    rng = np.random.default_rng(seed)
+    m = af.nn.MultiScaleRetention(d, H, **kw)
+    for name in ("w_q", "w_k", "w_v", "w_o"):
+        w = torch.from_numpy((0.02 * rng.standard_normal((d, d))).astype(np.float32)).bfloat16().float().numpy()
+        setattr(m, name, af.nn.Parameter(af.Tensor(w)))
+    m.ret_norm.weight = af.nn.Parameter(af.Tensor((1 + 0.1 * rng.standard_normal(d)).astype(np.float32)))
+    return m.to("cuda:0")
+
+
+def _module_ref(m, x64):
+    f = lambda p: p.numpy().astype(np.float64)  # noqa: E731
+    return R.msr_forward64(x64, f(m.w_q), f(m.w_k), f(m.w_v), f(m.w_o), m.num_heads, f(m.ret_norm.weight), 1e-6)
+
+
+def test_module_bf16_input_runs_tensor_core_prefill(dev):
+    """A bf16 prompt through af.nn.MultiScaleRetention(...).to('cuda') takes
+    the tensor-core chunkwise prefill: bf16 output within 2e-2 of float64,
+    and library launches (no host arithmetic)."""
+    import aceflow_b200 as af
+    from aceflow_b200 import _lib
+
+    B, T, d, H = 2, 150, 512, 2
+    m = _module(d, H, 61)
+    x = torch.from_numpy(np.random.default_rng(62).standard_normal((B, T, d)).astype(np.float32)).to(dev).bfloat16()
+    n0 = _lib.launch_count(0)
+    out = m(af.Tensor(x, device="cuda:0", dtype="bfloat16"))
+    assert _lib.launch_count(0) - n0 >= 3  # QKV GEMM, chunkwise kernel, W_o GEMM
+    assert out.dtype == "bfloat16"
+    assert rel_err(out.numpy(), _module_ref(m, x.float().cpu().numpy())) < TOL
+
+
+def test_module_fp32_input_exact_by_default_and_tensor_cores_on_request(dev):
+    """fp32 prompts: the exact fp32 path by default (1e-4 of float64); with
+    prefill_dtype='bfloat16' the tensor-core path (2e-2), output fp32."""
+    import aceflow_b200 as af
+
+    B, T, d, H = 2, 130, 512, 2
+    x = np.random.default_rng(63).standard_normal((B, T, d)).astype(np.float32)
+    exact = _module(d, H, 64)
+    ref = _module_ref(exact, x)
+    out = exact(af.Tensor(x, device="cuda:0"))
+    assert out.dtype == "float32" and rel_err(out.numpy(), ref) < 1e-4
+    tc = _module(d, H, 64, prefill_dtype="bfloat16")
+    out = tc(af.Tensor(x, device="cuda:0"))
+    assert out.dtype == "float32" and rel_err(out.numpy(), ref) < TOL
+
+
+def test_module_forward_chunkwise_state_hands_over_to_decode(dev):
+    """forward_chunkwise over two prompt pieces (the second from the first's
+    state), then forward_recurrent steps from the returned state, equal the
+    float64 forward over the whole sequence."""
+    import aceflow_b200 as af
+
+    B, d, H, T1, T2, n = 2, 512, 2, 100, 77, 3
+    m = _module(d, H, 65)
+    x = np.random.default_rng(66).standard_normal((B, T1 + T2 + n, d)).astype(np.float32)
+    xb = torch.from_numpy(x).bfloat16().float().numpy()  # the values the bf16 prefill reads
+    ref = _module_ref(m, xb)
+    t = lambda a: af.Tensor(np.ascontiguousarray(a), device="cuda:0", dtype="bfloat16")  # noqa: E731
+    o1, st = m.forward_chunkwise(t(xb[:, :T1]))
+    o2, st = m.forward_chunkwise(t(xb[:, T1:T1 + T2]), state=st)
+    assert st.shape == [B, H, 256, 256]
+    assert rel_err(np.concatenate([o1.numpy(), o2.numpy()], 1), ref[:, :T1 + T2]) < TOL
+    outs = []
+    for i in range(n):
+        o, st = m.forward_recurrent(af.Tensor(xb[:, T1 + T2 + i], device="cuda:0"), st)
+        outs.append(o.numpy())
+    assert rel_err(np.stack(outs, 1), ref[:, T1 + T2:]) < TOL
+
+
+def test_module_forward_chunkwise_needs_head_dim_256(dev):
+    import aceflow_b200 as af
+
+    m = af.nn.MultiScaleRetention(64, 4).to("cuda:0")
+    with pytest.raises(ValueError, match="head_dim 256"):
+        m.forward_chunkwise(af.Tensor(np.zeros((1, 8, 64), np.float32), device="cuda:0"))
+    with pytest.raises(ValueError, match="chunk"):
+        _module(512, 2, 1).forward_chunkwise(af.Tensor(np.zeros((1, 8, 512), np.float32), device="cuda:0"), chunk=48)

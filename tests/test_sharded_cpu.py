@@ -72,10 +72,13 @@ def _inputs(B, T, H):
     return x, wqkv, wo, rw
 
 
-def _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, eps=1e-6, groups=1):
+def _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, eps=1e-6, groups=1, layout="columns"):
     """One rank's share of the layer in float64, step for step as
     af_prefill_head_sharded lays it out (`groups` head groups, each gathered
-    separately, W_o summed over groups with the row scale applied last)."""
+    separately, W_o summed over groups with the row scale applied last), or,
+    for layout "rows", as af_prefill_head_sharded_rows does (each rank
+    receives every rank's head outputs for its own rows, block p holding
+    rank p's heads, and applies the full W_o)."""
     from aceflow_b200.sharded import chunkwise_plan, head_range, shard_weights
     from oracle import retention_ref as R
 
@@ -106,6 +109,15 @@ def _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, eps=1e-6, groups=1):
     o_w = o * rw[rank * dl:(rank + 1) * dl]
     # partial sums of squares per (head, 128-wide value slice): [N][Hl*2]
     ss = (o.reshape(N, Hl * 2, 128) ** 2).sum(-1)
+    if layout == "rows":
+        from aceflow_b200.sharded import row_range
+
+        o_all, ss_all = gather(o_w), gather(ss)  # what every rank sends, stacked by rank
+        r0, nr = row_range(N, world, rank)
+        A = np.concatenate([o_all[p * N + r0:p * N + r0 + nr] for p in range(world)], axis=1)
+        parts = np.concatenate([ss_all[p * N + r0:p * N + r0 + nr] for p in range(world)], axis=1)
+        assert A.shape == (nr, d) and parts.shape == (nr, H * 2)
+        return (1.0 / np.sqrt(parts.sum(1, keepdims=True) / d + eps)) * (A @ wo.T)
     hg = Hl // groups
     dlg, pb = hg * dh, hg * 2
     acc = np.zeros((N, dl))
@@ -126,7 +138,7 @@ def _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, eps=1e-6, groups=1):
     return (scale * acc).reshape(B, T, dl)
 
 
-def _worker(rank, world, port, B, T, H, outdir, groups):
+def _worker(rank, world, port, B, T, H, outdir, groups, layout="columns"):
     import datetime
 
     import torch.distributed as dist
@@ -141,7 +153,7 @@ def _worker(rank, world, port, B, T, H, outdir, groups):
             return torch.cat(parts, 0).numpy()
 
         x, wqkv, wo, rw = _inputs(B, T, H)
-        out = _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, groups=groups)
+        out = _rank_layer(x, wqkv, wo, rw, H, world, rank, gather, groups=groups, layout=layout)
         np.save(os.path.join(outdir, f"out{rank}.npy"), out)
         dist.barrier()
     finally:
@@ -165,3 +177,97 @@ def test_head_sharded_decomposition_two_gloo_ranks(groups):
     wq, wk, wv = np.split(wqkv, 3)
     ref = R.msr_forward64(x, wq, wk, wv, wo, H, rw, 1e-6)
     assert rel_err(out, ref) < 1e-10
+
+
+@pytest.mark.parametrize("B,T", [(1, 300), (3, 101)])
+def test_head_sharded_rows_decomposition_two_gloo_ranks(B, T):
+    """The all-to-all layout: rank r's rows [r*c, r*c + n_r) of the layer
+    output from the K-blocked receive buffer and the full W_o (ragged last
+    block when B*T is odd)."""
+    import torch.multiprocessing as mp
+
+    from aceflow_b200.sharded import row_range
+    from oracle import retention_ref as R
+
+    H = 4
+    assert row_range(303, 2, 1) == (152, 151) and row_range(1, 2, 1) == (1, 0)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as outdir:
+        mp.spawn(_worker, args=(WORLD, port, B, T, H, outdir, 1, "rows"), nprocs=WORLD, join=True)
+        out = np.concatenate([np.load(os.path.join(outdir, f"out{r}.npy")) for r in range(WORLD)], 0)
+    x, wqkv, wo, rw = _inputs(B, T, H)
+    wq, wk, wv = np.split(wqkv, 3)
+    ref = R.msr_forward64(x, wq, wk, wv, wo, H, rw, 1e-6)
+    assert rel_err(out.reshape(ref.shape), ref) < 1e-10
+
+
+# ---- failure detection on the host (gloo ranks, no GPU) --------------------
+def _agree_worker(rank, world, port, outdir, mode):
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    from aceflow_b200.sharded import agree_on_layout, share_comm_id
+
+    timeout = 3 if mode == "absent" else 60
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout))
+    t0 = time.time()
+    result = "ok"
+    try:
+        if mode == "mismatch":  # the ranks were handed different shard sizes
+            agree_on_layout(dict(batch=1, seq_len=4096 if rank == 0 else 2048, d_model=4096))
+        elif mode == "absent":  # rank 1 never joins the exchange
+            if rank == 1:
+                time.sleep(3 * timeout)
+            else:
+                agree_on_layout(dict(batch=1, seq_len=4096, d_model=4096))
+        elif mode == "id":
+            got = share_comm_id(bytes(range(128)) if rank == 0 else None)
+            result = "ok" if got == bytes(range(128)) else "wrong id"
+            agree_on_layout(dict(batch=1, seq_len=4096, d_model=4096))  # equal layouts pass
+    except ValueError as e:
+        result = f"ValueError: {e}"
+    except Exception as e:  # the process group's timeout (or a closed peer)
+        result = f"{type(e).__name__}: {e}"
+    with open(os.path.join(outdir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{time.time() - t0:.1f}\n{result}")
+    if mode != "absent":
+        dist.destroy_process_group()
+
+
+def _run_agree(mode):
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as outdir:
+        mp.spawn(_agree_worker, args=(WORLD, port, outdir, mode), nprocs=WORLD, join=True)
+        res = []
+        for r in range(WORLD):
+            with open(os.path.join(outdir, f"r{r}.txt")) as f:
+                secs, msg = f.read().split("\n", 1)
+            res.append((float(secs), msg))
+    return res
+
+
+def test_mismatched_shard_sizes_fail_uniformly_on_every_rank():
+    res = _run_agree("mismatch")
+    assert all(msg.startswith("ValueError") and "seq_len" in msg for _, msg in res), res
+    assert res[0][1] == res[1][1]  # the same message everywhere
+
+
+def test_rank_that_never_joins_ends_the_wait_with_an_error():
+    res = _run_agree("absent")
+    secs, msg = res[0]
+    assert msg != "ok" and not msg.startswith("ValueError"), res
+    assert secs < 30, res  # the process group's 3 s timeout, not a hang
+
+
+def test_comm_id_exchange_and_equal_layouts_pass():
+    res = _run_agree("id")
+    assert [m for _, m in res] == ["ok", "ok"], res

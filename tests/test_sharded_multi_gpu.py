@@ -1,6 +1,7 @@
-"""Head-sharded prefill on 2 GPUs (one process per GPU, NCCL all-gather in
-the C library) against the float64 layer.  Skipped with fewer than 2 GPUs.
-NVLS is switched off for the test's NCCL communicators."""
+"""Head-sharded prefill on 2 GPUs (one process per GPU; NCCL all-gather, or
+all-to-all for the row layout, in the C library) against the float64 layer.
+Skipped with fewer than 2 GPUs.  NVLS is switched off for the test's NCCL
+communicators."""
 import os
 import tempfile
 
@@ -25,7 +26,7 @@ def _inputs(B, T, H):
     return x, wqkv, wo, rw
 
 
-def _worker(rank, world, port, B, T, H, outdir, groups):
+def _worker(rank, world, port, B, T, H, outdir, groups, layout="columns"):
     import torch.distributed as dist
 
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -40,7 +41,7 @@ def _worker(rank, world, port, B, T, H, outdir, groups):
         dev = torch.device("cuda", rank)
         x, wqkv, wo, rw = _inputs(B, T, H)
         tb = lambda a: torch.from_numpy(a).to(dev).bfloat16()  # noqa: E731
-        sp = HeadShardedPrefill(tb(wqkv), tb(wo), torch.from_numpy(rw).to(dev), H, 1e-6)
+        sp = HeadShardedPrefill(tb(wqkv), tb(wo), torch.from_numpy(rw).to(dev), H, 1e-6, layout=layout)
         st = torch.empty(B, H // world, 256, 256, device=dev)
         out = sp(tb(x), state_out=st)
         torch.cuda.synchronize()
@@ -55,8 +56,8 @@ def _worker(rank, world, port, B, T, H, outdir, groups):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-@pytest.mark.parametrize("groups", [0, 2])
-def test_head_sharded_prefill_two_gpus(groups):
+@pytest.mark.parametrize("groups,layout", [(0, "columns"), (2, "columns"), (0, "rows")])
+def test_head_sharded_prefill_two_gpus(groups, layout):
     import socket
 
     import torch.multiprocessing as mp
@@ -68,14 +69,15 @@ def test_head_sharded_prefill_two_gpus(groups):
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     with tempfile.TemporaryDirectory() as outdir:
-        mp.spawn(_worker, args=(WORLD, port, B, T, H, outdir, groups), nprocs=WORLD, join=True)
+        mp.spawn(_worker, args=(WORLD, port, B, T, H, outdir, groups, layout), nprocs=WORLD, join=True)
         outs = [np.load(os.path.join(outdir, f"out{r}.npy")) for r in range(WORLD)]
         states = [np.load(os.path.join(outdir, f"state{r}.npy")) for r in range(WORLD)]
     x, wqkv, wo, rw = _inputs(B, T, H)
     bf = lambda a: torch.from_numpy(a).bfloat16().double().numpy()  # noqa: E731
     wq, wk, wv = np.split(bf(wqkv), 3)
     ref = R.msr_forward64(bf(x), wq, wk, wv, bf(wo), H, rw.astype(np.float64), 1e-6)
-    assert rel_err(np.concatenate(outs, -1), ref) < TOL
+    full = np.concatenate(outs, -1) if layout == "columns" else np.concatenate(outs, 0).reshape(ref.shape)
+    assert rel_err(full, ref) < TOL
     d = H * 256
     q, k, v = (bf(x).reshape(B * T, d) @ w.T for w in (wq, wk, wv))
     sh = lambda a: a.reshape(B, T, H, 256).transpose(0, 2, 1, 3)  # noqa: E731
