@@ -45,12 +45,12 @@ SIGNATURES = {
     "af_add_f32": [_vp, _vp, _vp, _vp, _i64, _i64, _f, _vp],
     "af_linear_f32": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "af_linear_bf16": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
-    "af_chunkwise_plan": [_i, _i, _i, _i, _i, _vp, _vp],
+    "af_chunkwise_plan": [_i, _i, _i, _i, _i, _i, _vp, _vp],
     "af_comm_unique_id": [_vp],
     "af_comm_init": [_vp, _i, _i, _vp],
     "af_comm_destroy": [_vp],
-    "af_prefill_head_sharded": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp],
-    "af_prefill_head_sharded_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp],
+    "af_prefill_head_sharded": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp],
+    "af_prefill_head_sharded_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp],
     "af_phase_times": [_vp, ctypes.POINTER(_f), ctypes.POINTER(ctypes.c_char_p), _i, ctypes.POINTER(_i)],
     "af_gemm_bf16": [_vp, _vp, _i64, _i, _vp, _i64, _i, _i, _i, _vp, _i64, _i, _vp, _vp, _i64, _vp, _i, _i, _f, _f, _i,
                      _vp],
@@ -60,8 +60,9 @@ SIGNATURES = {
     "af_linear_f32_split": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "af_msr_decode_step_f32_split": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
     "af_msr_decode_step_f32_noalloc": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
-    "af_retention_chunkwise_bf16": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp],
-    "af_msr_prefill_bf16": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp],
+    "af_retention_chunkwise_backward_bf16": [_vp, _vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp],
+    "af_retention_chunkwise_bf16": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
+    "af_msr_prefill_bf16": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp],
     "af_pack_gate_up": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "af_decoder_layer_decode": [_vp, _vp, _i, _vp, _vp, _i64, _vp, _f, _i, _i, _i, _i, _vp],
     "af_decoder_layer_prefill": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _i, _vp],

@@ -51,7 +51,7 @@ int workspace(af_ctx *ctx, size_t bytes, void **out, const char *fn) {
 
 extern "C" {
 
-int af_abi_version(void) { return 1; }
+int af_abi_version(void) { return 2; }
 
 const char *af_last_error(void) { return af::g_error; }
 
@@ -174,6 +174,9 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
   } else if (!strcmp(name, "comm_reserve_sms")) {
     if (value < 0 || value > 64) return af::fail(AF_ERR_ARG, "af_set_option: comm_reserve_sms 0..64");
     ctx->comm_reserve_sms = (int)value;
+  } else if (!strcmp(name, "chunk_len")) {
+    if (value != 64 && value != 128) return af::fail(AF_ERR_ARG, "af_set_option: chunk_len must be 64 or 128");
+    ctx->chunk_len = (int)value;
   } else if (!strcmp(name, "chunkwise_segments")) {
     if (value < 0 || value > 4096) return af::fail(AF_ERR_ARG, "af_set_option: chunkwise_segments 0..4096");
     ctx->chunk_segments = (int)value;

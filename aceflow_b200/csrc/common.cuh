@@ -33,6 +33,7 @@ struct af_ctx {
   int decode_head_groups = 1;
   int decode_slice_rows = 0;  // batch rows per overlapped slice; 0 = one sequential pass (faster today)
   int chunk_segments = 0;     // sequence segments per stream in the chunkwise prefill; 0 = fill the SMs
+  int chunk_len = 64;         // tokens per chunk of the chunkwise prefill when a call passes 0 (64 or 128)
   // NCCL communicator of the head-sharded prefill (sharded_prefill.cu)
   void *comm = nullptr;
   int comm_nranks = 0, comm_rank = 0;
@@ -131,14 +132,23 @@ int rmsnorm_to_bf16(af_ctx *ctx, const float *x, const float *w, uint16_t *y, in
 // nseg segments of seg_len tokens (seg_len a multiple of the chunk length).
 struct ChunkPlan {
   int nseg, seg_len;
+  int chunk;  // tokens per chunk: 64 or 128
 };
-ChunkPlan chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req);
+ChunkPlan chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req, int chunk);
 size_t chunkwise_seg_state_bytes(int B, int H, const ChunkPlan &pl);
+// ldo: output row stride (0: H*256); out_reverse: token t of each stream is
+// written to row T-1-t.  Both need pl.chunk == 128.
 int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
                              const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
-                             const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn);
+                             const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn, int64_t ldo = 0,
+                             bool out_reverse = false);
 int chunkwise_head_dim();
-int chunkwise_parts();
+// Per-head partial sums of squares per output row for that chunk length.
+int chunkwise_parts(int chunk);
+// The context's chunk length (af_set_option "chunk_len"; 64 or 128).
+int chunkwise_default_chunk(const af_ctx *ctx);
+// The chunk length of a call (0: the context's), checked.
+int resolve_chunk(const af_ctx *ctx, int chunk, int *out, const char *fn);
 
 // af_check_device(NULL, ...): the allocation-free decode step's error word on
 // the current device (decode_noalloc.cu).

@@ -430,11 +430,12 @@ extern "C" int af_decoder_layer_prefill(af_ctx *ctx, const af_layer_weights *w, 
   AF_REQUIRE((int64_t)B * T <= 65535LL * 128, "af_decoder_layer_prefill", "batch*T too large");
   if (B == 0 || T == 0) return AF_OK;
   const int N = B * T;
-  const int parts = H * af::chunkwise_parts();
+  const int C = af::chunkwise_default_chunk(ctx);
+  const int parts = H * af::chunkwise_parts(C);
   const size_t h_b = af::align256((size_t)N * d * 2), qkv_b = af::align256((size_t)N * 3 * d * 2),
                o_b = af::align256((size_t)N * d * 2), ss_b = af::align256((size_t)N * parts * 4),
                hid_b = af::align256((size_t)N * f * 2);
-  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments, C);
   const size_t seg_b = af::chunkwise_seg_state_bytes(B, H, pl);
   void *ws = nullptr;
   rc = af::workspace(ctx, h_b + qkv_b + o_b + ss_b + hid_b + seg_b, &ws, fn);

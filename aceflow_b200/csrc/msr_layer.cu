@@ -303,25 +303,39 @@ extern "C" int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *
 //   2. chunkwise retention      -> bf16 O * ret_norm_w, per-row partial sum O^2, final state
 //   3. out = diag(1/rms) (O*w) . W_o^T   bf16 GEMM with the row scale in its epilogue
 
-extern "C" int af_chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req, int *nseg, int *seg_len) {
-  AF_REQUIRE(num_sms > 0 && B >= 0 && T >= 0 && H > 0 && nseg_req >= 0 && nseg && seg_len, "af_chunkwise_plan",
-             "bad arguments");
-  const af::ChunkPlan pl = af::chunkwise_plan(num_sms, B, T, H, nseg_req);
+extern "C" int af_chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req, int chunk, int *nseg,
+                                 int *seg_len) {
+  AF_REQUIRE(num_sms > 0 && B >= 0 && T >= 0 && H > 0 && nseg_req >= 0 && nseg && seg_len &&
+                 (chunk == 0 || chunk == 64 || chunk == 128),
+             "af_chunkwise_plan", "bad arguments");
+  const af::ChunkPlan pl = af::chunkwise_plan(num_sms, B, T, H, nseg_req, chunk ? chunk : 64);
   *nseg = pl.nseg;
   *seg_len = pl.seg_len;
   return AF_OK;
 }
 
+namespace af {
+// The chunk length of a call: 0 takes the context's default.
+int resolve_chunk(const af_ctx *ctx, int chunk, int *out, const char *fn) {
+  if (chunk != 0 && chunk != 64 && chunk != 128) return fail(AF_ERR_ARG, "%s: chunk must be 64 or 128 (or 0)", fn);
+  *out = chunk ? chunk : chunkwise_default_chunk(ctx);
+  return AF_OK;
+}
+}  // namespace af
+
 extern "C" int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int B, int T, int H, const float *gamma,
                                            const float *state_in, float *state_out, uint16_t *out,
-                                           const float *norm_w, float *sumsq, af_stream_t stream) {
+                                           const float *norm_w, float *sumsq, int chunk, af_stream_t stream) {
   const char *fn = "af_retention_chunkwise_bf16";
   AF_ENTER(ctx, fn);
   AF_REQUIRE(qkv && gamma && out, "af_retention_chunkwise_bf16", "null pointer");
   AF_REQUIRE(B >= 0 && T >= 0 && H > 0, "af_retention_chunkwise_bf16", "bad sizes B=%d T=%d H=%d", B, T, H);
-  AF_REQUIRE(af::aligned16(qkv), "af_retention_chunkwise_bf16", "qkv must be 16-byte aligned");
+  AF_REQUIRE(af::aligned16(qkv) && af::aligned16(out), "af_retention_chunkwise_bf16",
+             "qkv and out must be 16-byte aligned");
+  int C = 0;
+  if (int rc = af::resolve_chunk(ctx, chunk, &C, fn)) return rc;
   if (B == 0 || T == 0) return AF_OK;
-  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments, C);
   void *ws = nullptr;
   const size_t seg_bytes = af::chunkwise_seg_state_bytes(B, H, pl);
   if (seg_bytes) {
@@ -335,7 +349,7 @@ extern "C" int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int
 
 extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv, const uint16_t *w_o,
                                    const float *ret_norm_w, const float *gamma, float eps, int B, int T, int d, int H,
-                                   const float *state_in, float *state_out, void *out, int out_bf16,
+                                   const float *state_in, float *state_out, void *out, int out_bf16, int chunk,
                                    af_stream_t stream) {
   const char *fn = "af_msr_prefill_bf16";
   AF_ENTER(ctx, fn);
@@ -345,13 +359,15 @@ extern "C" int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_
   AF_REQUIRE(af::aligned16(x) && af::aligned16(w_qkv) && af::aligned16(w_o), "af_msr_prefill_bf16",
              "x and weights must be 16-byte aligned");
   AF_REQUIRE((int64_t)B * T <= 65535LL * 128, "af_msr_prefill_bf16", "B*T too large");
+  int C = 0;
+  if (int rc = af::resolve_chunk(ctx, chunk, &C, fn)) return rc;
   if (B == 0 || T == 0) return AF_OK;
   const int64_t N = (int64_t)B * T;
-  const int parts = H * af::chunkwise_parts();
+  const int parts = H * af::chunkwise_parts(C);
   const size_t qkv_bytes = ((size_t)N * 3 * d * 2 + 255) & ~size_t(255);
   const size_t o_bytes = ((size_t)N * d * 2 + 255) & ~size_t(255);
   const size_t ss_bytes = ((size_t)N * parts * 4 + 255) & ~size_t(255);
-  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments, C);
   const size_t seg_bytes = af::chunkwise_seg_state_bytes(B, H, pl);
   void *ws = nullptr;
   int rc = af::workspace(ctx, qkv_bytes + o_bytes + ss_bytes + seg_bytes, &ws, fn);

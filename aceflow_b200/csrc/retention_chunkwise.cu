@@ -89,6 +89,8 @@ struct ChunkParams {
   const float *norm_w;    // [H*DH] or null
   float *sumsq;           // [B*T][H*NSL] or null
   int *err;
+  int64_t ldo = 0;        // output row stride in elements (0: H*DH; 128-token kernel only)
+  int out_reverse = 0;    // token t of a stream is written to row T-1-t (128-token kernel only)
 };
 
 // MN-major SW128 descriptor: 64-element MN blocks `lbo` bytes apart, 8-row
@@ -579,6 +581,376 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 128-token chunks.  Same CTA split (stream, segment, head, 128-wide value
+// slice) and the same fp32 state S^T in TMEM, with a data flow that fits 128
+// tokens into 227 KB of shared memory:
+//   * the masked scores P live in TMEM as bf16 and are the A operand of the
+//     intra-chunk MMA (tcgen05.mma with A in tensor memory), so P needs no
+//     shared memory;
+//   * the decay is folded into V' = diag(gamma^-(j+1)) V (j = position in the
+//     chunk), scaled in place where V landed, which serves as both
+//         O_c = diag(gamma^(i+1)) (Q S + mask(Q K^T) V')          (O: tokens x v)
+//         S  <- gamma^L (S + K^T V')     (the gamma^L applied when the next
+//                                         chunk reads S, or to the final state)
+//     so no second scaled copy of V is kept (gamma^-128 <= 58 at gamma = 1 - 2^-5);
+//   * the output is computed non-transposed (TMEM lane = token), so each math
+//     thread owns one token row and stores its 128 contiguous bytes directly.
+// Shared memory: Q, K [128 tok x 256 k], V' [128 tok x 128 v], bf16(S^T)
+// [128 v x 256 k] = 224 KB.  TMEM: S^T 256 columns, scores/P 128, O 128.
+// Per chunk: 16 MMAs O = Q . S (N=128), 16 scores (N=128), 8 intra (A from
+// TMEM), 8 state updates (N=256): 48 MMAs per 128 tokens against 80 for two
+// 64-token chunks.  The load of the next chunk's Q overlaps this chunk's intra
+// and update MMAs.
+namespace c128 {
+constexpr int C = 128;
+constexpr int SLICE = 128 * 64 * 2;          // one [128 rows x 64] bf16 SW128 tile: 16 KB
+constexpr int Q_OFF = 0;                     // 4 K-slices [128 tok x 64 k]
+constexpr int K_OFF = Q_OFF + 4 * SLICE;     // 4 K-slices [128 tok x 64 k]
+constexpr int V_OFF = K_OFF + 4 * SLICE;     // 2 boxes [128 tok x 64 v], scaled in place to V'
+constexpr int SOP_OFF = V_OFF + 2 * SLICE;   // bf16(S^T): 4 K-slices [128 v x 64 k]
+constexpr int TILE_BYTES = SOP_OFF + 4 * SLICE;  // 224 KB
+constexpr int NBAR = 8;
+// tail: barriers, TMEM slot (16 bytes), this CTA's 128 norm weights
+constexpr size_t TAIL_BYTES = NBAR * 8 + 16 + VS * 4;
+constexpr size_t SMEM = 1024 + TILE_BYTES + TAIL_BYTES;
+static_assert(SMEM <= 232448, "227 KB of shared memory per CTA");
+constexpr uint32_t TM_S = 0, TM_SC = 256, TM_O = 384, TM_COLS = 512;
+constexpr int PARTS = NSL * 2;  // sum-of-squares parts per head: value slice x column half
+}  // namespace c128
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__global__ void __launch_bounds__(320, 1)
+    retention_chunk128_kernel(const __grid_constant__ CUtensorMap tm, ChunkParams p) {
+  // this kernel's layout (shadows the 64-token kernel's constants)
+  constexpr int C = c128::C, SLICE = c128::SLICE, Q_OFF = c128::Q_OFF, K_OFF = c128::K_OFF, V_OFF = c128::V_OFF,
+                SOP_OFF = c128::SOP_OFF, TILE_BYTES = c128::TILE_BYTES, NBAR = c128::NBAR, PARTS = c128::PARTS;
+  constexpr uint32_t TM_S = c128::TM_S, TM_SC = c128::TM_SC, TM_O = c128::TM_O, TM_COLS = c128::TM_COLS;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + TILE_BYTES);
+  uint64_t *bar_q = bars + 0, *bar_kv = bars + 1, *bar_sc = bars + 2, *bar_sop = bars + 3, *bar_math = bars + 4,
+           *bar_o = bars + 5, *bar_ofree = bars + 6, *bar_upd = bars + 7;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
+  float *wsl = reinterpret_cast<float *>(bars + NBAR + 2);  // norm weights of this slice
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slice = blockIdx.x % NSL;
+  const int bsh = blockIdx.x / NSL;  // ((b * nseg) + s) * H + h
+  const int h = bsh % p.H, bs = bsh / p.H;
+  const int b = bs / p.nseg, s = bs % p.nseg;
+  const int d = p.H * DH;
+  const int tb = s * p.seg_len;
+  const int te = min(p.T, tb + p.seg_len);
+  const int nch = (te - tb + C - 1) / C;
+  const float lg = log2f(p.gamma[h]);
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    mbar_init(bar_q, 1);
+    mbar_init(bar_kv, 1);
+    mbar_init(bar_sc, 1);
+    mbar_init(bar_sop, MATH_THREADS);
+    mbar_init(bar_math, MATH_THREADS);
+    mbar_init(bar_o, 1);
+    mbar_init(bar_ofree, MATH_THREADS);
+    mbar_init(bar_upd, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tm);
+  }
+  if (threadIdx.x >= 64 && threadIdx.x < 64 + VS) {
+    const int i = threadIdx.x - 64;
+    wsl[i] = p.norm_w ? p.norm_w[h * DH + slice * VS + i] : 1.f;
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&]() {
+    s_abort = 1;
+    atomicOr(p.err, 1 << AF_ERR_TIMEOUT);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int q_issued = 0, kv_issued = 0;
+      for (int c = 0; c < nch && !s_abort; ++c) {
+        const int t0 = tb + c * C;
+        // Q(c-1) is consumed once chunk c-1's scores (issued after its O = Q S) completed
+        if (c > 0 && !mbar_wait(bar_sc, (c - 1) & 1)) { fail(); break; }
+        mbar_arrive_expect_tx(bar_q, 4 * SLICE);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + Q_OFF + kk * SLICE, &tm, bar_q, h * DH + kk * 64, t0, b);
+        q_issued = c + 1;
+        // K(c-1) and V'(c-1) are consumed once chunk c-1's state update completed
+        if (c > 0 && !mbar_wait(bar_upd, (c - 1) & 1)) { fail(); break; }
+        mbar_arrive_expect_tx(bar_kv, 6 * SLICE);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + K_OFF + kk * SLICE, &tm, bar_kv, d + h * DH + kk * 64, t0, b);
+#pragma unroll
+        for (int vb = 0; vb < 2; ++vb)
+          tma_load_3d(sm + V_OFF + vb * SLICE, &tm, bar_kv, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
+        kv_issued = c + 1;
+      }
+      // loads still in flight land before the CTA may exit
+      if (q_issued > 0 && !mbar_wait(bar_q, (q_issued - 1) & 1)) fail();
+      if (kv_issued > 0 && !mbar_wait(bar_kv, (kv_issued - 1) & 1)) fail();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t id_nn = idesc_f32acc(kFmtBF16, 128, 128);                       // A, B K-major
+    constexpr uint32_t id_intra = idesc_f32acc(kFmtBF16, 128, 128) | (1u << 16);       // A in TMEM, B MN-major
+    constexpr uint32_t id_upd = idesc_f32acc(kFmtBF16, 128, 256) | (1u << 15) | (1u << 16);  // A, B MN-major
+    for (int c = 0; c < nch; ++c) {
+      // O = Q . S  (K = 256 keys) once Q landed, bf16(S) is written and the
+      // previous chunk's O has been read out
+      bool ok = mbar_wait(bar_q, c & 1) && mbar_wait(bar_sop, c & 1);
+      if (ok && c > 0) ok = mbar_wait(bar_ofree, (c - 1) & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t da = sdesc_k_sw128(sm + Q_OFF + kk * SLICE) + ((k * 32) >> 4);
+            const uint64_t db = sdesc_k_sw128(sm + SOP_OFF + kk * SLICE) + ((k * 32) >> 4);
+            umma_bf16(tmem + TM_O, da, db, id_nn, (kk | k) != 0);
+          }
+      }
+      __syncwarp();
+      // scores Q . K^T (K = 256 keys)
+      ok = mbar_wait(bar_kv, c & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t da = sdesc_k_sw128(sm + Q_OFF + kk * SLICE) + ((k * 32) >> 4);
+            const uint64_t db = sdesc_k_sw128(sm + K_OFF + kk * SLICE) + ((k * 32) >> 4);
+            umma_bf16(tmem + TM_SC, da, db, id_nn, (kk | k) != 0);
+          }
+        umma_commit(bar_sc);
+      }
+      __syncwarp();
+      // once P (TMEM) and V' (shared memory) are written:
+      ok = mbar_wait(bar_math, c & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
+      tc_fence_after();
+      if (lane == 0) {
+        //   O += P . V'   (K = 128 tokens; P's columns: j < 64 from TM_SC, j >= 64 from TM_SC + 64)
+#pragma unroll
+        for (int kj = 0; kj < 8; ++kj) {
+          const uint32_t pa = tmem + TM_SC + (kj < 4 ? 8 * kj : 64 + 8 * (kj - 4));
+          const uint64_t db = sdesc_mn_sw128(sm + V_OFF + kj * 2048, SLICE);
+          umma_bf16_ts(tmem + TM_O, pa, db, id_intra, 1);
+        }
+        umma_commit(bar_o);
+        //   S^T += V'^T . K   (K = 128 tokens, N = 256 keys)
+#pragma unroll
+        for (int kt = 0; kt < 8; ++kt) {
+          const uint64_t da = sdesc_mn_sw128(sm + V_OFF + kt * 2048, SLICE);
+          const uint64_t db = sdesc_mn_sw128(sm + K_OFF + kt * 2048, SLICE);
+          umma_bf16(tmem + TM_S, da, db, id_upd, 1);
+        }
+        umma_commit(bar_upd);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ math warps
+    const int q = warp & 3;            // TMEM lane quadrant
+    const int half = (warp - 2) >> 2;  // which half of the columns this warp takes
+    const int mt = threadIdx.x - 64;   // 0..255
+    const int row = q * 32 + lane;     // TMEM lane: value index (state) or token (scores, O)
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    // initial state S^T[v][k] = S[k][v]
+    {
+      const float *sin = p.state_in ? p.state_in + ((size_t)bsh * DH) * DH + slice * VS + row : nullptr;
+#pragma unroll 1
+      for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 16) {
+        float x[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[j] = sin ? sin[(size_t)(k0 + j) * DH] : 0.f;
+        __syncwarp();
+        tmem_st16(tmem + lane_base + TM_S + k0, x);
+      }
+      tmem_wait_st();
+    }
+    const float gC = exp2f((float)C * lg);
+    for (int c = 0; c < nch; ++c) {
+      const int t0 = tb + c * C;
+      const int L = min(C, te - t0);
+      // (A) S = gamma^C S_acc (the previous chunk's decay, deferred); bf16(S^T) -> shared memory
+      bool ok = true;
+      if (c > 0) ok = mbar_wait(bar_upd, (c - 1) & 1);
+      if (!ok) s_abort = 1;
+      if (math_sync_or(s_abort != 0)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 64) {
+        float x[64];
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          tmem_ld16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+        tmem_wait_ld();
+        if (c > 0) {
+#pragma unroll
+          for (int j = 0; j < 64; ++j) x[j] *= gC;
+        }
+        uint8_t *slice_base = sm + SOP_OFF + (k0 >> 6) * SLICE;
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16) {
+          const float *y = x + 8 * c16;
+          *reinterpret_cast<uint4 *>(slice_base + sw128(row, c16)) =
+              make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+        }
+        if (c > 0) {
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            tmem_st16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+        }
+      }
+      tmem_wait_st();
+      fence_proxy_async_smem();  // bf16(S^T) (generic stores) before the MMAs that read it
+      tc_fence_before();
+      mbar_arrive(bar_sop);
+      // (B) V' = diag(gamma^-(j+1)) V in place
+      ok = mbar_wait(bar_kv, c & 1);
+      if (!ok) s_abort = 1;
+      if (ok) {
+#pragma unroll 2
+        for (int i = mt; i < 2 * SLICE / 16; i += MATH_THREADS) {
+          const int off = i * 16;
+          const int j = (off % SLICE) / 128;  // token row of this 16-byte chunk
+          const float sc = exp2f(-(float)(j + 1) * lg);
+          uint4 raw = *reinterpret_cast<const uint4 *>(sm + V_OFF + off);
+          __nv_bfloat162 *e = reinterpret_cast<__nv_bfloat162 *>(&raw);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float2 f = __bfloat1622float2(e[u]);
+            e[u] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+          }
+          *reinterpret_cast<uint4 *>(sm + V_OFF + off) = raw;
+        }
+      }
+      fence_proxy_async_smem();
+      // (C) P = bf16(Q K^T masked to j <= i), written back into the scores'
+      //     columns: this warp's 64 columns j become 32 packed columns at
+      //     TM_SC + 64 * half, inside the range it read
+      ok = ok && mbar_wait(bar_sc, c & 1);
+      if (!ok) s_abort = 1;
+      if (ok) {
+        tc_fence_after();
+        const int j0 = half * 64;
+        float x[64];
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          tmem_ld16(tmem + lane_base + TM_SC + j0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+        tmem_wait_ld();
+        uint32_t pk[32];
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) {
+          const int j = j0 + 2 * jj;
+          pk[jj] = pack_bf16(j <= row ? x[2 * jj] : 0.f, j + 1 <= row ? x[2 * jj + 1] : 0.f);
+        }
+        __syncwarp();
+        tmem_st16u(tmem + lane_base + TM_SC + j0, *reinterpret_cast<uint32_t(*)[16]>(pk));
+        tmem_st16u(tmem + lane_base + TM_SC + j0 + 16, *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(bar_math);
+      if (math_sync_or(s_abort != 0)) break;
+      // (D) token row i = row: O = gamma^(i+1) O_acc; bf16 O * w straight to
+      //     global memory (this warp's 64 values: 128 contiguous bytes); the
+      //     partial sum of O^2 of those values
+      ok = mbar_wait(bar_o, c & 1);
+      if (!ok) s_abort = 1;
+      if (math_sync_or(s_abort != 0)) break;
+      tc_fence_after();
+      float x[64];
+      __syncwarp();
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        tmem_ld16(tmem + lane_base + TM_O + half * 64 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(bar_ofree);  // O is in registers: the next chunk's MMAs may overwrite it
+      if (row < L) {
+        const float f = exp2f((float)(row + 1) * lg);
+        const size_t r = (size_t)b * p.T + t0 + row;
+        const size_t ro = p.out_reverse ? (size_t)b * p.T + (p.T - 1 - (t0 + row)) : r;
+        uint4 *dst = reinterpret_cast<uint4 *>(p.out + ro * (p.ldo ? p.ldo : d) + h * DH + slice * VS + half * 64);
+        const float *w = wsl + half * 64;
+        float ss = 0.f;
+#pragma unroll
+        for (int c16 = 0; c16 < 8; ++c16) {
+          float y[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float o = x[8 * c16 + u] * f;
+            ss = fmaf(o, o, ss);
+            y[u] = o * w[8 * c16 + u];
+          }
+          dst[c16] = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]),
+                                pack_bf16(y[6], y[7]));
+        }
+        if (p.sumsq) p.sumsq[r * (p.H * PARTS) + h * PARTS + slice * 2 + half] = ss;
+      }
+    }
+    // final state S[k][v] = gamma^L_last (S_acc^T[v][k]) of the last segment
+    const bool aborted = math_sync_or(s_abort != 0);
+    const bool write_state = p.state_out && s == p.nseg - 1;
+    if (!aborted && nch > 0) {
+      bool ok = mbar_wait(bar_upd, (nch - 1) & 1);  // last MMAs retired before TMEM is read or freed
+      if (!ok) s_abort = 1;
+      if (!math_sync_or(s_abort != 0) && write_state) {
+        tc_fence_after();
+        const float gl = exp2f((float)(te - (tb + (nch - 1) * C)) * lg);
+        float *so = p.state_out + ((size_t)(b * p.H + h) * DH) * DH + slice * VS + row;
+#pragma unroll 1
+        for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 16) {
+          float x[16];
+          __syncwarp();
+          tmem_ld16(tmem + lane_base + TM_S + k0, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) so[(size_t)(k0 + j) * DH] = x[j] * gl;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TM_COLS);
+  }
+}
+
 // Turns segment end states dS_s ([B][nseg][H][DH*DH], zero-start) into the
 // state before each segment, in place:  S_in[0] = state_in (or 0),
 // S_in[s+1] = gamma^seg_len S_in[s] + dS_s.  One thread per 4 state entries.
@@ -613,20 +985,30 @@ int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const CUtensorMap &tm_o
   return af::launched(ctx, fn);
 }
 
+int launch_chunk128(af_ctx *ctx, const CUtensorMap &tm, const ChunkParams &p, cudaStream_t st, const char *fn) {
+  static std::atomic<unsigned long long> attr_devices{0};
+  if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(retention_chunk128_kernel), c128::SMEM,
+                              attr_devices, fn))
+    return arc;
+  retention_chunk128_kernel<<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, c128::SMEM, st>>>(tm, p);
+  return af::launched(ctx, fn);
+}
+
 }  // namespace
 
 namespace af {
 
-ChunkPlan chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req) {
-  ChunkPlan pl{1, T > 0 ? ((T + C - 1) / C) * C : C};
+ChunkPlan chunkwise_plan(int num_sms, int B, int T, int H, int nseg_req, int chunk) {
+  const int Cc = chunk == c128::C ? c128::C : C;
+  ChunkPlan pl{1, T > 0 ? ((T + Cc - 1) / Cc) * Cc : Cc, Cc};
   if (B <= 0 || T <= 0 || H <= 0) return pl;
-  const int chunks = (T + C - 1) / C;
+  const int chunks = (T + Cc - 1) / Cc;
   const int ctas = B * H * NSL;
   int nseg = nseg_req > 0 ? nseg_req : num_sms / ctas;  // one CTA per SM
   if (nseg < 1) nseg = 1;
   if (nseg > chunks) nseg = chunks;
   const int per = (chunks + nseg - 1) / nseg;
-  pl.seg_len = per * C;
+  pl.seg_len = per * Cc;
   pl.nseg = (chunks + per - 1) / per;
   return pl;
 }
@@ -635,11 +1017,27 @@ size_t chunkwise_seg_state_bytes(int B, int H, const ChunkPlan &pl) {
   return pl.nseg > 1 ? (size_t)B * pl.nseg * H * DH * DH * sizeof(float) : 0;
 }
 
-// Chunkwise retention over a bf16 QKV buffer [B*T][3d] (row stride 3d).
-// seg_states: chunkwise_seg_state_bytes() of scratch when pl.nseg > 1.
+static int encode_qkv_map(CUtensorMap *tm, const void *qkv, int B, int T, int d, int rows, const char *fn) {
+  cuuint64_t dims[3] = {(cuuint64_t)(3 * d), (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)3 * d * 2, (cuuint64_t)T * 3 * d * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = g_encode3(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(qkv), dims, strides, box, es,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: tensor map encode failed (%d)", fn, (int)r);
+  return AF_OK;
+}
+
+// Chunkwise retention over a bf16 QKV buffer [B*T][3d] (row stride 3d) in
+// chunks of pl.chunk (64 or 128) tokens.  seg_states:
+// chunkwise_seg_state_bytes() of scratch when pl.nseg > 1.  The segment state
+// pass always walks 64-token tiles (it only accumulates K^T V); segment
+// boundaries are multiples of pl.chunk.
 int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
                              const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
-                             const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn) {
+                             const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn, int64_t ldo,
+                             bool out_reverse) {
   if (!g_encode3) {
     void *fp = nullptr;
     cudaDriverEntryPointQueryResult qr;
@@ -647,37 +1045,41 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
       return fail(AF_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", fn);
     g_encode3 = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fp);
   }
-  if (pl.nseg < 1 || pl.seg_len % C != 0 || (int64_t)pl.nseg * pl.seg_len < T ||
-      (int64_t)(pl.nseg - 1) * pl.seg_len >= T)
-    return fail(AF_ERR_ARG, "%s: bad segment plan (%d x %d tokens for T=%d)", fn, pl.nseg, pl.seg_len, T);
+  if ((pl.chunk != C && pl.chunk != c128::C) || pl.nseg < 1 || pl.seg_len % pl.chunk != 0 ||
+      (int64_t)pl.nseg * pl.seg_len < T || (int64_t)(pl.nseg - 1) * pl.seg_len >= T)
+    return fail(AF_ERR_ARG, "%s: bad segment plan (%d x %d tokens in chunks of %d for T=%d)", fn, pl.nseg,
+                pl.seg_len, pl.chunk, T);
   if (pl.nseg > 1 && !seg_states) return fail(AF_ERR_ARG, "%s: segment states scratch missing", fn);
   if ((int64_t)B * pl.nseg * H * NSL > 0x7fffffff) return fail(AF_ERR_ARG, "%s: grid too large", fn);
+  if (!out) return fail(AF_ERR_ARG, "%s: output is NULL", fn);
   const int d = H * DH;
-  CUtensorMap tm;
-  cuuint64_t dims[3] = {(cuuint64_t)(3 * d), (cuuint64_t)T, (cuuint64_t)B};
-  cuuint64_t strides[2] = {(cuuint64_t)3 * d * 2, (cuuint64_t)T * 3 * d * 2};
-  cuuint32_t box[3] = {64, (cuuint32_t)C, 1};
-  cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = g_encode3(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(qkv), dims, strides, box, es,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: tensor map encode failed (%d)", fn, (int)r);
-  // output [B][T][d] bf16 for the TMA stores: [64 tok x 64 v] boxes, the T edge clipped per stream
+  if ((ldo != 0 || out_reverse) && (pl.chunk != c128::C || (ldo != 0 && (ldo < d || ldo % 8 != 0))))
+    return fail(AF_ERR_ARG, "%s: an output stride or reversed rows need chunk 128 and a stride >= d, 8 | stride", fn);
+  CUtensorMap tm, tm128;
+  int rc = encode_qkv_map(&tm, qkv, B, T, d, C, fn);
+  if (rc) return rc;
+  const bool big = pl.chunk == c128::C;
+  if (big && (rc = encode_qkv_map(&tm128, qkv, B, T, d, c128::C, fn))) return rc;
+  // output [B][T][d] bf16 for the TMA stores of the 64-token kernel: [64 tok
+  // x 64 v] boxes, the T edge clipped per stream
   CUtensorMap tm_out = tm;
-  if (out) {
+  if (!big) {
     cuuint64_t odims[3] = {(cuuint64_t)d, (cuuint64_t)T, (cuuint64_t)B};
     cuuint64_t ostrides[2] = {(cuuint64_t)d * 2, (cuuint64_t)T * d * 2};
     cuuint32_t obox[3] = {64, (cuuint32_t)C, 1};
-    r = g_encode3(&tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, odims, ostrides, obox, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = g_encode3(&tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, odims, ostrides, obox, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: output tensor map encode failed (%d)", fn, (int)r);
   }
   ChunkParams p{B,       T,         H,       pl.nseg, pl.seg_len, gamma, state_in, state_out,
-                reinterpret_cast<__nv_bfloat16 *>(out), norm_w, sumsq, ctx->dev_err};
-  if (!out) return fail(AF_ERR_ARG, "%s: output is NULL", fn);
+                reinterpret_cast<__nv_bfloat16 *>(out), norm_w, sumsq, ctx->dev_err, ldo, out_reverse ? 1 : 0};
+  auto full_pass = [&](const ChunkParams &pp) {
+    return big ? launch_chunk128(ctx, tm128, pp, st, fn) : launch_chunkwise<false>(ctx, tm, tm_out, pp, st, fn);
+  };
   if (pl.nseg == 1) {
-    const int rc = launch_chunkwise<false>(ctx, tm, tm_out, p, st, fn);
+    rc = full_pass(p);
     mark(ctx, "chunkwise", st);
     return rc;
   }
@@ -688,7 +1090,7 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   ps.out = nullptr;
   ps.norm_w = nullptr;
   ps.sumsq = nullptr;
-  int rc = launch_chunkwise<true>(ctx, tm, tm, ps, st, fn);
+  rc = launch_chunkwise<true>(ctx, tm, tm, ps, st, fn);
   if (rc) return rc;
   mark(ctx, "chunk_state", st);
   // 2. states before each segment
@@ -701,12 +1103,13 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   mark(ctx, "chunk_scan", st);
   // 3. the full pass from each segment's state
   p.state_in = seg_states;
-  rc = launch_chunkwise<false>(ctx, tm, tm_out, p, st, fn);
+  rc = full_pass(p);
   mark(ctx, "chunkwise", st);
   return rc;
 }
 
 int chunkwise_head_dim() { return DH; }
-int chunkwise_parts() { return NSL; }
+int chunkwise_parts(int chunk) { return chunk == c128::C ? c128::PARTS : NSL; }
+int chunkwise_default_chunk(const af_ctx *ctx) { return ctx->chunk_len == c128::C ? c128::C : C; }
 
 }  // namespace af

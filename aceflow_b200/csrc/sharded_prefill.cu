@@ -149,9 +149,12 @@ int af_comm_destroy(af_ctx *ctx) {
 
 int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv_local, const uint16_t *w_o_rows,
                             const float *ret_norm_w, const float *gamma, float eps, int B, int T, int d, int H,
-                            const float *state_in, float *state_out, void *out, int out_bf16, af_stream_t stream) {
+                            const float *state_in, float *state_out, void *out, int out_bf16, int chunk,
+                            af_stream_t stream) {
   const char *fn = "af_prefill_head_sharded";
   AF_ENTER(ctx, fn);
+  int C = 0;
+  if (int rc0 = af::resolve_chunk(ctx, chunk, &C, fn)) return rc0;
   AF_REQUIRE(ctx->comm, "af_prefill_head_sharded", "no communicator: call af_comm_init first");
   const int g = ctx->comm_nranks, r = ctx->comm_rank;
   const int dh = af::chunkwise_head_dim();
@@ -175,9 +178,9 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
   if (B > 1 && (state_in || state_out)) G = 1;
   while (G > 1 && Hl % G != 0) --G;
   if (G > af_ctx::kMaxSlices) G = af_ctx::kMaxSlices;
-  const int hg = Hl / G, dlg = hg * dh, P = hg * af::chunkwise_parts();
+  const int hg = Hl / G, dlg = hg * dh, P = hg * af::chunkwise_parts(C);
   const int reserve = G > 1 && g > 1 ? ctx->comm_reserve_sms : 0;  // SMs left to the concurrent all-gather
-  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms - reserve, B, T, hg, ctx->chunk_segments);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms - reserve, B, T, hg, ctx->chunk_segments, C);
   const size_t qkv_b = align256((size_t)N * 3 * dlg * 2), o_b = align256((size_t)G * g * N * dlg * 2),
                ss_b = align256((size_t)G * g * N * P * 4), seg_b = align256(af::chunkwise_seg_state_bytes(B, hg, pl)),
                wo_b = G > 1 ? align256((size_t)dl * d * 2) : 0;
@@ -277,10 +280,12 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
 // heads = columns p*dl.. of O, W_o's natural K order).
 int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv_local, const uint16_t *w_o,
                                  const float *ret_norm_w, const float *gamma, float eps, int B, int T, int d, int H,
-                                 const float *state_in, float *state_out, void *out, int out_bf16,
+                                 const float *state_in, float *state_out, void *out, int out_bf16, int chunk,
                                  af_stream_t stream) {
   const char *fn = "af_prefill_head_sharded_rows";
   AF_ENTER(ctx, fn);
+  int C = 0;
+  if (int rc0 = af::resolve_chunk(ctx, chunk, &C, fn)) return rc0;
   AF_REQUIRE(ctx->comm, "af_prefill_head_sharded_rows", "no communicator: call af_comm_init first");
   const int g = ctx->comm_nranks, r = ctx->comm_rank;
   const int dh = af::chunkwise_head_dim();
@@ -291,7 +296,7 @@ int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t 
              "af_prefill_head_sharded_rows", "x, weights and out must be 16-byte aligned");
   AF_REQUIRE((int64_t)B * T <= 65535LL * 128, "af_prefill_head_sharded_rows", "B*T too large");
   if (B == 0 || T == 0) return AF_OK;
-  const int Hl = H / g, dl = Hl * dh, P = Hl * af::chunkwise_parts();
+  const int Hl = H / g, dl = Hl * dh, P = Hl * af::chunkwise_parts(C);
   const int64_t N = (int64_t)B * T;
   const int64_t c = (N + g - 1) / g;  // rows per rank (the last ranks may hold fewer)
   auto rows_of = [&](int s) -> int64_t {
@@ -299,7 +304,7 @@ int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t 
     return lo >= N ? 0 : (N - lo < c ? N - lo : c);
   };
   const int64_t nr = rows_of(r);
-  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, Hl, ctx->chunk_segments);
+  const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, Hl, ctx->chunk_segments, C);
   const size_t qkv_b = align256((size_t)N * 3 * dl * 2), o_b = align256((size_t)N * dl * 2),
                ss_b = align256((size_t)N * P * 4), ro_b = align256((size_t)g * c * dl * 2),
                rss_b = align256((size_t)g * c * P * 4), seg_b = align256(af::chunkwise_seg_state_bytes(B, Hl, pl));

@@ -13,7 +13,12 @@ from . import _lib
 
 F32 = torch.float32
 BF16 = torch.bfloat16
-CHUNKS = (64,)  # chunk lengths of the tensor-core chunkwise prefill
+CHUNKS = (64, 128)  # chunk lengths of the tensor-core chunkwise prefill
+
+
+def chunk_parts(chunk: int) -> int:
+    """Per-head partial sums of squares per row the chunkwise kernel writes."""
+    return 4 if chunk == 128 else 2
 
 
 def _dev(t: torch.Tensor) -> int:
@@ -208,8 +213,9 @@ def linear_bf16(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = No
 def retention_chunkwise_bf16(qkv: torch.Tensor, B: int, T: int, H: int, gamma: torch.Tensor,
                              state_in: torch.Tensor | None = None, norm_w: torch.Tensor | None = None,
                              want_state: bool = True, chunk: int = 64):
-    """Tensor-core chunkwise retention over a bf16 QKV buffer [B*T, 3*H*256].
-    Returns (out bf16 [B*T, H*256] (times norm_w), sumsq [B*T, 2H], state_out
+    """Tensor-core chunkwise retention over a bf16 QKV buffer [B*T, 3*H*256]
+    in chunks of `chunk` tokens (64 or 128).  Returns (out bf16 [B*T, H*256]
+    (times norm_w), sumsq [B*T, P*H] (P = chunk_parts(chunk)), state_out
     [B, H, 256, 256] fp32 or None)."""
     if chunk not in CHUNKS:
         raise ValueError(f"chunk must be one of {CHUNKS}, got {chunk}")
@@ -225,11 +231,37 @@ def retention_chunkwise_bf16(qkv: torch.Tensor, B: int, T: int, H: int, gamma: t
     if norm_w is not None:
         _need(norm_w, F32, "norm_w")
     out = torch.empty(B * T, d, dtype=BF16, device=qkv.device)
-    sumsq = torch.empty(B * T, 2 * H, dtype=F32, device=qkv.device)
+    sumsq = torch.empty(B * T, chunk_parts(chunk) * H, dtype=F32, device=qkv.device)
     state_out = torch.empty(B, H, 256, 256, dtype=F32, device=qkv.device) if want_state else None
     _lib.call("af_retention_chunkwise_bf16", _ctx(qkv), _p(qkv), B, T, H, _p(gamma), _p(state_in), _p(state_out),
-              _p(out), _p(norm_w), _p(sumsq), _stream(qkv))
+              _p(out), _p(norm_w), _p(sumsq), int(chunk), _stream(qkv))
     return out, sumsq, state_out
+
+
+def retention_chunkwise_backward_bf16(qkv: torch.Tensor, dout: torch.Tensor, B: int, T: int, H: int,
+                                      gamma: torch.Tensor, state_in: torch.Tensor | None = None,
+                                      want_dstate: bool = False):
+    """Gradients of retention_chunkwise_bf16's output (before norm_w) for the
+    upstream gradient dout [B*T, H*256] bf16: (dqkv bf16 [B*T, 3*H*256] =
+    dQ | dK | dV, dstate_in fp32 [B, H, 256, 256] or None)
+    (af_retention_chunkwise_backward_bf16)."""
+    _need(qkv, BF16, "qkv")
+    _need(dout, BF16, "dout")
+    d = H * 256
+    if tuple(qkv.shape) != (B * T, 3 * d) or tuple(dout.shape) != (B * T, d):
+        raise ValueError(f"qkv must be [{B * T}, {3 * d}] and dout [{B * T}, {d}] (head_dim 256)")
+    _need(gamma, F32, "gamma")
+    if gamma.numel() != H:
+        raise ValueError(f"gamma must hold {H} values")
+    if state_in is not None:
+        _need(state_in, F32, "state_in")
+        if tuple(state_in.shape) != (B, H, 256, 256):
+            raise ValueError(f"state_in must be [{B}, {H}, 256, 256]")
+    dqkv = torch.empty(B * T, 3 * d, dtype=BF16, device=qkv.device)
+    dstate = torch.empty(B, H, 256, 256, dtype=F32, device=qkv.device) if want_dstate else None
+    _lib.call("af_retention_chunkwise_backward_bf16", _ctx(qkv), _p(qkv), _p(dout), B, T, H, _p(gamma),
+              _p(state_in), _p(dqkv), _p(dstate), _stream(qkv))
+    return dqkv, dstate
 
 
 def msr_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, ret_norm_w: torch.Tensor,
@@ -258,7 +290,7 @@ def msr_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, re
     out = torch.empty(B, T, d, dtype=out_dtype, device=x.device)
     state_out = torch.empty(B, H, 256, 256, dtype=F32, device=x.device) if want_state else None
     _lib.call("af_msr_prefill_bf16", _ctx(x), _p(x), _p(w_qkv), _p(w_o), _p(ret_norm_w), _p(gamma), float(eps),
-              B, T, d, H, _p(state_in), _p(state_out), _p(out), int(out_dtype == BF16), _stream(x))
+              B, T, d, H, _p(state_in), _p(state_out), _p(out), int(out_dtype == BF16), int(chunk), _stream(x))
     return out, state_out
 
 

@@ -109,11 +109,12 @@ def row_range(n_rows: int, world: int, rank: int) -> Tuple[int, int]:
     return min(lo, n_rows), max(0, min(c, n_rows - lo))
 
 
-def chunkwise_plan(num_sms: int, batch: int, T: int, num_heads: int, nseg_req: int = 0) -> Tuple[int, int]:
-    """(segments, tokens per segment) the chunkwise prefill uses (af_chunkwise_plan;
-    host-only)."""
+def chunkwise_plan(num_sms: int, batch: int, T: int, num_heads: int, nseg_req: int = 0,
+                   chunk: int = 64) -> Tuple[int, int]:
+    """(segments, tokens per segment) the chunkwise prefill uses for chunks of
+    `chunk` tokens (af_chunkwise_plan; host-only)."""
     n, L = ctypes.c_int(), ctypes.c_int()
-    _lib.call("af_chunkwise_plan", num_sms, batch, T, num_heads, nseg_req, ctypes.byref(n), ctypes.byref(L))
+    _lib.call("af_chunkwise_plan", num_sms, batch, T, num_heads, nseg_req, chunk, ctypes.byref(n), ctypes.byref(L))
     return n.value, L.value
 
 
@@ -131,7 +132,7 @@ class HeadShardedPrefill:
                  rank instead of (g-1)/g; af_prefill_head_sharded_rows)."""
 
     def __init__(self, w_qkv, w_o, ret_norm_w, num_heads: int, eps: float = 1e-6, group=None,
-                 layout: str = "columns"):
+                 layout: str = "columns", chunk: int = 0):
         import torch
         import torch.distributed as dist
 
@@ -139,7 +140,10 @@ class HeadShardedPrefill:
 
         if layout not in ("columns", "rows"):
             raise ValueError("layout must be 'columns' or 'rows'")
+        if chunk not in (0, 64, 128):
+            raise ValueError("chunk must be 64 or 128 (0: the library's default)")
         self.layout = layout
+        self.chunk = chunk
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -213,7 +217,7 @@ class HeadShardedPrefill:
         _lib.call(entry, self._ctx, cuda_ops._p(x), cuda_ops._p(self.w_qkv_local),
                   cuda_ops._p(self.w_o_used), cuda_ops._p(self.ret_norm_w), cuda_ops._p(self.gamma), self.eps, B, T,
                   self.d, self.H, cuda_ops._p(state_in), cuda_ops._p(state_out), cuda_ops._p(out),
-                  int(out.dtype == torch.bfloat16), cuda_ops._stream(x))
+                  int(out.dtype == torch.bfloat16), self.chunk, cuda_ops._stream(x))
         return out
 
     def gather_output(self, out_local, batch: Optional[int] = None, seq_len: Optional[int] = None):

@@ -372,7 +372,8 @@ def run_ours(args):
         if args.only == "prefill":
             sec = bench_prefill(dev, args.prefill_passes, peaks, 0.0, args.chunk)
         elif args.only == "longctx":
-            sec = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier1, max1)
+            sec = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier1, max1, 0.0,
+                                args.longctx_chunk)
         else:
             sec = bench_stack(dev, peaks)
         if rank == 0:
@@ -523,7 +524,7 @@ def run_ours(args):
         line["prefill"] = bench_prefill(dev, args.prefill_passes, peaks, sub_cpu, args.chunk)
     if not args.no_longctx and HEADS_LONGCTX % world == 0:
         line["longctx"] = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier, max_over_ranks,
-                                        sub_cpu)
+                                        sub_cpu, args.longctx_chunk)
     if world == 1 and not args.no_stack:
         line["stack"] = bench_stack(dev, peaks, sub_cpu)
     if world == 1 and rank == 0 and not args.no_cpu:
@@ -707,7 +708,7 @@ LONGCTX = dict(B=1, T=65536, d=4096, H=16, C=64)
 HEADS_LONGCTX = LONGCTX["H"]
 
 
-def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_seconds=0.0):
+def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_seconds=0.0, chunk=64):
     """Head-sharded prefill of one 65536-token stream (d_model 4096, 16 heads)
     over all ranks: QKV of the rank's heads, chunkwise retention (sequence
     segments), the exchange of head outputs, output projection.  Two
@@ -729,11 +730,11 @@ def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_
     rw = torch.ones(d, device=dev)
     stream = torch.cuda.current_stream(dev)
     check_rows = [(0, 128), (T // 2 - 64, T // 2 + 64), (T - 128, T)]
-    proj, intra, inter = prefill_flops(B, T, d, H, c["C"])
+    proj, intra, inter = prefill_flops(B, T, d, H, chunk)
     total = proj + intra + inter
     res = {}
     for layout in ("columns", "rows"):
-        sp = HeadShardedPrefill(w_qkv, w_o, rw, H, EPS, layout=layout)
+        sp = HeadShardedPrefill(w_qkv, w_o, rw, H, EPS, layout=layout, chunk=chunk)
         if layout == "columns":
             out = torch.empty(B, T, d // world, device=dev)
         else:
@@ -773,7 +774,8 @@ def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_
         res[layout] = {"ms_per_pass": ms, "value": B * T / (ms / 1e3), "phases_ms_rank0": phases,
                        "max_rel_err_rank0": err, "frac_per_gpu": per_gpu_tfl / peaks["bf16_tflops"],
                        "achieved_per_gpu": per_gpu_tfl}
-    nseg, seg_len = chunkwise_plan(torch.cuda.get_device_properties(dev).multi_processor_count, B, T, H // world)
+    nseg, seg_len = chunkwise_plan(torch.cuda.get_device_properties(dev).multi_processor_count, B, T, H // world,
+                                   chunk=chunk)
     gather_bytes = (world - 1) * B * T * (d // world) * 2  # bf16 head outputs received per rank
     a2a_bytes = (world - 1) * (-(-B * T // world)) * (d // world) * 2
     col = res["columns"]
@@ -782,7 +784,7 @@ def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_
         "value": col["value"], "unit": "tok/s", "ms_per_pass": col["ms_per_pass"], "passes": passes,
         "n_gpus": world, "scaling": "strong", "dtype": "bf16 (fp32 accumulate)",
         "config": {"workload": "MultiScaleRetention prefill, d_model=4096, 16 heads (head_dim 256), B=1, T=65536, "
-                               f"chunk {c['C']}", "parallelism": f"head-sharded x{world}, {H // world} heads per GPU, "
+                               f"chunk {chunk}", "parallelism": f"head-sharded x{world}, {H // world} heads per GPU, "
                                                              "one NCCL all-gather before W_o",
                    "segments": {"nseg": nseg, "seg_len": seg_len},
                    "l2": "inputs larger than L2 (x 512 MiB, qkv per GPU >= 192 MiB)"},
@@ -873,6 +875,7 @@ def main():
     ap.add_argument("--sub-cpu-seconds", type=float, default=4.0,
                     help="seconds of each CPU baseline of the prefill, long-context and stack workloads (N=1)")
     ap.add_argument("--chunk", type=int, default=64, help="chunk length of the prefill workload")
+    ap.add_argument("--longctx-chunk", type=int, default=64, help="chunk length of the long-context workload")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -74,6 +74,8 @@ int af_selftest_bounded_wait(af_ctx *ctx, int64_t limit_ns, af_stream_t stream);
  *   "allow_split_k"      0/1   small-M GEMMs may split K with fp32 atomics (default 1;
  *                              0 makes results bitwise reproducible run to run)
  *   "decode_slice_rows"  >= 0  batch slices of af_msr_decode_step_f32 (default 0: none)
+ *   "chunk_len"          64/128 tokens per chunk of the chunkwise prefill when a call passes
+ *                              chunk 0, and of af_decoder_layer_prefill (default 64)
  *   "chunkwise_segments" >= 0  sequence segments per stream in the chunkwise prefill
  *                              (default 0: enough to put one CTA on every SM; 1: none)
  *   "sharded_head_groups" 0..8 head groups af_prefill_head_sharded pipelines against
@@ -255,29 +257,49 @@ int af_msr_decode_step_f32_noalloc(const float *x, float *state, const float *ga
                                    af_stream_t stream);
 
 /* Chunkwise-parallel retention core on the bf16 tensor cores (head_dim 256,
- * chunk 64).  The parallel form (aceflow/nn/retention.py:51-61) computed
- * chunk by chunk with the carried state of recurrence.rs:28-39.
+ * chunks of `chunk` = 64 or 128 tokens; 0 takes the context's "chunk_len").
+ * The parallel form (aceflow/nn/retention.py:51-61) computed chunk by chunk
+ * with the carried state of recurrence.rs:28-39; the result does not depend
+ * on the chunk length beyond rounding.
  *   qkv       [batch*T][3*H*256] bf16: q | k | v per row (a QKV projection).
  *   state_in  [batch][H][256][256] fp32 initial state, or NULL for zeros.
  *   state_out same layout, the state after the last token, or NULL.
  *   out       [batch*T][H*256] bf16: retention output times norm_w (or 1).
- *   sumsq     [batch*T][2*H] fp32 partial sums of the unscaled output's
- *             squares (row r's RMS is sqrt(sum(sumsq[r]) / d)), or NULL.
+ *   sumsq     [batch*T][P*H] fp32 partial sums of the unscaled output's
+ *             squares (row r's RMS is sqrt(sum(sumsq[r]) / d)), or NULL;
+ *             P = 2 for chunk 64, 4 for chunk 128.
  * When batch*H*2 CTAs cannot fill the GPU, each stream is cut into sequence
  * segments (af_chunkwise_plan): a state pass, a scan over segment states
  * and the full pass from each segment's state; workspace
  * batch*nseg*H*256 KiB when nseg > 1. */
 int af_retention_chunkwise_bf16(af_ctx *ctx, const uint16_t *qkv, int batch, int T, int num_heads,
                                 const float *gamma, const float *state_in, float *state_out,
-                                uint16_t *out, const float *norm_w, float *sumsq, af_stream_t stream);
+                                uint16_t *out, const float *norm_w, float *sumsq, int chunk, af_stream_t stream);
+
+/* Backward of af_retention_chunkwise_bf16 for training: given the forward's
+ * qkv [batch*T][3*H*256] bf16 (q | k | v), its initial state (state_in,
+ * [batch][H][256][256] fp32, or NULL for zeros) and the gradient of the
+ * retention output dout [batch*T][H*256] bf16 (the output before norm_w),
+ * writes dqkv [batch*T][3*H*256] bf16 (dQ | dK | dV) and, if dstate_in is
+ * non-NULL, the gradient of the initial state [batch][H][256][256] fp32.
+ * The loss is taken to depend on the outputs only (not on the final state).
+ * Each gradient is a retention form of its own (dQ = Retention(dO, V, K)
+ * from S_0^T; dK and dV are Retention(V, dO, Q) and Retention(K, Q, dO) over
+ * reversed time), so three passes of the 128-token tensor-core kernel do
+ * the work; bf16 results, fp32 accumulation.  No reference counterpart: the
+ * reference trains through PyTorch only (aceflow/trainers).  Workspace
+ * batch*T*6*d bytes (+ batch*H*256 KiB with a state, + segment states). */
+int af_retention_chunkwise_backward_bf16(af_ctx *ctx, const uint16_t *qkv, const uint16_t *dout, int batch, int T,
+                                         int num_heads, const float *gamma, const float *state_in, uint16_t *dqkv,
+                                         float *dstate_in, af_stream_t stream);
 
 /* The sequence segmentation the chunkwise prefill uses for `batch` streams
  * of T tokens and `num_heads` heads on a GPU with num_sms SMs (host-only,
  * needs no GPU).  nseg_req > 0 forces that many segments (capped by the
  * chunk count); 0 picks enough for one CTA per SM.  Outputs the segment
- * count and length (a multiple of 64 tokens; the last segment may be
- * shorter). */
-int af_chunkwise_plan(int num_sms, int batch, int T, int num_heads, int nseg_req, int *nseg,
+ * count and length (a multiple of `chunk` tokens, 64 or 128, 0 = 64; the
+ * last segment may be shorter). */
+int af_chunkwise_plan(int num_sms, int batch, int T, int num_heads, int nseg_req, int chunk, int *nseg,
                       int *seg_len);
 
 /* MultiScaleRetention forward over a prompt on the bf16 tensor cores:
@@ -286,12 +308,12 @@ int af_chunkwise_plan(int num_sms, int batch, int T, int num_heads, int nseg_req
  * for bf16 inputs (fp32 accumulation, tolerance 2e-2) and the token-serial
  * AceEngine.prefill_recurrent (aceflow-core/src/cpu/mod.rs:547-587).
  *   w_qkv [3d][d] bf16 (rows q, k, v); w_o [d][d] bf16; ret_norm_w [d] fp32;
- *   state_in/state_out as for af_retention_chunkwise_bf16.
- * head_dim must be 256.  Workspace: batch*T*(8*d + 8*H) bytes. */
+ *   state_in/state_out and chunk as for af_retention_chunkwise_bf16.
+ * head_dim must be 256.  Workspace: batch*T*(8*d + 16*H) bytes. */
 int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv, const uint16_t *w_o,
                         const float *ret_norm_w, const float *gamma, float eps, int batch, int T,
                         int d_model, int num_heads, const float *state_in, float *state_out,
-                        void *out, int out_bf16, af_stream_t stream);
+                        void *out, int out_bf16, int chunk, af_stream_t stream);
 
 /* ------------------------------------------------------- decoder stack */
 /* Weights of one decoder layer (AceEngine's LayerWeights,
@@ -403,7 +425,7 @@ int af_comm_destroy(af_ctx *ctx);
 int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv_local,
                             const uint16_t *w_o_rows, const float *ret_norm_w, const float *gamma,
                             float eps, int batch, int T, int d_model, int num_heads,
-                            const float *state_in, float *state_out, void *out, int out_bf16,
+                            const float *state_in, float *state_out, void *out, int out_bf16, int chunk,
                             af_stream_t stream);
 
 /* The same layer, row-sharded: the exchange is an all-to-all (ncclSend /
@@ -420,7 +442,7 @@ int af_prefill_head_sharded(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qk
 int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv_local, const uint16_t *w_o,
                                  const float *ret_norm_w, const float *gamma, float eps, int batch, int T,
                                  int d_model, int num_heads, const float *state_in, float *state_out, void *out,
-                                 int out_bf16, af_stream_t stream);
+                                 int out_bf16, int chunk, af_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -328,6 +328,33 @@ def retention_chunkwise64(q, k, v, gamma, chunk: int, state0=None):
     return out, S
 
 
+def retention_backward64(q, k, v, gamma, dout, state0=None):
+    """Gradients of the parallel form O = (Q K^T * D) V (+ diag(gamma^(t+1)) Q S_0)
+    in float64, closed form: with A = (dO V^T) * D,
+        dQ = A K + diag(gamma^(t+1)) dO S_0^T,   dK = A^T Q,
+        dV = ((Q K^T) * D)^T dO,                 dS_0 = sum_t gamma^(t+1) q_t^T do_t.
+    No reference counterpart (the reference has no backward); this is the
+    derivative of retention.py:51-61.  q, k, v, dout: [B, H, T, dh]."""
+    q, k, v, do = (np.asarray(a, np.float64) for a in (q, k, v, dout))
+    B, H, T, dh = q.shape
+    idx = np.arange(T)
+    dist = idx[:, None] - idx[None, :]
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(k), np.zeros_like(v)
+    dS = np.zeros((B, H, dh, dh))
+    for h in range(H):
+        g = float(gamma[h])
+        D = np.where(dist >= 0, g ** np.maximum(dist, 0), 0.0)
+        A = np.matmul(do[:, h], v[:, h].transpose(0, 2, 1)) * D
+        dq[:, h] = np.matmul(A, k[:, h])
+        dk[:, h] = np.matmul(A.transpose(0, 2, 1), q[:, h])
+        dv[:, h] = np.matmul((np.matmul(q[:, h], k[:, h].transpose(0, 2, 1)) * D).transpose(0, 2, 1), do[:, h])
+        w = g ** (idx + 1.0)
+        if state0 is not None:
+            dq[:, h] += w[None, :, None] * np.matmul(do[:, h], np.asarray(state0, np.float64)[:, h].transpose(0, 2, 1))
+        dS[:, h] = np.matmul((q[:, h] * w[None, :, None]).transpose(0, 2, 1), do[:, h])
+    return dq, dk, dv, dS
+
+
 def msr_forward64(x, w_q, w_k, w_v, w_o, num_heads, ret_norm_w=None, eps=1e-6):
     """The Python module's forward (retention.py:44-66) in float64, through the
     chunkwise identity; used as the exact target for low-precision paths."""

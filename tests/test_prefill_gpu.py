@@ -33,14 +33,16 @@ def _core_ref(qkv, B, T, H, state0=None):
     return o.transpose(0, 2, 1, 3).reshape(B * T, d), S
 
 
-@pytest.mark.parametrize("B,T,H", [(1, 64, 1), (2, 100, 2), (1, 257, 2), (3, 200, 1), (1, 1000, 8)])
-def test_chunkwise_core_matches_oracle(dev, B, T, H):
+@pytest.mark.parametrize("chunk", [64, 128])
+@pytest.mark.parametrize("B,T,H", [(1, 64, 1), (2, 100, 2), (1, 257, 2), (3, 200, 1), (1, 1000, 8), (2, 128, 1),
+                                   (1, 129, 1)])
+def test_chunkwise_core_matches_oracle(dev, B, T, H, chunk):
     from aceflow_b200 import _lib, cuda_ops
 
     qkv = _qkv(B, T, H, B * 1000 + T + H, dev, scale=0.5)
     gamma = cuda_ops.gammas(H, dev)
     w = (1 + 0.1 * torch.randn(H * 256, device=dev))
-    out, ss, st = cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=w)
+    out, ss, st = cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=w, chunk=chunk)
     torch.cuda.synchronize()
     assert _lib.check_device(0) == 0
     ref, S = _core_ref(qkv, B, T, H)
@@ -51,7 +53,8 @@ def test_chunkwise_core_matches_oracle(dev, B, T, H):
     assert rel_err(rs, (ref * ref).sum(1)) < TOL
 
 
-def test_chunkwise_state_carry(dev):
+@pytest.mark.parametrize("chunk", [64, 128])
+def test_chunkwise_state_carry(dev, chunk):
     """Two calls chained through the state equal one call over the whole
     sequence (and a non-zero initial state is honoured)."""
     from aceflow_b200 import cuda_ops
@@ -59,20 +62,21 @@ def test_chunkwise_state_carry(dev):
     B, H, T1, T2 = 2, 2, 130, 70
     qkv = _qkv(B, T1 + T2, H, 7, dev, scale=0.5)
     gamma = cuda_ops.gammas(H, dev)
-    full, _, S_full = cuda_ops.retention_chunkwise_bf16(qkv, B, T1 + T2, H, gamma)
+    full, _, S_full = cuda_ops.retention_chunkwise_bf16(qkv, B, T1 + T2, H, gamma, chunk=chunk)
     q3 = qkv.view(B, T1 + T2, -1)
     a = q3[:, :T1].contiguous().view(B * T1, -1)
     b = q3[:, T1:].contiguous().view(B * T2, -1)
-    o1, _, S1 = cuda_ops.retention_chunkwise_bf16(a, B, T1, H, gamma)
-    o2, _, S2 = cuda_ops.retention_chunkwise_bf16(b, B, T2, H, gamma, state_in=S1)
+    o1, _, S1 = cuda_ops.retention_chunkwise_bf16(a, B, T1, H, gamma, chunk=chunk)
+    o2, _, S2 = cuda_ops.retention_chunkwise_bf16(b, B, T2, H, gamma, state_in=S1, chunk=chunk)
     f = full.float().view(B, T1 + T2, -1)
     assert rel_err(o1.float().view(B, T1, -1).cpu().numpy(), f[:, :T1].cpu().numpy()) < 1e-2
     assert rel_err(o2.float().view(B, T2, -1).cpu().numpy(), f[:, T1:].cpu().numpy()) < TOL
     assert rel_err(S2.cpu().numpy(), S_full.cpu().numpy()) < TOL
 
 
+@pytest.mark.parametrize("chunk", [64, 128])
 @pytest.mark.parametrize("B,T,H", [(2, 96, 2), (1, 300, 8)])
-def test_msr_prefill_matches_float64(dev, B, T, H):
+def test_msr_prefill_matches_float64(dev, B, T, H, chunk):
     from aceflow_b200 import _lib, cuda_ops
 
     d = H * 256
@@ -82,7 +86,8 @@ def test_msr_prefill_matches_float64(dev, B, T, H):
     rw = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
     tb = lambda a: torch.from_numpy(a).to(dev).bfloat16()  # noqa: E731
     xb, wqkv, wob = tb(x), tb(np.concatenate([wq, wk, wv])), tb(wo)
-    out, st = cuda_ops.msr_prefill_bf16(xb, wqkv, wob, torch.from_numpy(rw).to(dev), cuda_ops.gammas(H, dev), 1e-6)
+    out, st = cuda_ops.msr_prefill_bf16(xb, wqkv, wob, torch.from_numpy(rw).to(dev), cuda_ops.gammas(H, dev), 1e-6,
+                                        chunk=chunk)
     torch.cuda.synchronize()
     assert _lib.check_device(0) == 0
     f = lambda t: t.float().cpu().numpy().astype(np.float64)  # noqa: E731
@@ -116,8 +121,9 @@ def test_prefill_then_decode_continues_the_state(dev):
     assert rel_err(out.cpu().numpy(), ref) < TOL
 
 
+@pytest.mark.parametrize("chunk", [64, 128])
 @pytest.mark.parametrize("nseg", [1, 3, 0])
-def test_chunkwise_segments_match_single_pass(dev, nseg):
+def test_chunkwise_segments_match_single_pass(dev, nseg, chunk):
     """Sequence segments (state pass + scan + full pass) give the recurrence's
     result: forced 1 (single pass), 3 (ragged last segment) and auto."""
     from aceflow_b200 import _lib, cuda_ops
@@ -129,7 +135,7 @@ def test_chunkwise_segments_match_single_pass(dev, nseg):
     s0 = 0.05 * torch.randn(B, H, 256, 256, generator=g, device=dev)
     _lib.set_option(0, "chunkwise_segments", nseg)
     try:
-        out, ss, st = cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, state_in=s0)
+        out, ss, st = cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, state_in=s0, chunk=chunk)
         torch.cuda.synchronize()
     finally:
         _lib.set_option(0, "chunkwise_segments", 0)
@@ -162,8 +168,9 @@ def test_gemm_bf16_kblocked_operand_and_blocked_parts(dev):
     assert rel_err(plain.cpu().numpy(), ref.cpu().numpy()) < 1e-5
 
 
-@pytest.mark.parametrize("groups,layout", [(0, "columns"), (2, "columns"), (0, "rows")])
-def test_head_sharded_prefill_single_rank(dev, groups, layout):
+@pytest.mark.parametrize("groups,layout,chunk", [(0, "columns", 64), (2, "columns", 64), (0, "rows", 64),
+                                                 (0, "columns", 128), (0, "rows", 128)])
+def test_head_sharded_prefill_single_rank(dev, groups, layout, chunk):
     """af_prefill_head_sharded (columns: all-gather; in one piece or as two
     head groups) and af_prefill_head_sharded_rows (rows: all-to-all) on a
     1-rank communicator equal the float64 layer and af_msr_prefill_bf16."""
@@ -178,7 +185,7 @@ def test_head_sharded_prefill_single_rank(dev, groups, layout):
     wqkv = tb((0.02 * rng.standard_normal((3 * d, d))).astype(np.float32))
     wo = tb((0.02 * rng.standard_normal((d, d))).astype(np.float32))
     rw = torch.from_numpy((1 + 0.1 * rng.standard_normal(d)).astype(np.float32)).to(dev)
-    sp = HeadShardedPrefill(wqkv, wo, rw, H, 1e-6, layout=layout)
+    sp = HeadShardedPrefill(wqkv, wo, rw, H, 1e-6, layout=layout, chunk=chunk)
     _lib.set_option(0, "sharded_head_groups", groups)
     try:
         st = torch.empty(B, H, 256, 256, device=dev)
@@ -282,3 +289,53 @@ def test_module_forward_chunkwise_needs_head_dim_256(dev):
         m.forward_chunkwise(af.Tensor(np.zeros((1, 8, 64), np.float32), device="cuda:0"))
     with pytest.raises(ValueError, match="chunk"):
         _module(512, 2, 1).forward_chunkwise(af.Tensor(np.zeros((1, 8, 512), np.float32), device="cuda:0"), chunk=48)
+
+
+# ---- backward of the chunkwise form ---------------------------------------
+@pytest.mark.parametrize("B,T,H,with_state", [(1, 128, 1, False), (2, 200, 2, True), (1, 777, 2, True),
+                                              (3, 65, 1, False)])
+def test_chunkwise_backward_matches_float64_gradients(dev, B, T, H, with_state):
+    """dQ, dK, dV and the initial state's gradient of the chunkwise kernel
+    (three passes of the 128-token kernel, two over reversed time) against
+    the float64 closed form of the parallel form's gradients; 2e-2 each."""
+    from aceflow_b200 import _lib, cuda_ops
+
+    d = H * 256
+    qkv = _qkv(B, T, H, 300 + T, dev, scale=0.5)
+    g = torch.Generator(device=dev).manual_seed(301)
+    dout = torch.randn(B * T, d, generator=g, device=dev).bfloat16()
+    s0 = 0.05 * torch.randn(B, H, 256, 256, generator=g, device=dev) if with_state else None
+    gamma = cuda_ops.gammas(H, dev)
+    dqkv, dS = cuda_ops.retention_chunkwise_backward_bf16(qkv, dout, B, T, H, gamma, state_in=s0, want_dstate=True)
+    torch.cuda.synchronize()
+    assert _lib.check_device(0) == 0
+    a = qkv.float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256)
+    q, k, v = (a[:, :, i].transpose(0, 2, 1, 3) for i in range(3))
+    do = dout.float().cpu().numpy().astype(np.float64).reshape(B, T, H, 256).transpose(0, 2, 1, 3)
+    ref = R.retention_backward64(q, k, v, R.gammas(H), do, None if s0 is None else s0.cpu().numpy())
+    got = dqkv.float().cpu().numpy().reshape(B, T, 3, H, 256)
+    for i, name in enumerate(("dq", "dk", "dv")):
+        assert rel_err(got[:, :, i].transpose(0, 2, 1, 3), ref[i]) < TOL, name
+    assert rel_err(dS.cpu().numpy(), ref[3]) < TOL
+
+
+def test_chunkwise_backward_matches_finite_differences_of_the_forward(dev):
+    """<dO, O(q + e dq)> changes by e <dO, dQ . dq> to first order: the
+    gradient agrees with the forward kernel itself (directional derivative,
+    centred differences in float64 on the oracle forward)."""
+    from aceflow_b200 import cuda_ops
+
+    B, T, H = 1, 300, 1
+    qkv = _qkv(B, T, H, 311, dev, scale=0.5)
+    dout = torch.randn(B * T, 256, device=dev).bfloat16()
+    dqkv, _ = cuda_ops.retention_chunkwise_backward_bf16(qkv, dout, B, T, H, cuda_ops.gammas(H, dev))
+    a = qkv.float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256).transpose(2, 0, 3, 1, 4)
+    do = dout.float().cpu().numpy().astype(np.float64).reshape(B, T, H, 256).transpose(0, 2, 1, 3)
+    rng = np.random.default_rng(5)
+    dirs = rng.standard_normal(a.shape)
+    eps = 1e-3
+    f = lambda x: float((R.retention_chunkwise64(x[0], x[1], x[2], R.gammas(H), 64)[0] * do).sum())  # noqa: E731
+    fd = (f(a + eps * dirs) - f(a - eps * dirs)) / (2 * eps)
+    g = dqkv.float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256).transpose(2, 0, 3, 1, 4)
+    an = float((g * dirs).sum())
+    assert abs(an - fd) <= 2e-2 * abs(fd)
