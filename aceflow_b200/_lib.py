@@ -64,6 +64,10 @@ SIGNATURES = {
     "af_retention_chunkwise_bf16": [_vp, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp],
     "af_msr_prefill_bf16": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp],
     "af_pack_gate_up": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "af_group_norm_gate": [_vp, _vp, _i, _vp, _i, _vp, _vp, _vp, _i, _i64, _i, _i, _f, _vp],
+    "af_msr_gated_decode_step_f32": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _vp, _vp],
+    "af_msr_gated_prefill_bf16": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i,
+                                  _vp],
     "af_decoder_layer_decode": [_vp, _vp, _i, _vp, _vp, _i64, _vp, _f, _i, _i, _i, _i, _vp],
     "af_decoder_layer_prefill": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _i, _i, _i, _vp],
     "af_embed_gather": [_vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _vp],

@@ -294,6 +294,76 @@ def msr_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, re
     return out, state_out
 
 
+def group_norm_gate(o: torch.Tensor, g: torch.Tensor, num_heads: int, gn_w: torch.Tensor | None = None,
+                    gn_b: torch.Tensor | None = None, eps: float = 1e-6, out_dtype=None) -> torch.Tensor:
+    """swish(g) * GroupNorm_H(o) over rows [..., d] (af_group_norm_gate);
+    o and g fp32 or bf16; output in out_dtype (default o's)."""
+    if o.shape != g.shape:
+        raise ValueError("o and g must have one shape")
+    for n, t in (("o", o), ("g", g)):
+        if t.dtype not in (F32, BF16) or not t.is_contiguous():
+            raise ValueError(f"{n}: expected a contiguous fp32 or bf16 tensor")
+    d = o.shape[-1]
+    for n, t in (("gn_w", gn_w), ("gn_b", gn_b)):
+        if t is not None:
+            _need(t, F32, n)
+            if t.numel() != d:
+                raise ValueError(f"{n} must hold {d} values")
+    out_dtype = o.dtype if out_dtype is None else out_dtype
+    y = torch.empty(o.shape, dtype=out_dtype, device=o.device)
+    _lib.call("af_group_norm_gate", _ctx(o), _p(o), int(o.dtype == BF16), _p(g), int(g.dtype == BF16), _p(gn_w),
+              _p(gn_b), _p(y), int(out_dtype == BF16), o.numel() // d if d else 0, d, num_heads, float(eps), _stream(o))
+    return y
+
+
+def msr_gated_decode_step(x: torch.Tensor, state: torch.Tensor, gamma: torch.Tensor, w_qkv: torch.Tensor,
+                          w_g: torch.Tensor, w_o: torch.Tensor, gn_w: torch.Tensor | None, gn_b: torch.Tensor | None,
+                          eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One decode step of the gated layer (af_msr_gated_decode_step_f32): x [B, d] fp32."""
+    B, d = x.shape
+    H = state.shape[1]
+    for n, t in (("x", x), ("state", state), ("gamma", gamma), ("w_qkv", w_qkv), ("w_g", w_g), ("w_o", w_o)):
+        _need(t, F32, n)
+    if tuple(state.shape) != (B, H, d // H, d // H):
+        raise ValueError(f"state shape {tuple(state.shape)} != {(B, H, d // H, d // H)}")
+    if tuple(w_qkv.shape) != (3 * d, d) or tuple(w_g.shape) != (d, d) or tuple(w_o.shape) != (d, d):
+        raise ValueError("w_qkv must be [3d, d], w_g and w_o [d, d]")
+    if out is None:
+        out = torch.empty(B, d, dtype=F32, device=x.device)
+    _lib.call("af_msr_gated_decode_step_f32", _ctx(x), _p(x), _p(state), _p(gamma), _p(w_qkv), _p(w_g), _p(w_o),
+              _p(gn_w), _p(gn_b), float(eps), B, d, H, _p(out), _stream(x))
+    return out
+
+
+def msr_gated_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_g: torch.Tensor, w_o: torch.Tensor,
+                           gn_w: torch.Tensor | None, gn_b: torch.Tensor | None, gamma: torch.Tensor, eps: float,
+                           state_in: torch.Tensor | None = None, out_dtype=torch.float32, want_state: bool = True,
+                           chunk: int = 64):
+    """The gated layer over a bf16 prompt x [B, T, d] on the tensor cores
+    (af_msr_gated_prefill_bf16): (out [B, T, d], final state or None)."""
+    if chunk not in CHUNKS:
+        raise ValueError(f"chunk must be one of {CHUNKS}, got {chunk}")
+    _need(x, BF16, "x")
+    B, T, d = x.shape
+    H = d // 256
+    if d % 256:
+        raise ValueError(f"the tensor-core prefill needs head_dim 256 (d_model {d})")
+    for n, t in (("w_qkv", w_qkv), ("w_g", w_g), ("w_o", w_o)):
+        _need(t, BF16, n)
+    if tuple(w_qkv.shape) != (3 * d, d) or tuple(w_g.shape) != (d, d) or tuple(w_o.shape) != (d, d):
+        raise ValueError("w_qkv must be [3d, d], w_g and w_o [d, d]")
+    if state_in is not None:
+        _need(state_in, F32, "state_in")
+        if tuple(state_in.shape) != (B, H, 256, 256):
+            raise ValueError(f"state_in must be [{B}, {H}, 256, 256]")
+    out = torch.empty(B, T, d, dtype=out_dtype, device=x.device)
+    state_out = torch.empty(B, H, 256, 256, dtype=F32, device=x.device) if want_state else None
+    _lib.call("af_msr_gated_prefill_bf16", _ctx(x), _p(x), _p(w_qkv), _p(w_g), _p(w_o), _p(gn_w), _p(gn_b),
+              _p(gamma), float(eps), B, T, d, H, _p(state_in), _p(state_out), _p(out), int(out_dtype == BF16),
+              int(chunk), _stream(x))
+    return out, state_out
+
+
 def msr_decode_step_noalloc(x: torch.Tensor, state: torch.Tensor, gamma: torch.Tensor, w_qkv: torch.Tensor,
                             w_o: torch.Tensor, ret_norm_w: torch.Tensor, eps: float,
                             out: torch.Tensor | None = None) -> torch.Tensor:

@@ -29,6 +29,13 @@ of two paths:
     3xTF32 W_o GEMM; 1e-4 of the reference), which any head_dim can take.
 The output's dtype is the input's.  forward_recurrent is one fused fp32
 decode step (af_msr_decode_step_f32_split).
+
+gated=True (an extension; the reference has no gate): RetNet's layer as
+published (Sun et al. 2023, eq. 8), out = (swish(x W_g^T) * GroupNorm_H(O))
+W_o^T with O the reference's retention; the group norm (per head: mean 0,
+variance 1, eps of ret_norm, then group_norm_weight / group_norm_bias) takes
+the place of ret_norm.  w_g is drawn after the reference's four weights, so
+a seeded gated module has the same w_q, w_k, w_v, w_o as an ungated one.
 """
 from __future__ import annotations
 
@@ -48,7 +55,7 @@ DEFAULT_CHUNK = 64  # tokens per chunk of the chunkwise prefill
 class MultiScaleRetention(Module):
     """Multi-Scale Retention (MSR) layer."""
 
-    def __init__(self, d_model: int, num_heads: int, *, prefill_dtype: Optional[str] = None):
+    def __init__(self, d_model: int, num_heads: int, *, prefill_dtype: Optional[str] = None, gated: bool = False):
         super().__init__()
         if prefill_dtype not in (None, "float32", "bfloat16"):
             raise ValueError("prefill_dtype must be None, 'float32' or 'bfloat16'")
@@ -64,6 +71,11 @@ class MultiScaleRetention(Module):
         self.w_v = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
         self.w_o = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
         self.ret_norm = RMSNorm(d_model)
+        self.gated = bool(gated)
+        if self.gated:
+            self.w_g = Parameter(Tensor(np.random.uniform(-k, k, (d_model, d_model)).astype(np.float32)))
+            self.group_norm_weight = Parameter(Tensor(np.ones(d_model, np.float32)))
+            self.group_norm_bias = Parameter(Tensor(np.zeros(d_model, np.float32)))
         # "bfloat16": fp32 prompts on CUDA also take the tensor-core chunkwise
         # prefill (2e-2 tolerance); None/"float32": they take the exact path
         self.prefill_dtype = prefill_dtype
@@ -80,7 +92,9 @@ class MultiScaleRetention(Module):
             dev = self.w_q.torch.device
             w_qkv = torch.cat([self.w_q.torch, self.w_k.torch, self.w_v.torch], 0).contiguous()
             self._dev = dict(w_qkv=w_qkv, w_o=self.w_o.torch, gamma=cuda_ops.gammas(self.num_heads, dev))
-            if self.head_dim in (64, 128, 256):
+            if self.gated:
+                self._dev["w_g"] = self.w_g.torch.contiguous()
+            elif self.head_dim in (64, 128, 256):
                 # decode reads head-major, tf32-split weights (exact: hi + lo == w), prepared once here
                 self._dev["w_qkv_split"], self._dev["w_o_split"] = cuda_ops.prepare_decode_weights(
                     w_qkv, self.w_o.torch, self.num_heads)
@@ -105,7 +119,23 @@ class MultiScaleRetention(Module):
 
             p["w_qkv_bf16"] = cuda_ops.to_bf16(p["w_qkv"])
             p["w_o_bf16"] = cuda_ops.to_bf16(p["w_o"].contiguous())
+            if self.gated:
+                p["w_g_bf16"] = cuda_ops.to_bf16(p["w_g"])
         return p
+
+    def _gn_params(self):
+        return self.group_norm_weight.torch, self.group_norm_bias.torch
+
+    def _gate_numpy(self, o: np.ndarray, x: np.ndarray) -> np.ndarray:
+        """swish(x W_g^T) * GroupNorm_H(o) on the host (fp32 numpy)."""
+        H = self.num_heads
+        oh = o.reshape(*o.shape[:-1], H, self.head_dim)
+        mean = oh.mean(-1, keepdims=True)
+        var = ((oh - mean) ** 2).mean(-1, keepdims=True)
+        y = ((oh - mean) / np.sqrt(var + self.ret_norm.eps)).reshape(o.shape)
+        y = y * self.group_norm_weight.numpy() + self.group_norm_bias.numpy()
+        g = x @ self.w_g.numpy().T
+        return ((g / (1.0 + np.exp(-g))) * y).astype(np.float32)
 
     def init_state(self, batch: int, device=None) -> Tensor:
         """Zero recurrent state [batch, H, dh, dh] fp32 (AceEngine.reset_memory,
@@ -137,6 +167,8 @@ class MultiScaleRetention(Module):
             decay[h] = np.where(dist >= 0, self.gamma[h] ** dist, 0.0)
         out = np.matmul(np.matmul(q, k.transpose(0, 1, 3, 2)) * decay[None], v)
         out = out.transpose(0, 2, 1, 3).reshape(b, n, d)
+        if self.gated:
+            return Tensor(np.matmul(self._gate_numpy(out, arr), self.w_o.numpy().T), x.device)
         normed = self.ret_norm(Tensor(out, x.device))
         return Tensor(np.matmul(normed.numpy(), self.w_o.numpy().T), x.device)
 
@@ -176,9 +208,15 @@ class MultiScaleRetention(Module):
             st_in = state.torch
             if st_in.dtype != torch.float32 or not st_in.is_contiguous() or st_in.device != xt.device:
                 raise ValueError("state must be a contiguous fp32 tensor on the input's device")
-        out, st = cuda_ops.msr_prefill_bf16(xb, p["w_qkv_bf16"], p["w_o_bf16"], self.ret_norm.weight.torch,
-                                            p["gamma"], self.ret_norm.eps, state_in=st_in, out_dtype=xt.dtype,
-                                            want_state=want_state, chunk=chunk)
+        if self.gated:
+            gw, gb = self._gn_params()
+            out, st = cuda_ops.msr_gated_prefill_bf16(xb, p["w_qkv_bf16"], p["w_g_bf16"], p["w_o_bf16"], gw, gb,
+                                                      p["gamma"], self.ret_norm.eps, state_in=st_in,
+                                                      out_dtype=xt.dtype, want_state=want_state, chunk=chunk)
+        else:
+            out, st = cuda_ops.msr_prefill_bf16(xb, p["w_qkv_bf16"], p["w_o_bf16"], self.ret_norm.weight.torch,
+                                                p["gamma"], self.ret_norm.eps, state_in=st_in, out_dtype=xt.dtype,
+                                                want_state=want_state, chunk=chunk)
         return Tensor._wrap(out, x.device), (Tensor._wrap(st, x.device) if st is not None else None)
 
     def _prefill_exact(self, x: Tensor, state: Optional[Tensor]) -> Tuple[Tensor, Tensor]:
@@ -195,7 +233,12 @@ class MultiScaleRetention(Module):
         st = state.torch
         qkv = cuda_ops.linear(x.torch.reshape(B * T, d), p["w_qkv"]).reshape(B, T, 3 * d)
         o = cuda_ops.retention_scan(st, p["gamma"], qkv[:, :, :d], qkv[:, :, d:2 * d], qkv[:, :, 2 * d:])
-        normed = cuda_ops.rms_norm(o, self.ret_norm.weight.torch, self.ret_norm.eps)
+        if self.gated:
+            g = cuda_ops.linear(x.torch.reshape(B * T, d), p["w_g"]).reshape(B, T, d)
+            gw, gb = self._gn_params()
+            normed = cuda_ops.group_norm_gate(o, g, self.num_heads, gw, gb, self.ret_norm.eps)
+        else:
+            normed = cuda_ops.rms_norm(o, self.ret_norm.weight.torch, self.ret_norm.eps)
         out = cuda_ops.linear(normed, p["w_o"])
         return Tensor._wrap(out, x.device), state
 
@@ -208,7 +251,11 @@ class MultiScaleRetention(Module):
             from .. import cuda_ops
 
             p = self._packed(x_t)
-            if "w_qkv_split" in p:
+            if self.gated:
+                gw, gb = self._gn_params()
+                out = cuda_ops.msr_gated_decode_step(x_t.torch.contiguous(), state.torch, p["gamma"], p["w_qkv"],
+                                                     p["w_g"], p["w_o"], gw, gb, self.ret_norm.eps)
+            elif "w_qkv_split" in p:
                 out = cuda_ops.msr_decode_step_split(x_t.torch.contiguous(), state.torch, p["gamma"], p["w_qkv_split"],
                                                      p["w_o_split"], self.ret_norm.weight.torch, self.ret_norm.eps)
             else:
@@ -223,5 +270,8 @@ class MultiScaleRetention(Module):
         S = state.numpy()
         S = self.gamma[None, :, None, None] * S + k[:, :, :, None] * v[:, :, None, :]
         o = np.einsum("bhi,bhij->bhj", q, S).reshape(B, d).astype(np.float32)
+        if self.gated:
+            return (Tensor(self._gate_numpy(o, arr) @ self.w_o.numpy().T, x_t.device),
+                    Tensor(S.astype(np.float32), x_t.device))
         normed = self.ret_norm(Tensor(o, x_t.device))
         return Tensor(normed.numpy() @ self.w_o.numpy().T, x_t.device), Tensor(S.astype(np.float32), x_t.device)

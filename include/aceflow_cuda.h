@@ -315,6 +315,35 @@ int af_msr_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv, c
                         int d_model, int num_heads, const float *state_in, float *state_out,
                         void *out, int out_bf16, int chunk, af_stream_t stream);
 
+/* ------------------------------------------------- gated MSR (opt-in mode)
+ * RetNet's gate and per-head GroupNorm (Sun et al. 2023, eq. 8):
+ *   out = (swish(x W_g^T) (.) GroupNorm_H(Retention(x))) W_o^T
+ * in place of the reference's RMSNorm(Retention(x)) W_o^T.  No reference
+ * counterpart: the reference has neither a gate nor a group norm
+ * (aceflow/nn/retention.py:44-66); these entry points are an extension,
+ * checked against their own float64 restatement. */
+/* y = swish(g) * (gn_weight * (o - mean_h) / sqrt(var_h + eps) + gn_bias) for
+ * each row and head h (mean and variance over the head's d/H values); o, g, y
+ * fp32 or bf16 (the *_bf16 flags) [rows][d]; gn_weight/gn_bias [d] or NULL
+ * (1 / 0).  y must not overlap o or g.  head_dim a multiple of 8, <= 1024. */
+int af_group_norm_gate(af_ctx *ctx, const void *o, int o_bf16, const void *g, int g_bf16, const float *gn_weight,
+                       const float *gn_bias, void *y, int y_bf16, int64_t rows, int d_model, int num_heads, float eps,
+                       af_stream_t stream);
+/* One recurrent decode step of the gated layer (fp32, 3xTF32 projections):
+ * x [batch][d]; w_qkv [3d][d] (rows q, k, v); w_g [d][d]; w_o [d][d];
+ * state [batch][H][d/H][d/H] in place; out [batch][d].  Workspace 6*batch*d
+ * floats. */
+int af_msr_gated_decode_step_f32(af_ctx *ctx, const float *x, float *state, const float *gamma, const float *w_qkv,
+                                 const float *w_g, const float *w_o, const float *gn_weight, const float *gn_bias,
+                                 float eps, int batch, int d_model, int num_heads, float *out, af_stream_t stream);
+/* The gated layer over a prompt on the bf16 tensor cores (head_dim 256):
+ * x [batch*T][d] bf16, weights bf16, state_in/state_out and chunk as for
+ * af_retention_chunkwise_bf16; out fp32 (or bf16 if out_bf16). */
+int af_msr_gated_prefill_bf16(af_ctx *ctx, const uint16_t *x, const uint16_t *w_qkv, const uint16_t *w_g,
+                              const uint16_t *w_o, const float *gn_weight, const float *gn_bias, const float *gamma,
+                              float eps, int batch, int T, int d_model, int num_heads, const float *state_in,
+                              float *state_out, void *out, int out_bf16, int chunk, af_stream_t stream);
+
 /* ------------------------------------------------------- decoder stack */
 /* Weights of one decoder layer (AceEngine's LayerWeights,
  * aceflow-core/src/cpu/mod.rs:18-28), device pointers.  Matrices are fp32 or

@@ -371,6 +371,41 @@ def msr_forward64(x, w_q, w_k, w_v, w_o, num_heads, ret_norm_w=None, eps=1e-6):
     return o @ w_o.T.astype(np.float64)
 
 
+def group_norm_gate64(o, g, num_heads, gn_w=None, gn_b=None, eps=1e-6):
+    """swish(g) * GroupNorm_H(o) per row in float64: each head's d/H values
+    normalised to mean 0, variance 1 (eps inside the square root), then
+    gn_w * . + gn_b per channel.  RetNet's gate and group norm (Sun et al.
+    2023, eq. 8); no reference counterpart (aceflow has neither)."""
+    o = np.asarray(o, np.float64)
+    g = np.asarray(g, np.float64)
+    shp = o.shape
+    d = shp[-1]
+    oh = o.reshape(-1, num_heads, d // num_heads)
+    mean = oh.mean(-1, keepdims=True)
+    var = ((oh - mean) ** 2).mean(-1, keepdims=True)
+    y = ((oh - mean) / np.sqrt(var + eps)).reshape(shp)
+    if gn_w is not None:
+        y = y * np.asarray(gn_w, np.float64)
+    if gn_b is not None:
+        y = y + np.asarray(gn_b, np.float64)
+    return (g / (1.0 + np.exp(-g))) * y
+
+
+def msr_gated_forward64(x, w_q, w_k, w_v, w_g, w_o, num_heads, gn_w=None, gn_b=None, eps=1e-6, state0=None):
+    """The gated layer (swish(x W_g^T) * GroupNorm_H(Retention(x))) W_o^T in
+    float64, the retention being the reference's (retention.py:51-61, no
+    1/sqrt(d_h)).  Returns (out [B,T,d], final state [B,H,dh,dh])."""
+    x = np.asarray(x, np.float64)
+    B, T, d = x.shape
+    hd = d // num_heads
+    sh = lambda a: a.reshape(B, T, num_heads, hd).transpose(0, 2, 1, 3)  # noqa: E731
+    q, k, v = (sh(x @ np.asarray(w, np.float64).T) for w in (w_q, w_k, w_v))
+    o, S = retention_chunkwise64(q, k, v, gammas(num_heads), 64, state0)
+    o = o.transpose(0, 2, 1, 3).reshape(B, T, d)
+    y = group_norm_gate64(o, x @ np.asarray(w_g, np.float64).T, num_heads, gn_w, gn_b, eps)
+    return y @ np.asarray(w_o, np.float64).T, S
+
+
 def decoder_layer64(x, layer: dict, state, gamma, eps):
     """AceEngine.forward_layer_internal (aceflow-core/src/cpu/mod.rs:646-706)
     for a batch of streams at one token, in float64.

@@ -130,3 +130,30 @@ def test_noalloc_wrapper_rejects_bad_shapes_before_any_launch():
         cuda_ops.msr_decode_step_noalloc(x, state, gamma, w_qkv, w_o, rw, 1e-6, out=torch.zeros(B, d + 1))
     with pytest.raises(ValueError, match="CUDA"):  # well-shaped CPU tensors: the device check
         cuda_ops.msr_decode_step_noalloc(x, state, gamma, w_qkv, w_o, rw, 1e-6)
+
+
+def test_gated_module_cpu_matches_float64_restatement():
+    """gated=True (RetNet's gate and group norm, no reference counterpart):
+    the CPU parallel and recurrent forms equal the oracle's float64
+    restatement, and the reference's four weights are drawn unchanged."""
+    from oracle import retention_ref as R
+
+    np.random.seed(3)
+    m = af.nn.MultiScaleRetention(64, 4, gated=True)
+    m.group_norm_weight = af.nn.Parameter(af.Tensor(np.linspace(0.5, 1.5, 64).astype(np.float32)))
+    m.group_norm_bias = af.nn.Parameter(af.Tensor(np.linspace(-0.1, 0.1, 64).astype(np.float32)))
+    x = np.random.randn(2, 10, 64).astype(np.float32)
+    f = lambda p: p.numpy().astype(np.float64)  # noqa: E731
+    ref, _ = R.msr_gated_forward64(x, f(m.w_q), f(m.w_k), f(m.w_v), f(m.w_g), f(m.w_o), 4,
+                                   f(m.group_norm_weight), f(m.group_norm_bias), 1e-6)
+    assert rel_err(m(af.Tensor(x)).numpy(), ref) < 1e-5
+    st = m.init_state(2)
+    outs = []
+    for t in range(10):
+        o, st = m.forward_recurrent(af.Tensor(x[:, t]), st)
+        outs.append(o.numpy())
+    assert rel_err(np.stack(outs, 1), ref) < 1e-5
+    np.random.seed(3)
+    plain = af.nn.MultiScaleRetention(64, 4)
+    for n in ("w_q", "w_k", "w_v", "w_o"):
+        assert np.array_equal(getattr(m, n).numpy(), getattr(plain, n).numpy())

@@ -202,7 +202,7 @@ def test_head_sharded_prefill_single_rank(dev, groups, layout, chunk):
     wq_, wk_, wv_ = np.split(f(wqkv), 3)
     ref = R.msr_forward64(f(x), wq_, wk_, wv_, f(wo), H, f(rw), 1e-6)
     assert rel_err(out.cpu().numpy(), ref) < TOL
-    one, st1 = cuda_ops.msr_prefill_bf16(x, wqkv, wo, rw, cuda_ops.gammas(H, dev), 1e-6)
+    one, st1 = cuda_ops.msr_prefill_bf16(x, wqkv, wo, rw, cuda_ops.gammas(H, dev), 1e-6, chunk=chunk)
     assert rel_err(out.cpu().numpy(), one.cpu().numpy()) < 1e-3
     assert rel_err(st.cpu().numpy(), st1.cpu().numpy()) < 1e-3
 
