@@ -263,6 +263,15 @@ __global__ void __launch_bounds__(320, 1)
         for (int vb = 0; vb < 2; ++vb)
           tma_load_3d(sm + V_OFF + vb * BOX, &tm, bar_load, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
         issued = c + 1;
+        if (c + 1 < nch) {  // the next chunk's tiles into L2 (its loads wait for this chunk's update)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            if (!STATE_ONLY) tma_prefetch_3d(&tm, h * DH + kk * 64, t0 + C, b);
+            tma_prefetch_3d(&tm, d + h * DH + kk * 64, t0 + C, b);
+          }
+#pragma unroll
+          for (int vb = 0; vb < 2; ++vb) tma_prefetch_3d(&tm, 2 * d + h * DH + slice * VS + vb * 64, t0 + C, b);
+        }
       }
       if (issued > 0 && !mbar_wait(bar_load, (issued - 1) & 1)) fail();  // last load landed
     }
@@ -705,6 +714,17 @@ __global__ void __launch_bounds__(320, 1)
         for (int vb = 0; vb < 2; ++vb)
           tma_load_3d(sm + V_OFF + vb * SLICE, &tm, bar_kv, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
         kv_issued = c + 1;
+        // the next chunk's tiles into L2 while this chunk computes, so its
+        // loads (issued only once this chunk's MMAs free the buffers) hit L2
+        if (c + 1 < nch) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            tma_prefetch_3d(&tm, h * DH + kk * 64, t0 + C, b);
+            tma_prefetch_3d(&tm, d + h * DH + kk * 64, t0 + C, b);
+          }
+#pragma unroll
+          for (int vb = 0; vb < 2; ++vb) tma_prefetch_3d(&tm, 2 * d + h * DH + slice * VS + vb * 64, t0 + C, b);
+        }
       }
       // loads still in flight land before the CTA may exit
       if (q_issued > 0 && !mbar_wait(bar_q, (q_issued - 1) & 1)) fail();

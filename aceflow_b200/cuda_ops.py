@@ -264,6 +264,33 @@ def retention_chunkwise_backward_bf16(qkv: torch.Tensor, dout: torch.Tensor, B: 
     return dqkv, dstate
 
 
+class _RetentionChunkwise(torch.autograd.Function):
+    """Autograd node of the chunkwise retention core: forward
+    af_retention_chunkwise_bf16 (no norm weight), backward
+    af_retention_chunkwise_backward_bf16."""
+
+    @staticmethod
+    def forward(ctx, qkv, B, T, H, gamma, chunk):
+        out, _, _ = retention_chunkwise_bf16(qkv, B, T, H, gamma, want_state=False, chunk=chunk)
+        ctx.save_for_backward(qkv, gamma)
+        ctx.dims = (B, T, H)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        qkv, gamma = ctx.saved_tensors
+        B, T, H = ctx.dims
+        dqkv, _ = retention_chunkwise_backward_bf16(qkv, dout.to(BF16).contiguous(), B, T, H, gamma)
+        return dqkv, None, None, None, None, None
+
+
+def retention_chunkwise_autograd(qkv: torch.Tensor, B: int, T: int, H: int, gamma: torch.Tensor,
+                                 chunk: int = 128) -> torch.Tensor:
+    """The chunkwise retention core [B*T, 3*H*256] bf16 -> [B*T, H*256] bf16
+    as a differentiable torch op (training: gradients flow to qkv)."""
+    return _RetentionChunkwise.apply(qkv, B, T, H, gamma, chunk)
+
+
 def msr_prefill_bf16(x: torch.Tensor, w_qkv: torch.Tensor, w_o: torch.Tensor, ret_norm_w: torch.Tensor,
                      gamma: torch.Tensor, eps: float, state_in: torch.Tensor | None = None,
                      out_dtype=torch.float32, want_state: bool = True, chunk: int = 64):

@@ -79,6 +79,7 @@ class MultiScaleRetention(Module):
         # "bfloat16": fp32 prompts on CUDA also take the tensor-core chunkwise
         # prefill (2e-2 tolerance); None/"float32": they take the exact path
         self.prefill_dtype = prefill_dtype
+        self.prefill_chunk = DEFAULT_CHUNK  # chunk length of forward()'s tensor-core prefill (64 or 128)
         self._dev = None  # packed device weights
 
     # ------------------------------------------------------------ device pack
@@ -150,7 +151,7 @@ class MultiScaleRetention(Module):
     def forward_parallel(self, x: Tensor) -> Tensor:
         if x.device.is_cuda:
             if self._use_tensor_cores(x):
-                out, _ = self._prefill_tensor_cores(x, DEFAULT_CHUNK, None, want_state=False)
+                out, _ = self._prefill_tensor_cores(x, self.prefill_chunk, None, want_state=False)
             else:
                 out, _ = self._prefill_exact(x, None)
             return out

@@ -621,10 +621,12 @@ def _phase_times(dev, fn):
         _lib.set_option(idx, "phase_marks", 0)
 
 
-def bench_prefill(dev, passes, peaks, cpu_seconds=0.0, chunk=64):
+def bench_prefill(dev, passes, peaks, cpu_seconds=0.0, chunk=None):
     """The prefill workload through the reference's module API:
     af.nn.MultiScaleRetention(2048, 8).to("cuda:0") called on a bf16 prompt
-    (the tensor-core chunkwise prefill), bf16 output."""
+    (the tensor-core chunkwise prefill), bf16 output, at the workload's chunk
+    length (64) and at 128.  FLOPs are counted by the workload's definition
+    (chunk 64) for both, so the two fractions compare time only."""
     import torch
 
     import aceflow_b200 as af
@@ -640,61 +642,67 @@ def bench_prefill(dev, passes, peaks, cpu_seconds=0.0, chunk=64):
         setattr(m, name, af.nn.Parameter(af.Tensor(w.float())))
     m.to(str(dev))
     xt = af.Tensor(x, device=str(dev), dtype="bfloat16")
-
-    def run():
-        return m.forward_chunkwise(xt, chunk=chunk)[0] if chunk != 64 else m(xt)
-
-    out = None
-    for _ in range(3):
-        out = run()
-    torch.cuda.synchronize()
     stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(passes):
-        out = run()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / passes
-    phases = _phase_times(dev, run)
-    # parity: stream 0's first and last 128 rows against float64
-    w_qkv = torch.cat(ws[:3]).contiguous()
-    rows = [(0, 128), (T - 128, T)]
-    ref = msr_rows_reference(x[0], w_qkv, ws[3], torch.ones(d, device=dev), H, EPS, rows)
-    err = max_rel_err([out.torch[0, r0:r1] for r0, r1 in rows], ref)
-    # the retention core alone (chunkwise kernel), CUDA events on its stream
+    proj, intra, inter = prefill_flops(B, T, d, H, c["C"])
+    total = proj + intra + inter
     qkv = torch.randn(B * T, 3 * d, generator=g, device=dev).bfloat16()
     rw = torch.ones(d, device=dev)
     gamma = cuda_ops.gammas(H, dev)
-    for _ in range(2):
-        cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False, chunk=chunk)
-    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2.record(stream)
-    for _ in range(passes):
-        cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False, chunk=chunk)
-    e3.record(stream)
-    torch.cuda.synchronize()
-    core_ms = e2.elapsed_time(e3) / passes
-    _lib.check_device(dev.index or 0)
-    proj, intra, inter = prefill_flops(B, T, d, H, chunk)
-    total = proj + intra + inter
-    tfl = total / (ms / 1e3) / 1e12
-    core_tfl = (intra + inter) / (core_ms / 1e3) / 1e12
+    w_qkv = torch.cat(ws[:3]).contiguous()
+    rows = [(0, 128), (T - 128, T)]
+    ref = msr_rows_reference(x[0], w_qkv, ws[3], torch.ones(d, device=dev), H, EPS, rows)
+
+    def measure(ck):
+        m.prefill_chunk = ck
+        out = None
+        for _ in range(3):
+            out = m(xt)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(passes):
+            out = m(xt)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / passes
+        phases = _phase_times(dev, lambda: m(xt))
+        err = max_rel_err([out.torch[0, r0:r1] for r0, r1 in rows], ref)
+        # the retention core alone (chunkwise kernel), CUDA events on its stream
+        for _ in range(2):
+            cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False, chunk=ck)
+        e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2.record(stream)
+        for _ in range(passes):
+            cuda_ops.retention_chunkwise_bf16(qkv, B, T, H, gamma, norm_w=rw, want_state=False, chunk=ck)
+        e3.record(stream)
+        torch.cuda.synchronize()
+        core_ms = e2.elapsed_time(e3) / passes
+        _lib.check_device(dev.index or 0)
+        tfl = total / (ms / 1e3) / 1e12
+        core_tfl = (intra + inter) / (core_ms / 1e3) / 1e12
+        kernel = "retention_chunk128_kernel" if ck == 128 else "retention_chunkwise_kernel<0>"
+        return {"ms_per_pass": ms, "value": B * T / (ms / 1e3), "max_rel_err": err, "phases_ms": phases,
+                "roofline": {"bound": "tensor", "achieved": tfl, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": tfl / peaks["bf16_tflops"], "algorithmic_flop": total},
+                "retention_core": {"kernel": kernel, "ms": core_ms, "achieved": core_tfl, "unit": "TFLOP/s",
+                                   "frac": core_tfl / peaks["bf16_tflops"], "algorithmic_flop": intra + inter}}
+
+    main = measure(c["C"] if chunk is None else chunk)
+    alt = measure(128) if chunk is None else None
+    m.prefill_chunk = 64
     res = {
-        "metric": "retention prefill tok/s (B=8,T=4096,d=2048)", "value": B * T / (ms / 1e3), "unit": "tok/s",
-        "ms_per_pass": ms, "passes": passes, "dtype": "bf16 (fp32 accumulate)",
-        "config": {"workload": f"MultiScaleRetention prefill, d_model=2048, 8 heads, B=8, T=4096, chunk {chunk}",
+        "metric": "retention prefill tok/s (B=8,T=4096,d=2048)", "value": main["value"], "unit": "tok/s",
+        "ms_per_pass": main["ms_per_pass"], "passes": passes, "dtype": "bf16 (fp32 accumulate)",
+        "config": {"workload": f"MultiScaleRetention prefill, d_model=2048, 8 heads, B=8, T=4096, "
+                               f"chunk {c['C'] if chunk is None else chunk}",
                    "api": "af.nn.MultiScaleRetention(2048, 8).to('cuda') on a bf16 prompt",
                    "l2": "inputs larger than L2 (x 128 MiB, qkv 384 MiB)"},
-        "max_rel_err": err, "tolerance": 2e-2,
+        "max_rel_err": main["max_rel_err"], "tolerance": 2e-2,
         "parity_rows": "stream 0, rows 0-127 and 3968-4095, against float64",
-        "phases_ms": phases,
-        "roofline": {"bound": "tensor", "achieved": tfl, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": tfl / peaks["bf16_tflops"], "algorithmic_flop": total},
-        "retention_core": {"kernel": "retention_chunkwise_kernel", "ms": core_ms, "achieved": core_tfl,
-                           "unit": "TFLOP/s", "frac": core_tfl / peaks["bf16_tflops"],
-                           "algorithmic_flop": intra + inter},
+        "phases_ms": main["phases_ms"], "roofline": main["roofline"], "retention_core": main["retention_core"],
     }
+    if alt is not None:
+        res["chunk128"] = alt
     if cpu_seconds > 0:
         v, toks, b, el, thr = cpu_prefill_sample(cpu_seconds, host_threads(), d, H, B)
         res["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": thr, "kind": "port",
@@ -704,7 +712,7 @@ def bench_prefill(dev, passes, peaks, cpu_seconds=0.0, chunk=64):
 
 
 # ---------------------------------------------------------------- long context
-LONGCTX = dict(B=1, T=65536, d=4096, H=16, C=64)
+LONGCTX = dict(B=1, T=65536, d=4096, H=16, C=128)
 HEADS_LONGCTX = LONGCTX["H"]
 
 
@@ -874,8 +882,10 @@ def main():
     ap.add_argument("--longctx-passes", type=int, default=5)
     ap.add_argument("--sub-cpu-seconds", type=float, default=4.0,
                     help="seconds of each CPU baseline of the prefill, long-context and stack workloads (N=1)")
-    ap.add_argument("--chunk", type=int, default=64, help="chunk length of the prefill workload")
-    ap.add_argument("--longctx-chunk", type=int, default=64, help="chunk length of the long-context workload")
+    ap.add_argument("--chunk", type=int, default=None,
+                    help="chunk length of the prefill workload (default: the workload's 64, and 128 reported beside)")
+    ap.add_argument("--longctx-chunk", type=int, default=LONGCTX["C"],
+                    help="chunk length of the long-context workload (default: the workload's 128)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

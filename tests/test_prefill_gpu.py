@@ -339,3 +339,23 @@ def test_chunkwise_backward_matches_finite_differences_of_the_forward(dev):
     g = dqkv.float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256).transpose(2, 0, 3, 1, 4)
     an = float((g * dirs).sum())
     assert abs(an - fd) <= 2e-2 * abs(fd)
+
+
+def test_chunkwise_autograd_function(dev):
+    """retention_chunkwise_autograd: loss.backward() through the tensor-core
+    forward gives the float64 closed-form gradient of the parallel form."""
+    from aceflow_b200 import cuda_ops
+
+    B, T, H = 2, 150, 1
+    qkv = _qkv(B, T, H, 321, dev, scale=0.5).requires_grad_(True)
+    g = torch.Generator(device=dev).manual_seed(322)
+    w = torch.randn(B * T, H * 256, generator=g, device=dev)
+    out = cuda_ops.retention_chunkwise_autograd(qkv, B, T, H, cuda_ops.gammas(H, dev))
+    (out.float() * w).sum().backward()
+    a = qkv.detach().float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256)
+    q, k, v = (a[:, :, i].transpose(0, 2, 1, 3) for i in range(3))
+    do = w.bfloat16().double().cpu().numpy().reshape(B, T, H, 256).transpose(0, 2, 1, 3)
+    ref = R.retention_backward64(q, k, v, R.gammas(H), do)
+    got = qkv.grad.float().cpu().numpy().reshape(B, T, 3, H, 256)
+    for i in range(3):
+        assert rel_err(got[:, :, i].transpose(0, 2, 1, 3), ref[i]) < TOL
