@@ -603,8 +603,12 @@ __global__ void __launch_bounds__(320, 1)
 //         S  <- gamma^L (S + K^T V')     (the gamma^L applied when the next
 //                                         chunk reads S, or to the final state)
 //     so no second scaled copy of V is kept (gamma^-128 <= 58 at gamma = 1 - 2^-5);
-//   * the output is computed non-transposed (TMEM lane = token), so each math
-//     thread owns one token row and stores its 128 contiguous bytes directly.
+//   * the output is computed non-transposed (TMEM lane = token): each math
+//     thread owns one token row and writes its 128 bytes into a swizzled
+//     staging box in the bf16(S^T) region (free from the chunk's last MMA to
+//     the next chunk's read-back), from which one thread issues two TMA
+//     stores; rows written back to front (the backward's reversed passes)
+//     are stored directly.
 // Shared memory: Q, K [128 tok x 256 k], V' [128 tok x 128 v], bf16(S^T)
 // [128 v x 256 k] = 224 KB.  TMEM: S^T 256 columns, scores/P 128, O 128.
 // Per chunk: 16 MMAs O = Q . S (N=128), 16 scores (N=128), 8 intra (A from
@@ -638,7 +642,8 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
 }
 
 __global__ void __launch_bounds__(320, 1)
-    retention_chunk128_kernel(const __grid_constant__ CUtensorMap tm, ChunkParams p) {
+    retention_chunk128_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_out,
+                              ChunkParams p) {
   // this kernel's layout (shadows the 64-token kernel's constants)
   constexpr int C = c128::C, SLICE = c128::SLICE, Q_OFF = c128::Q_OFF, K_OFF = c128::K_OFF, V_OFF = c128::V_OFF,
                 SOP_OFF = c128::SOP_OFF, TILE_BYTES = c128::TILE_BYTES, NBAR = c128::NBAR, PARTS = c128::PARTS;
@@ -675,6 +680,7 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(bar_upd, 1);
     fence_barrier_init();
     prefetch_tmap(&tm);
+    if (!p.out_reverse) prefetch_tmap(&tm_out);
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + VS) {
     const int i = threadIdx.x - 64;
@@ -824,6 +830,7 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       if (c > 0) ok = mbar_wait(bar_upd, (c - 1) & 1);
       if (!ok) s_abort = 1;
+      if (mt == 0 && c > 0) bulk_wait_read<0>();  // the previous chunk's staged output has been read
       if (math_sync_or(s_abort != 0)) break;
       tc_fence_after();
 #pragma unroll 1
@@ -904,9 +911,12 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       mbar_arrive(bar_math);
       if (math_sync_or(s_abort != 0)) break;
-      // (D) token row i = row: O = gamma^(i+1) O_acc; bf16 O * w straight to
-      //     global memory (this warp's 64 values: 128 contiguous bytes); the
-      //     partial sum of O^2 of those values
+      // (D) token row i = row: O = gamma^(i+1) O_acc, bf16 O * w, and the
+      //     partial sum of O^2 of this warp's 64 values.  The bf16 row (128
+      //     bytes) goes to a 128-byte-swizzled staging box in the bf16(S^T)
+      //     region, free until the next chunk's (A), and one thread stores
+      //     both boxes [128 tok x 64 v] with TMA (rows past T are clipped by
+      //     the tensor map); direct stores only for reversed rows.
       ok = mbar_wait(bar_o, c & 1);
       if (!ok) s_abort = 1;
       if (math_sync_or(s_abort != 0)) break;
@@ -919,12 +929,15 @@ __global__ void __launch_bounds__(320, 1)
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(bar_ofree);  // O is in registers: the next chunk's MMAs may overwrite it
-      if (row < L) {
+      {
         const float f = exp2f((float)(row + 1) * lg);
         const size_t r = (size_t)b * p.T + t0 + row;
-        const size_t ro = p.out_reverse ? (size_t)b * p.T + (p.T - 1 - (t0 + row)) : r;
-        uint4 *dst = reinterpret_cast<uint4 *>(p.out + ro * (p.ldo ? p.ldo : d) + h * DH + slice * VS + half * 64);
         const float *w = wsl + half * 64;
+        uint8_t *box = sm + SOP_OFF + half * SLICE;
+        uint4 *dst = nullptr;
+        if (p.out_reverse && row < L)
+          dst = reinterpret_cast<uint4 *>(p.out + ((size_t)b * p.T + (p.T - 1 - (t0 + row))) * (p.ldo ? p.ldo : d) +
+                                          h * DH + slice * VS + half * 64);
         float ss = 0.f;
 #pragma unroll
         for (int c16 = 0; c16 < 8; ++c16) {
@@ -935,12 +948,28 @@ __global__ void __launch_bounds__(320, 1)
             ss = fmaf(o, o, ss);
             y[u] = o * w[8 * c16 + u];
           }
-          dst[c16] = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]),
-                                pack_bf16(y[6], y[7]));
+          const uint4 v16 = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]),
+                                       pack_bf16(y[6], y[7]));
+          if (p.out_reverse) {
+            if (dst) dst[c16] = v16;
+          } else {
+            *reinterpret_cast<uint4 *>(box + sw128(row, c16)) = v16;
+          }
         }
-        if (p.sumsq) p.sumsq[r * (p.H * PARTS) + h * PARTS + slice * 2 + half] = ss;
+        if (p.sumsq && row < L) p.sumsq[r * (p.H * PARTS) + h * PARTS + slice * 2 + half] = ss;
+      }
+      if (!p.out_reverse) {
+        fence_proxy_async_smem();  // staged rows before the TMA stores read them
+        math_sync();
+        if (mt == 0) {
+          const int col = h * DH + slice * VS;
+          tma_store_3d(&tm_out, sm + SOP_OFF, col, t0, b);
+          tma_store_3d(&tm_out, sm + SOP_OFF + SLICE, col + 64, t0, b);
+          bulk_commit();
+        }
       }
     }
+    if (mt == 0) bulk_wait_all();  // the output stores have completed
     // final state S[k][v] = gamma^L_last (S_acc^T[v][k]) of the last segment
     const bool aborted = math_sync_or(s_abort != 0);
     const bool write_state = p.state_out && s == p.nseg - 1;
@@ -1005,12 +1034,13 @@ int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const CUtensorMap &tm_o
   return af::launched(ctx, fn);
 }
 
-int launch_chunk128(af_ctx *ctx, const CUtensorMap &tm, const ChunkParams &p, cudaStream_t st, const char *fn) {
+int launch_chunk128(af_ctx *ctx, const CUtensorMap &tm, const CUtensorMap &tm_out, const ChunkParams &p,
+                    cudaStream_t st, const char *fn) {
   static std::atomic<unsigned long long> attr_devices{0};
   if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(retention_chunk128_kernel), c128::SMEM,
                               attr_devices, fn))
     return arc;
-  retention_chunk128_kernel<<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, c128::SMEM, st>>>(tm, p);
+  retention_chunk128_kernel<<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, c128::SMEM, st>>>(tm, tm_out, p);
   return af::launched(ctx, fn);
 }
 
@@ -1080,9 +1110,22 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   if (rc) return rc;
   const bool big = pl.chunk == c128::C;
   if (big && (rc = encode_qkv_map(&tm128, qkv, B, T, d, c128::C, fn))) return rc;
-  // output [B][T][d] bf16 for the TMA stores of the 64-token kernel: [64 tok
-  // x 64 v] boxes, the T edge clipped per stream
+  // output [B][T][d] bf16 for the TMA stores: [64 tok x 64 v] plain boxes
+  // (64-token kernel) or [128 tok x 64 v] 128-byte-swizzled boxes with row
+  // stride ldo (128-token kernel); the T edge is clipped per stream
   CUtensorMap tm_out = tm;
+  if (big && !out_reverse) {
+    const cuuint64_t ld = (cuuint64_t)(ldo ? ldo : d);
+    cuuint64_t odims[3] = {(cuuint64_t)d, (cuuint64_t)T, (cuuint64_t)B};
+    cuuint64_t ostrides[2] = {ld * 2, (cuuint64_t)T * ld * 2};
+    cuuint32_t obox[3] = {64, (cuuint32_t)c128::C, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (!aligned16(out)) return fail(AF_ERR_ARG, "%s: output must be 16-byte aligned", fn);
+    CUresult r = g_encode3(&tm_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, odims, ostrides, obox, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: output tensor map encode failed (%d)", fn, (int)r);
+  }
   if (!big) {
     cuuint64_t odims[3] = {(cuuint64_t)d, (cuuint64_t)T, (cuuint64_t)B};
     cuuint64_t ostrides[2] = {(cuuint64_t)d * 2, (cuuint64_t)T * d * 2};
@@ -1096,7 +1139,7 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   ChunkParams p{B,       T,         H,       pl.nseg, pl.seg_len, gamma, state_in, state_out,
                 reinterpret_cast<__nv_bfloat16 *>(out), norm_w, sumsq, ctx->dev_err, ldo, out_reverse ? 1 : 0};
   auto full_pass = [&](const ChunkParams &pp) {
-    return big ? launch_chunk128(ctx, tm128, pp, st, fn) : launch_chunkwise<false>(ctx, tm, tm_out, pp, st, fn);
+    return big ? launch_chunk128(ctx, tm128, tm_out, pp, st, fn) : launch_chunkwise<false>(ctx, tm, tm_out, pp, st, fn);
   };
   if (pl.nseg == 1) {
     rc = full_pass(p);
