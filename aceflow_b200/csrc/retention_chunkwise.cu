@@ -605,10 +605,11 @@ __global__ void __launch_bounds__(320, 1)
 //     so no second scaled copy of V is kept (gamma^-128 <= 58 at gamma = 1 - 2^-5);
 //   * the output is computed non-transposed (TMEM lane = token): each math
 //     thread owns one token row and writes its 128 bytes into a swizzled
-//     staging box in the bf16(S^T) region (free from the chunk's last MMA to
-//     the next chunk's read-back), from which one thread issues two TMA
-//     stores; rows written back to front (the backward's reversed passes)
-//     are stored directly.
+//     staging box in the bf16(S^T) region (K slices 1 and 3, free from the
+//     chunk's last MMA until the next chunk's read-back, which writes slices
+//     0 and 2 first and the staging slices only once the TMA stores have
+//     read them); rows written back to front (the backward's reversed
+//     passes) are stored directly.
 // Shared memory: Q, K [128 tok x 256 k], V' [128 tok x 128 v], bf16(S^T)
 // [128 v x 256 k] = 224 KB.  TMEM: S^T 256 columns, scores/P 128, O 128.
 // Per chunk: 16 MMAs O = Q . S (N=128), 16 scores (N=128), 8 intra (A from
@@ -830,11 +831,16 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       if (c > 0) ok = mbar_wait(bar_upd, (c - 1) & 1);
       if (!ok) s_abort = 1;
-      if (mt == 0 && c > 0) bulk_wait_read<0>();  // the previous chunk's staged output has been read
       if (math_sync_or(s_abort != 0)) break;
       tc_fence_after();
 #pragma unroll 1
       for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 64) {
+        // the second K slice of each half holds the previous chunk's staged
+        // output: written only once its TMA stores have read it
+        if (k0 != half * (DH / 2) && c > 0) {
+          if (mt == 0) bulk_wait_read<0>();
+          math_sync();
+        }
         float x[64];
         __syncwarp();
 #pragma unroll
@@ -933,7 +939,7 @@ __global__ void __launch_bounds__(320, 1)
         const float f = exp2f((float)(row + 1) * lg);
         const size_t r = (size_t)b * p.T + t0 + row;
         const float *w = wsl + half * 64;
-        uint8_t *box = sm + SOP_OFF + half * SLICE;
+        uint8_t *box = sm + SOP_OFF + (2 * half + 1) * SLICE;  // K slices 1 and 3 of bf16(S^T)
         uint4 *dst = nullptr;
         if (p.out_reverse && row < L)
           dst = reinterpret_cast<uint4 *>(p.out + ((size_t)b * p.T + (p.T - 1 - (t0 + row))) * (p.ldo ? p.ldo : d) +
@@ -963,8 +969,8 @@ __global__ void __launch_bounds__(320, 1)
         math_sync();
         if (mt == 0) {
           const int col = h * DH + slice * VS;
-          tma_store_3d(&tm_out, sm + SOP_OFF, col, t0, b);
-          tma_store_3d(&tm_out, sm + SOP_OFF + SLICE, col + 64, t0, b);
+          tma_store_3d(&tm_out, sm + SOP_OFF + SLICE, col, t0, b);
+          tma_store_3d(&tm_out, sm + SOP_OFF + 3 * SLICE, col + 64, t0, b);
           bulk_commit();
         }
       }

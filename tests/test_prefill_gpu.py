@@ -293,7 +293,7 @@ def test_module_forward_chunkwise_needs_head_dim_256(dev):
 
 # ---- backward of the chunkwise form ---------------------------------------
 @pytest.mark.parametrize("B,T,H,with_state", [(1, 128, 1, False), (2, 200, 2, True), (1, 777, 2, True),
-                                              (3, 65, 1, False)])
+                                              (3, 65, 1, False), (1, 300, 1, False), (2, 300, 1, True)])
 def test_chunkwise_backward_matches_float64_gradients(dev, B, T, H, with_state):
     """dQ, dK, dV and the initial state's gradient of the chunkwise kernel
     (three passes of the 128-token kernel, two over reversed time) against
@@ -320,23 +320,24 @@ def test_chunkwise_backward_matches_float64_gradients(dev, B, T, H, with_state):
 
 
 def test_chunkwise_backward_matches_finite_differences_of_the_forward(dev):
-    """<dO, O(q + e dq)> changes by e <dO, dQ . dq> to first order: the
-    gradient agrees with the forward kernel itself (directional derivative,
-    centred differences in float64 on the oracle forward)."""
+    """Along the direction of the GPU's own gradient g, the oracle forward's
+    loss <dO, O(x + e g)> changes by e <g_true, g>, which must equal |g|^2
+    to within 2e-2 (central differences in float64; along g the sum has no
+    cancellation, so bf16 rounding of single entries cannot dominate it)."""
     from aceflow_b200 import cuda_ops
 
     B, T, H = 1, 300, 1
     qkv = _qkv(B, T, H, 311, dev, scale=0.5)
-    dout = torch.randn(B * T, 256, device=dev).bfloat16()
+    g0 = torch.Generator(device=dev).manual_seed(312)
+    dout = torch.randn(B * T, 256, generator=g0, device=dev).bfloat16()
     dqkv, _ = cuda_ops.retention_chunkwise_backward_bf16(qkv, dout, B, T, H, cuda_ops.gammas(H, dev))
     a = qkv.float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256).transpose(2, 0, 3, 1, 4)
     do = dout.float().cpu().numpy().astype(np.float64).reshape(B, T, H, 256).transpose(0, 2, 1, 3)
-    rng = np.random.default_rng(5)
-    dirs = rng.standard_normal(a.shape)
+    g = dqkv.float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256).transpose(2, 0, 3, 1, 4)
+    dirs = g / np.linalg.norm(g)
     eps = 1e-3
     f = lambda x: float((R.retention_chunkwise64(x[0], x[1], x[2], R.gammas(H), 64)[0] * do).sum())  # noqa: E731
     fd = (f(a + eps * dirs) - f(a - eps * dirs)) / (2 * eps)
-    g = dqkv.float().cpu().numpy().astype(np.float64).reshape(B, T, 3, H, 256).transpose(2, 0, 3, 1, 4)
     an = float((g * dirs).sum())
     assert abs(an - fd) <= 2e-2 * abs(fd)
 
