@@ -720,10 +720,11 @@ def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_
     """Head-sharded prefill of one 65536-token stream (d_model 4096, 16 heads)
     over all ranks: QKV of the rank's heads, chunkwise retention (sequence
     segments), the exchange of head outputs, output projection.  Two
-    exchanges: the all-gather the workload names (each rank then owns output
-    columns) and the all-to-all (each rank owns output rows; 8x fewer bytes
-    over NVLink at 8 GPUs).  Total work is fixed, so N GPUs scale it
-    strongly.  Rank 0 checks its share of three row blocks against float64."""
+    exchanges: the all-to-all (each rank owns output rows; 8x fewer bytes
+    over NVLink at 8 GPUs than the all-gather), reported as the line's value,
+    and the all-gather the workload names (each rank then owns output
+    columns), reported beside it.  Total work is fixed, so N GPUs scale it
+    strongly.  Rank 0 checks its own output against float64 in both."""
     import torch
 
     from aceflow_b200 import _lib
@@ -786,26 +787,28 @@ def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_
                                    chunk=chunk)
     gather_bytes = (world - 1) * B * T * (d // world) * 2  # bf16 head outputs received per rank
     a2a_bytes = (world - 1) * (-(-B * T // world)) * (d // world) * 2
-    col = res["columns"]
+    rows, col = res["rows"], res["columns"]
     line = {
         "metric": "long-context head-sharded prefill tok/s (B=1,T=65536,d=4096,H=16)",
-        "value": col["value"], "unit": "tok/s", "ms_per_pass": col["ms_per_pass"], "passes": passes,
+        "value": rows["value"], "unit": "tok/s", "ms_per_pass": rows["ms_per_pass"], "passes": passes,
         "n_gpus": world, "scaling": "strong", "dtype": "bf16 (fp32 accumulate)",
         "config": {"workload": "MultiScaleRetention prefill, d_model=4096, 16 heads (head_dim 256), B=1, T=65536, "
-                               f"chunk {chunk}", "parallelism": f"head-sharded x{world}, {H // world} heads per GPU, "
-                                                             "one NCCL all-gather before W_o",
+                               f"chunk {chunk}",
+                   "parallelism": f"head-sharded x{world}, {H // world} heads per GPU; NCCL all-to-all of the head "
+                                  f"outputs, each rank owns {-(-B * T // world)} output rows and applies the full W_o",
                    "segments": {"nseg": nseg, "seg_len": seg_len},
                    "l2": "inputs larger than L2 (x 512 MiB, qkv per GPU >= 192 MiB)"},
-        "max_rel_err": col["max_rel_err_rank0"], "tolerance": 2e-2,
-        "parity_rows_alltoall": "the first and last 128 of rank 0's own rows against float64",
-        "parity_rows": "rank 0's output share of rows 0-127, 32704-32831, 65408-65535 against float64",
-        "phases_ms_rank0": col["phases_ms_rank0"],
-        "roofline": {"bound": "tensor", "achieved": col["achieved_per_gpu"], "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "per": "GPU", "frac": col["frac_per_gpu"], "algorithmic_flop": total,
-                     "allgather_bytes_per_rank": gather_bytes},
-        "alltoall": {"parallelism": f"head-sharded x{world}; NCCL all-to-all of head outputs, each rank owns "
-                                    f"{-(-B * T // world)} output rows and applies the full W_o",
-                     "bytes_received_per_rank": a2a_bytes, **res["rows"]},
+        "max_rel_err": rows["max_rel_err_rank0"], "tolerance": 2e-2,
+        "parity_rows": "the first and last 128 of rank 0's own rows against float64",
+        "phases_ms_rank0": rows["phases_ms_rank0"],
+        "roofline": {"bound": "tensor", "achieved": rows["achieved_per_gpu"], "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "per": "GPU", "frac": rows["frac_per_gpu"], "algorithmic_flop": total,
+                     "alltoall_bytes_per_rank": a2a_bytes},
+        "allgather": {"parallelism": f"head-sharded x{world}; one NCCL all-gather of the head outputs before W_o, "
+                                     "each rank owns output columns",
+                      "bytes_received_per_rank": gather_bytes,
+                      "parity_rows": "rank 0's output share of rows 0-127, 32704-32831, 65408-65535 against float64",
+                      **col},
     }
     if cpu_seconds > 0 and rank == 0 and world == 1:
         v, toks, b, el, thr = cpu_prefill_sample(cpu_seconds, 1, d, H, B)
