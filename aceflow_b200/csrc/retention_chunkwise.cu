@@ -605,17 +605,24 @@ __global__ void __launch_bounds__(320, 1)
 //     so no second scaled copy of V is kept (gamma^-128 <= 58 at gamma = 1 - 2^-5);
 //   * the output is computed non-transposed (TMEM lane = token): each math
 //     thread owns one token row and writes its 128 bytes into a swizzled
-//     staging box in the bf16(S^T) region (K slices 1 and 3, free from the
-//     chunk's last MMA until the next chunk's read-back, which writes slices
-//     0 and 2 first and the staging slices only once the TMA stores have
-//     read them); rows written back to front (the backward's reversed
-//     passes) are stored directly.
+//     staging box in the bf16(S^T) region (K slices 1 and 3), stored with
+//     TMA; rows written back to front (the backward's reversed passes) are
+//     stored directly.
 // Shared memory: Q, K [128 tok x 256 k], V' [128 tok x 128 v], bf16(S^T)
 // [128 v x 256 k] = 224 KB.  TMEM: S^T 256 columns, scores/P 128, O 128.
-// Per chunk: 16 MMAs O = Q . S (N=128), 16 scores (N=128), 8 intra (A from
-// TMEM), 8 state updates (N=256): 48 MMAs per 128 tokens against 80 for two
-// 64-token chunks.  The load of the next chunk's Q overlaps this chunk's intra
-// and update MMAs.
+// Per chunk: 16 MMAs O = Q . S (N=128), 16 scores (N=128), 8 state updates
+// (N=256), 8 intra (A from TMEM): 48 MMAs per 128 tokens against 80 for two
+// 64-token chunks.
+// Schedule.  The state is the serial chain: chunk c's update, then chunk
+// c+1's read-back of S (A), then its update again.  So the update is issued
+// before the intra MMAs, and the math warps take chunk c+1's read-back
+// before chunk c's output: iteration c of the math loop runs (A) of chunk c,
+// (D1) of chunk c-1 (O out of TMEM into registers, which frees O for chunk
+// c's O = Q S), (B) V' and (C) P of chunk c, then (D2) of chunk c-1 (staging
+// and TMA store, once chunk c's O = Q S has read the staging slices).  Each
+// operand has its own load barrier and is reloaded as soon as its last
+// reader retired, so K and V' of the next chunk load while this chunk's
+// output is written.
 namespace c128 {
 constexpr int C = 128;
 constexpr int SLICE = 128 * 64 * 2;          // one [128 rows x 64] bf16 SW128 tile: 16 KB
@@ -624,7 +631,7 @@ constexpr int K_OFF = Q_OFF + 4 * SLICE;     // 4 K-slices [128 tok x 64 k]
 constexpr int V_OFF = K_OFF + 4 * SLICE;     // 2 boxes [128 tok x 64 v], scaled in place to V'
 constexpr int SOP_OFF = V_OFF + 2 * SLICE;   // bf16(S^T): 4 K-slices [128 v x 64 k]
 constexpr int TILE_BYTES = SOP_OFF + 4 * SLICE;  // 224 KB
-constexpr int NBAR = 8;
+constexpr int NBAR = 10;
 // tail: barriers, TMEM slot (16 bytes), this CTA's 128 norm weights
 constexpr size_t TAIL_BYTES = NBAR * 8 + 16 + VS * 4;
 constexpr size_t SMEM = 1024 + TILE_BYTES + TAIL_BYTES;
@@ -652,8 +659,11 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + TILE_BYTES);
-  uint64_t *bar_q = bars + 0, *bar_kv = bars + 1, *bar_sc = bars + 2, *bar_sop = bars + 3, *bar_math = bars + 4,
-           *bar_o = bars + 5, *bar_ofree = bars + 6, *bar_upd = bars + 7;
+  // loads landed: bar_q, bar_k, bar_v; MMAs retired: bar_sc (O = Q S and the
+  // scores), bar_upd (state update), bar_o (intra, the chunk's last); math
+  // warps done: bar_sop (bf16 S^T), bar_vs (V'), bar_math (P), bar_ofree (O read)
+  uint64_t *bar_q = bars + 0, *bar_k = bars + 1, *bar_sc = bars + 2, *bar_sop = bars + 3, *bar_math = bars + 4,
+           *bar_o = bars + 5, *bar_ofree = bars + 6, *bar_upd = bars + 7, *bar_v = bars + 8, *bar_vs = bars + 9;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + NBAR);
   float *wsl = reinterpret_cast<float *>(bars + NBAR + 2);  // norm weights of this slice
   __shared__ volatile int s_abort;
@@ -672,13 +682,15 @@ __global__ void __launch_bounds__(320, 1)
   if (threadIdx.x == 0) {
     s_abort = 0;
     mbar_init(bar_q, 1);
-    mbar_init(bar_kv, 1);
+    mbar_init(bar_k, 1);
+    mbar_init(bar_v, 1);
     mbar_init(bar_sc, 1);
-    mbar_init(bar_sop, MATH_THREADS);
-    mbar_init(bar_math, MATH_THREADS);
-    mbar_init(bar_o, 1);
-    mbar_init(bar_ofree, MATH_THREADS);
     mbar_init(bar_upd, 1);
+    mbar_init(bar_o, 1);
+    mbar_init(bar_sop, MATH_THREADS);
+    mbar_init(bar_vs, MATH_THREADS);
+    mbar_init(bar_math, MATH_THREADS);
+    mbar_init(bar_ofree, MATH_THREADS);
     fence_barrier_init();
     prefetch_tmap(&tm);
     if (!p.out_reverse) prefetch_tmap(&tm_out);
@@ -702,25 +714,29 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // Each operand is reloaded as soon as its last reader of the previous
+    // chunk retired: Q after the scores (issued after O = Q S), K after the
+    // state update, V' after the intra MMAs (the MMAs run in that order).
     if (lane == 0) {
-      int q_issued = 0, kv_issued = 0;
+      int q_issued = 0, k_issued = 0, v_issued = 0;
       for (int c = 0; c < nch && !s_abort; ++c) {
         const int t0 = tb + c * C;
-        // Q(c-1) is consumed once chunk c-1's scores (issued after its O = Q S) completed
         if (c > 0 && !mbar_wait(bar_sc, (c - 1) & 1)) { fail(); break; }
         mbar_arrive_expect_tx(bar_q, 4 * SLICE);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + Q_OFF + kk * SLICE, &tm, bar_q, h * DH + kk * 64, t0, b);
         q_issued = c + 1;
-        // K(c-1) and V'(c-1) are consumed once chunk c-1's state update completed
         if (c > 0 && !mbar_wait(bar_upd, (c - 1) & 1)) { fail(); break; }
-        mbar_arrive_expect_tx(bar_kv, 6 * SLICE);
+        mbar_arrive_expect_tx(bar_k, 4 * SLICE);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + K_OFF + kk * SLICE, &tm, bar_kv, d + h * DH + kk * 64, t0, b);
+        for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + K_OFF + kk * SLICE, &tm, bar_k, d + h * DH + kk * 64, t0, b);
+        k_issued = c + 1;
+        if (c > 0 && !mbar_wait(bar_o, (c - 1) & 1)) { fail(); break; }
+        mbar_arrive_expect_tx(bar_v, 2 * SLICE);
 #pragma unroll
         for (int vb = 0; vb < 2; ++vb)
-          tma_load_3d(sm + V_OFF + vb * SLICE, &tm, bar_kv, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
-        kv_issued = c + 1;
+          tma_load_3d(sm + V_OFF + vb * SLICE, &tm, bar_v, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
+        v_issued = c + 1;
         // the next chunk's tiles into L2 while this chunk computes, so its
         // loads (issued only once this chunk's MMAs free the buffers) hit L2
         if (c + 1 < nch) {
@@ -735,10 +751,14 @@ __global__ void __launch_bounds__(320, 1)
       }
       // loads still in flight land before the CTA may exit
       if (q_issued > 0 && !mbar_wait(bar_q, (q_issued - 1) & 1)) fail();
-      if (kv_issued > 0 && !mbar_wait(bar_kv, (kv_issued - 1) & 1)) fail();
+      if (k_issued > 0 && !mbar_wait(bar_k, (k_issued - 1) & 1)) fail();
+      if (v_issued > 0 && !mbar_wait(bar_v, (v_issued - 1) & 1)) fail();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Per chunk, in this order: O = Q . S, the scores Q . K^T, the state
+    // update S^T += V'^T K, then O += P . V'.  The update goes before the
+    // intra MMAs because the next chunk's read-back of S is the longer chain.
     constexpr uint32_t id_nn = idesc_f32acc(kFmtBF16, 128, 128);                       // A, B K-major
     constexpr uint32_t id_intra = idesc_f32acc(kFmtBF16, 128, 128) | (1u << 16);       // A in TMEM, B MN-major
     constexpr uint32_t id_upd = idesc_f32acc(kFmtBF16, 128, 256) | (1u << 15) | (1u << 16);  // A, B MN-major
@@ -762,7 +782,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       __syncwarp();
       // scores Q . K^T (K = 256 keys)
-      ok = mbar_wait(bar_kv, c & 1);
+      ok = mbar_wait(bar_k, c & 1);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
       tc_fence_after();
@@ -778,21 +798,12 @@ __global__ void __launch_bounds__(320, 1)
         umma_commit(bar_sc);
       }
       __syncwarp();
-      // once P (TMEM) and V' (shared memory) are written:
-      ok = mbar_wait(bar_math, c & 1);
+      // S^T += V'^T . K  (K = 128 tokens, N = 256 keys) once V' is scaled
+      ok = mbar_wait(bar_vs, c & 1);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
       tc_fence_after();
       if (lane == 0) {
-        //   O += P . V'   (K = 128 tokens; P's columns: j < 64 from TM_SC, j >= 64 from TM_SC + 64)
-#pragma unroll
-        for (int kj = 0; kj < 8; ++kj) {
-          const uint32_t pa = tmem + TM_SC + (kj < 4 ? 8 * kj : 64 + 8 * (kj - 4));
-          const uint64_t db = sdesc_mn_sw128(sm + V_OFF + kj * 2048, SLICE);
-          umma_bf16_ts(tmem + TM_O, pa, db, id_intra, 1);
-        }
-        umma_commit(bar_o);
-        //   S^T += V'^T . K   (K = 128 tokens, N = 256 keys)
 #pragma unroll
         for (int kt = 0; kt < 8; ++kt) {
           const uint64_t da = sdesc_mn_sw128(sm + V_OFF + kt * 2048, SLICE);
@@ -802,9 +813,31 @@ __global__ void __launch_bounds__(320, 1)
         umma_commit(bar_upd);
       }
       __syncwarp();
+      // O += P . V'  (K = 128 tokens; P's columns: j < 64 from TM_SC, j >= 64
+      // from TM_SC + 64) once P is written
+      ok = mbar_wait(bar_math, c & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || __any_sync(0xffffffffu, s_abort != 0)) { if (!ok && lane == 0) fail(); break; }
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kj = 0; kj < 8; ++kj) {
+          const uint32_t pa = tmem + TM_SC + (kj < 4 ? 8 * kj : 64 + 8 * (kj - 4));
+          const uint64_t db = sdesc_mn_sw128(sm + V_OFF + kj * 2048, SLICE);
+          umma_bf16_ts(tmem + TM_O, pa, db, id_intra, 1);
+        }
+        umma_commit(bar_o);
+      }
+      __syncwarp();
     }
   } else {
     // ------------------------------------------------------------ math warps
+    // Iteration c does chunk c's (A) read-back of S, the first half of chunk
+    // c-1's output (D1: O out of TMEM), chunk c's (B) V' and (C) P, then
+    // the second half of chunk c-1's output (D2: staging and TMA store).
+    // Chunk c-1's output thus waits behind chunk c's read-back, which is on
+    // the state's critical path, and its staging slices are free again once
+    // chunk c's O = Q S (which reads them as part of bf16(S^T)) retired.
     const int q = warp & 3;            // TMEM lane quadrant
     const int half = (warp - 2) >> 2;  // which half of the columns this warp takes
     const int mt = threadIdx.x - 64;   // 0..255
@@ -824,154 +857,171 @@ __global__ void __launch_bounds__(320, 1)
       tmem_wait_st();
     }
     const float gC = exp2f((float)C * lg);
-    for (int c = 0; c < nch; ++c) {
-      const int t0 = tb + c * C;
-      const int L = min(C, te - t0);
-      // (A) S = gamma^C S_acc (the previous chunk's decay, deferred); bf16(S^T) -> shared memory
-      bool ok = true;
-      if (c > 0) ok = mbar_wait(bar_upd, (c - 1) & 1);
-      if (!ok) s_abort = 1;
-      if (math_sync_or(s_abort != 0)) break;
-      tc_fence_after();
+    const float fo = exp2f((float)(row + 1) * lg);  // the output row's decay gamma^(i+1)
+    uint32_t ob[32];                                // chunk c-1's bf16 output row, (D1) -> (D2)
 #pragma unroll 1
-      for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 64) {
-        // the second K slice of each half holds the previous chunk's staged
-        // output: written only once its TMA stores have read it
-        if (k0 != half * (DH / 2) && c > 0) {
-          if (mt == 0) bulk_wait_read<0>();
-          math_sync();
-        }
-        float x[64];
-        __syncwarp();
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          tmem_ld16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
-        tmem_wait_ld();
-        if (c > 0) {
-#pragma unroll
-          for (int j = 0; j < 64; ++j) x[j] *= gC;
-        }
-        uint8_t *slice_base = sm + SOP_OFF + (k0 >> 6) * SLICE;
-#pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16) {
-          const float *y = x + 8 * c16;
-          *reinterpret_cast<uint4 *>(slice_base + sw128(row, c16)) =
-              make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
-        }
-        if (c > 0) {
+    for (int c = 0; c <= nch; ++c) {
+      const bool cur = c < nch, prev = c > 0;
+      if (cur) {
+        // (A) S = gamma^C S_acc (the previous chunk's decay, deferred); bf16(S^T) -> shared memory
+        bool ok = true;
+        if (c > 0) ok = mbar_wait(bar_upd, (c - 1) & 1);
+        if (!ok) s_abort = 1;
+        if (math_sync_or(s_abort != 0)) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int k0 = half * (DH / 2); k0 < (half + 1) * (DH / 2); k0 += 64) {
+          float x[64];
           __syncwarp();
 #pragma unroll
           for (int u = 0; u < 4; ++u)
-            tmem_st16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
-        }
-      }
-      tmem_wait_st();
-      fence_proxy_async_smem();  // bf16(S^T) (generic stores) before the MMAs that read it
-      tc_fence_before();
-      mbar_arrive(bar_sop);
-      // (B) V' = diag(gamma^-(j+1)) V in place
-      ok = mbar_wait(bar_kv, c & 1);
-      if (!ok) s_abort = 1;
-      if (ok) {
-#pragma unroll 2
-        for (int i = mt; i < 2 * SLICE / 16; i += MATH_THREADS) {
-          const int off = i * 16;
-          const int j = (off % SLICE) / 128;  // token row of this 16-byte chunk
-          const float sc = exp2f(-(float)(j + 1) * lg);
-          uint4 raw = *reinterpret_cast<const uint4 *>(sm + V_OFF + off);
-          __nv_bfloat162 *e = reinterpret_cast<__nv_bfloat162 *>(&raw);
+            tmem_ld16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+          tmem_wait_ld();
+          if (c > 0) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            float2 f = __bfloat1622float2(e[u]);
-            e[u] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+            for (int j = 0; j < 64; ++j) x[j] *= gC;
+            __syncwarp();
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              tmem_st16(tmem + lane_base + TM_S + k0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
           }
-          *reinterpret_cast<uint4 *>(sm + V_OFF + off) = raw;
+          // the second K slice of each half holds chunk c-2's staged output:
+          // written only once its TMA stores have read it
+          if (k0 != half * (DH / 2) && c > 1 && !p.out_reverse) {
+            if (mt == 0) bulk_wait_read<0>();
+            math_sync();
+          }
+          uint8_t *slice_base = sm + SOP_OFF + (k0 >> 6) * SLICE;
+#pragma unroll
+          for (int c16 = 0; c16 < 8; ++c16) {
+            const float *y = x + 8 * c16;
+            *reinterpret_cast<uint4 *>(slice_base + sw128(row, c16)) =
+                make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]), pack_bf16(y[6], y[7]));
+          }
         }
+        tmem_wait_st();
+        fence_proxy_async_smem();  // bf16(S^T) (generic stores) before the MMAs that read it
+        tc_fence_before();
+        mbar_arrive(bar_sop);
       }
-      fence_proxy_async_smem();
-      // (C) P = bf16(Q K^T masked to j <= i), written back into the scores'
-      //     columns: this warp's 64 columns j become 32 packed columns at
-      //     TM_SC + 64 * half, inside the range it read
-      ok = ok && mbar_wait(bar_sc, c & 1);
-      if (!ok) s_abort = 1;
-      if (ok) {
+      if (prev) {
+        // (D1) chunk c-1, token row i = row: O = gamma^(i+1) O_acc, bf16 O * w
+        // into registers, and the partial sum of O^2 of this warp's 64 values
+        const int tp = tb + (c - 1) * C;
+        const int Lp = min(C, te - tp);
+        bool ok = mbar_wait(bar_o, (c - 1) & 1);
+        if (!ok) s_abort = 1;
+        if (math_sync_or(s_abort != 0)) break;
         tc_fence_after();
-        const int j0 = half * 64;
         float x[64];
         __syncwarp();
 #pragma unroll
         for (int u = 0; u < 4; ++u)
-          tmem_ld16(tmem + lane_base + TM_SC + j0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+          tmem_ld16(tmem + lane_base + TM_O + half * 64 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
         tmem_wait_ld();
-        uint32_t pk[32];
-#pragma unroll
-        for (int jj = 0; jj < 32; ++jj) {
-          const int j = j0 + 2 * jj;
-          pk[jj] = pack_bf16(j <= row ? x[2 * jj] : 0.f, j + 1 <= row ? x[2 * jj + 1] : 0.f);
-        }
-        __syncwarp();
-        tmem_st16u(tmem + lane_base + TM_SC + j0, *reinterpret_cast<uint32_t(*)[16]>(pk));
-        tmem_st16u(tmem + lane_base + TM_SC + j0 + 16, *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
-        tmem_wait_st();
-      }
-      tc_fence_before();
-      mbar_arrive(bar_math);
-      if (math_sync_or(s_abort != 0)) break;
-      // (D) token row i = row: O = gamma^(i+1) O_acc, bf16 O * w, and the
-      //     partial sum of O^2 of this warp's 64 values.  The bf16 row (128
-      //     bytes) goes to a 128-byte-swizzled staging box in the bf16(S^T)
-      //     region, free until the next chunk's (A), and one thread stores
-      //     both boxes [128 tok x 64 v] with TMA (rows past T are clipped by
-      //     the tensor map); direct stores only for reversed rows.
-      ok = mbar_wait(bar_o, c & 1);
-      if (!ok) s_abort = 1;
-      if (math_sync_or(s_abort != 0)) break;
-      tc_fence_after();
-      float x[64];
-      __syncwarp();
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        tmem_ld16(tmem + lane_base + TM_O + half * 64 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(bar_ofree);  // O is in registers: the next chunk's MMAs may overwrite it
-      {
-        const float f = exp2f((float)(row + 1) * lg);
-        const size_t r = (size_t)b * p.T + t0 + row;
+        tc_fence_before();
+        mbar_arrive(bar_ofree);  // O is in registers: chunk c's O = Q S may overwrite it
         const float *w = wsl + half * 64;
-        uint8_t *box = sm + SOP_OFF + (2 * half + 1) * SLICE;  // K slices 1 and 3 of bf16(S^T)
-        uint4 *dst = nullptr;
-        if (p.out_reverse && row < L)
-          dst = reinterpret_cast<uint4 *>(p.out + ((size_t)b * p.T + (p.T - 1 - (t0 + row))) * (p.ldo ? p.ldo : d) +
-                                          h * DH + slice * VS + half * 64);
         float ss = 0.f;
 #pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16) {
-          float y[8];
+        for (int jj = 0; jj < 32; ++jj) {
+          const float o0 = x[2 * jj] * fo, o1 = x[2 * jj + 1] * fo;
+          ss = fmaf(o0, o0, ss);
+          ss = fmaf(o1, o1, ss);
+          ob[jj] = pack_bf16(o0 * w[2 * jj], o1 * w[2 * jj + 1]);
+        }
+        if (p.sumsq && row < Lp)
+          p.sumsq[((size_t)b * p.T + tp + row) * (p.H * PARTS) + h * PARTS + slice * 2 + half] = ss;
+      }
+      if (cur) {
+        // (B) V' = diag(gamma^-(j+1)) V in place
+        bool ok = mbar_wait(bar_v, c & 1);
+        if (!ok) s_abort = 1;
+        if (ok) {
+#pragma unroll 2
+          for (int i = mt; i < 2 * SLICE / 16; i += MATH_THREADS) {
+            const int off = i * 16;
+            const int j = (off % SLICE) / 128;  // token row of this 16-byte chunk
+            const float sc = exp2f(-(float)(j + 1) * lg);
+            uint4 raw = *reinterpret_cast<const uint4 *>(sm + V_OFF + off);
+            __nv_bfloat162 *e = reinterpret_cast<__nv_bfloat162 *>(&raw);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const float o = x[8 * c16 + u] * f;
-            ss = fmaf(o, o, ss);
-            y[u] = o * w[8 * c16 + u];
-          }
-          const uint4 v16 = make_uint4(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]), pack_bf16(y[4], y[5]),
-                                       pack_bf16(y[6], y[7]));
-          if (p.out_reverse) {
-            if (dst) dst[c16] = v16;
-          } else {
-            *reinterpret_cast<uint4 *>(box + sw128(row, c16)) = v16;
+            for (int u = 0; u < 4; ++u) {
+              float2 f = __bfloat1622float2(e[u]);
+              e[u] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+            }
+            *reinterpret_cast<uint4 *>(sm + V_OFF + off) = raw;
           }
         }
-        if (p.sumsq && row < L) p.sumsq[r * (p.H * PARTS) + h * PARTS + slice * 2 + half] = ss;
+        fence_proxy_async_smem();  // V' (generic stores) before the MMAs that read it
+        mbar_arrive(bar_vs);
+        // (C) P = bf16(Q K^T masked to j <= i), written back into the scores'
+        //     columns: this warp's 64 columns j become 32 packed columns at
+        //     TM_SC + 64 * half, inside the range it read
+        ok = ok && mbar_wait(bar_sc, c & 1);
+        if (!ok) s_abort = 1;
+        if (ok) {
+          tc_fence_after();
+          const int j0 = half * 64;
+          float x[64];
+          __syncwarp();
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            tmem_ld16(tmem + lane_base + TM_SC + j0 + 16 * u, *reinterpret_cast<float(*)[16]>(x + 16 * u));
+          tmem_wait_ld();
+          uint32_t pk[32];
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int j = j0 + 2 * jj;
+            pk[jj] = pack_bf16(j <= row ? x[2 * jj] : 0.f, j + 1 <= row ? x[2 * jj + 1] : 0.f);
+          }
+          __syncwarp();
+          tmem_st16u(tmem + lane_base + TM_SC + j0, *reinterpret_cast<uint32_t(*)[16]>(pk));
+          tmem_st16u(tmem + lane_base + TM_SC + j0 + 16, *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        mbar_arrive(bar_math);
+        if (math_sync_or(s_abort != 0)) break;
       }
-      if (!p.out_reverse) {
-        fence_proxy_async_smem();  // staged rows before the TMA stores read them
-        math_sync();
-        if (mt == 0) {
-          const int col = h * DH + slice * VS;
-          tma_store_3d(&tm_out, sm + SOP_OFF + SLICE, col, t0, b);
-          tma_store_3d(&tm_out, sm + SOP_OFF + 3 * SLICE, col + 64, t0, b);
-          bulk_commit();
+      if (prev) {
+        // (D2) chunk c-1's rows (128 bytes each) to a 128-byte-swizzled
+        //      staging box in K slices 1 and 3 of the bf16(S^T) region - free
+        //      once chunk c's O = Q S retired, which the scores (waited in
+        //      (C)) follow - and one thread stores both boxes [128 tok x 64 v]
+        //      with TMA (rows past T are clipped by the tensor map); rows
+        //      written back to front (the backward's reversed passes) are
+        //      stored directly
+        const int tp = tb + (c - 1) * C;
+        const int Lp = min(C, te - tp);
+        if (p.out_reverse) {
+          if (row < Lp) {
+            uint4 *dst = reinterpret_cast<uint4 *>(p.out + ((size_t)b * p.T + (p.T - 1 - (tp + row))) *
+                                                               (p.ldo ? p.ldo : d) +
+                                                   h * DH + slice * VS + half * 64);
+#pragma unroll
+            for (int c16 = 0; c16 < 8; ++c16)
+              dst[c16] = make_uint4(ob[4 * c16], ob[4 * c16 + 1], ob[4 * c16 + 2], ob[4 * c16 + 3]);
+          }
+        } else {
+          // after the last chunk no read-back waited for chunk c-2's stores
+          if (!cur && c > 1) {
+            if (mt == 0) bulk_wait_read<0>();
+            math_sync();
+          }
+          uint8_t *box = sm + SOP_OFF + (2 * half + 1) * SLICE;
+#pragma unroll
+          for (int c16 = 0; c16 < 8; ++c16)
+            *reinterpret_cast<uint4 *>(box + sw128(row, c16)) =
+                make_uint4(ob[4 * c16], ob[4 * c16 + 1], ob[4 * c16 + 2], ob[4 * c16 + 3]);
+          fence_proxy_async_smem();  // staged rows before the TMA stores read them
+          math_sync();
+          if (mt == 0) {
+            const int col = h * DH + slice * VS;
+            tma_store_3d(&tm_out, sm + SOP_OFF + SLICE, col, tp, b);
+            tma_store_3d(&tm_out, sm + SOP_OFF + 3 * SLICE, col + 64, tp, b);
+            bulk_commit();
+          }
         }
       }
     }
@@ -981,6 +1031,7 @@ __global__ void __launch_bounds__(320, 1)
     const bool write_state = p.state_out && s == p.nseg - 1;
     if (!aborted && nch > 0) {
       bool ok = mbar_wait(bar_upd, (nch - 1) & 1);  // last MMAs retired before TMEM is read or freed
+      if (ok) ok = mbar_wait(bar_o, (nch - 1) & 1);
       if (!ok) s_abort = 1;
       if (!math_sync_or(s_abort != 0) && write_state) {
         tc_fence_after();
