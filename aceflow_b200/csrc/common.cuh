@@ -242,6 +242,13 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Programmatic dependent launch: wait until the previous kernel on the
 // stream has completed and its memory is visible (a no-op otherwise).
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel on the stream (a programmatic dependent launch) be
+// scheduled once every CTA of this grid has executed it: its CTAs then take
+// free SMs and run their prologue (barriers, TMEM, the first weight tiles)
+// while this grid works, and block in griddep_wait() before touching this
+// grid's results.  Issued after a CTA's own TMEM allocation, so a dependent
+// CTA never holds TMEM that a CTA of this grid still has to allocate.
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ float4 ld_stream(const float4 *p) {
   float4 v;

@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(256)
   constexpr int D4 = 256 * V4;
   __shared__ float red[8];
   const size_t off = (size_t)blockIdx.x * D4;
+  griddep_launch();
   griddep_wait();  // x comes from the kernel before (programmatic launch)
   float4 a[V4];
   float ss = 0.f;

@@ -521,6 +521,7 @@ __global__ void __launch_bounds__(kMaxGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_launch();
 
   auto stage_a = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES; };
   auto stage_b = [&](int i) { return smem + (size_t)i * C::STAGE_BYTES + C::A_BYTES; };

@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(THREADS)
   const float *qh = q + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
   const float *kh = k + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
   const float *vh = v + (size_t)b * qs + (size_t)hl * hg.qkv_head_stride;
+  griddep_launch();
   griddep_wait();  // q, k, v come from the kernel before (programmatic launch)
   for (int i = threadIdx.x; i < DH; i += THREADS) {
     float kk = kh[i], qq = qh[i];
