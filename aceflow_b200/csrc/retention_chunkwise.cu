@@ -737,17 +737,6 @@ __global__ void __launch_bounds__(320, 1)
         for (int vb = 0; vb < 2; ++vb)
           tma_load_3d(sm + V_OFF + vb * SLICE, &tm, bar_v, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
         v_issued = c + 1;
-        // the next chunk's tiles into L2 while this chunk computes, so its
-        // loads (issued only once this chunk's MMAs free the buffers) hit L2
-        if (c + 1 < nch) {
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            tma_prefetch_3d(&tm, h * DH + kk * 64, t0 + C, b);
-            tma_prefetch_3d(&tm, d + h * DH + kk * 64, t0 + C, b);
-          }
-#pragma unroll
-          for (int vb = 0; vb < 2; ++vb) tma_prefetch_3d(&tm, 2 * d + h * DH + slice * VS + vb * 64, t0 + C, b);
-        }
       }
       // loads still in flight land before the CTA may exit
       if (q_issued > 0 && !mbar_wait(bar_q, (q_issued - 1) & 1)) fail();
@@ -858,6 +847,11 @@ __global__ void __launch_bounds__(320, 1)
     }
     const float gC = exp2f((float)C * lg);
     const float fo = exp2f((float)(row + 1) * lg);  // the output row's decay gamma^(i+1)
+    // (B) scales the 16-byte chunks mt + 256 r of the two V boxes: token row
+    // j = mt / 8 + 32 (r % 4), the same rows every chunk
+    float vsc[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) vsc[r] = exp2f(-(float)(mt / 8 + 32 * r + 1) * lg);
     uint32_t ob[32];                                // chunk c-1's bf16 output row, (D1) -> (D2)
 #pragma unroll 1
     for (int c = 0; c <= nch; ++c) {
@@ -938,19 +932,19 @@ __global__ void __launch_bounds__(320, 1)
         bool ok = mbar_wait(bar_v, c & 1);
         if (!ok) s_abort = 1;
         if (ok) {
-#pragma unroll 2
-          for (int i = mt; i < 2 * SLICE / 16; i += MATH_THREADS) {
-            const int off = i * 16;
-            const int j = (off % SLICE) / 128;  // token row of this 16-byte chunk
-            const float sc = exp2f(-(float)(j + 1) * lg);
-            uint4 raw = *reinterpret_cast<const uint4 *>(sm + V_OFF + off);
-            __nv_bfloat162 *e = reinterpret_cast<__nv_bfloat162 *>(&raw);
+          static_assert(2 * SLICE / 16 == 8 * MATH_THREADS, "eight 16-byte chunks per math thread");
+          uint4 raw[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) raw[r] = *reinterpret_cast<const uint4 *>(sm + V_OFF + (mt + r * MATH_THREADS) * 16);
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            __nv_bfloat162 *e = reinterpret_cast<__nv_bfloat162 *>(&raw[r]);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               float2 f = __bfloat1622float2(e[u]);
-              e[u] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+              e[u] = __floats2bfloat162_rn(f.x * vsc[r & 3], f.y * vsc[r & 3]);
             }
-            *reinterpret_cast<uint4 *>(sm + V_OFF + off) = raw;
+            *reinterpret_cast<uint4 *>(sm + V_OFF + (mt + r * MATH_THREADS) * 16) = raw[r];
           }
         }
         fence_proxy_async_smem();  // V' (generic stores) before the MMAs that read it
