@@ -375,7 +375,7 @@ def run_ours(args):
             sec = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier1, max1, 0.0,
                                 args.longctx_chunk)
         else:
-            sec = bench_stack(dev, peaks)
+            sec = bench_stack(dev, peaks, steps=args.stack_steps)
         if rank == 0:
             print(json.dumps({"section": args.only, **sec}), flush=True)
         if world > 1:
@@ -526,7 +526,7 @@ def run_ours(args):
         line["longctx"] = bench_longctx(dev, world, rank, args.longctx_passes, peaks, barrier, max_over_ranks,
                                         sub_cpu, args.longctx_chunk)
     if world == 1 and not args.no_stack:
-        line["stack"] = bench_stack(dev, peaks, sub_cpu)
+        line["stack"] = bench_stack(dev, peaks, sub_cpu, steps=args.stack_steps)
     if world == 1 and rank == 0 and not args.no_cpu:
         nthreads = host_threads()
         v, steps, b, el = cpu_decode_sample(args.cpu_seconds, nthreads)
@@ -822,7 +822,7 @@ def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_
 STACK = dict(L=24, d=2048, H=8, f=5632, V=32000, B=64, P=512, n=256)
 
 
-def bench_stack(dev, peaks, cpu_seconds=0.0):
+def bench_stack(dev, peaks, cpu_seconds=0.0, steps=None):
     import torch
 
     from aceflow_b200 import _lib
@@ -830,6 +830,7 @@ def bench_stack(dev, peaks, cpu_seconds=0.0):
 
     c = STACK
     L, d, H, f, V, B, P, n = (c[k] for k in ("L", "d", "H", "f", "V", "B", "P", "n"))
+    n = steps or n
     g = torch.Generator(device=dev).manual_seed(11)
     eng = AceEngine(L, d, H, (0.02 * torch.randn(V, d, generator=g, device=dev)), batch=B,
                     device=str(dev), weight_dtype="bfloat16", eps=1e-6)
@@ -883,6 +884,8 @@ def main():
     ap.add_argument("--only", choices=["prefill", "longctx", "stack"], default=None,
                     help="run one secondary workload alone and print its object (profiling)")
     ap.add_argument("--longctx-passes", type=int, default=5)
+    ap.add_argument("--stack-steps", type=int, default=None,
+                    help="greedy steps of the stack workload (default: the workload's 256; fewer for profiling)")
     ap.add_argument("--sub-cpu-seconds", type=float, default=4.0,
                     help="seconds of each CPU baseline of the prefill, long-context and stack workloads (N=1)")
     ap.add_argument("--chunk", type=int, default=None,
