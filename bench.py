@@ -126,7 +126,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- checker
-def msr_rows_reference(x, w_qkv, w_o, ret_w, num_heads, eps, row_sets, col_range=None):
+def msr_rows_reference(x, w_qkv, w_o, ret_w, num_heads, eps, row_sets, col_range=None, w_g=None):
     """Rows of the MultiScaleRetention forward (aceflow/nn/retention.py:44-66:
     parallel retention, RMSNorm over d_model, W_o) for ONE stream, in float64
     on x's device, used as the parity checker of the large workloads.
@@ -134,7 +134,9 @@ def msr_rows_reference(x, w_qkv, w_o, ret_w, num_heads, eps, row_sets, col_range
     x [T, d] (any float dtype: the values the kernels read), w_qkv [3d, d]
     (rows q | k | v), w_o [d, d], ret_w [d]; row_sets: (r0, r1) ranges of
     output rows; col_range (c0, c1): only those output columns (the W_o rows a
-    head-sharded rank owns).  The state before row r0 is formed in one
+    head-sharded rank owns); w_g [d, d]: the opt-in gated layer instead -
+    swish(x W_g^T) * GroupNorm per head (mean 0, variance 1, eps inside the
+    square root) replaces the RMSNorm (RetNet's gate, no reference counterpart).  The state before row r0 is formed in one
     product, S = K[:r0]^T diag(gamma^(r0-1-t)) V[:r0], so the cost does not
     grow with the number of chunks.  Returns one [r1 - r0, cols] tensor per set."""
     import torch
@@ -168,7 +170,13 @@ def msr_rows_reference(x, w_qkv, w_o, ret_w, num_heads, eps, row_sets, col_range
                 inter = (g ** (i + 1))[:, None] * (q[:, sl] @ S)
             D = torch.where(dist >= 0, g ** dist.clamp(min=0), torch.zeros((), dtype=f64, device=dev))
             o[:, sl] = inter + ((q[:, sl] @ K[r0:r1, sl].T) * D) @ V[r0:r1, sl]
-        o = o / torch.sqrt((o * o).mean(-1, keepdim=True) + eps) * rw
+        if w_g is None:
+            o = o / torch.sqrt((o * o).mean(-1, keepdim=True) + eps) * rw
+        else:
+            oh = o.view(R, H, dh)
+            oh = (oh - oh.mean(-1, keepdim=True)) / torch.sqrt(oh.var(-1, unbiased=False, keepdim=True) + eps)
+            gg = x64[r0:r1] @ w_g.to(f64).T
+            o = gg / (1.0 + torch.exp(-gg)) * oh.reshape(R, d)
         outs.append(o @ Wo.T)
     return outs
 
@@ -687,6 +695,82 @@ def bench_prefill(dev, passes, peaks, cpu_seconds=0.0, chunk=None):
                 "retention_core": {"kernel": kernel, "ms": core_ms, "achieved": core_tfl, "unit": "TFLOP/s",
                                    "frac": core_tfl / peaks["bf16_tflops"], "algorithmic_flop": intra + inter}}
 
+    def measure_backward():
+        """Backward of the chunkwise core (three retention passes, 128-token
+        chunks): dQ, dK, dV for an upstream gradient, no initial state.  FLOPs:
+        three cores by the workload's definition.  Checked on stream 0, heads 0
+        and H-1: dQ on rows 0-127 (no earlier rows) and dK, dV on rows
+        T-128..T-1 (no later rows), in float64."""
+        dout = torch.randn(B * T, d, generator=g, device=dev).bfloat16()
+        for _ in range(2):
+            dq = cuda_ops.retention_chunkwise_backward_bf16(qkv, dout, B, T, H, gamma)[0]
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(passes):
+            dq = cuda_ops.retention_chunkwise_backward_bf16(qkv, dout, B, T, H, gamma)[0]
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / passes
+        _lib.check_device(dev.index or 0)
+        f64 = torch.float64
+        got, ref = [], []
+        i = torch.arange(128, device=dev, dtype=f64)
+        for h in (0, H - 1):
+            gm = 1.0 - 2.0 ** (-5 - h)
+            D = torch.where(i[:, None] >= i[None, :], gm ** (i[:, None] - i[None, :]).clamp(min=0),
+                            torch.zeros((), dtype=f64, device=dev))  # D[t, s]
+            cols = slice(h * 256, (h + 1) * 256)
+            for r0, which in ((0, "dq"), (T - 128, "dkdv")):
+                Q, K, V = (qkv[r0:r0 + 128, part * d:(part + 1) * d][:, cols].to(f64) for part in range(3))
+                dO = dout[r0:r0 + 128, cols].to(f64)
+                if which == "dq":
+                    ref.append(((dO @ V.T) * D) @ K)
+                    got.append(dq[r0:r0 + 128, cols])
+                else:
+                    ref.append(((dO @ V.T) * D).T @ Q)
+                    got.append(dq[r0:r0 + 128, d:2 * d][:, cols])
+                    ref.append(((Q @ K.T) * D).T @ dO)
+                    got.append(dq[r0:r0 + 128, 2 * d:3 * d][:, cols])
+        err = max(max_rel_err([gt], [rf]) for gt, rf in zip(got, ref))
+        flop = 3 * (intra + inter)
+        tfl = flop / (ms / 1e3) / 1e12
+        return {"workload": f"backward of the chunkwise core, B={B}, T={T}, {H} heads, 128-token chunks "
+                            "(dQ, dK, dV; af_retention_chunkwise_backward_bf16)",
+                "ms": ms, "value": B * T / (ms / 1e3), "unit": "tok/s", "max_rel_err": err, "tolerance": 2e-2,
+                "parity_rows": "stream 0, heads 0 and 7: dQ rows 0-127, dK and dV rows 3968-4095, against float64",
+                "roofline": {"bound": "tensor", "achieved": tfl, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": tfl / peaks["bf16_tflops"], "algorithmic_flop": flop}}
+
+    def measure_gated():
+        """The opt-in gated layer (swish gate, per-head GroupNorm) over the same
+        prompt at chunk 64: five projections and the core."""
+        wg = (0.02 * torch.randn(d, d, generator=g, device=dev)).bfloat16()
+        out = None
+        for _ in range(2):
+            out, _ = cuda_ops.msr_gated_prefill_bf16(x, w_qkv, wg, ws[3], None, None, gamma, EPS,
+                                                     out_dtype=torch.bfloat16, want_state=False)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(passes):
+            out, _ = cuda_ops.msr_gated_prefill_bf16(x, w_qkv, wg, ws[3], None, None, gamma, EPS,
+                                                     out_dtype=torch.bfloat16, want_state=False)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / passes
+        _lib.check_device(dev.index or 0)
+        gref = msr_rows_reference(x[0], w_qkv, ws[3], rw, H, EPS, rows, w_g=wg)
+        err = max_rel_err([out[0, r0:r1] for r0, r1 in rows], gref)
+        flop = total + 2 * B * T * d * d
+        tfl = flop / (ms / 1e3) / 1e12
+        return {"workload": f"gated MultiScaleRetention prefill (opt-in; no reference counterpart), B={B}, T={T}, "
+                            f"d_model={d}, {H} heads, chunk 64 (af_msr_gated_prefill_bf16)",
+                "ms_per_pass": ms, "value": B * T / (ms / 1e3), "unit": "tok/s", "max_rel_err": err,
+                "tolerance": 2e-2, "parity_rows": "stream 0, rows 0-127 and 3968-4095, against float64",
+                "roofline": {"bound": "tensor", "achieved": tfl, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": tfl / peaks["bf16_tflops"], "algorithmic_flop": flop}}
+
     main = measure(c["C"] if chunk is None else chunk)
     alt = measure(128) if chunk is None else None
     m.prefill_chunk = 64
@@ -703,6 +787,8 @@ def bench_prefill(dev, passes, peaks, cpu_seconds=0.0, chunk=None):
     }
     if alt is not None:
         res["chunk128"] = alt
+        res["backward"] = measure_backward()
+        res["gated"] = measure_gated()
     if cpu_seconds > 0:
         v, toks, b, el, thr = cpu_prefill_sample(cpu_seconds, host_threads(), d, H, B)
         res["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": thr, "kind": "port",
