@@ -181,6 +181,35 @@ def msr_rows_reference(x, w_qkv, w_o, ret_w, num_heads, eps, row_sets, col_range
     return outs
 
 
+def backward_blocks_reference(qkv, dout, d, heads, T, n=128):
+    """float64 gradients of the retention core (o_t = sum_{s<=t}
+    gamma^(t-s) (q_t . k_s) v_s, aceflow/nn/retention.py:51-61) for one stream
+    of T rows with no initial state, on blocks that need no other rows: dQ of
+    rows [0, n) (no earlier rows) and dK, dV of rows [T-n, T) (no later rows),
+    for each head in `heads`.  qkv [T, 3d] (q | k | v), dout [T, d], any float
+    dtype, head_dim 256.  Returns {(h, "dq" | "dk" | "dv"): [n, 256]}."""
+    import torch
+
+    f64 = torch.float64
+    dev = qkv.device
+    i = torch.arange(n, device=dev, dtype=f64)
+    res = {}
+    for h in heads:
+        gm = 1.0 - 2.0 ** (-5 - h)
+        D = torch.where(i[:, None] >= i[None, :], gm ** (i[:, None] - i[None, :]).clamp(min=0),
+                        torch.zeros((), dtype=f64, device=dev))  # D[t, s]
+        cols = slice(h * 256, (h + 1) * 256)
+        for r0, which in ((0, "dq"), (T - n, "dkdv")):
+            Q, K, V = (qkv[r0:r0 + n, part * d:(part + 1) * d][:, cols].to(f64) for part in range(3))
+            dO = dout[r0:r0 + n, cols].to(f64)
+            if which == "dq":
+                res[(h, "dq")] = ((dO @ V.T) * D) @ K
+            else:
+                res[(h, "dk")] = ((dO @ V.T) * D).T @ Q
+                res[(h, "dv")] = ((Q @ K.T) * D).T @ dO
+    return res
+
+
 def max_rel_err(got_sets, ref_sets) -> float:
     """max |got - ref| / max |ref| over all sets (the parity metric)."""
     num = max(float((g.double() - r).abs().max()) for g, r in zip(got_sets, ref_sets))
@@ -713,25 +742,13 @@ def bench_prefill(dev, passes, peaks, cpu_seconds=0.0, chunk=None):
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / passes
         _lib.check_device(dev.index or 0)
-        f64 = torch.float64
+        blocks = backward_blocks_reference(qkv[:T], dout[:T], d, (0, H - 1), T)
         got, ref = [], []
-        i = torch.arange(128, device=dev, dtype=f64)
-        for h in (0, H - 1):
-            gm = 1.0 - 2.0 ** (-5 - h)
-            D = torch.where(i[:, None] >= i[None, :], gm ** (i[:, None] - i[None, :]).clamp(min=0),
-                            torch.zeros((), dtype=f64, device=dev))  # D[t, s]
-            cols = slice(h * 256, (h + 1) * 256)
-            for r0, which in ((0, "dq"), (T - 128, "dkdv")):
-                Q, K, V = (qkv[r0:r0 + 128, part * d:(part + 1) * d][:, cols].to(f64) for part in range(3))
-                dO = dout[r0:r0 + 128, cols].to(f64)
-                if which == "dq":
-                    ref.append(((dO @ V.T) * D) @ K)
-                    got.append(dq[r0:r0 + 128, cols])
-                else:
-                    ref.append(((dO @ V.T) * D).T @ Q)
-                    got.append(dq[r0:r0 + 128, d:2 * d][:, cols])
-                    ref.append(((Q @ K.T) * D).T @ dO)
-                    got.append(dq[r0:r0 + 128, 2 * d:3 * d][:, cols])
+        for (hh, which), rf in blocks.items():
+            part = {"dq": 0, "dk": 1, "dv": 2}[which]
+            r0 = 0 if which == "dq" else T - 128
+            got.append(dq[r0:r0 + 128, part * d + hh * 256:part * d + (hh + 1) * 256])
+            ref.append(rf)
         err = max(max_rel_err([gt], [rf]) for gt, rf in zip(got, ref))
         flop = 3 * (intra + inter)
         tfl = flop / (ms / 1e3) / 1e12
