@@ -105,6 +105,7 @@ int af_cuda_init(int device, af_ctx **out) {
     if (v >= 1 && v <= 4) ctx->gemm_producers = v;
   }
   if (const char *env = getenv("AF_COMM_RESERVE_SMS")) ctx->comm_reserve_sms = atoi(env);
+  if (const char *env = getenv("AF_SHARDED_ROW_SLABS")) ctx->sharded_row_slabs = atoi(env);
   ctx->magic = kCtxMagic;
   *out = ctx;
   return AF_OK;
@@ -171,6 +172,9 @@ int af_set_option(af_ctx *ctx, const char *name, int64_t value) {
   } else if (!strcmp(name, "sharded_head_groups")) {
     if (value < 0 || value > af_ctx::kMaxSlices) return af::fail(AF_ERR_ARG, "af_set_option: sharded_head_groups 0..8");
     ctx->sharded_head_groups = (int)value;
+  } else if (!strcmp(name, "sharded_row_slabs")) {
+    if (value < 0 || value > af_ctx::kMaxSlices) return af::fail(AF_ERR_ARG, "af_set_option: sharded_row_slabs 0..8");
+    ctx->sharded_row_slabs = (int)value;
   } else if (!strcmp(name, "comm_reserve_sms")) {
     if (value < 0 || value > 64) return af::fail(AF_ERR_ARG, "af_set_option: comm_reserve_sms 0..64");
     ctx->comm_reserve_sms = (int)value;

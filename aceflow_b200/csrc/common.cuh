@@ -45,6 +45,9 @@ struct af_ctx {
   int decode_transposed = 15;
   int sharded_head_groups = 0;  // head groups pipelined against the all-gather (0: auto; 1: one gather)
   int comm_reserve_sms = 16;    // SMs the overlapped kernels leave to NCCL
+  // row slabs af_prefill_head_sharded_rows pipelines (slab j+1's all-to-all
+  // under slab j's W_o GEMM); 0: auto, 1: one exchange
+  int sharded_row_slabs = 0;
   // Phase marks (af_set_option "phase_marks"): timing events the prefill
   // entry points record on the caller's stream at their phase boundaries,
   // read back by af_phase_times.

@@ -1770,9 +1770,10 @@ int dispatch(af_ctx *ctx, const void *A, const void *A2, int64_t lda, const void
     else if (a.trans && ep.atomic) ep.staged = kStageTransAdd;
     else if (!a.trans && ep.atomic && !ep.residual && !a.bias) ep.staged = kStageAdd;
   }
-  // large bf16 GEMMs (two or more waves of tiles): persistent kernel
-  if (MODE == kBF16 && splits == 1 && !a.trans && !a.pair && (bn == 256 || bn == 128) && tiles(bn) >= 2 * sms &&
-      !getenv("AF_GEMM_NO_PERSIST")) {
+  // large bf16 GEMMs (two or more waves of tiles), or a CTA cap (SMs left to
+  // a concurrent kernel): persistent kernel
+  if (MODE == kBF16 && splits == 1 && !a.trans && !a.pair && (bn == 256 || bn == 128) &&
+      (tiles(bn) >= 2 * sms || a.max_ctas > 0) && !getenv("AF_GEMM_NO_PERSIST")) {
     if (bn == 256 && ctx->gemm_pair && !a.max_ctas && M >= 256 && N >= 256)
       return launch_pair(ctx, A, lda, B, ldb, M, N, K, ep, st, fn);
     if (bn == 256) return launch_persistent<256>(ctx, A, lda, B, ldb, M, N, K, ep, st, fn, a.max_ctas);

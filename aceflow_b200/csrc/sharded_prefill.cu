@@ -304,10 +304,24 @@ int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t 
     return lo >= N ? 0 : (N - lo < c ? N - lo : c);
   };
   const int64_t nr = rows_of(r);
+  // Row slabs: each rank's row block is exchanged in S slabs of cs rows; the
+  // W_o GEMM of slab j runs while slab j+1 crosses NVLink on a side stream
+  // (the GEMM leaves comm_reserve_sms SMs to NCCL).  0 = auto = 1: measured on
+  // B200 at T=65536, d=4096, 2 GPUs, 3.79 ms per pass with one exchange
+  // against 3.84 with 2 slabs and 3.89 with 4 (the exchange and the GEMM
+  // slow each other more than the overlap saves).
+  int S = ctx->sharded_row_slabs > 0 ? ctx->sharded_row_slabs : 1;
+  if (g == 1) S = 1;
+  if (S > af_ctx::kMaxSlices) S = af_ctx::kMaxSlices;
+  const int64_t cs = (c + S - 1) / S;
+  auto slab_rows = [&](int s, int j) -> int64_t {  // rows of slab j of rank s's block
+    const int64_t ns = rows_of(s), lo = (int64_t)j * cs;
+    return lo >= ns ? 0 : (ns - lo < cs ? ns - lo : cs);
+  };
   const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, Hl, ctx->chunk_segments, C);
   const size_t qkv_b = align256((size_t)N * 3 * dl * 2), o_b = align256((size_t)N * dl * 2),
-               ss_b = align256((size_t)N * P * 4), ro_b = align256((size_t)g * c * dl * 2),
-               rss_b = align256((size_t)g * c * P * 4), seg_b = align256(af::chunkwise_seg_state_bytes(B, Hl, pl));
+               ss_b = align256((size_t)N * P * 4), ro_b = align256((size_t)S * g * cs * dl * 2),
+               rss_b = align256((size_t)S * g * cs * P * 4), seg_b = align256(af::chunkwise_seg_state_bytes(B, Hl, pl));
   void *ws = nullptr;
   int rc = af::workspace(ctx, qkv_b + o_b + ss_b + ro_b + rss_b + seg_b, &ws, fn);
   if (rc) return rc;
@@ -315,10 +329,10 @@ int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t 
   uint16_t *qkv = reinterpret_cast<uint16_t *>(base);
   uint16_t *o_loc = reinterpret_cast<uint16_t *>(base + qkv_b);                      // [N][dl]
   float *ss_loc = reinterpret_cast<float *>(base + qkv_b + o_b);                     // [N][P]
-  uint16_t *o_rows = reinterpret_cast<uint16_t *>(base + qkv_b + o_b + ss_b);        // [g][nr][dl]
-  float *ss_rows = reinterpret_cast<float *>(base + qkv_b + o_b + ss_b + ro_b);      // [g][nr][P]
+  uint16_t *o_rows = reinterpret_cast<uint16_t *>(base + qkv_b + o_b + ss_b);        // [S][g][slab rows][dl]
+  float *ss_rows = reinterpret_cast<float *>(base + qkv_b + o_b + ss_b + ro_b);      // [S][g][slab rows][P]
   float *seg = seg_b ? reinterpret_cast<float *>(base + qkv_b + o_b + ss_b + ro_b + rss_b) : nullptr;
-  cudaStream_t st = af::stream_of(stream);
+  cudaStream_t st = af::stream_of(stream), xs = S > 1 ? ctx->side[0] : st;
   ncclComm_t comm = static_cast<ncclComm_t>(ctx->comm);
   af::mark_begin(ctx, st);
   // 1. projections of this rank's heads
@@ -335,46 +349,61 @@ int af_prefill_head_sharded_rows(af_ctx *ctx, const uint16_t *x, const uint16_t 
   rc = af::retention_chunkwise_bf16(ctx, qkv, B, T, Hl, gamma + (size_t)r * Hl, state_in, state_out, o_loc,
                                     ret_norm_w + (size_t)r * dl, ss_loc, pl, seg, st, fn);
   if (rc) return rc;
-  // 3. all-to-all: rows of rank s go to rank s; rank p's heads land in block p
-  if (g > 1) {
-    ncclResult_t nr_ = g_nccl.group_start();
-    for (int s2 = 0; s2 < g && nr_ == ncclSuccess; ++s2) {
-      const int64_t ns = rows_of(s2);
-      if (ns > 0) {
-        nr_ = g_nccl.send(o_loc + (size_t)s2 * c * dl, (size_t)ns * dl, ncclBfloat16, s2, comm, st);
-        if (nr_ == ncclSuccess)
-          nr_ = g_nccl.send(ss_loc + (size_t)s2 * c * P, (size_t)ns * P, ncclFloat32, s2, comm, st);
-      }
-      if (nr > 0 && nr_ == ncclSuccess) {
-        nr_ = g_nccl.recv(o_rows + (size_t)s2 * nr * dl, (size_t)nr * dl, ncclBfloat16, s2, comm, st);
-        if (nr_ == ncclSuccess)
-          nr_ = g_nccl.recv(ss_rows + (size_t)s2 * nr * P, (size_t)nr * P, ncclFloat32, s2, comm, st);
-      }
-    }
-    const ncclResult_t ne = g_nccl.group_end();
-    if (nr_ == ncclSuccess) nr_ = ne;
-    if (nr_ != ncclSuccess) return nccl_fail(nr_, fn, "ncclSend/ncclRecv");
-  } else {
-    AF_CUDA(cudaMemcpyAsync(o_rows, o_loc, (size_t)N * dl * 2, cudaMemcpyDeviceToDevice, st), fn);
-    AF_CUDA(cudaMemcpyAsync(ss_rows, ss_loc, (size_t)N * P * 4, cudaMemcpyDeviceToDevice, st), fn);
+  if (S > 1) {
+    AF_CUDA(cudaEventRecord(ctx->ev_fork, st), fn);
+    AF_CUDA(cudaStreamWaitEvent(xs, ctx->ev_fork, 0), fn);
   }
-  af::mark(ctx, "alltoall", st);
-  if (nr == 0) return AF_OK;
-  // 4. this rank's rows of the output: RMSNorm row scale from all heads' partial
-  //    sums, then the full W_o
-  af::GemmEpilogueArgs e;
-  e.out = out;
-  e.ldo = d;
-  e.out_bf16 = out_bf16;
-  e.a_kblock = dl;
-  e.row_parts = ss_rows;
-  e.nparts = g * P;
-  e.parts_block = P;
-  e.inv_d = 1.0f / (float)d;
-  e.eps = eps;
-  rc = af::tc_gemm(ctx, o_rows, dl, w_o, d, (int)nr, d, d, false, e, st, fn);
-  if (rc) return rc;
-  af::mark(ctx, "w_o", st);
+  // 3. all-to-all, slab by slab: slab j of rank s's rows goes to rank s;
+  //    rank p's heads land in block p of the slab's buffer [g][slab rows]
+  for (int j = 0; j < S; ++j) {
+    const int64_t nrj = slab_rows(r, j);
+    uint16_t *o_slab = o_rows + (size_t)j * g * cs * dl;
+    float *ss_slab = ss_rows + (size_t)j * g * cs * P;
+    if (g > 1) {
+      ncclResult_t nr_ = g_nccl.group_start();
+      for (int s2 = 0; s2 < g && nr_ == ncclSuccess; ++s2) {
+        const int64_t ns = slab_rows(s2, j), row0 = (int64_t)s2 * c + (int64_t)j * cs;
+        if (ns > 0) {
+          nr_ = g_nccl.send(o_loc + (size_t)row0 * dl, (size_t)ns * dl, ncclBfloat16, s2, comm, xs);
+          if (nr_ == ncclSuccess) nr_ = g_nccl.send(ss_loc + (size_t)row0 * P, (size_t)ns * P, ncclFloat32, s2, comm, xs);
+        }
+        if (nrj > 0 && nr_ == ncclSuccess) {
+          nr_ = g_nccl.recv(o_slab + (size_t)s2 * nrj * dl, (size_t)nrj * dl, ncclBfloat16, s2, comm, xs);
+          if (nr_ == ncclSuccess)
+            nr_ = g_nccl.recv(ss_slab + (size_t)s2 * nrj * P, (size_t)nrj * P, ncclFloat32, s2, comm, xs);
+        }
+      }
+      const ncclResult_t ne = g_nccl.group_end();
+      if (nr_ == ncclSuccess) nr_ = ne;
+      if (nr_ != ncclSuccess) return nccl_fail(nr_, fn, "ncclSend/ncclRecv");
+      if (S > 1) AF_CUDA(cudaEventRecord(ctx->ev_a[j], xs), fn);
+    } else {
+      AF_CUDA(cudaMemcpyAsync(o_slab, o_loc, (size_t)N * dl * 2, cudaMemcpyDeviceToDevice, st), fn);
+      AF_CUDA(cudaMemcpyAsync(ss_slab, ss_loc, (size_t)N * P * 4, cudaMemcpyDeviceToDevice, st), fn);
+    }
+  }
+  if (S == 1) af::mark(ctx, "alltoall", st);
+  // 4. this rank's rows of the output, slab by slab: RMSNorm row scale from
+  //    all heads' partial sums, then the full W_o
+  for (int j = 0; j < S; ++j) {
+    const int64_t nrj = slab_rows(r, j);
+    if (S > 1) AF_CUDA(cudaStreamWaitEvent(st, ctx->ev_a[j], 0), fn);  // every slab, so st joins the side stream
+    if (nrj == 0) continue;
+    af::GemmEpilogueArgs e;
+    e.out = static_cast<uint8_t *>(out) + (size_t)j * cs * d * (out_bf16 ? 2 : 4);
+    e.ldo = d;
+    e.out_bf16 = out_bf16;
+    e.a_kblock = dl;
+    e.row_parts = ss_rows + (size_t)j * g * cs * P;
+    e.nparts = g * P;
+    e.parts_block = P;
+    e.inv_d = 1.0f / (float)d;
+    e.eps = eps;
+    e.max_ctas = j + 1 < S ? ctx->num_sms - ctx->comm_reserve_sms : 0;  // SMs left to the next slab's exchange
+    rc = af::tc_gemm(ctx, o_rows + (size_t)j * g * cs * dl, dl, w_o, d, (int)nrj, d, d, false, e, st, fn);
+    if (rc) return rc;
+  }
+  af::mark(ctx, S > 1 ? "alltoall_w_o" : "w_o", st);
   return AF_OK;
 }
 

@@ -80,6 +80,9 @@ int af_selftest_bounded_wait(af_ctx *ctx, int64_t limit_ns, af_stream_t stream);
  *                              (default 0: enough to put one CTA on every SM; 1: none)
  *   "sharded_head_groups" 0..8 head groups af_prefill_head_sharded pipelines against
  *                              its all-gather (default 0 = 1: measured not to pay)
+ *   "sharded_row_slabs"  0..8  row slabs af_prefill_head_sharded_rows pipelines, the all-to-all of
+ *                              slab j+1 under the W_o GEMM of slab j (default 0 = 1:
+ *                              measured not to pay at 2 GPUs)
  *   "comm_reserve_sms"   0..64 SMs the overlapped kernels leave to the collective (default 16)
  *   "decode_transposed"  0..15 bf16 af_decoder_layer_decode projections computed as
  *                              W . x^T (bit 0 QKV, 1 W_o, 2 gate/up, 3 down; default 15)

@@ -1,5 +1,7 @@
 """Head-sharded prefill on 2 GPUs (one process per GPU; NCCL all-gather, or
-all-to-all for the row layout, in the C library) against the float64 layer.
+all-to-all for the row layout, in the C library) against the float64 layer,
+with one exchange and pipelined (two head groups of the all-gather, three
+row slabs of the all-to-all, the last one ragged).
 Skipped with fewer than 2 GPUs.  NVLS is switched off for the test's NCCL
 communicators."""
 import os
@@ -30,7 +32,10 @@ def _worker(rank, world, port, B, T, H, outdir, groups, layout="columns"):
     import torch.distributed as dist
 
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    os.environ["AF_SHARDED_HEAD_GROUPS"] = str(groups)  # read when the context is created
+    # read when the context is created: head groups of the all-gather layout,
+    # row slabs of the all-to-all layout
+    os.environ["AF_SHARDED_HEAD_GROUPS"] = str(groups)
+    os.environ["AF_SHARDED_ROW_SLABS"] = str(groups)
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=__import__("datetime").timedelta(seconds=120))
@@ -56,7 +61,7 @@ def _worker(rank, world, port, B, T, H, outdir, groups, layout="columns"):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-@pytest.mark.parametrize("groups,layout", [(0, "columns"), (2, "columns"), (0, "rows")])
+@pytest.mark.parametrize("groups,layout", [(0, "columns"), (2, "columns"), (0, "rows"), (3, "rows")])
 def test_head_sharded_prefill_two_gpus(groups, layout):
     import socket
 
