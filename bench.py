@@ -40,6 +40,14 @@ EPS = 1e-6
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
+def sustained(achieved, peaks):
+    """The fraction of the sustained bf16 peak (a matmul loop of seconds, at
+    the 1 kW power cap), the denominator for work timed inside a long step
+    (the long-context passes, the stack prefill); {} without that figure."""
+    ps = peaks.get("bf16_tflops_sustained")
+    return {"peak_sustained": ps, "frac_sustained": achieved / ps} if ps else {}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -906,7 +914,7 @@ def bench_longctx(dev, world, rank, passes, peaks, barrier, max_over_ranks, cpu_
         "phases_ms_rank0": rows["phases_ms_rank0"],
         "roofline": {"bound": "tensor", "achieved": rows["achieved_per_gpu"], "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "per": "GPU", "frac": rows["frac_per_gpu"], "algorithmic_flop": total,
-                     "alltoall_bytes_per_rank": a2a_bytes},
+                     "alltoall_bytes_per_rank": a2a_bytes, **sustained(rows["achieved_per_gpu"], peaks)},
         "allgather": {"parallelism": f"head-sharded x{world}; one NCCL all-gather of the head outputs before W_o, "
                                      "each rank owns output columns",
                       "bytes_received_per_rank": gather_bytes,
@@ -959,6 +967,7 @@ def bench_stack(dev, peaks, cpu_seconds=0.0, steps=None):
         "prefill_tok_s": B * P / (t["prefill_ms"] / 1e3), "prefill_ms": t["prefill_ms"],
         "prefill_tflops": pre_flop / (t["prefill_ms"] / 1e3) / 1e12,
         "prefill_frac": pre_flop / (t["prefill_ms"] / 1e3) / 1e12 / peaks["bf16_tflops"],
+        "prefill_frac_sustained": sustained(pre_flop / (t["prefill_ms"] / 1e3) / 1e12, peaks).get("frac_sustained"),
         "decode_tok_s": B / (dec_ms / 1e3), "decode_ms_per_step": dec_ms,
         "decode_hbm_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
         "decode_frac": dec_bytes / (dec_ms / 1e3) / 1e9 / peaks["hbm_gbs"],
