@@ -145,6 +145,17 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
                              const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
                              const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn, int64_t ldo = 0,
                              bool out_reverse = false);
+// The same with q, k and v read from separate bf16 row-major buffers: row
+// b*T + t of each, head h's columns h*256.. after the pointer, rows ldq / ldk
+// / ldv elements apart (16-byte aligned pointers, strides multiples of 8).
+struct ChunkSrc {
+  const void *q, *k, *v;
+  int64_t ldq, ldk, ldv;
+};
+int retention_chunkwise_bf16(af_ctx *ctx, const ChunkSrc &src, int B, int T, int H, const float *gamma,
+                             const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
+                             const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn, int64_t ldo,
+                             bool out_reverse);
 int chunkwise_head_dim();
 // Per-head partial sums of squares per output row for that chunk length.
 int chunkwise_parts(int chunk);

@@ -12,9 +12,10 @@
 //     dS_0 = sum_t gamma^(t+1) q_t^T do_t = gamma * (the final state of the
 //            dV pass, whose keys are q and values do)
 // so the backward runs the tensor-core chunkwise forward kernel (128-token
-// chunks, the state in TMEM) three times on assembled operand buffers
-// [B*T][q' | k' | v'] (bf16), the two reversed passes writing their rows back
-// in forward order through the kernel's reversed output rows.  The reference
+// chunks, the state in TMEM) three times, each pass reading its q', k', v'
+// through separate tensor maps: the dQ pass straight from dO and qkv, the two
+// reversed passes from one time-reversed copy of qkv and dO, writing their
+// rows back in forward order through the kernel's reversed output rows.  The reference
 // has no backward (its trainers are PyTorch-only); the float64 oracle's closed
 // form gradients of the parallel form pin this one.
 #include "common.cuh"
@@ -25,22 +26,16 @@ constexpr int DH = 256;
 
 inline size_t align256(size_t b) { return (b + 255) & ~size_t(255); }
 
-// dst[b*T + t] = (q' | k' | v') with each part taken from src_p (row stride
-// ld_p elements) at row b*T + t, or b*T + T-1-t when `reverse`; 16-byte units.
-__global__ void assemble_qkv_kernel(uint4 *__restrict__ dst, const uint16_t *__restrict__ s0, int64_t ld0,
-                                    const uint16_t *__restrict__ s1, int64_t ld1, const uint16_t *__restrict__ s2,
-                                    int64_t ld2, int B, int T, int d8, int reverse) {
+// dst row b*T + t = src row b*T + T-1-t, rows of `w` 16-byte units
+// (src rows `lds` units apart, dst rows `w` apart).
+__global__ void reverse_rows_kernel(uint4 *__restrict__ dst, const uint4 *__restrict__ src, int64_t lds, int B, int T,
+                                    int w) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t total = (int64_t)B * T * 3 * d8;
-  if (idx >= total) return;
-  const int c = (int)(idx % (3 * d8));
-  const int64_t r = idx / (3 * d8);
-  const int part = c / d8, u = c % d8;
+  if (idx >= (int64_t)B * T * w) return;
+  const int u = (int)(idx % w);
+  const int64_t r = idx / w;
   const int64_t b = r / T, t = r % T;
-  const int64_t rs = b * T + (reverse ? T - 1 - t : t);
-  const uint16_t *src = part == 0 ? s0 : part == 1 ? s1 : s2;
-  const int64_t ld = part == 0 ? ld0 : part == 1 ? ld1 : ld2;
-  dst[idx] = reinterpret_cast<const uint4 *>(src + rs * ld)[u];
+  dst[idx] = src[(b * T + (T - 1 - t)) * lds + u];
 }
 
 // dst[bh][v][k] = src[bh][k][v] (fp32 [DH][DH] blocks), 32 x 32 tiles.
@@ -84,48 +79,48 @@ extern "C" int af_retention_chunkwise_backward_bf16(af_ctx *ctx, const uint16_t 
   const int d = H * DH;
   const int64_t N = (int64_t)B * T;
   const af::ChunkPlan pl = af::chunkwise_plan(ctx->num_sms, B, T, H, ctx->chunk_segments, 128);
-  const size_t buf_b = align256((size_t)N * 3 * d * 2), st_b = state_in ? align256((size_t)B * H * DH * DH * 4) : 0,
+  const size_t rq_b = align256((size_t)N * 3 * d * 2), rd_b = align256((size_t)N * d * 2),
+               st_b = state_in ? align256((size_t)B * H * DH * DH * 4) : 0,
                seg_b = align256(af::chunkwise_seg_state_bytes(B, H, pl));
   void *ws = nullptr;
-  int rc = af::workspace(ctx, buf_b + st_b + seg_b, &ws, fn);
+  int rc = af::workspace(ctx, rq_b + rd_b + st_b + seg_b, &ws, fn);
   if (rc) return rc;
   uint8_t *base = static_cast<uint8_t *>(ws);
-  uint16_t *buf = reinterpret_cast<uint16_t *>(base);
-  float *s0t = state_in ? reinterpret_cast<float *>(base + buf_b) : nullptr;
-  float *seg = seg_b ? reinterpret_cast<float *>(base + buf_b + st_b) : nullptr;
+  uint16_t *rqkv = reinterpret_cast<uint16_t *>(base);         // qkv, each stream's rows in reverse
+  uint16_t *rdout = reinterpret_cast<uint16_t *>(base + rq_b);  // dout likewise
+  float *s0t = state_in ? reinterpret_cast<float *>(base + rq_b + rd_b) : nullptr;
+  float *seg = seg_b ? reinterpret_cast<float *>(base + rq_b + rd_b + st_b) : nullptr;
   cudaStream_t st = af::stream_of(stream);
-  const uint16_t *Q = qkv, *K = qkv + d, *V = qkv + 2 * d;
+  const uint16_t *K = qkv + d, *V = qkv + 2 * d;
   const int64_t ld = 3 * (int64_t)d;
-  const int d8 = d / 8;
-  const int64_t total = N * 3 * d8;
-  const unsigned blocks = (unsigned)((total + 255) / 256);
-  auto assemble = [&](const uint16_t *a, int64_t la, const uint16_t *b2, int64_t lb, const uint16_t *c, int64_t lc,
-                      int reverse) {
-    assemble_qkv_kernel<<<blocks, 256, 0, st>>>(reinterpret_cast<uint4 *>(buf), a, la, b2, lb, c, lc, B, T, d8,
-                                                 reverse);
-    return af::launched(ctx, fn);
-  };
   af::mark_begin(ctx, st);
   // dQ = Retention(dO, V, K) from S_0^T, written to dqkv[:, 0:d]
   if (state_in) {
     transpose_states_kernel<<<dim3(DH / 32, DH / 32, B * H), dim3(32, 8), 0, st>>>(state_in, s0t);
     if ((rc = af::launched(ctx, fn))) return rc;
   }
-  if ((rc = assemble(dout, d, V, ld, K, ld, 0))) return rc;
-  rc = af::retention_chunkwise_bf16(ctx, buf, B, T, H, gamma, s0t, nullptr, dqkv, nullptr, nullptr, pl, seg, st, fn,
-                                    ld, false);
+  rc = af::retention_chunkwise_bf16(ctx, af::ChunkSrc{dout, V, K, d, ld, ld}, B, T, H, gamma, s0t, nullptr, dqkv,
+                                    nullptr, nullptr, pl, seg, st, fn, ld, false);
   if (rc) return rc;
   af::mark(ctx, "dq", st);
+  // the time-reversed operands of the other two passes
+  for (int part = 0; part < 2; ++part) {
+    const int w = (part == 0 ? 3 * d : d) / 8;
+    const int64_t n = N * w;
+    reverse_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        reinterpret_cast<uint4 *>(part == 0 ? rqkv : rdout), reinterpret_cast<const uint4 *>(part == 0 ? qkv : dout),
+        w, B, T, w);
+    if ((rc = af::launched(ctx, fn))) return rc;
+  }
+  const uint16_t *rQ = rqkv, *rK = rqkv + d, *rV = rqkv + 2 * d;
   // dK = reversed Retention(V, dO, Q), rows written back in forward order to dqkv[:, d:2d]
-  if ((rc = assemble(V, ld, dout, d, Q, ld, 1))) return rc;
-  rc = af::retention_chunkwise_bf16(ctx, buf, B, T, H, gamma, nullptr, nullptr, dqkv + d, nullptr, nullptr, pl, seg,
-                                    st, fn, ld, true);
+  rc = af::retention_chunkwise_bf16(ctx, af::ChunkSrc{rV, rdout, rQ, ld, d, ld}, B, T, H, gamma, nullptr, nullptr,
+                                    dqkv + d, nullptr, nullptr, pl, seg, st, fn, ld, true);
   if (rc) return rc;
   af::mark(ctx, "dk", st);
   // dV = reversed Retention(K, Q, dO) to dqkv[:, 2d:3d]; its final state * gamma = dS_0
-  if ((rc = assemble(K, ld, Q, ld, dout, d, 1))) return rc;
-  rc = af::retention_chunkwise_bf16(ctx, buf, B, T, H, gamma, nullptr, dstate_in, dqkv + 2 * d, nullptr, nullptr, pl,
-                                    seg, st, fn, ld, true);
+  rc = af::retention_chunkwise_bf16(ctx, af::ChunkSrc{rK, rQ, rdout, ld, ld, d}, B, T, H, gamma, nullptr, dstate_in,
+                                    dqkv + 2 * d, nullptr, nullptr, pl, seg, st, fn, ld, true);
   if (rc) return rc;
   if (dstate_in) {
     const int64_t n4 = (int64_t)B * H * DH * DH / 4;

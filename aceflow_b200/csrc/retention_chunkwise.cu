@@ -164,7 +164,8 @@ __device__ __forceinline__ bool math_sync_or(bool pred) {
 
 template <bool STATE_ONLY>
 __global__ void __launch_bounds__(320, 1)
-    retention_chunkwise_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_out,
+    retention_chunkwise_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                               const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tm_out,
                                ChunkParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -184,7 +185,6 @@ __global__ void __launch_bounds__(320, 1)
   const int bsh = blockIdx.x / NSL;   // ((b * nseg) + s) * H + h
   const int h = bsh % p.H, bs = bsh / p.H;
   const int b = bs / p.nseg, s = bs % p.nseg;
-  const int d = p.H * DH;
   const int tb = s * p.seg_len;                      // first token of this segment
   const int te = min(p.T, tb + p.seg_len);           // one past its last token
   const int nch = (te - tb + C - 1) / C;
@@ -206,7 +206,9 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&bar_ups[i], 1);
     }
     fence_barrier_init();
-    prefetch_tmap(&tm);
+    if (!STATE_ONLY) prefetch_tmap(&tmq);
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
     if (!STATE_ONLY) prefetch_tmap(&tm_out);
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + C + 1) {
@@ -240,10 +242,10 @@ __global__ void __launch_bounds__(320, 1)
         mbar_arrive_expect_tx(&bar_lds[sl], K_BYTES + V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          tma_load_3d(base + kk * BOX, &tm, &bar_lds[sl], d + h * DH + kk * 64, t0, b);
+          tma_load_3d(base + kk * BOX, &tmk, &bar_lds[sl], h * DH + kk * 64, t0, b);
 #pragma unroll
         for (int vb = 0; vb < 2; ++vb)
-          tma_load_3d(base + K_BYTES + vb * BOX, &tm, &bar_lds[sl], 2 * d + h * DH + slice * VS + vb * 64, t0, b);
+          tma_load_3d(base + K_BYTES + vb * BOX, &tmv, &bar_lds[sl], h * DH + slice * VS + vb * 64, t0, b);
         issued = c + 1;
       }
       for (int c = issued - SO_NS < 0 ? 0 : issued - SO_NS; c < issued; ++c)  // loads still in flight
@@ -256,21 +258,21 @@ __global__ void __launch_bounds__(320, 1)
         mbar_arrive_expect_tx(bar_load, (STATE_ONLY ? 0 : Q_BYTES) + K_BYTES + V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          if (!STATE_ONLY) tma_load_3d(sm + Q_OFF + kk * BOX, &tm, bar_load, h * DH + kk * 64, t0, b);
-          tma_load_3d(sm + K_OFF + kk * BOX, &tm, bar_load, d + h * DH + kk * 64, t0, b);
+          if (!STATE_ONLY) tma_load_3d(sm + Q_OFF + kk * BOX, &tmq, bar_load, h * DH + kk * 64, t0, b);
+          tma_load_3d(sm + K_OFF + kk * BOX, &tmk, bar_load, h * DH + kk * 64, t0, b);
         }
 #pragma unroll
         for (int vb = 0; vb < 2; ++vb)
-          tma_load_3d(sm + V_OFF + vb * BOX, &tm, bar_load, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
+          tma_load_3d(sm + V_OFF + vb * BOX, &tmv, bar_load, h * DH + slice * VS + vb * 64, t0, b);
         issued = c + 1;
         if (c + 1 < nch) {  // the next chunk's tiles into L2 (its loads wait for this chunk's update)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            if (!STATE_ONLY) tma_prefetch_3d(&tm, h * DH + kk * 64, t0 + C, b);
-            tma_prefetch_3d(&tm, d + h * DH + kk * 64, t0 + C, b);
+            if (!STATE_ONLY) tma_prefetch_3d(&tmq, h * DH + kk * 64, t0 + C, b);
+            tma_prefetch_3d(&tmk, h * DH + kk * 64, t0 + C, b);
           }
 #pragma unroll
-          for (int vb = 0; vb < 2; ++vb) tma_prefetch_3d(&tm, 2 * d + h * DH + slice * VS + vb * 64, t0 + C, b);
+          for (int vb = 0; vb < 2; ++vb) tma_prefetch_3d(&tmv, h * DH + slice * VS + vb * 64, t0 + C, b);
         }
       }
       if (issued > 0 && !mbar_wait(bar_load, (issued - 1) & 1)) fail();  // last load landed
@@ -650,7 +652,8 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
 }
 
 __global__ void __launch_bounds__(320, 1)
-    retention_chunk128_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tm_out,
+    retention_chunk128_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                              const __grid_constant__ CUtensorMap tmv, const __grid_constant__ CUtensorMap tm_out,
                               ChunkParams p) {
   // this kernel's layout (shadows the 64-token kernel's constants)
   constexpr int C = c128::C, SLICE = c128::SLICE, Q_OFF = c128::Q_OFF, K_OFF = c128::K_OFF, V_OFF = c128::V_OFF,
@@ -692,7 +695,9 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(bar_math, MATH_THREADS);
     mbar_init(bar_ofree, MATH_THREADS);
     fence_barrier_init();
-    prefetch_tmap(&tm);
+    prefetch_tmap(&tmq);
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
     if (!p.out_reverse) prefetch_tmap(&tm_out);
   }
   if (threadIdx.x >= 64 && threadIdx.x < 64 + VS) {
@@ -724,18 +729,18 @@ __global__ void __launch_bounds__(320, 1)
         if (c > 0 && !mbar_wait(bar_sc, (c - 1) & 1)) { fail(); break; }
         mbar_arrive_expect_tx(bar_q, 4 * SLICE);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + Q_OFF + kk * SLICE, &tm, bar_q, h * DH + kk * 64, t0, b);
+        for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + Q_OFF + kk * SLICE, &tmq, bar_q, h * DH + kk * 64, t0, b);
         q_issued = c + 1;
         if (c > 0 && !mbar_wait(bar_upd, (c - 1) & 1)) { fail(); break; }
         mbar_arrive_expect_tx(bar_k, 4 * SLICE);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + K_OFF + kk * SLICE, &tm, bar_k, d + h * DH + kk * 64, t0, b);
+        for (int kk = 0; kk < 4; ++kk) tma_load_3d(sm + K_OFF + kk * SLICE, &tmk, bar_k, h * DH + kk * 64, t0, b);
         k_issued = c + 1;
         if (c > 0 && !mbar_wait(bar_o, (c - 1) & 1)) { fail(); break; }
         mbar_arrive_expect_tx(bar_v, 2 * SLICE);
 #pragma unroll
         for (int vb = 0; vb < 2; ++vb)
-          tma_load_3d(sm + V_OFF + vb * SLICE, &tm, bar_v, 2 * d + h * DH + slice * VS + vb * 64, t0, b);
+          tma_load_3d(sm + V_OFF + vb * SLICE, &tmv, bar_v, h * DH + slice * VS + vb * 64, t0, b);
         v_issued = c + 1;
       }
       // loads still in flight land before the CTA may exit
@@ -1075,23 +1080,25 @@ __global__ void seg_scan_kernel(float4 *__restrict__ states, const float4 *__res
 PFN_cuTensorMapEncodeTiled_v12000 g_encode3 = nullptr;
 
 template <bool SO>
-int launch_chunkwise(af_ctx *ctx, const CUtensorMap &tm, const CUtensorMap &tm_out, const ChunkParams &p,
+int launch_chunkwise(af_ctx *ctx, const CUtensorMap (&tms)[3], const CUtensorMap &tm_out, const ChunkParams &p,
                      cudaStream_t st, const char *fn) {
   static std::atomic<unsigned long long> attr_devices{0};
   if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(retention_chunkwise_kernel<SO>), SMEM,
                               attr_devices, fn))
     return arc;
-  retention_chunkwise_kernel<SO><<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, SMEM, st>>>(tm, tm_out, p);
+  retention_chunkwise_kernel<SO><<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, SMEM, st>>>(tms[0], tms[1], tms[2],
+                                                                                            tm_out, p);
   return af::launched(ctx, fn);
 }
 
-int launch_chunk128(af_ctx *ctx, const CUtensorMap &tm, const CUtensorMap &tm_out, const ChunkParams &p,
+int launch_chunk128(af_ctx *ctx, const CUtensorMap (&tms)[3], const CUtensorMap &tm_out, const ChunkParams &p,
                     cudaStream_t st, const char *fn) {
   static std::atomic<unsigned long long> attr_devices{0};
   if (int arc = af::smem_attr(ctx, reinterpret_cast<const void *>(retention_chunk128_kernel), c128::SMEM,
                               attr_devices, fn))
     return arc;
-  retention_chunk128_kernel<<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, c128::SMEM, st>>>(tm, tm_out, p);
+  retention_chunk128_kernel<<<p.B * p.nseg * p.H * NSL, 64 + MATH_THREADS, c128::SMEM, st>>>(tms[0], tms[1], tms[2],
+                                                                                              tm_out, p);
   return af::launched(ctx, fn);
 }
 
@@ -1118,16 +1125,31 @@ size_t chunkwise_seg_state_bytes(int B, int H, const ChunkPlan &pl) {
   return pl.nseg > 1 ? (size_t)B * pl.nseg * H * DH * DH * sizeof(float) : 0;
 }
 
-static int encode_qkv_map(CUtensorMap *tm, const void *qkv, int B, int T, int d, int rows, const char *fn) {
-  cuuint64_t dims[3] = {(cuuint64_t)(3 * d), (cuuint64_t)T, (cuuint64_t)B};
-  cuuint64_t strides[2] = {(cuuint64_t)3 * d * 2, (cuuint64_t)T * 3 * d * 2};
+// One operand of the chunkwise kernels: `d` columns (every head) of a bf16
+// [B][T][ld] buffer starting at `base`, [64 col x rows tok] 128-byte-swizzled
+// boxes.
+static int encode_operand_map(CUtensorMap *tm, const void *base, int64_t ld, int B, int T, int d, int rows,
+                              const char *fn) {
+  if (!aligned16(base) || ld % 8 != 0 || ld < d)
+    return fail(AF_ERR_ARG, "%s: q/k/v operands need 16-byte aligned bases and row strides (>= d) of 8k elements",
+                fn);
+  cuuint64_t dims[3] = {(cuuint64_t)d, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)T * ld * 2};
   cuuint32_t box[3] = {64, (cuuint32_t)rows, 1};
   cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = g_encode3(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(qkv), dims, strides, box, es,
+  CUresult r = g_encode3(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, es,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(AF_ERR_ARG, "%s: tensor map encode failed (%d)", fn, (int)r);
   return AF_OK;
+}
+
+static int encode_operand_maps(CUtensorMap (&tms)[3], const ChunkSrc &src, int B, int T, int d, int rows,
+                               const char *fn) {
+  int rc = encode_operand_map(&tms[0], src.q, src.ldq, B, T, d, rows, fn);
+  if (!rc) rc = encode_operand_map(&tms[1], src.k, src.ldk, B, T, d, rows, fn);
+  if (!rc) rc = encode_operand_map(&tms[2], src.v, src.ldv, B, T, d, rows, fn);
+  return rc;
 }
 
 // Chunkwise retention over a bf16 QKV buffer [B*T][3d] (row stride 3d) in
@@ -1136,6 +1158,17 @@ static int encode_qkv_map(CUtensorMap *tm, const void *qkv, int B, int T, int d,
 // pass always walks 64-token tiles (it only accumulates K^T V); segment
 // boundaries are multiples of pl.chunk.
 int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, const float *gamma,
+                             const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
+                             const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn, int64_t ldo,
+                             bool out_reverse) {
+  const int d = H * DH;
+  const uint16_t *b16 = static_cast<const uint16_t *>(qkv);
+  const ChunkSrc src{b16, b16 + d, b16 + 2 * d, 3 * (int64_t)d, 3 * (int64_t)d, 3 * (int64_t)d};
+  return retention_chunkwise_bf16(ctx, src, B, T, H, gamma, state_in, state_out, out, norm_w, sumsq, pl, seg_states,
+                                  st, fn, ldo, out_reverse);
+}
+
+int retention_chunkwise_bf16(af_ctx *ctx, const ChunkSrc &src, int B, int T, int H, const float *gamma,
                              const float *state_in, float *state_out, void *out, const float *norm_w, float *sumsq,
                              const ChunkPlan &pl, float *seg_states, cudaStream_t st, const char *fn, int64_t ldo,
                              bool out_reverse) {
@@ -1156,15 +1189,15 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   const int d = H * DH;
   if ((ldo != 0 || out_reverse) && (pl.chunk != c128::C || (ldo != 0 && (ldo < d || ldo % 8 != 0))))
     return fail(AF_ERR_ARG, "%s: an output stride or reversed rows need chunk 128 and a stride >= d, 8 | stride", fn);
-  CUtensorMap tm, tm128;
-  int rc = encode_qkv_map(&tm, qkv, B, T, d, C, fn);
+  CUtensorMap tm[3], tm128[3];
+  int rc = encode_operand_maps(tm, src, B, T, d, C, fn);
   if (rc) return rc;
   const bool big = pl.chunk == c128::C;
-  if (big && (rc = encode_qkv_map(&tm128, qkv, B, T, d, c128::C, fn))) return rc;
+  if (big && (rc = encode_operand_maps(tm128, src, B, T, d, c128::C, fn))) return rc;
   // output [B][T][d] bf16 for the TMA stores: [64 tok x 64 v] plain boxes
   // (64-token kernel) or [128 tok x 64 v] 128-byte-swizzled boxes with row
   // stride ldo (128-token kernel); the T edge is clipped per stream
-  CUtensorMap tm_out = tm;
+  CUtensorMap tm_out = tm[0];
   if (big && !out_reverse) {
     const cuuint64_t ld = (cuuint64_t)(ldo ? ldo : d);
     cuuint64_t odims[3] = {(cuuint64_t)d, (cuuint64_t)T, (cuuint64_t)B};
@@ -1204,7 +1237,7 @@ int retention_chunkwise_bf16(af_ctx *ctx, const void *qkv, int B, int T, int H, 
   ps.out = nullptr;
   ps.norm_w = nullptr;
   ps.sumsq = nullptr;
-  rc = launch_chunkwise<true>(ctx, tm, tm, ps, st, fn);
+  rc = launch_chunkwise<true>(ctx, tm, tm[0], ps, st, fn);
   if (rc) return rc;
   mark(ctx, "chunk_state", st);
   // 2. states before each segment
