@@ -15,8 +15,7 @@
 //
 // The array's name is a host-side stand-in in host code, not a device
 // address: the device address is looked up with cudaGetSymbolAddress once
-// per device, with that device current, by the first call made on it (so
-// that first call should come before any stream capture).  The cached
+// per device, with that device current, by the first call made on it.  The cached
 // address belongs to the device's current primary context: after
 // cudaDeviceReset the entry point must not be called again in the process.
 //

@@ -248,9 +248,8 @@ int af_msr_decode_step_f32_split(af_ctx *ctx, const float *x, float *state, cons
  * held on every GPU that loads the library until the process exits; larger
  * sizes return AF_ERR_ARG.  The call allocates nothing and takes no context;
  * the current device is used.  The first call on a device looks up the
- * array's device address (and loads the library's kernels there): make it
- * before any stream capture, and do not call the entry point again after
- * cudaDeviceReset.  All calls on a device share the array and keep the last
+ * array's device address (and loads the library's kernels there, a one-time
+ * set-up); do not call the entry point again after cudaDeviceReset.  All calls on a device share the array and keep the last
  * call's contents, so calls that overlap on the GPU (concurrent streams)
  * race: at most one call in flight per device.  A bounded-wait timeout in its
  * kernels is reported by af_check_device(NULL, ...). */
