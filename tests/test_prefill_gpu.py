@@ -35,7 +35,7 @@ def _core_ref(qkv, B, T, H, state0=None):
 
 @pytest.mark.parametrize("chunk", [64, 128])
 @pytest.mark.parametrize("B,T,H", [(1, 64, 1), (2, 100, 2), (1, 257, 2), (3, 200, 1), (1, 1000, 8), (2, 128, 1),
-                                   (1, 129, 1)])
+                                   (1, 129, 1), (1, 1, 1), (2, 3, 2)])
 def test_chunkwise_core_matches_oracle(dev, B, T, H, chunk):
     from aceflow_b200 import _lib, cuda_ops
 
@@ -293,7 +293,8 @@ def test_module_forward_chunkwise_needs_head_dim_256(dev):
 
 # ---- backward of the chunkwise form ---------------------------------------
 @pytest.mark.parametrize("B,T,H,with_state", [(1, 128, 1, False), (2, 200, 2, True), (1, 777, 2, True),
-                                              (3, 65, 1, False), (1, 300, 1, False), (2, 300, 1, True)])
+                                              (3, 65, 1, False), (1, 300, 1, False), (2, 300, 1, True),
+                                              (1, 1, 1, True), (2, 3, 2, False)])
 def test_chunkwise_backward_matches_float64_gradients(dev, B, T, H, with_state):
     """dQ, dK, dV and the initial state's gradient of the chunkwise kernel
     (three passes of the 128-token kernel, two over reversed time) against
